@@ -1,0 +1,352 @@
+"""Benchmark of the ShadowKV sparse decode step on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config config1]
+
+One step = one decode step of one layer through ``ShadowAttention.decode_fused``:
+RoPE of the new q/k, append, landmark scoring + top-k + reuse diff, zero-copy
+fetch of the missed value chunks from pinned host memory (copy stream),
+tensor-core key reconstruction + RoPE (main stream), split-K GQA attention.
+The workload is BASELINE configs[1] (Llama-3-8B shape, 122880 context, budget
+2048, rank 160) with seeded synthetic inputs; every rank runs its own
+sequence (batch-sharded weak scaling, no collective on the data path).
+
+Printed: one JSON line (rank 0).  ``value`` = tokens/s of the whole job with
+inputs resident (device-timed, CUDA events, max over ranks); ``e2e`` = the
+same through the host API with the query/new-token inputs copied from pinned
+host memory and the attention output copied back every step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+HBM_FALLBACK_GBS = 6650.0
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d.get("hbm_gbs", HBM_FALLBACK_GBS)), "measured"
+    return HBM_FALLBACK_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if len(r) > 2 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) > 2 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in self.rows:
+            for i, n in enumerate(names):
+                if len(r) > 5 + i and r[5 + i].lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(self.rows)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+
+
+def link_bandwidth_gbs(nbytes=256 << 20, reps=5) -> float:
+    """Measured host->device bandwidth (copy engine, pinned source), best of reps."""
+    src = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    best = 0.0
+    for _ in range(reps + 1):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        dst.copy_(src, non_blocking=True)
+        e.record()
+        e.synchronize()
+        best = max(best, nbytes / (s.elapsed_time(e) * 1e-3) / 1e9)
+    del src, dst
+    return best
+
+
+def algorithmic_bytes(cache, misses: int, seq_len: int):
+    """HBM and host-link bytes of one step (per-unit figures of the roofline model)."""
+    B, H, D = cache.batch_size, cache.num_key_value_heads, cache.head_dim
+    L = cache.k_landmark.shape[-2]
+    r = cache.rank
+    hbm = (B * H * L * D * 2               # landmark scan
+           + misses * 8 * r * 2            # gathered U rows
+           + B * H * D * r * 2             # SV^T
+           + misses * 2048 * 2             # K and V slot writes
+           + B * H * seq_len * D * 2 * 2)  # attention K + V read
+    host = misses * 2048
+    return hbm, host
+
+
+def run_b200(args, world, rank, local):
+    from shadowkv_b200 import workload
+    from shadowkv_b200._lib import device_errors
+
+    if os.environ.get("SKV_NUMA_BIND", "1") == "1":
+        from shadowkv_b200 import numa
+        numa.bind_to_gpu_numa(local)
+    cfg = workload.CONFIGS[args.config]
+    cfg.gen_len = max(cfg.gen_len, args.steps + args.warmup + 16)
+    torch.manual_seed(0)
+    layer = workload.Layer(cfg, device=f"cuda:{local}", seed=1000 + rank)
+    cache, attn = layer.cache, layer.attn
+    B, Hq, Hkv = cfg.batch, cfg.q_heads, cfg.kv_heads
+    n = args.steps + args.warmup
+    inputs = [layer.next_inputs() for _ in range(n)]
+    pos0 = cfg.ctx
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")  # > 126 MB L2
+
+    hbm_peak, peak_kind = measured_peaks()
+    link_peak = link_bandwidth_gbs()
+    main = torch.cuda.current_stream()
+    copy_stream = cache.copy_stream
+
+    def step(i, ev=None):
+        q, k, v = inputs[i]
+        pos = torch.full((B, 1), pos0 + i, dtype=torch.int64, device="cuda")
+        kv = cache
+        qr, kr = attn.apply_rotary_pos_emb(q, k, pos)
+        kv.update_kv_cache(kr, v, 0)
+        kv.select_fused(0, qr, attn.cos_sin_cache)
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_stream(main)
+            if ev is not None:
+                ev[0].record(copy_stream)
+            kv.fetch_values_fused(0, copy_stream)
+            if ev is not None:
+                ev[1].record(copy_stream)
+        kv.reconstruct_keys_fused(0, attn.cos_sin_cache)
+        main.wait_stream(copy_stream)
+        seq_len = kv.sparse_end + kv._gen_offset(0)
+        out = kv.attention(0, qr, seq_len)
+        return out, seq_len
+
+    # warm-up
+    for i in range(args.warmup):
+        step(i)
+    barrier(world)
+
+    per_step, fetch_ms, misses_all, seqlens = [], [], [], []
+    with ClockSampler(local) as clk:
+        barrier(world)
+        t_wall = time.perf_counter()
+        for i in range(args.warmup, n):
+            flush.zero_()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            fe = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            s.record(main)
+            out, seq_len = step(i, fe)
+            e.record(main)
+            e.synchronize()
+            per_step.append(s.elapsed_time(e))
+            fetch_ms.append(fe[0].elapsed_time(fe[1]))
+            misses_all.append(int(cache._fused_ws.miss_count.sum().item()))
+            seqlens.append(seq_len)
+        barrier(world)
+        t_wall = time.perf_counter() - t_wall
+    errs = device_errors()[0]
+    if errs:
+        raise RuntimeError(f"{errs} device-side index errors during the benchmark")
+
+    ms_step = sum(per_step) / len(per_step)
+    ms_step_max = max_over_ranks(ms_step, world)
+    tokens = B * world
+    value = tokens / (ms_step_max / 1e3)
+    misses = statistics.mean(misses_all)
+    hit_rate = 1.0 - misses / (B * Hkv * cache.select_sets)
+    hbm_b, host_b = algorithmic_bytes(cache, misses, statistics.mean(seqlens))
+    t_roof = max(hbm_b / (hbm_peak * 1e9), host_b / (link_peak * 1e9))
+    fetch_avg = statistics.mean(fetch_ms)
+    link_achieved = host_b / (fetch_avg * 1e-3) / 1e9 if fetch_avg > 0 else 0.0
+
+    # ---- e2e through the host API: inputs from pinned host, output back to pinned host
+    h_in = [tuple(t.cpu().pin_memory() for t in inp) for inp in inputs]
+    h_out = torch.empty(B, Hq, 128, dtype=torch.bfloat16).pin_memory()
+    d_in = [torch.empty_like(t) for t in inputs[0]]
+    e2e_ms = []
+    cache.gen_offset = 0
+    for i in range(args.warmup, n):
+        flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(main)
+        for dt, ht in zip(d_in, h_in[i]):
+            dt.copy_(ht, non_blocking=True)
+        pos = torch.full((B, 1), pos0 + i, dtype=torch.int64, device="cuda")
+        out = attn.decode_fused(d_in[0], d_in[1], d_in[2], pos, 0)
+        h_out.copy_(out.view(B, Hq, 128), non_blocking=True)
+        e.record(main)
+        e.synchronize()
+        e2e_ms.append(s.elapsed_time(e))
+    e2e_step = max_over_ranks(sum(e2e_ms) / len(e2e_ms), world)
+    h2d = sum(t.numel() * t.element_size() for t in h_in[0])
+    d2h = h_out.numel() * h_out.element_size()
+
+    res = {
+        "metric": "sparse-attn decode tokens/s (Llama-3-8B shape, 122k ctx)",
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_step_max,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded; BASELINE configs[1] shapes and distributions)",
+        "config": {"workload": f"{cfg.name}: one decode layer, B={B}/GPU, {Hq}q/{Hkv}kv heads, ctx {cfg.ctx}, "
+                               f"budget {cfg.budget}, rank {cfg.rank}, V in pinned host memory",
+                   "global_batch": B * world, "seq_len": cfg.ctx, "parallelism": f"batch-sharded x{world}",
+                   "l2": "flushed between timed steps (256 MB write)", "hit_rate": hit_rate},
+        "roofline": {"kernel": "fetch_misses_kernel (zero-copy V gather)", "bound": "host_link",
+                     "achieved": link_achieved, "peak": link_peak, "unit": "GB/s",
+                     "frac": link_achieved / link_peak if link_peak else None, "traffic": None,
+                     "peak_kind": "measured in-run: pinned H2D copy-engine bandwidth"},
+        "step_roofline": {"t_roof_us": t_roof * 1e6, "t_step_us": ms_step * 1e3,
+                          "frac": t_roof / (ms_step * 1e-3), "hbm_bytes": hbm_b, "host_bytes": host_b,
+                          "hbm_peak_gbs": hbm_peak, "hbm_peak_kind": peak_kind, "link_peak_gbs": link_peak},
+        "e2e": {"value": tokens / (e2e_step / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": 8 * args.steps,
+        "clocks": clk.summary(),
+        "wall_s": t_wall,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline(layer, inputs, seconds=args.cpu_seconds)
+    return res
+
+
+def cpu_baseline(layer, inputs, seconds=15.0):
+    """The oracle port of the reference's torch-eager decode step, timed on the host cores."""
+    import numpy as np
+    from oracle import shadowkv_oracle as o
+    st = export_state(layer)
+    cores = len(os.sched_getaffinity(0))
+    times = []
+    t_end = time.perf_counter() + seconds
+    i = 0
+    while time.perf_counter() < t_end and i < len(inputs):
+        q = inputs[i][0].float().cpu().numpy()[:, :, 0, :]
+        t0 = time.perf_counter()
+        o.torch_path_decode_step(st, q, st.sparse_end)
+        times.append(time.perf_counter() - t0)
+        i += 1
+    med = statistics.median(times)
+    return {"value": layer.cfg.batch / med, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{len(times)} full config1 decode steps of the numpy port (median)"}
+
+
+def export_state(layer):
+    import numpy as np
+    from oracle import shadowkv_oracle as o
+    c = layer.cache
+    f = lambda t: t.float().cpu().numpy()
+    H, D = c.num_key_value_heads, c.head_dim
+    v_full = f(c.v_cache_cpu[0]).reshape(c.batch_size, H, -1, D)
+    st = o.TorchPathDecodeState(
+        k_landmark=f(c.k_landmark[0]), k_landmark_idx=c.k_landmark_idx[0].cpu().numpy(), U=f(c.U[0]),
+        SV=np.ascontiguousarray(f(c.SV[0]).transpose(0, 1, 3, 2)), v_full=v_full, k_buf=f(c.k_cache_buffer[0]),
+        v_buf=f(c.v_cache_buffer[0]), cos_sin=f(layer.cos_sin), sparse_start=c.sparse_start,
+        sparse_end=c.sparse_end, select_sets=c.select_sets)
+    return st
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", default="config1")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    args = ap.parse_args()
+    world, rank, local = dist_setup()
+    if args.impl == "reference":
+        from oracle import cpu_reference
+        res = cpu_reference.run(args, world, rank)
+    else:
+        res = run_b200(args, world, rank, local)
+    if rank == 0 and res is not None:
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

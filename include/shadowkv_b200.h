@@ -1,0 +1,281 @@
+/*
+ * shadowkv_b200 -- C ABI of the B200 (sm_100a) kernels for ShadowKV's sparse
+ * decode-attention step.
+ *
+ * Conventions
+ *  - Every entry point returns an int status (skv_status).  On failure the
+ *    message of the calling thread's last error is available from
+ *    skv_last_error().  Nothing in the library exits the process.
+ *  - Pointers are plain device pointers, except the `values` argument of the
+ *    V-gather functions, which must be page-locked host memory mapped into
+ *    the device address space (cudaHostAlloc / cudaHostRegister with
+ *    cudaHostRegisterMapped, or torch pin_memory).  That pointer is checked
+ *    with cudaPointerGetAttributes before launch; pageable memory is
+ *    rejected with SKV_ERR_NOT_PINNED.
+ *  - `stream` is a cudaStream_t passed as void* (NULL = legacy default
+ *    stream).  Every launch goes to that stream; no call synchronizes.
+ *  - bf16 arrays are passed as void* (2-byte elements); ids are int64_t or
+ *    int32_t exactly as in the reference binding.
+ *  - Index errors that can only be seen on the device (a chunk id beyond the
+ *    host buffer, a slot beyond the budget) are counted by the kernels into
+ *    a per-device error word and the access is skipped;
+ *    skv_device_errors() reads and clears it.
+ *
+ * The first twelve functions are the reference's Python bindings
+ * (kernels/main.cu:24-37, C++ signatures kernels/functions.h:23-121) with
+ * the same argument order and meaning; the torch::Tensor arguments become
+ * raw pointers.  The skv_decode_* functions are the fused decode path of
+ * this library (no reference counterpart as single calls; they implement
+ * models/kvcache/shadow.py:547-597 and models/attention/shadow.py:22-48).
+ */
+#ifndef SHADOWKV_B200_H
+#define SHADOWKV_B200_H
+
+#include <stdint.h>
+#include <stddef.h>
+
+#if defined(__GNUC__)
+#define SKV_API __attribute__((visibility("default")))
+#else
+#define SKV_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    SKV_OK = 0,
+    SKV_ERR_INVALID_ARGUMENT = 1, /* bad size / null pointer / misaligned pointer */
+    SKV_ERR_UNSUPPORTED = 2,      /* shape outside what the kernels implement */
+    SKV_ERR_CUDA = 3,             /* a CUDA runtime call or launch failed */
+    SKV_ERR_NOT_PINNED = 4,       /* host pointer is not device-accessible */
+} skv_status;
+
+/* Message of the calling thread's last failing call ("" if none). */
+SKV_API const char *skv_last_error(void);
+
+/* Library version (major*10000 + minor*100 + patch). */
+SKV_API int skv_version(void);
+
+/* Read (and clear) the device-side error counter of the current device.
+ * *count = number of skipped out-of-range accesses since the last call,
+ * *first_code = kind of the first one (1 host chunk id, 2 slot, 3 row). */
+SKV_API int skv_device_errors(uint32_t *count, uint32_t *first_code);
+
+/* ---------------------------------------------------------------------
+ * Reuse cache (reference kernels/gather_copy.cu, copy.cuh, map.cuh)
+ * ------------------------------------------------------------------- */
+
+/* Replaces gather_copy (kernels/functions.h:23-25; gather_copy.cu:47-109).
+ * For block bid = b*heads+h and slot i < map_size: the 2048-byte chunk
+ * position_ids[bid*map_size+i] of host region bid*cpu_v_length (bf16
+ * elements) is copied to device region bid*gpu_v_length, slot i. */
+SKV_API int skv_gather_copy(const void *values, void *v_cache_buffer, const int64_t *position_ids,
+                    int batch_size, int heads, int cpu_v_length, int gpu_v_length, int map_size,
+                    void *stream);
+
+/* Replaces gather_copy_d2d_with_offsets (kernels/functions.h:27-35;
+ * gather_copy.cu:112-185).  In-place compaction of cache hits in the K
+ * buffer: slot i < cnts[bid] of region bid*gpu_k_stride + gpu_k_offset gets
+ * the old slot offsets[bid*map_size+i].  gpu_k_length is accepted for
+ * signature parity (it sized the reference's temp buffer). */
+SKV_API int skv_gather_copy_d2d_with_offsets(void *keys, const int32_t *offsets, const int32_t *cnts,
+                                     int batch_size, int heads, int gpu_k_length, int gpu_k_offset,
+                                     int gpu_k_stride, int map_size, void *stream);
+
+/* Replaces reorder_keys_and_compute_offsets (kernels/functions.h:37-42;
+ * gather_copy.cu:189-235; map.cuh:475-516).  cached_pos_ids is in/out:
+ * on entry the cached chunk ids (slot order), on exit the new ids reordered
+ * as hits (sorted by old slot) then misses (sorted by id).  offsets: hit ->
+ * old slot, miss -> chunk id.  cnts: hits per block.  map_size 1..1024. */
+SKV_API int skv_reorder_keys_and_compute_offsets(int64_t *cached_pos_ids, const int64_t *cur_pos_ids,
+                                         int32_t *offsets, int32_t *cnts, int batch_size,
+                                         int heads, int map_size, void *stream);
+
+/* Replaces gather_copy_with_offsets (kernels/functions.h:44-51;
+ * gather_copy.cu:239-324; copy.cuh:438-498).  Slot i < cnts[bid] of region
+ * bid*gpu_v_stride+gpu_v_offset gets old slot offsets[i] (in place);
+ * slot i >= cnts[bid] gets host chunk offsets[i] of region
+ * bid*cpu_v_length.  temp and signals are accepted for signature parity and
+ * are not touched (no inter-CTA signalling is used). */
+SKV_API int skv_gather_copy_with_offsets(const void *values, void *v_cache_buffer, void *temp,
+                                 const int32_t *offsets, const int32_t *cnts, int32_t *signals,
+                                 int batch_size, int heads, int cpu_v_length, int gpu_v_length,
+                                 int gpu_v_offset, int gpu_v_stride, int map_size, void *stream);
+
+/* ---------------------------------------------------------------------
+ * RoPE (reference kernels/rope.cu, rope_new.cu)
+ * All strides are in elements.  Arithmetic is bf16 op by op: each multiply
+ * and add is rounded to bf16, as __hmul/__hadd in the reference.
+ * ------------------------------------------------------------------- */
+
+/* Replaces apply_rotary_pos_emb (kernels/functions.h:53-59; rope.cu:26-87):
+ * separate cos and sin tables of width 2*half_dim. */
+SKV_API int skv_apply_rotary_pos_emb(const void *x, const void *cos, const void *sin,
+                             const int64_t *position_ids, void *output, int batch_size, int heads,
+                             int seq_len, int embed_dim, int stride_xb, int stride_xh,
+                             int stride_xs, int stride_xe, int stride_cos, int stride_sin,
+                             int stride_pid_b, int stride_pid_h, int stride_pid_s, int half_dim,
+                             void *stream);
+
+/* Replaces apply_rotary_pos_emb_new (kernels/functions.h:61-67;
+ * rope_new.cu:26-84): cos_sin row = cos[0:half] | sin[0:half], token
+ * positions int64. */
+SKV_API int skv_apply_rotary_pos_emb_new(const void *x, const void *cos_sin, const int64_t *position_ids,
+                                 void *output, int batch_size, int heads, int seq_len,
+                                 int embed_dim, int stride_xb, int stride_xh, int stride_xs,
+                                 int stride_xe, int stride_cos_sin, int stride_pid_b,
+                                 int stride_pid_h, int stride_pid_s, int half_dim, void *stream);
+
+/* Replaces apply_rotary_pos_emb_new_v2 (kernels/functions.h:69-75;
+ * rope_new.cu:86-144): int32 chunk ids, position = id*chunk + s%chunk. */
+SKV_API int skv_apply_rotary_pos_emb_new_v2(const void *x, const void *cos_sin,
+                                    const int32_t *position_ids, void *output, int batch_size,
+                                    int heads, int seq_len, int embed_dim, int stride_xb,
+                                    int stride_xh, int stride_xs, int stride_xe,
+                                    int stride_cos_sin, int stride_pid_b, int stride_pid_h,
+                                    int stride_pid_s, int half_dim, int chunk_size, void *stream);
+
+/* Replaces apply_rotary_pos_emb_push_cache (kernels/functions.h:77-86;
+ * rope_new.cu:146-222) and apply_rotary_pos_emb_push_cache_opt
+ * (functions.h:88-97; rope_new.cu:224-302), which compute the same values:
+ * rows s with s/chunk >= cnts[b*heads+h] and offset_output_s_start+s <
+ * offset_output_s_end are rotated and written to output row
+ * offset_output_s_start+s. */
+SKV_API int skv_apply_rotary_pos_emb_push_cache(const void *x, const void *cos_sin,
+                                        const int32_t *position_ids, void *output,
+                                        const int32_t *cnts, int batch_size, int heads,
+                                        int seq_len, int embed_dim, int stride_xb, int stride_xh,
+                                        int stride_xs, int stride_xe, int stride_cos_sin,
+                                        int stride_pid_b, int stride_pid_h, int stride_pid_s,
+                                        int stride_output_b, int stride_output_h,
+                                        int stride_output_s, int offset_output_s_start,
+                                        int offset_output_s_end, int half_dim, int chunk_size,
+                                        void *stream);
+SKV_API int skv_apply_rotary_pos_emb_push_cache_opt(
+    const void *x, const void *cos_sin, const int32_t *position_ids, void *output,
+    const int32_t *cnts, int batch_size, int heads, int seq_len, int embed_dim, int stride_xb,
+    int stride_xh, int stride_xs, int stride_xe, int stride_cos_sin, int stride_pid_b,
+    int stride_pid_h, int stride_pid_s, int stride_output_b, int stride_output_h,
+    int stride_output_s, int offset_output_s_start, int offset_output_s_end, int half_dim,
+    int chunk_size, void *stream);
+
+/* Replaces apply_rotary_pos_emb_push_cache_opt_glm (kernels/functions.h:
+ * 99-108; rope_new.cu:305-404): GLM partial interleaved rotary on dims
+ * 0..63 (pairs 2t,2t+1; cos = cs[t], sin = cs[t+32]); dims 64..127 copied. */
+SKV_API int skv_apply_rotary_pos_emb_push_cache_opt_glm(
+    const void *x, const void *cos_sin, const int32_t *position_ids, void *output,
+    const int32_t *cnts, int batch_size, int heads, int seq_len, int embed_dim, int stride_xb,
+    int stride_xh, int stride_xs, int stride_xe, int stride_cos_sin, int stride_pid_b,
+    int stride_pid_h, int stride_pid_s, int stride_output_b, int stride_output_h,
+    int stride_output_s, int offset_output_s_start, int offset_output_s_end, int half_dim,
+    int chunk_size, void *stream);
+
+/* ---------------------------------------------------------------------
+ * Low-rank key reconstruction (reference kernels/batch_gather_gemm.cu)
+ * ------------------------------------------------------------------- */
+
+/* Replaces batch_gather_gemm (kernels/functions.h:110-116;
+ * batch_gather_gemm.cu:136-213).  a = U [batch][seq_len][rank] bf16,
+ * b = SV^T [batch][heads][embed_dim][rank] bf16, position_ids int32
+ * [batch][heads][sparse_budget/chunk_size] chunk ids, output bf16
+ * [batch][heads][sparse_budget][embed_dim].  Row r of head (b,h) with
+ * r/chunk >= offset_array[b*heads+h] gets
+ *   bf16( sum_k a[b][id*chunk + r%chunk][k] * b[b][h][n][k] ).
+ * Rows of cache hits are not written.  cos/sin are accepted for signature
+ * parity (the reference's RoPE epilogue is disabled).  embed_dim must be
+ * 128, rank a multiple of 16 and <= 256, chunk_size 8. */
+SKV_API int skv_batch_gather_gemm(const void *a, const void *b, const void *cos, const void *sin,
+                          const int32_t *position_ids, void *output, int batch_size, int heads,
+                          int seq_len, int embed_dim, int rank, int sparse_budget,
+                          int max_seq_len, int chunk_size, const int32_t *offset_array,
+                          void *stream);
+
+/* ---------------------------------------------------------------------
+ * Landmark scoring (reference kernels/batch_gemm_softmax.cu)
+ * ------------------------------------------------------------------- */
+
+/* Replaces batch_gemm_softmax (kernels/functions.h:118-121;
+ * batch_gemm_softmax.cu:143-196).  A [batch][m][k] bf16, B [batch][n][k]
+ * bf16 (the column-major k x n operand), D and Softmax [batch][m][n] bf16,
+ * Norm and Sum [batch][ceil(n/256)][m] fp32.  D = bf16(alpha*A.B^T);
+ * Norm/Sum hold per-256-column partial max / sum-exp of the fp32 values and
+ * block 0 is overwritten with the row max and 1/row-sum;
+ * Softmax = bf16(exp(float(D) - max) * (1/sum)).  beta is ignored (the
+ * reference passes no C operand).  k must be 128, m <= 64. */
+SKV_API int skv_batch_gemm_softmax(const void *A, const void *B, void *D, float *Norm, float *Sum,
+                           void *Softmax, int batch_count, int m, int n, int k, float alpha,
+                           float beta, void *stream);
+
+/* ---------------------------------------------------------------------
+ * Fused decode path (this library)
+ * ------------------------------------------------------------------- */
+
+/* Geometry of one layer of the decode state. */
+typedef struct {
+    int batch;          /* sequences */
+    int kv_heads;       /* key/value heads */
+    int q_heads;        /* query heads (multiple of kv_heads, group <= 16) */
+    int head_dim;       /* must be 128 */
+    int rank;           /* low-rank width of U / SV (multiple of 16, <= 256) */
+    int chunk_size;     /* tokens per chunk, must be 8 */
+    int select_sets;    /* chunks selected per head (budget / chunk_size), <= 1024 */
+    int num_landmarks;  /* landmarks per head */
+    int num_chunks;     /* chunk ids are in [0, num_chunks) */
+    int ctx_len;        /* rows of U per sequence */
+    int buf_len;        /* rows of each K/V buffer per head */
+    int sparse_start;   /* first buffer row of the selected chunks */
+    int rope_mode;      /* 0: rotate-half (cos_sin width 128), 1: GLM (width 64) */
+    int cos_sin_stride; /* elements per cos_sin row */
+    int cos_sin_rows;   /* rows of the cos_sin table */
+    float scale;        /* softmax scale for scoring and attention, usually 1/sqrt(128) */
+} skv_decode_geom;
+
+/* Bytes of caller-provided scratch the selection needs. */
+SKV_API size_t skv_decode_select_workspace(const skv_decode_geom *g);
+
+/* Landmark scoring + top-k + slot-stable reuse-cache diff for one layer.
+ * q [batch][q_heads][128] bf16 (post-RoPE), landmarks [batch][kv][L][128]
+ * bf16, landmark_idx [batch][kv][L] int64 chunk ids, slots
+ * [batch][kv][select_sets] int32 in/out: slot s holds the chunk id cached
+ * in buffer rows sparse_start + 8s .. +8.  Hits keep their slot; the slots
+ * of chunks that dropped out are refilled (ascending slot) with the missed
+ * ids (ascending id).  miss_slot/miss_chunk [batch][kv][select_sets] int32
+ * and miss_count [batch][kv] int32 list the refilled slots. */
+SKV_API int skv_decode_select(const skv_decode_geom *g, const void *q, const void *landmarks,
+                      const int64_t *landmark_idx, int32_t *slots, int32_t *miss_slot,
+                      int32_t *miss_chunk, int32_t *miss_count, void *workspace,
+                      size_t workspace_bytes, void *stream);
+
+/* Zero-copy fetch of the missed value chunks from page-locked host memory:
+ * v_host [batch][kv][num_chunks][8*128] bf16 -> v_buf rows
+ * sparse_start + 8*slot of [batch][kv][buf_len][128]. */
+SKV_API int skv_decode_gather_values(const skv_decode_geom *g, const void *v_host, void *v_buf,
+                             const int32_t *miss_slot, const int32_t *miss_chunk,
+                             const int32_t *miss_count, void *stream);
+
+/* Reconstruction of the missed keys: U [batch][ctx_len][rank] bf16 times
+ * SV^T [batch][kv][128][rank] bf16 on tensor cores, fp32 accumulation,
+ * bf16 result, RoPE at the original positions (rope_mode, cos_sin) in bf16
+ * op-by-op arithmetic, written to k_buf rows sparse_start + 8*slot. */
+SKV_API int skv_decode_reconstruct_keys(const skv_decode_geom *g, const void *U, const void *SVt,
+                                const void *cos_sin, void *k_buf, const int32_t *miss_slot,
+                                const int32_t *miss_chunk, const int32_t *miss_count,
+                                void *stream);
+
+/* Bytes of caller-provided scratch the attention needs for seq_len rows. */
+SKV_API size_t skv_decode_attention_workspace(const skv_decode_geom *g, int seq_len);
+
+/* Split-K GQA decode attention over buffer rows [0, seq_len):
+ * q [batch][q_heads][128] bf16, k_buf/v_buf [batch][kv][buf_len][128] bf16
+ * -> out [batch][q_heads][128] bf16. */
+SKV_API int skv_decode_attention(const skv_decode_geom *g, const void *q, const void *k_buf,
+                         const void *v_buf, int seq_len, void *out, void *workspace,
+                         size_t workspace_bytes, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SHADOWKV_B200_H */

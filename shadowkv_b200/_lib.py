@@ -1,0 +1,93 @@
+"""ctypes binding of ``libshadowkv_b200.so`` (C ABI in include/shadowkv_b200.h).
+
+The library is built in-tree by ``shadowkv_b200/build.py``.  There is no
+fallback: if the shared library is missing or a symbol is absent, importing
+this module raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libshadowkv_b200.so")
+
+SKV_OK = 0
+_STATUS = {1: "invalid argument", 2: "unsupported", 3: "CUDA error", 4: "host memory not pinned/mapped"}
+
+c_int, c_float, c_size_t, c_void_p = ctypes.c_int, ctypes.c_float, ctypes.c_size_t, ctypes.c_void_p
+c_char_p = ctypes.c_char_p
+P = c_void_p
+
+
+class DecodeGeom(ctypes.Structure):
+    """``skv_decode_geom`` of include/shadowkv_b200.h."""
+
+    _fields_ = [
+        ("batch", c_int), ("kv_heads", c_int), ("q_heads", c_int), ("head_dim", c_int),
+        ("rank", c_int), ("chunk_size", c_int), ("select_sets", c_int), ("num_landmarks", c_int),
+        ("num_chunks", c_int), ("ctx_len", c_int), ("buf_len", c_int), ("sparse_start", c_int),
+        ("rope_mode", c_int), ("cos_sin_stride", c_int), ("cos_sin_rows", c_int), ("scale", c_float),
+    ]
+
+
+# name -> argument types (every function returns int status unless listed in _RET)
+SIGNATURES = {
+    "skv_last_error": [],
+    "skv_version": [],
+    "skv_device_errors": [P, P],
+    "skv_gather_copy": [P, P, P, c_int, c_int, c_int, c_int, c_int, P],
+    "skv_gather_copy_d2d_with_offsets": [P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, P],
+    "skv_reorder_keys_and_compute_offsets": [P, P, P, P, c_int, c_int, c_int, P],
+    "skv_gather_copy_with_offsets": [P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int, P],
+    "skv_apply_rotary_pos_emb": [P, P, P, P, P] + [c_int] * 16 + [P],
+    "skv_apply_rotary_pos_emb_new": [P, P, P, P] + [c_int] * 14 + [P],
+    "skv_apply_rotary_pos_emb_new_v2": [P, P, P, P] + [c_int] * 15 + [P],
+    "skv_apply_rotary_pos_emb_push_cache": [P, P, P, P, P] + [c_int] * 20 + [P],
+    "skv_apply_rotary_pos_emb_push_cache_opt": [P, P, P, P, P] + [c_int] * 20 + [P],
+    "skv_apply_rotary_pos_emb_push_cache_opt_glm": [P, P, P, P, P] + [c_int] * 20 + [P],
+    "skv_batch_gather_gemm": [P, P, P, P, P, P] + [c_int] * 8 + [P, P],
+    "skv_batch_gemm_softmax": [P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_float, c_float, P],
+    "skv_decode_select_workspace": [ctypes.POINTER(DecodeGeom)],
+    "skv_decode_select": [ctypes.POINTER(DecodeGeom), P, P, P, P, P, P, P, P, c_size_t, P],
+    "skv_decode_gather_values": [ctypes.POINTER(DecodeGeom), P, P, P, P, P, P],
+    "skv_decode_reconstruct_keys": [ctypes.POINTER(DecodeGeom), P, P, P, P, P, P, P, P],
+    "skv_decode_attention_workspace": [ctypes.POINTER(DecodeGeom), c_int],
+    "skv_decode_attention": [ctypes.POINTER(DecodeGeom), P, P, P, c_int, P, P, c_size_t, P],
+}
+_RET = {"skv_last_error": c_char_p, "skv_decode_select_workspace": c_size_t,
+        "skv_decode_attention_workspace": c_size_t}
+
+
+def _load():
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"{LIB_PATH} is missing: build it with `python -m shadowkv_b200.build` "
+            "(the decode path has no CPU fallback)")
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, args in SIGNATURES.items():
+        fn = getattr(lib, name)  # AttributeError if the symbol is absent
+        fn.argtypes = args
+        fn.restype = _RET.get(name, c_int)
+    return lib
+
+
+lib = _load()
+
+
+class ShadowKVError(RuntimeError):
+    """Raised when a library call returns a non-zero status."""
+
+
+def check(status: int, what: str) -> None:
+    if status != SKV_OK:
+        msg = lib.skv_last_error().decode(errors="replace")
+        raise ShadowKVError(f"{what}: {_STATUS.get(status, status)}: {msg}")
+
+
+def device_errors() -> tuple[int, int]:
+    """(count, first_code) of device-side index errors since the last call; clears them."""
+    c = ctypes.c_uint32(0)
+    f = ctypes.c_uint32(0)
+    check(lib.skv_device_errors(ctypes.byref(c), ctypes.byref(f)), "skv_device_errors")
+    return int(c.value), int(f.value)

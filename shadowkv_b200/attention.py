@@ -1,0 +1,78 @@
+"""``ShadowAttention`` for B200 (reference models/attention/shadow.py:6-49).
+
+``decode`` follows the reference step for step: RoPE of the new q/k, append
+to the K/V buffers, chunk selection, value fetch on the cache's copy stream
+overlapped with key reconstruction on the current stream, join, attention.
+The attention is the library's split-K GQA kernel instead of
+``flash_attn_with_kvcache``; the q/k RoPE uses the library's RoPE binding
+instead of vllm's ``rotary_embedding`` custom op (llama.py:149-154).
+``decode_fused`` runs the same step on the fused slot-stable kernels.
+
+Prefill is outside the accelerated path; ``prefill`` builds the cache state
+with torch (SVD, landmarks, outliers) and returns no attention output.
+"""
+from __future__ import annotations
+
+import torch
+
+from .kvcache import ShadowKVCache_CPU
+from .tensor_op import apply_rotary_pos_emb_cuda
+
+
+class ShadowAttention:
+    def __init__(self, kv_cache: ShadowKVCache_CPU, num_key_value_groups, head_dim, hidden_size,
+                 cos_sin_cache: torch.Tensor):
+        self.kv_cache = kv_cache
+        self.num_key_value_groups = num_key_value_groups
+        self.head_dim = head_dim
+        self.hidden_size = hidden_size
+        self.cos_sin_cache = cos_sin_cache
+
+    def apply_rotary_pos_emb(self, q: torch.Tensor, k: torch.Tensor, position_ids: torch.Tensor):
+        """RoPE of q [B, Hq, S, D] and k [B, Hkv, S, D] at token positions [B, S] (int64)."""
+        B, Hq, S, D = q.shape
+        Hk = k.shape[1]
+        pq = position_ids.view(B, 1, S).expand(B, Hq, S)
+        pk = position_ids.view(B, 1, S).expand(B, Hk, S)
+        return apply_rotary_pos_emb_cuda(q, self.cos_sin_cache, pq), apply_rotary_pos_emb_cuda(k, self.cos_sin_cache, pk)
+
+    def prefill(self, query_states, key_states, value_states, position_ids, layer_idx):
+        """Build the cache state of one layer (pre-RoPE k -> SVD; post-RoPE k -> landmarks)."""
+        kv = self.kv_cache
+        kv.get_svd(key_states, layer_idx=layer_idx)
+        q, k = self.apply_rotary_pos_emb(query_states, key_states, position_ids)
+        kv.prefill_kv_cache(value_states, layer_idx, k, q[:, :, -1:])
+
+    def decode(self, query_states, key_states, value_states, position_ids, layer_idx):
+        """models/attention/shadow.py:22-48 -> attention output [B, 1, Hq, D]."""
+        kv = self.kv_cache
+        query_states, key_states = self.apply_rotary_pos_emb(query_states, key_states, position_ids)
+        kv.update_kv_cache(key_states, value_states, layer_idx)
+        pos = kv.get_retrieval_position_ids(layer_idx=layer_idx, query_states=query_states)
+        curr = torch.cuda.current_stream()
+        copy_stream = kv.copy_stream
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_stream(curr)
+            value_states = kv.get_value_cache(layer_idx, pos)
+        key_states = kv.get_key_cache(layer_idx=layer_idx, position_ids=pos, rope_func=None,
+                                      cos_sin_cache=self.cos_sin_cache)
+        curr.wait_stream(copy_stream)
+        out = kv.attention(layer_idx, query_states, key_states.shape[2])
+        return out.view(out.shape[0], 1, out.shape[1], out.shape[2])
+
+    def decode_fused(self, query_states, key_states, value_states, position_ids, layer_idx):
+        """Same step on the fused kernels (slot-stable reuse cache)."""
+        kv = self.kv_cache
+        query_states, key_states = self.apply_rotary_pos_emb(query_states, key_states, position_ids)
+        kv.update_kv_cache(key_states, value_states, layer_idx)
+        kv.select_fused(layer_idx, query_states, self.cos_sin_cache)
+        curr = torch.cuda.current_stream()
+        copy_stream = kv.copy_stream
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_stream(curr)
+            kv.fetch_values_fused(layer_idx, copy_stream)
+        kv.reconstruct_keys_fused(layer_idx, self.cos_sin_cache)
+        curr.wait_stream(copy_stream)
+        seq_len = kv.sparse_end + kv._gen_offset(layer_idx)
+        out = kv.attention(layer_idx, query_states, seq_len)
+        return out.view(out.shape[0], 1, out.shape[1], out.shape[2])

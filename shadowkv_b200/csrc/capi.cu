@@ -1,0 +1,80 @@
+// Error plumbing shared by all entry points of the C ABI.
+#include "common.cuh"
+
+#include <string.h>
+
+namespace skv {
+
+static thread_local char t_last_error[512] = "";
+
+void set_error(const char *fmt, ...)
+{
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(t_last_error, sizeof(t_last_error), fmt, ap);
+    va_end(ap);
+}
+
+void clear_error() { t_last_error[0] = '\0'; }
+
+int check_launch(const char *what)
+{
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        set_error("launch of %s failed: %s", what, cudaGetErrorString(e));
+        return SKV_ERR_CUDA;
+    }
+    return SKV_OK;
+}
+
+int host_to_device_ptr(const void *p, const void **dev, const char *name)
+{
+    if (p == nullptr) {
+        set_error("%s is null", name);
+        return SKV_ERR_INVALID_ARGUMENT;
+    }
+    cudaPointerAttributes attr;
+    cudaError_t e = cudaPointerGetAttributes(&attr, p);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        set_error("%s: cudaPointerGetAttributes failed: %s", name, cudaGetErrorString(e));
+        return SKV_ERR_NOT_PINNED;
+    }
+    if (attr.type != cudaMemoryTypeHost) {
+        set_error("%s must be page-locked host memory mapped into the device address space "
+                  "(pointer type %d)", name, (int)attr.type);
+        return SKV_ERR_NOT_PINNED;
+    }
+    if (attr.devicePointer == nullptr) {
+        set_error("%s is page-locked but not mapped for the device", name);
+        return SKV_ERR_NOT_PINNED;
+    }
+    // the device pointer of the start of the allocation plus p's offset
+    *dev = attr.devicePointer;
+    return SKV_OK;
+}
+
+__device__ unsigned int g_dev_err_count = 0;
+__device__ unsigned int g_dev_err_first = 0;
+
+}  // namespace skv
+
+extern "C" {
+
+const char *skv_last_error(void) { return skv::t_last_error; }
+
+int skv_version(void) { return 1 * 10000 + 0 * 100 + 0; }
+
+int skv_device_errors(uint32_t *count, uint32_t *first_code)
+{
+    unsigned int c = 0, f = 0, zero = 0;
+    SKV_CUDA(cudaMemcpyFromSymbol(&c, skv::g_dev_err_count, sizeof(c)));
+    SKV_CUDA(cudaMemcpyFromSymbol(&f, skv::g_dev_err_first, sizeof(f)));
+    SKV_CUDA(cudaMemcpyToSymbol(skv::g_dev_err_count, &zero, sizeof(zero)));
+    SKV_CUDA(cudaMemcpyToSymbol(skv::g_dev_err_first, &zero, sizeof(zero)));
+    if (count) *count = c;
+    if (first_code) *first_code = f;
+    return SKV_OK;
+}
+
+}  // extern "C"

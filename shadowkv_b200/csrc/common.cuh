@@ -1,0 +1,153 @@
+// Shared helpers of the shadowkv_b200 CUDA library (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdarg.h>
+
+#include "../../include/shadowkv_b200.h"
+
+namespace skv {
+
+// ---------------------------------------------------------------------------
+// Host-side error reporting (thread-local last message, status codes)
+// ---------------------------------------------------------------------------
+void set_error(const char *fmt, ...);
+void clear_error();
+
+#define SKV_CHECK_ARG(cond, ...)                     \
+    do {                                             \
+        if (!(cond)) {                               \
+            ::skv::set_error(__VA_ARGS__);           \
+            return SKV_ERR_INVALID_ARGUMENT;         \
+        }                                            \
+    } while (0)
+
+#define SKV_CHECK_SUPPORTED(cond, ...)               \
+    do {                                             \
+        if (!(cond)) {                               \
+            ::skv::set_error(__VA_ARGS__);           \
+            return SKV_ERR_UNSUPPORTED;              \
+        }                                            \
+    } while (0)
+
+#define SKV_CUDA(call)                                                              \
+    do {                                                                            \
+        cudaError_t e_ = (call);                                                    \
+        if (e_ != cudaSuccess) {                                                    \
+            ::skv::set_error("%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), \
+                             __FILE__, __LINE__);                                   \
+            return SKV_ERR_CUDA;                                                    \
+        }                                                                           \
+    } while (0)
+
+// Check the launch that was just issued.
+int check_launch(const char *what);
+
+// Verify that `p` is page-locked host memory mapped for the current device;
+// on success *dev holds the device-side address of p.
+int host_to_device_ptr(const void *p, const void **dev, const char *name);
+
+inline bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// ---------------------------------------------------------------------------
+// Device-side error counter: a kernel that finds an index out of range skips
+// the access and records it here (read back by skv_device_errors()).
+// ---------------------------------------------------------------------------
+enum DevErr : uint32_t { DEV_ERR_HOST_CHUNK = 1, DEV_ERR_SLOT = 2, DEV_ERR_ROW = 3 };
+
+extern __device__ unsigned int g_dev_err_count;
+extern __device__ unsigned int g_dev_err_first;
+
+__device__ __forceinline__ void report_dev_error(uint32_t code)
+{
+    unsigned int prev = atomicAdd(&g_dev_err_count, 1u);
+    if (prev == 0) atomicExch(&g_dev_err_first, code);
+}
+
+// ---------------------------------------------------------------------------
+// Device helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint4 ld_nc_v4(const void *p)
+{
+    uint4 r;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+// Streaming 128-bit load that does not allocate in L1 (host / one-touch data).
+__device__ __forceinline__ uint4 ld_stream_v4(const void *p)
+{
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ uint4 ld_v4(const void *p)
+{
+    return *reinterpret_cast<const uint4 *>(p);
+}
+
+__device__ __forceinline__ void st_v4(void *p, uint4 v)
+{
+    *reinterpret_cast<uint4 *>(p) = v;
+}
+
+__device__ __forceinline__ float bf2f(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ __nv_bfloat16 f2bf(float v) { return __float2bfloat16_rn(v); }
+
+// bf16 multiply / add with a single rounding.  The product of two bf16
+// values is exact in fp32 and fp32 has more than 2*8+2 significand bits, so
+// fp32 arithmetic followed by one round-to-nearest-even to bf16 gives the
+// correctly rounded bf16 result.  __fmul_rn/__fadd_rn keep the compiler from
+// contracting the pair into an FMA.
+__device__ __forceinline__ float bmul(float a, float b) { return bf2f(f2bf(__fmul_rn(a, b))); }
+__device__ __forceinline__ float badd(float a, float b) { return bf2f(f2bf(__fadd_rn(a, b))); }
+
+__device__ __forceinline__ float bf_lo(uint32_t w)
+{
+    return __uint_as_float(w << 16);
+}
+__device__ __forceinline__ float bf_hi(uint32_t w)
+{
+    return __uint_as_float(w & 0xffff0000u);
+}
+__device__ __forceinline__ uint32_t pack_bf2(float lo, float hi)
+{
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&v);
+}
+
+// mma.sync m16n8k16, bf16 inputs, fp32 accumulators (D = A*B + C in place).
+__device__ __forceinline__ void mma_bf16_16816(float *c, uint32_t a0, uint32_t a1, uint32_t a2,
+                                               uint32_t a3, uint32_t b0, uint32_t b1)
+{
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ float warp_max(float v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ float warp_sum(float v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__host__ __device__ __forceinline__ int ceil_div(int a, int b) { return (a + b - 1) / b; }
+
+}  // namespace skv

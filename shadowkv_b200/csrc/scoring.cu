@@ -1,0 +1,614 @@
+// Landmark scoring and chunk selection.
+//
+// Reference: kernels/batch_gemm_softmax.cu:143-196 with
+// kernels/batch_gemm_softmax.h:66-523 (CUTLASS 2.x GEMM + epilogue visitor +
+// final reduction + softmax apply, three launches), then torch.max /
+// torch.topk / gather in models/kvcache/shadow.py:547-576, then the reuse
+// diff of kernels/map.cuh:475-516.
+//
+// The scoring GEMM has M = landmarks (thousands) and N = query heads of one
+// GQA group (4 for Llama, 16 for GLM), K = 128.  It is bound by the landmark
+// read.  Each warp multiplies 16 landmark rows with mma.sync m16n8k16; the K
+// (head_dim) axis is permuted identically for A and B so that each thread
+// feeds its fragments from four 16-byte loads per row straight from global
+// memory -- no shared-memory staging and fully coalesced 256-byte rows.
+#include "common.cuh"
+
+namespace skv {
+
+constexpr int SC_THREADS = 256;   // 8 warps
+constexpr int SC_ROWS_PER_PASS = 16 * (SC_THREADS / 32);
+constexpr int SEL_THREADS = 1024;
+
+// q fragments for one n-tile of 8 query rows: thread (g = lane>>2, j = lane&3)
+// holds row nt*8+g, elements (i*4+j)*8 .. +8 for i = 0..3.
+__device__ __forceinline__ void load_q_frag(uint4 (&qf)[4], const __nv_bfloat16 *qrows, int nrows,
+                                            int nt, int lane)
+{
+    const int n = nt * 8 + (lane >> 2), j = lane & 3;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        if (n < nrows) qf[i] = ld_nc_v4(qrows + (int64_t)n * 128 + (i * 4 + j) * 8);
+        else qf[i] = make_uint4(0, 0, 0, 0);
+    }
+}
+
+__device__ __forceinline__ uint32_t wsel(const uint4 &v, int w)
+{
+    return w == 0 ? v.x : (w == 1 ? v.y : (w == 2 ? v.z : v.w));
+}
+
+// 16 rows x (8*NT) logits.  ra/rb: rows g and g+8 (4 x uint4 each).
+template <int NT>
+__device__ __forceinline__ void tile_mma(float (&acc)[NT][4], const uint4 (&ra)[4],
+                                         const uint4 (&rb)[4], const uint4 (&qf)[NT][4])
+{
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+        const int i = s >> 1, w = (s & 1) * 2;
+        const uint32_t a0 = wsel(ra[i], w), a2 = wsel(ra[i], w + 1);
+        const uint32_t a1 = wsel(rb[i], w), a3 = wsel(rb[i], w + 1);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+            mma_bf16_16816(acc[nt], a0, a1, a2, a3, wsel(qf[nt][i], w), wsel(qf[nt][i], w + 1));
+    }
+}
+
+__device__ __forceinline__ void online_update(float &m, float &s, float x)
+{
+    if (x > m) {
+        s = s * __expf(m - x) + 1.f;
+        m = x;
+    } else {
+        s += __expf(x - m);
+    }
+}
+
+__device__ __forceinline__ void merge_stats(float &m, float &s, float m2, float s2)
+{
+    const float mm = fmaxf(m, m2);
+    if (mm == -INFINITY) return;
+    s = s * __expf(m - mm) + s2 * __expf(m2 - mm);
+    m = mm;
+}
+
+// ---------------------------------------------------------------------------
+// Fused path, kernel 1: logits[bh][c][g] = scale * q_g . LM_c and per-split
+// online (max, sum-exp) per query head.
+// grid = (nsplit, B*Hkv), rows [split*rows_per_split, ...).
+// ---------------------------------------------------------------------------
+template <int NT>
+__global__ void __launch_bounds__(SC_THREADS) score_kernel(
+    const __nv_bfloat16 *__restrict__ q, const __nv_bfloat16 *__restrict__ lm,
+    float *__restrict__ logits, float2 *__restrict__ part, int Hkv, int G, int L,
+    int rows_per_split, float scale)
+{
+    const int bh = blockIdx.y, split = blockIdx.x, nsplit = gridDim.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, j = lane & 3;
+    const int b = bh / Hkv, h = bh % Hkv;
+    const __nv_bfloat16 *qrows = q + ((int64_t)b * Hkv * G + (int64_t)h * G) * 128;
+    const __nv_bfloat16 *lmh = lm + (int64_t)bh * L * 128;
+    float *lg = logits + (int64_t)bh * L * G;
+
+    uint4 qf[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) load_q_frag(qf[nt], qrows, G, nt, lane);
+
+    float m[NT][2], s[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) m[nt][0] = m[nt][1] = -INFINITY, s[nt][0] = s[nt][1] = 0.f;
+
+    const int r_begin = split * rows_per_split;
+    const int r_end = min(L, r_begin + rows_per_split);
+    for (int r0 = r_begin + warp * 16; r0 < r_end; r0 += SC_ROWS_PER_PASS) {
+        const int rowa = r0 + g, rowb = r0 + g + 8;
+        uint4 ra[4], rb[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            ra[i] = rowa < r_end ? ld_stream_v4(lmh + (int64_t)rowa * 128 + (i * 4 + j) * 8) : make_uint4(0, 0, 0, 0);
+            rb[i] = rowb < r_end ? ld_stream_v4(lmh + (int64_t)rowb * 128 + (i * 4 + j) * 8) : make_uint4(0, 0, 0, 0);
+        }
+        float acc[NT][4];
+        tile_mma<NT>(acc, ra, rb, qf);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const int n0 = nt * 8 + 2 * j;
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int row = u ? rowb : rowa;
+                const float x0 = acc[nt][2 * u] * scale, x1 = acc[nt][2 * u + 1] * scale;
+                if (row < r_end) {
+                    if (n0 < G) {
+                        lg[(int64_t)row * G + n0] = x0;
+                        online_update(m[nt][0], s[nt][0], x0);
+                    }
+                    if (n0 + 1 < G) {
+                        lg[(int64_t)row * G + n0 + 1] = x1;
+                        online_update(m[nt][1], s[nt][1], x1);
+                    }
+                }
+            }
+        }
+    }
+    // reduce over the 8 lanes sharing j, then over warps
+    __shared__ float2 s_part[SC_THREADS / 32][16];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            float mm = m[nt][u], ss = s[nt][u];
+#pragma unroll
+            for (int o = 4; o < 32; o <<= 1) {
+                const float m2 = __shfl_xor_sync(0xffffffffu, mm, o);
+                const float s2 = __shfl_xor_sync(0xffffffffu, ss, o);
+                merge_stats(mm, ss, m2, s2);
+            }
+            const int n = nt * 8 + 2 * j + u;
+            if (g == 0 && n < 16) s_part[warp][n] = make_float2(mm, ss);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < G) {
+        float mm = -INFINITY, ss = 0.f;
+        for (int w = 0; w < SC_THREADS / 32; ++w) merge_stats(mm, ss, s_part[w][threadIdx.x].x, s_part[w][threadIdx.x].y);
+        part[((int64_t)bh * nsplit + split) * G + threadIdx.x] = make_float2(mm, ss);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Fused path, kernel 2: per (b,h) top-k over max_g softmax_g, then the
+// slot-stable reuse diff.  One 1024-thread CTA per (b,h).
+// ---------------------------------------------------------------------------
+struct SelectArgs {
+    const float *logits;
+    const float2 *part;
+    uint32_t *gkeys;              // global key scratch (large L) or null
+    const int64_t *landmark_idx;  // [BH][L]
+    int32_t *slots;               // [BH][K] in/out
+    int32_t *miss_slot, *miss_chunk, *miss_count;
+    int G, L, K, nsplit, num_chunks;
+};
+
+__device__ int block_excl_scan_1024(int v, int *total, int *s_warp)
+{
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) s_warp[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        const int w = s_warp[lane];
+        int wi = w;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, wi, o);
+            if (lane >= o) wi += y;
+        }
+        s_warp[lane] = wi - w;
+        if (lane == 31) s_warp[32] = wi;
+    }
+    __syncthreads();
+    const int r = s_warp[warp] + x - v;
+    *total = s_warp[32];
+    __syncthreads();
+    return r;
+}
+
+__global__ void __launch_bounds__(SEL_THREADS) select_kernel(SelectArgs a)
+{
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ float s_M[16], s_invZ[16];
+    __shared__ int s_hist[256];
+    __shared__ int s_warp[33];
+    __shared__ int s_sel[1024];   // selected landmark index, then chunk id
+    __shared__ int s_misssorted[1024];
+    __shared__ int s_cnt, s_digit, s_above;
+
+    const int bh = blockIdx.x, tid = threadIdx.x;
+    const int G = a.G, L = a.L, K = a.K;
+    const int nbw = (a.num_chunks + 31) >> 5;
+    uint32_t *bmA = reinterpret_cast<uint32_t *>(smem_raw);
+    uint32_t *bmB = bmA + nbw;
+    uint32_t *keys = a.gkeys ? a.gkeys + (int64_t)bh * L : (bmB + nbw);
+
+    // 1) softmax normalizers of each query head
+    if (tid < G) {
+        float mm = -INFINITY, ss = 0.f;
+        for (int i = 0; i < a.nsplit; ++i) {
+            const float2 p = a.part[((int64_t)bh * a.nsplit + i) * G + tid];
+            merge_stats(mm, ss, p.x, p.y);
+        }
+        s_M[tid] = mm;
+        s_invZ[tid] = 1.f / ss;
+    }
+    __syncthreads();
+
+    // 2) scores as order-preserving keys (scores are >= 0)
+    const float *lg = a.logits + (int64_t)bh * L * G;
+    for (int c = tid; c < L; c += SEL_THREADS) {
+        float sc = 0.f;
+        for (int gg = 0; gg < G; ++gg) sc = fmaxf(sc, __expf(lg[(int64_t)c * G + gg] - s_M[gg]) * s_invZ[gg]);
+        keys[c] = __float_as_uint(sc);
+    }
+    __syncthreads();
+
+    // 3) radix select of the K-th largest key, 8 bits per pass
+    uint32_t prefix = 0, pmask = 0;
+    int remaining = K;
+    for (int pass = 0; pass < 4; ++pass) {
+        const int shift = 24 - 8 * pass;
+        if (tid < 256) s_hist[tid] = 0;
+        __syncthreads();
+        for (int c = tid; c < L; c += SEL_THREADS) {
+            const uint32_t k = keys[c];
+            if ((k & pmask) == prefix) atomicAdd(&s_hist[(k >> shift) & 255], 1);
+        }
+        __syncthreads();
+        if (tid < 32) {
+            // lane l owns digits 255-8l .. 248-8l (descending)
+            int cnt[8], tot = 0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                cnt[i] = s_hist[255 - 8 * tid - i];
+                tot += cnt[i];
+            }
+            int incl = tot;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (tid >= o) incl += y;
+            }
+            int above = incl - tot;  // count of digits higher than this lane's range
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                if (above < remaining && above + cnt[i] >= remaining) {
+                    s_digit = 255 - 8 * tid - i;
+                    s_above = above;
+                }
+                above += cnt[i];
+            }
+        }
+        __syncthreads();
+        const int d = s_digit;
+        remaining -= s_above;
+        prefix |= (uint32_t)d << shift;
+        pmask |= 255u << shift;
+        __syncthreads();
+    }
+    const uint32_t T = prefix;  // K-th largest key; take `remaining` of the keys equal to T
+
+    // 4) compaction: all keys > T, then the lowest-index `remaining` keys == T
+    if (tid == 0) s_cnt = 0;
+    __syncthreads();
+    for (int c = tid; c < L; c += SEL_THREADS)
+        if (keys[c] > T) s_sel[atomicAdd(&s_cnt, 1)] = c;
+    __syncthreads();
+    const int ngt = s_cnt;
+    int taken = 0;
+    for (int base = 0; base < L && taken < remaining; base += SEL_THREADS) {
+        const int c = base + tid;
+        const int f = (c < L && keys[c] == T) ? 1 : 0;
+        int tot;
+        const int r = block_excl_scan_1024(f, &tot, s_warp);
+        if (f && taken + r < remaining) s_sel[ngt + taken + r] = c;
+        taken += tot;
+    }
+    __syncthreads();
+
+    // 5) landmark index -> chunk id; bitmap A of the new set
+    for (int w = tid; w < 2 * nbw; w += SEL_THREADS) bmA[w] = 0;
+    __syncthreads();
+    const int64_t *lidx = a.landmark_idx + (int64_t)bh * L;
+    for (int jj = tid; jj < K; jj += SEL_THREADS) {
+        const int64_t cid = lidx[s_sel[jj]];
+        int v = -1;
+        if (cid >= 0 && cid < a.num_chunks) {
+            v = (int)cid;
+            atomicOr(&bmA[v >> 5], 1u << (v & 31));
+        } else {
+            report_dev_error(DEV_ERR_HOST_CHUNK);
+        }
+        s_sel[jj] = v;
+    }
+    __syncthreads();
+
+    // 6) classify the cached slots; bitmap B of the cached set
+    int32_t *slots = a.slots + (int64_t)bh * K;
+    const int s = tid;
+    int old = -1, hit = 0;
+    if (s < K) {
+        old = slots[s];
+        if (old >= 0 && old < a.num_chunks) {
+            hit = (bmA[old >> 5] >> (old & 31)) & 1;
+            atomicOr(&bmB[old >> 5], 1u << (old & 31));
+        }
+    }
+    __syncthreads();
+
+    // 7) misses in ascending id order: scan of popcount(A & ~B) over words
+    const int wpt = (nbw + SEL_THREADS - 1) / SEL_THREADS;
+    const int w0 = tid * wpt;
+    int local = 0;
+    for (int w = w0; w < min(nbw, w0 + wpt); ++w) local += __popc(bmA[w] & ~bmB[w]);
+    int nmiss;
+    int rank = block_excl_scan_1024(local, &nmiss, s_warp);
+    for (int w = w0; w < min(nbw, w0 + wpt); ++w) {
+        uint32_t bits = bmA[w] & ~bmB[w];
+        while (bits) {
+            const int bit = __ffs(bits) - 1;
+            bits &= bits - 1;
+            if (rank < 1024) s_misssorted[rank] = w * 32 + bit;
+            ++rank;
+        }
+    }
+    __syncthreads();
+
+    // 8) refill the free slots (ascending) with the misses (ascending)
+    const int is_free = (s < K && !hit) ? 1 : 0;
+    int nfree;
+    const int r = block_excl_scan_1024(is_free, &nfree, s_warp);
+    const int nassign = min(nfree, nmiss);
+    if (is_free && r < nassign) {
+        const int id = s_misssorted[r];
+        slots[s] = id;
+        a.miss_slot[(int64_t)bh * K + r] = s;
+        a.miss_chunk[(int64_t)bh * K + r] = id;
+    }
+    if (tid == 0) {
+        a.miss_count[bh] = nassign;
+        if (nfree != nmiss) report_dev_error(DEV_ERR_SLOT);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Drop-in batch_gemm_softmax, kernel 1: D, per-256-column partial stats.
+// grid = (ceil(n/256), batch), 256 threads; warp w covers rows 32w..32w+31.
+// ---------------------------------------------------------------------------
+template <int NT>
+__global__ void __launch_bounds__(SC_THREADS) bgs_gemm_kernel(
+    const __nv_bfloat16 *__restrict__ A, const __nv_bfloat16 *__restrict__ Bm,
+    __nv_bfloat16 *__restrict__ D, float *__restrict__ Norm, float *__restrict__ Sum, int m, int n,
+    float alpha)
+{
+    const int bt = blockIdx.y, blk = blockIdx.x, nblk = gridDim.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, j = lane & 3;
+    const __nv_bfloat16 *qrows = A + (int64_t)bt * m * 128;
+    const __nv_bfloat16 *lmh = Bm + (int64_t)bt * n * 128;
+    __nv_bfloat16 *Db = D + (int64_t)bt * m * n;
+
+    uint4 qf[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) load_q_frag(qf[nt], qrows, m, nt, lane);
+    float mx[NT][2], sm[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) mx[nt][0] = mx[nt][1] = -INFINITY, sm[nt][0] = sm[nt][1] = 0.f;
+
+    for (int t = 0; t < 2; ++t) {
+        const int r0 = blk * 256 + warp * 32 + t * 16;
+        const int rowa = r0 + g, rowb = r0 + g + 8;
+        uint4 ra[4], rb[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            ra[i] = rowa < n ? ld_nc_v4(lmh + (int64_t)rowa * 128 + (i * 4 + j) * 8) : make_uint4(0, 0, 0, 0);
+            rb[i] = rowb < n ? ld_nc_v4(lmh + (int64_t)rowb * 128 + (i * 4 + j) * 8) : make_uint4(0, 0, 0, 0);
+        }
+        float acc[NT][4];
+        tile_mma<NT>(acc, ra, rb, qf);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int row = u ? rowb : rowa;
+                if (row >= n) continue;
+#pragma unroll
+                for (int v = 0; v < 2; ++v) {
+                    const int mr = nt * 8 + 2 * j + v;
+                    if (mr >= m) continue;
+                    const float x = alpha * acc[nt][2 * u + v];
+                    Db[(int64_t)mr * n + row] = f2bf(x);
+                    online_update(mx[nt][v], sm[nt][v], x);
+                }
+            }
+        }
+    }
+    __shared__ float2 s_part[SC_THREADS / 32][32];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int v = 0; v < 2; ++v) {
+            float mm = mx[nt][v], ss = sm[nt][v];
+#pragma unroll
+            for (int o = 4; o < 32; o <<= 1) {
+                const float m2 = __shfl_xor_sync(0xffffffffu, mm, o);
+                const float s2 = __shfl_xor_sync(0xffffffffu, ss, o);
+                merge_stats(mm, ss, m2, s2);
+            }
+            const int mr = nt * 8 + 2 * j + v;
+            if (g == 0 && mr < 32) s_part[warp][mr] = make_float2(mm, ss);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < m) {
+        float mm = -INFINITY, ss = 0.f;
+        for (int w = 0; w < SC_THREADS / 32; ++w) merge_stats(mm, ss, s_part[w][threadIdx.x].x, s_part[w][threadIdx.x].y);
+        Norm[((int64_t)bt * nblk + blk) * m + threadIdx.x] = mm;
+        Sum[((int64_t)bt * nblk + blk) * m + threadIdx.x] = ss;
+    }
+}
+
+// kernel 2: final reduction into block 0 and the softmax of the bf16 D.
+// grid = (m, batch), 256 threads.
+__global__ void __launch_bounds__(256) bgs_softmax_kernel(const __nv_bfloat16 *__restrict__ D,
+                                                          float *Norm, float *Sum,
+                                                          __nv_bfloat16 *__restrict__ Soft, int m,
+                                                          int n, int nblk)
+{
+    const int mr = blockIdx.x, bt = blockIdx.y;
+    __shared__ float s_max, s_inv;
+    if (threadIdx.x < 32) {
+        float mm = -INFINITY, ss = 0.f;
+        for (int i = threadIdx.x; i < nblk; i += 32)
+            merge_stats(mm, ss, Norm[((int64_t)bt * nblk + i) * m + mr], Sum[((int64_t)bt * nblk + i) * m + mr]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float m2 = __shfl_xor_sync(0xffffffffu, mm, o);
+            const float s2 = __shfl_xor_sync(0xffffffffu, ss, o);
+            merge_stats(mm, ss, m2, s2);
+        }
+        if (threadIdx.x == 0) {
+            s_max = mm;
+            s_inv = 1.f / ss;
+        }
+    }
+    __syncthreads();
+    const float M = s_max, inv = s_inv;
+    if (threadIdx.x == 0) {
+        Norm[(int64_t)bt * nblk * m + mr] = M;
+        Sum[(int64_t)bt * nblk * m + mr] = inv;
+    }
+    const __nv_bfloat16 *Dr = D + ((int64_t)bt * m + mr) * n;
+    __nv_bfloat16 *Sr = Soft + ((int64_t)bt * m + mr) * n;
+    for (int c = threadIdx.x; c < n; c += 256) Sr[c] = f2bf(__expf(bf2f(Dr[c]) - M) * inv);
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+struct SelectPlan {
+    int nsplit, rows_per_split;
+    size_t off_logits, off_part, off_keys, total;
+    bool keys_global;
+    size_t sel_smem;
+};
+
+static SelectPlan plan_select(const skv_decode_geom *g)
+{
+    SelectPlan p = {};
+    const int G = g->q_heads / g->kv_heads;
+    const int BH = g->batch * g->kv_heads;
+    const int units = ceil_div(g->num_landmarks, SC_ROWS_PER_PASS);  // 128-row units per head
+    const int target_ctas = 2 * 148;
+    int per = ceil_div(units * BH, target_ctas);
+    if (per < 1) per = 1;
+    p.rows_per_split = per * SC_ROWS_PER_PASS;
+    p.nsplit = ceil_div(g->num_landmarks, p.rows_per_split);
+    const size_t nbw = (size_t)((g->num_chunks + 31) / 32);
+    const size_t bitmaps = 2 * nbw * 4;
+    const size_t keys_smem = (size_t)g->num_landmarks * 4;
+    p.keys_global = bitmaps + keys_smem > 190 * 1024;
+    p.sel_smem = bitmaps + (p.keys_global ? 0 : keys_smem);
+    auto align = [](size_t x) { return (x + 255) & ~(size_t)255; };
+    p.off_logits = 0;
+    p.off_part = align((size_t)BH * g->num_landmarks * G * 4);
+    p.off_keys = p.off_part + align((size_t)BH * p.nsplit * G * 8);
+    p.total = p.off_keys + (p.keys_global ? align((size_t)BH * g->num_landmarks * 4) : 0);
+    return p;
+}
+
+static int check_geom(const skv_decode_geom *g)
+{
+    SKV_CHECK_ARG(g != nullptr, "null geometry");
+    SKV_CHECK_ARG(g->batch > 0 && g->kv_heads > 0 && g->q_heads > 0, "sizes must be positive");
+    SKV_CHECK_SUPPORTED(g->head_dim == 128 && g->chunk_size == 8, "head_dim 128 and chunk 8 only");
+    SKV_CHECK_ARG(g->q_heads % g->kv_heads == 0, "q_heads must be a multiple of kv_heads");
+    SKV_CHECK_SUPPORTED(g->q_heads / g->kv_heads <= 16, "GQA group larger than 16");
+    SKV_CHECK_SUPPORTED(g->select_sets >= 1 && g->select_sets <= 1024, "select_sets outside 1..1024");
+    SKV_CHECK_ARG(g->num_landmarks >= g->select_sets, "fewer landmarks than selected chunks");
+    SKV_CHECK_ARG(g->num_chunks > 0 && g->num_chunks <= (1 << 22), "num_chunks outside 1..4M");
+    return SKV_OK;
+}
+
+}  // namespace skv
+
+using namespace skv;
+
+extern "C" {
+
+size_t skv_decode_select_workspace(const skv_decode_geom *g)
+{
+    if (check_geom(g) != SKV_OK) return 0;
+    return plan_select(g).total;
+}
+
+int skv_decode_select(const skv_decode_geom *g, const void *q, const void *landmarks,
+                      const int64_t *landmark_idx, int32_t *slots, int32_t *miss_slot,
+                      int32_t *miss_chunk, int32_t *miss_count, void *workspace,
+                      size_t workspace_bytes, void *stream)
+{
+    int st = check_geom(g);
+    if (st) return st;
+    SKV_CHECK_ARG(q && landmarks && landmark_idx && slots && miss_slot && miss_chunk && miss_count,
+                  "null pointer argument");
+    SKV_CHECK_ARG(aligned(q, 16) && aligned(landmarks, 16), "q and landmarks must be 16-byte aligned");
+    const SelectPlan p = plan_select(g);
+    SKV_CHECK_ARG(workspace != nullptr && workspace_bytes >= p.total,
+                  "workspace of %zu bytes needed, %zu given", p.total, workspace_bytes);
+    SKV_CHECK_ARG(aligned(workspace, 256), "workspace must be 256-byte aligned");
+    cudaStream_t s = (cudaStream_t)stream;
+    const int G = g->q_heads / g->kv_heads;
+    const int BH = g->batch * g->kv_heads;
+    unsigned char *ws = reinterpret_cast<unsigned char *>(workspace);
+    float *logits = reinterpret_cast<float *>(ws + p.off_logits);
+    float2 *part = reinterpret_cast<float2 *>(ws + p.off_part);
+    dim3 grid(p.nsplit, BH);
+    if (G <= 8)
+        score_kernel<1><<<grid, SC_THREADS, 0, s>>>((const __nv_bfloat16 *)q, (const __nv_bfloat16 *)landmarks,
+                                                   logits, part, g->kv_heads, G, g->num_landmarks,
+                                                   p.rows_per_split, g->scale);
+    else
+        score_kernel<2><<<grid, SC_THREADS, 0, s>>>((const __nv_bfloat16 *)q, (const __nv_bfloat16 *)landmarks,
+                                                   logits, part, g->kv_heads, G, g->num_landmarks,
+                                                   p.rows_per_split, g->scale);
+    st = check_launch("score_kernel");
+    if (st) return st;
+
+    SelectArgs a = {};
+    a.logits = logits;
+    a.part = part;
+    a.gkeys = p.keys_global ? reinterpret_cast<uint32_t *>(ws + p.off_keys) : nullptr;
+    a.landmark_idx = landmark_idx;
+    a.slots = slots;
+    a.miss_slot = miss_slot;
+    a.miss_chunk = miss_chunk;
+    a.miss_count = miss_count;
+    a.G = G, a.L = g->num_landmarks, a.K = g->select_sets, a.nsplit = p.nsplit;
+    a.num_chunks = g->num_chunks;
+    SKV_CUDA(cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.sel_smem));
+    select_kernel<<<BH, SEL_THREADS, p.sel_smem, s>>>(a);
+    return check_launch("select_kernel");
+}
+
+int skv_batch_gemm_softmax(const void *A, const void *B, void *D, float *Norm, float *Sum,
+                           void *Softmax, int batch_count, int m, int n, int k, float alpha,
+                           float beta, void *stream)
+{
+    (void)beta;
+    SKV_CHECK_ARG(A && B && D && Norm && Sum && Softmax, "null pointer argument");
+    SKV_CHECK_ARG(batch_count > 0 && m > 0 && n > 0, "sizes must be positive");
+    SKV_CHECK_SUPPORTED(k == 128, "k must be 128");
+    SKV_CHECK_SUPPORTED(m <= 32, "m must be <= 32");
+    SKV_CHECK_ARG(aligned(A, 16) && aligned(B, 16), "A and B must be 16-byte aligned");
+    cudaStream_t s = (cudaStream_t)stream;
+    const int nblk = ceil_div(n, 256);
+    dim3 grid(nblk, batch_count);
+    const int NT = ceil_div(m, 8);
+    const __nv_bfloat16 *a = (const __nv_bfloat16 *)A, *b = (const __nv_bfloat16 *)B;
+    __nv_bfloat16 *d = (__nv_bfloat16 *)D;
+    if (NT == 1) bgs_gemm_kernel<1><<<grid, SC_THREADS, 0, s>>>(a, b, d, Norm, Sum, m, n, alpha);
+    else if (NT == 2) bgs_gemm_kernel<2><<<grid, SC_THREADS, 0, s>>>(a, b, d, Norm, Sum, m, n, alpha);
+    else bgs_gemm_kernel<4><<<grid, SC_THREADS, 0, s>>>(a, b, d, Norm, Sum, m, n, alpha);
+    int st = check_launch("bgs_gemm_kernel");
+    if (st) return st;
+    bgs_softmax_kernel<<<dim3(m, batch_count), 256, 0, s>>>(d, Norm, Sum, (__nv_bfloat16 *)Softmax, m, n, nblk);
+    return check_launch("bgs_softmax_kernel");
+}
+
+}  // extern "C"

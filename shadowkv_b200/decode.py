@@ -1,0 +1,123 @@
+"""Fused decode path: thin torch wrappers of the ``skv_decode_*`` C ABI.
+
+One layer of one decode step of ShadowKV (models/kvcache/shadow.py:547-597
+and models/attention/shadow.py:22-48) as four launches groups:
+
+1. ``select``  -- landmark scoring, top-k, slot-stable reuse diff;
+2. ``gather_values`` -- zero-copy fetch of missed V chunks (copy stream);
+3. ``reconstruct_keys`` -- tensor-core U x SV^T + RoPE of the missed keys;
+4. ``attention`` -- split-K GQA attention over the buffer.
+
+The slot-stable cache keeps every hit chunk where it is and refills only the
+slots of chunks that dropped out, so no hit is ever moved (the reference
+compacts hits in place, kernels/copy.cuh:476-479).  ``slots[b,h,s]`` names
+the chunk cached in buffer rows ``sparse_start + 8s .. +8``.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+
+import torch
+
+from ._lib import DecodeGeom, check, lib
+
+
+@dataclass
+class Geometry:
+    batch: int
+    kv_heads: int
+    q_heads: int
+    rank: int
+    select_sets: int
+    num_landmarks: int
+    num_chunks: int
+    ctx_len: int
+    buf_len: int
+    sparse_start: int
+    rope_mode: int = 0          # 0 rotate-half (cos_sin width 128), 1 GLM (width 64)
+    cos_sin_stride: int = 128
+    cos_sin_rows: int = 0
+    head_dim: int = 128
+    chunk_size: int = 8
+    scale: float = 1.0 / math.sqrt(128)
+
+    def c(self) -> DecodeGeom:
+        return DecodeGeom(self.batch, self.kv_heads, self.q_heads, self.head_dim, self.rank, self.chunk_size,
+                          self.select_sets, self.num_landmarks, self.num_chunks, self.ctx_len, self.buf_len,
+                          self.sparse_start, self.rope_mode, self.cos_sin_stride, self.cos_sin_rows,
+                          float(self.scale))
+
+
+def _stream(stream=None) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def _req(t: torch.Tensor, name: str, dtype, shape=None):
+    if not t.is_cuda or t.dtype != dtype or not t.is_contiguous():
+        raise RuntimeError(f"{name} must be a contiguous CUDA {dtype} tensor "
+                           f"(got {t.dtype}, cuda={t.is_cuda}, contiguous={t.is_contiguous()})")
+    if shape is not None and tuple(t.shape) != tuple(shape):
+        raise RuntimeError(f"{name} must have shape {tuple(shape)}, got {tuple(t.shape)}")
+    return t.data_ptr()
+
+
+class DecodeWorkspace:
+    """Scratch of one decode layer: selection logits and attention partials."""
+
+    def __init__(self, geom: Geometry, device):
+        self.geom = geom
+        g = geom.c()
+        self.select_bytes = int(lib.skv_decode_select_workspace(ctypes.byref(g)))
+        self.attn_bytes = int(lib.skv_decode_attention_workspace(ctypes.byref(g), geom.buf_len))
+        if self.select_bytes == 0:
+            check(1, "skv_decode_select_workspace (geometry rejected)")
+        self.select_ws = torch.empty(self.select_bytes, dtype=torch.uint8, device=device)
+        self.attn_ws = torch.empty(max(self.attn_bytes, 256), dtype=torch.uint8, device=device)
+        bh = geom.batch * geom.kv_heads
+        self.miss_slot = torch.zeros(bh, geom.select_sets, dtype=torch.int32, device=device)
+        self.miss_chunk = torch.zeros(bh, geom.select_sets, dtype=torch.int32, device=device)
+        self.miss_count = torch.zeros(bh, dtype=torch.int32, device=device)
+
+
+def select(geom: Geometry, ws: DecodeWorkspace, q: torch.Tensor, landmarks: torch.Tensor,
+           landmark_idx: torch.Tensor, slots: torch.Tensor, stream=None) -> None:
+    g = geom.c()
+    check(lib.skv_decode_select(
+        ctypes.byref(g), _req(q, "q", torch.bfloat16), _req(landmarks, "landmarks", torch.bfloat16),
+        _req(landmark_idx, "landmark_idx", torch.int64), _req(slots, "slots", torch.int32),
+        ws.miss_slot.data_ptr(), ws.miss_chunk.data_ptr(), ws.miss_count.data_ptr(),
+        ws.select_ws.data_ptr(), ws.select_bytes, _stream(stream)), "skv_decode_select")
+
+
+def gather_values(geom: Geometry, ws: DecodeWorkspace, v_host: torch.Tensor, v_buf: torch.Tensor,
+                  stream=None) -> None:
+    if v_host.is_cuda or not v_host.is_pinned() or v_host.dtype != torch.bfloat16 or not v_host.is_contiguous():
+        raise RuntimeError("v_host must be a contiguous pinned CPU bf16 tensor")
+    g = geom.c()
+    check(lib.skv_decode_gather_values(
+        ctypes.byref(g), v_host.data_ptr(), _req(v_buf, "v_buf", torch.bfloat16),
+        ws.miss_slot.data_ptr(), ws.miss_chunk.data_ptr(), ws.miss_count.data_ptr(), _stream(stream)),
+        "skv_decode_gather_values")
+
+
+def reconstruct_keys(geom: Geometry, ws: DecodeWorkspace, U: torch.Tensor, SVt: torch.Tensor,
+                     cos_sin: torch.Tensor, k_buf: torch.Tensor, stream=None) -> None:
+    g = geom.c()
+    check(lib.skv_decode_reconstruct_keys(
+        ctypes.byref(g), _req(U, "U", torch.bfloat16), _req(SVt, "SVt", torch.bfloat16),
+        _req(cos_sin, "cos_sin", torch.bfloat16), _req(k_buf, "k_buf", torch.bfloat16),
+        ws.miss_slot.data_ptr(), ws.miss_chunk.data_ptr(), ws.miss_count.data_ptr(), _stream(stream)),
+        "skv_decode_reconstruct_keys")
+
+
+def attention(geom: Geometry, ws: DecodeWorkspace, q: torch.Tensor, k_buf: torch.Tensor, v_buf: torch.Tensor,
+              seq_len: int, out: torch.Tensor, stream=None) -> torch.Tensor:
+    g = geom.c()
+    check(lib.skv_decode_attention(
+        ctypes.byref(g), _req(q, "q", torch.bfloat16), _req(k_buf, "k_buf", torch.bfloat16),
+        _req(v_buf, "v_buf", torch.bfloat16), int(seq_len), _req(out, "out", torch.bfloat16),
+        ws.attn_ws.data_ptr(), ws.attn_bytes, _stream(stream)), "skv_decode_attention")
+    return out

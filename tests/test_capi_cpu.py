@@ -1,0 +1,68 @@
+"""CPU: the C-ABI library loads, exports every declared symbol, validates arguments."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    src = open(os.path.join(ROOT, "include", "shadowkv_b200.h")).read()
+    return sorted(set(re.findall(r"SKV_API\s+[\w\s\*]*?\b(skv_\w+)\s*\(", src)))
+
+
+def test_header_declares_the_reference_bindings_and_decode_api():
+    names = declared_symbols()
+    for n in ["skv_gather_copy", "skv_gather_copy_d2d_with_offsets", "skv_reorder_keys_and_compute_offsets",
+              "skv_gather_copy_with_offsets", "skv_apply_rotary_pos_emb", "skv_apply_rotary_pos_emb_new",
+              "skv_apply_rotary_pos_emb_new_v2", "skv_apply_rotary_pos_emb_push_cache",
+              "skv_apply_rotary_pos_emb_push_cache_opt", "skv_apply_rotary_pos_emb_push_cache_opt_glm",
+              "skv_batch_gather_gemm", "skv_batch_gemm_softmax", "skv_decode_select", "skv_decode_gather_values",
+              "skv_decode_reconstruct_keys", "skv_decode_attention"]:
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    from shadowkv_b200 import _lib
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    for n in declared_symbols():
+        assert hasattr(lib, n), n
+    assert set(_lib.SIGNATURES) >= set(declared_symbols())
+
+
+def test_version_and_empty_error():
+    from shadowkv_b200._lib import lib
+    assert lib.skv_version() >= 10000
+    assert isinstance(lib.skv_last_error(), bytes)
+
+
+def test_argument_errors_are_reported_without_launching():
+    from shadowkv_b200._lib import lib, ShadowKVError, check
+    rc = lib.skv_reorder_keys_and_compute_offsets(None, None, None, None, 1, 8, 256, None)
+    assert rc == 1
+    assert b"null" in lib.skv_last_error()
+    rc = lib.skv_reorder_keys_and_compute_offsets(8, 8, 8, 8, 1, 8, 2048, None)
+    assert rc == 2 and b"map_size" in lib.skv_last_error()
+    with pytest.raises(ShadowKVError):
+        check(rc, "reorder")
+    rc = lib.skv_batch_gather_gemm(16, 16, None, None, 16, 16, 1, 8, 1024, 128, 100, 2048, 1024, 8, 16, None)
+    assert rc == 2 and b"rank" in lib.skv_last_error()
+    rc = lib.skv_batch_gemm_softmax(16, 16, 16, 16, 16, 16, 8, 4, 1000, 64, 1.0, 0.0, None)
+    assert rc == 2 and b"k must be 128" in lib.skv_last_error()
+
+
+def test_decode_workspace_sizes_are_pure_host():
+    from shadowkv_b200.decode import Geometry
+    from shadowkv_b200._lib import lib
+    g = Geometry(batch=1, kv_heads=8, q_heads=32, rank=160, select_sets=256, num_landmarks=15308,
+                 num_chunks=15360, ctx_len=122880, buf_len=2720, sparse_start=416).c()
+    sel = lib.skv_decode_select_workspace(ctypes.byref(g))
+    # logits (8 heads x 15308 x 4 fp32) + partials
+    assert sel >= 8 * 15308 * 4 * 4
+    att = lib.skv_decode_attention_workspace(ctypes.byref(g), 2464)
+    assert att > 0
+    bad = Geometry(batch=1, kv_heads=8, q_heads=30, rank=160, select_sets=256, num_landmarks=15308,
+                   num_chunks=15360, ctx_len=122880, buf_len=2720, sparse_start=416).c()
+    assert lib.skv_decode_select_workspace(ctypes.byref(bad)) == 0
