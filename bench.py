@@ -335,12 +335,18 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     args = ap.parse_args()
-    world, rank, local = dist_setup()
     if args.impl == "reference":
+        # the CPU reference arm runs on rank 0 only; other ranks exit without work
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        if rank != 0:
+            return
         from oracle import cpu_reference
         res = cpu_reference.run(args, world, rank)
-    else:
-        res = run_b200(args, world, rank, local)
+        print(json.dumps(res), flush=True)
+        return
+    world, rank, local = dist_setup()
+    res = run_b200(args, world, rank, local)
     if rank == 0 and res is not None:
         print(json.dumps(res), flush=True)
     if world > 1:

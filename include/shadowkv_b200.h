@@ -256,9 +256,12 @@ SKV_API int skv_decode_gather_values(const skv_decode_geom *g, const void *v_hos
                              const int32_t *miss_count, void *stream);
 
 /* Reconstruction of the missed keys: U [batch][ctx_len][rank] bf16 times
- * SV^T [batch][kv][128][rank] bf16 on tensor cores, fp32 accumulation,
- * bf16 result, RoPE at the original positions (rope_mode, cos_sin) in bf16
- * op-by-op arithmetic, written to k_buf rows sparse_start + 8*slot. */
+ * SV^T [batch][kv][128][rank] bf16 on tensor cores with fp32 accumulation,
+ * RoPE at the original positions (rope_mode, cos_sin) applied to the fp32
+ * accumulator, one rounding to bf16, written to k_buf rows
+ * sparse_start + 8*slot.  (The reference's two-kernel path rounds the GEMM
+ * output and every RoPE term to bf16; skv_batch_gather_gemm +
+ * skv_apply_rotary_pos_emb_push_cache_opt keep that arithmetic.) */
 SKV_API int skv_decode_reconstruct_keys(const skv_decode_geom *g, const void *U, const void *SVt,
                                 const void *cos_sin, void *k_buf, const int32_t *miss_slot,
                                 const int32_t *miss_chunk, const int32_t *miss_count,

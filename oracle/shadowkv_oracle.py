@@ -453,6 +453,49 @@ def apply_rotary_pos_emb_push_cache_opt(x, cos_sin, chunk_ids, cache, cnts, spar
     return out
 
 
+def rope_rotate_half_fp32(x: np.ndarray, cos: np.ndarray, sin: np.ndarray) -> np.ndarray:
+    """Rotate-half RoPE in float64 math on unrounded inputs, fp32 result.
+
+    The arithmetic of the torch path (models/tensor_op.py:132-156) without
+    intermediate bf16 rounding; the fused CUDA epilogue computes this and
+    rounds once.  x: [..., 128]; cos/sin: [..., 64].
+    """
+    x = np.asarray(x, dtype=np.float64)
+    h = x.shape[-1] // 2
+    x1, x2 = x[..., :h], x[..., h:]
+    c, s = np.asarray(cos, np.float64), np.asarray(sin, np.float64)
+    return np.concatenate([x1 * c - x2 * s, x2 * c + x1 * s], axis=-1).astype(np.float32)
+
+
+def rope_glm_fp32(x: np.ndarray, cs: np.ndarray) -> np.ndarray:
+    """GLM partial interleaved RoPE (models/glm.py:207-230) in float64 math, fp32 result."""
+    x = np.asarray(x, dtype=np.float64)
+    out = x.copy()
+    c, s = np.asarray(cs[..., :32], np.float64), np.asarray(cs[..., 32:64], np.float64)
+    xe, xo = x[..., 0:64:2], x[..., 1:64:2]
+    out[..., 0:64:2] = xe * c - xo * s
+    out[..., 1:64:2] = xo * c + xe * s
+    return out.astype(np.float32)
+
+
+def reconstruct_keys_rope(U, SVt, chunk_ids, cos_sin, glm: bool = False, chunk_size: int = 8) -> np.ndarray:
+    """Keys of the fused CUDA path: ``bf16(rope(U_rows @ SVt^T))`` with one rounding.
+
+    Same values as the torch path (models/kvcache/shadow.py:239-256) up to
+    the final bf16 rounding.  U: [T, rank]; SVt: [D, rank]; chunk_ids [n].
+    Returns [n*chunk, D] float32 holding bf16 values.
+    """
+    ids = np.asarray(chunk_ids, dtype=np.int64)
+    rows = (ids[:, None] * chunk_size + np.arange(chunk_size)).reshape(-1)
+    x = np.asarray(U, np.float64)[rows] @ np.asarray(SVt, np.float64).T
+    cs = np.asarray(cos_sin, np.float32)[rows]
+    if glm:
+        y = rope_glm_fp32(x, cs)
+    else:
+        y = rope_rotate_half_fp32(x, cs[:, :64], cs[:, 64:128])
+    return round_bf16(y)
+
+
 def rope_torch_fp32(x: np.ndarray, cos_sin: np.ndarray, positions: np.ndarray) -> np.ndarray:
     """Rotate-half RoPE in fp32 as the torch path computes it.
 

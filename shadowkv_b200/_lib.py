@@ -40,12 +40,12 @@ SIGNATURES = {
     "skv_gather_copy_d2d_with_offsets": [P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, P],
     "skv_reorder_keys_and_compute_offsets": [P, P, P, P, c_int, c_int, c_int, P],
     "skv_gather_copy_with_offsets": [P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int, P],
-    "skv_apply_rotary_pos_emb": [P, P, P, P, P] + [c_int] * 16 + [P],
-    "skv_apply_rotary_pos_emb_new": [P, P, P, P] + [c_int] * 14 + [P],
-    "skv_apply_rotary_pos_emb_new_v2": [P, P, P, P] + [c_int] * 15 + [P],
-    "skv_apply_rotary_pos_emb_push_cache": [P, P, P, P, P] + [c_int] * 20 + [P],
-    "skv_apply_rotary_pos_emb_push_cache_opt": [P, P, P, P, P] + [c_int] * 20 + [P],
-    "skv_apply_rotary_pos_emb_push_cache_opt_glm": [P, P, P, P, P] + [c_int] * 20 + [P],
+    "skv_apply_rotary_pos_emb": [P, P, P, P, P] + [c_int] * 14 + [P],
+    "skv_apply_rotary_pos_emb_new": [P, P, P, P] + [c_int] * 13 + [P],
+    "skv_apply_rotary_pos_emb_new_v2": [P, P, P, P] + [c_int] * 14 + [P],
+    "skv_apply_rotary_pos_emb_push_cache": [P, P, P, P, P] + [c_int] * 19 + [P],
+    "skv_apply_rotary_pos_emb_push_cache_opt": [P, P, P, P, P] + [c_int] * 19 + [P],
+    "skv_apply_rotary_pos_emb_push_cache_opt_glm": [P, P, P, P, P] + [c_int] * 19 + [P],
     "skv_batch_gather_gemm": [P, P, P, P, P, P] + [c_int] * 8 + [P, P],
     "skv_batch_gemm_softmax": [P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_float, c_float, P],
     "skv_decode_select_workspace": [ctypes.POINTER(DecodeGeom)],

@@ -8,10 +8,10 @@
 //
 // One CTA computes 8 chunks (64 rows) x 128 output dims over the full rank.
 // U rows of one chunk are one contiguous 8*rank*2-byte run, staged with
-// cp.async; SV^T of the head is staged once per CTA.  The epilogue rounds to
-// bf16, applies RoPE in registers (the (t, t+64) pair of a row lives in the
-// same thread of the mma accumulator layout), stages the tile in shared
-// memory and writes 256-byte rows.
+// cp.async; SV^T of the head is staged once per CTA.  The epilogue applies
+// RoPE to the fp32 accumulators in registers (the (t, t+64) pair of a row
+// lives in the same thread of the mma accumulator layout), rounds once to
+// bf16, stages the tile in shared memory and writes 256-byte rows.
 #include "common.cuh"
 
 namespace skv {
@@ -144,34 +144,42 @@ __global__ void __launch_bounds__(GG_THREADS) gather_gemm_kernel(GatherGemmArgs 
         const int e = r >> 3;                    // chunk entry
         const int c = s_chunk[e];
         const int64_t pos = (int64_t)(c < 0 ? 0 : c) * 8 + (r & 7);
+        // Without RoPE the product is rounded to bf16 (batch_gather_gemm output).
+        // With RoPE the rotation is applied to the fp32 accumulator and the
+        // result is rounded once: the fused path does not round the GEMM
+        // output and each RoPE term to bf16 as the two-kernel reference does.
         float v[16][2];
 #pragma unroll
         for (int nt = 0; nt < 16; ++nt) {
-            v[nt][0] = bf2f(f2bf(acc[nt][half * 2 + 0]));
-            v[nt][1] = bf2f(f2bf(acc[nt][half * 2 + 1]));
+            v[nt][0] = acc[nt][half * 2 + 0];
+            v[nt][1] = acc[nt][half * 2 + 1];
         }
-        if (ROPE != 0 && c >= 0 && pos < a.cs_rows) {
-            const __nv_bfloat16 *cs = a.cos_sin + pos * a.cs_stride;
-            if (ROPE == 1) {
-#pragma unroll
-                for (int nt = 0; nt < 8; ++nt) {
-#pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        const int t = nt * 8 + t4 * 2 + u;
-                        const float cc = bf2f(cs[t]), ss = bf2f(cs[t + 64]);
-                        const float x1 = v[nt][u], x2 = v[nt + 8][u];
-                        v[nt][u] = badd(bmul(x1, cc), bmul(-x2, ss));
-                        v[nt + 8][u] = badd(bmul(x2, cc), bmul(x1, ss));
-                    }
-                }
+        if (ROPE != 0 && c >= 0) {
+            if (pos >= a.cs_rows) {
+                if (t4 == 0) report_dev_error(DEV_ERR_ROW);
             } else {
+                const __nv_bfloat16 *cs = a.cos_sin + pos * a.cs_stride;
+                if (ROPE == 1) {
 #pragma unroll
-                for (int nt = 0; nt < 8; ++nt) {
-                    const int tp = (nt * 8 + t4 * 2) >> 1;  // pair index < 32
-                    const float cc = bf2f(cs[tp]), ss = bf2f(cs[tp + 32]);
-                    const float xe = v[nt][0], xo = v[nt][1];
-                    v[nt][0] = badd(bmul(xe, cc), bmul(-xo, ss));
-                    v[nt][1] = badd(bmul(xo, cc), bmul(xe, ss));
+                    for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            const int t = nt * 8 + t4 * 2 + u;
+                            const float cc = bf2f(cs[t]), ss = bf2f(cs[t + 64]);
+                            const float x1 = v[nt][u], x2 = v[nt + 8][u];
+                            v[nt][u] = x1 * cc - x2 * ss;
+                            v[nt + 8][u] = x2 * cc + x1 * ss;
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int nt = 0; nt < 8; ++nt) {
+                        const int tp = (nt * 8 + t4 * 2) >> 1;  // pair index < 32
+                        const float cc = bf2f(cs[tp]), ss = bf2f(cs[tp + 32]);
+                        const float xe = v[nt][0], xo = v[nt][1];
+                        v[nt][0] = xe * cc - xo * ss;
+                        v[nt][1] = xo * cc + xe * ss;
+                    }
                 }
             }
         }

@@ -66,3 +66,14 @@ def test_decode_workspace_sizes_are_pure_host():
     bad = Geometry(batch=1, kv_heads=8, q_heads=30, rank=160, select_sets=256, num_landmarks=15308,
                    num_chunks=15360, ctx_len=122880, buf_len=2720, sparse_start=416).c()
     assert lib.skv_decode_select_workspace(ctypes.byref(bad)) == 0
+
+
+def test_ctypes_signatures_match_header_parameter_counts():
+    """Every ctypes argtypes list has as many entries as the C declaration has parameters."""
+    from shadowkv_b200 import _lib
+    src = open(os.path.join(ROOT, "include", "shadowkv_b200.h")).read()
+    decls = dict(re.findall(r"SKV_API\s+[\w\s\*]*?\b(skv_\w+)\s*\(([^)]*)\)", src, flags=re.S))
+    for name, params in decls.items():
+        params = params.strip()
+        n = 0 if params in ("", "void") else params.count(",") + 1
+        assert len(_lib.SIGNATURES[name]) == n, f"{name}: header {n} params, ctypes {len(_lib.SIGNATURES[name])}"
