@@ -45,53 +45,61 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """SM clocks and clock-event (throttle) reasons read through NVML every 10 ms
+    while the timed region runs (read-only queries; no setting is changed)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap"}
 
     def __init__(self, index: int):
         self.index = index
-        self.rows = []
-        self.proc = None
+        self.sm, self.reasons, self.max_sm = [], set(), None
+        self._stop = threading.Event()
+        self.ok = False
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except FileNotFoundError:
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            bus = torch.cuda.get_device_properties(self.index)
+            self.h = pynvml.nvmlDeviceGetHandleByPciBusId(
+                f"{bus.pci_domain_id:08x}:{bus.pci_bus_id:02x}:{bus.pci_device_id:02x}.0")
+            self.max_sm = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.nv = pynvml
+            self.ok = True
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        except Exception as e:  # pragma: no cover - reported in the JSON line
+            self.err = repr(e)
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.rows.append([x.strip() for x in line.split(",")])
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.sm.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                try:
+                    r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                except AttributeError:
+                    r = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.01)
 
     def __exit__(self, *a):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        self._stop.set()
+        if self.ok:
+            self.t.join(timeout=2)
 
     def summary(self):
-        if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in self.rows if len(r) > 2 and r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if len(r) > 2 and r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = set()
-        for r in self.rows:
-            for i, n in enumerate(names):
-                if len(r) > 5 + i and r[5 + i].lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(self.rows)}
+        if not self.ok or not self.sm:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_sm, "reasons": ["unsampled"],
+                    "error": getattr(self, "err", "no samples")}
+        return {"sm_mhz": statistics.median(self.sm), "sm_max_mhz": self.max_sm, "reasons": sorted(self.reasons),
+                "samples": len(self.sm), "source": "NVML, 10 ms"}
 
 
 def dist_setup():
@@ -160,13 +168,12 @@ def run_b200(args, world, rank, local):
         from shadowkv_b200 import numa
         numa.bind_to_gpu_numa(local)
     cfg = workload.CONFIGS[args.config]
-    cfg.gen_len = max(cfg.gen_len, args.steps + args.warmup + 16)
     torch.manual_seed(0)
     layer = workload.Layer(cfg, device=f"cuda:{local}", seed=1000 + rank)
     cache, attn = layer.cache, layer.attn
     B, Hq, Hkv = cfg.batch, cfg.q_heads, cfg.kv_heads
     n = args.steps + args.warmup
-    inputs = [layer.next_inputs() for _ in range(n)]
+    inputs = [layer.next_inputs() for _ in range(min(n, 256))]
     pos0 = cfg.ctx
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")  # > 126 MB L2
 
@@ -175,29 +182,63 @@ def run_b200(args, world, rank, local):
     main = torch.cuda.current_stream()
     copy_stream = cache.copy_stream
 
-    def step(i, ev=None):
-        q, k, v = inputs[i]
-        pos = torch.full((B, 1), pos0 + i, dtype=torch.int64, device="cuda")
-        kv = cache
-        qr, kr = attn.apply_rotary_pos_emb(q, k, pos)
-        kv.update_kv_cache(kr, v, 0)
-        kv.select_fused(0, qr, attn.cos_sin_cache)
+    # static inputs of the captured step
+    s_q = torch.empty_like(inputs[0][0])
+    s_k = torch.empty_like(inputs[0][1])
+    s_v = torch.empty_like(inputs[0][2])
+    s_pos = torch.full((B, 1), pos0, dtype=torch.int64, device="cuda")
+    s_out = torch.empty(B, Hq, 128, dtype=torch.bfloat16, device="cuda")
+    s_qr = torch.empty(B, Hq, 1, 128, dtype=torch.bfloat16, device="cuda")
+    cache.fused_geometry(attn.cos_sin_cache)
+
+    def load_inputs(i):
+        q, k, v = inputs[i % len(inputs)]
+        s_q.copy_(q)
+        s_k.copy_(k)
+        s_v.copy_(v)
+        s_pos.fill_(pos0 + i)
+
+    def step_body(ev=None):
+        """One decode step of one layer on the static inputs (appends at row sparse_end)."""
+        cache.gen_offset = 0
+        qr = cache.append_fused(0, s_q, s_k, s_v, s_pos, attn.cos_sin_cache, q_out=s_qr)
+        cache.select_fused(0, qr, attn.cos_sin_cache)
+        cur = torch.cuda.current_stream()
         with torch.cuda.stream(copy_stream):
-            copy_stream.wait_stream(main)
+            copy_stream.wait_stream(cur)
             if ev is not None:
                 ev[0].record(copy_stream)
-            kv.fetch_values_fused(0, copy_stream)
+            cache.fetch_values_fused(0, copy_stream)
             if ev is not None:
                 ev[1].record(copy_stream)
-        kv.reconstruct_keys_fused(0, attn.cos_sin_cache)
-        main.wait_stream(copy_stream)
-        seq_len = kv.sparse_end + kv._gen_offset(0)
-        out = kv.attention(0, qr, seq_len)
-        return out, seq_len
+        cache.reconstruct_keys_fused(0, attn.cos_sin_cache)
+        cur.wait_stream(copy_stream)
+        seq_len = cache.sparse_end + cache._gen_offset(0)
+        cache.attention(0, qr, seq_len, out=s_out)
+        cache.gen_offset = 0
+        return seq_len
 
-    # warm-up
+    # warm-up (eager), then capture one step as a CUDA graph
     for i in range(args.warmup):
-        step(i)
+        load_inputs(i)
+        seq_len = step_body()
+    torch.cuda.synchronize()
+    graph = None
+    if not args.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            seq_len = step_body()
+        torch.cuda.synchronize()
+
+    def run_step(i):
+        load_inputs(i)
+        if graph is not None:
+            graph.replay()
+        else:
+            step_body()
+
+    for i in range(2):  # replay warm-up
+        run_step(i)
     barrier(world)
 
     per_step, fetch_ms, misses_all, seqlens = [], [], [], []
@@ -206,14 +247,16 @@ def run_b200(args, world, rank, local):
         t_wall = time.perf_counter()
         for i in range(args.warmup, n):
             flush.zero_()
+            load_inputs(i)
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            fe = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             s.record(main)
-            out, seq_len = step(i, fe)
+            if graph is not None:
+                graph.replay()
+            else:
+                step_body()
             e.record(main)
             e.synchronize()
             per_step.append(s.elapsed_time(e))
-            fetch_ms.append(fe[0].elapsed_time(fe[1]))
             misses_all.append(int(cache._fused_ws.miss_count.sum().item()))
             seqlens.append(seq_len)
         barrier(world)
@@ -221,6 +264,40 @@ def run_b200(args, world, rank, local):
     errs = device_errors()[0]
     if errs:
         raise RuntimeError(f"{errs} device-side index errors during the benchmark")
+
+    # ---- per-kernel times: the same steps launched eagerly, one kernel group at a time,
+    # each bracketed by CUDA events on the stream it runs on (L2 flushed before each step)
+    parts = {"append": [], "select": [], "fetch_values": [], "reconstruct_keys": [], "attention": []}
+    for i in range(args.warmup, min(n, args.warmup + 100)):
+        flush.zero_()
+        load_inputs(i)
+        cache.gen_offset = 0
+        torch.cuda.synchronize()
+
+        def timed(name, fn, stream):
+            # a GPU-side sleep keeps the stream busy until the launch is enqueued, so the
+            # events bracket device execution only, not host launch latency
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                torch.cuda._sleep(400_000)
+                a.record(stream)
+                r = fn()
+                b.record(stream)
+            b.synchronize()
+            parts[name].append(a.elapsed_time(b))
+            return r
+
+        qr = timed("append", lambda: cache.append_fused(0, s_q, s_k, s_v, s_pos, attn.cos_sin_cache, q_out=s_qr),
+                   main)
+        timed("select", lambda: cache.select_fused(0, qr, attn.cos_sin_cache), main)
+        timed("fetch_values", lambda: cache.fetch_values_fused(0, copy_stream), copy_stream)
+        timed("reconstruct_keys", lambda: cache.reconstruct_keys_fused(0, attn.cos_sin_cache), main)
+        sl = cache.sparse_end + cache._gen_offset(0)
+        timed("attention", lambda: cache.attention(0, qr, sl, out=s_out), main)
+        misses_all.append(int(cache._fused_ws.miss_count.sum().item()))
+        cache.gen_offset = 0
+    fetch_ms = parts["fetch_values"]
+    kernel_us = {k: 1e3 * statistics.mean(v) for k, v in parts.items() if v}
 
     ms_step = sum(per_step) / len(per_step)
     ms_step_max = max_over_ranks(ms_step, world)
@@ -233,27 +310,34 @@ def run_b200(args, world, rank, local):
     fetch_avg = statistics.mean(fetch_ms)
     link_achieved = host_b / (fetch_avg * 1e-3) / 1e9 if fetch_avg > 0 else 0.0
 
-    # ---- e2e through the host API: inputs from pinned host, output back to pinned host
+    # ---- e2e: inputs copied from pinned host memory, the output copied back, every step
     h_in = [tuple(t.cpu().pin_memory() for t in inp) for inp in inputs]
+    h_pos = torch.empty(B, 1, dtype=torch.int64).pin_memory()
     h_out = torch.empty(B, Hq, 128, dtype=torch.bfloat16).pin_memory()
-    d_in = [torch.empty_like(t) for t in inputs[0]]
+    nin = len(inputs)
     e2e_ms = []
-    cache.gen_offset = 0
     for i in range(args.warmup, n):
         flush.zero_()
+        h_pos.fill_(pos0 + i)
+        torch.cuda.synchronize()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record(main)
-        for dt, ht in zip(d_in, h_in[i]):
+        for dt, ht in zip((s_q, s_k, s_v), h_in[i % nin]):
             dt.copy_(ht, non_blocking=True)
-        pos = torch.full((B, 1), pos0 + i, dtype=torch.int64, device="cuda")
-        out = attn.decode_fused(d_in[0], d_in[1], d_in[2], pos, 0)
-        h_out.copy_(out.view(B, Hq, 128), non_blocking=True)
+        s_pos.copy_(h_pos, non_blocking=True)
+        if graph is not None:
+            graph.replay()
+        else:
+            step_body()
+        h_out.copy_(s_out, non_blocking=True)
         e.record(main)
         e.synchronize()
         e2e_ms.append(s.elapsed_time(e))
     e2e_step = max_over_ranks(sum(e2e_ms) / len(e2e_ms), world)
-    h2d = sum(t.numel() * t.element_size() for t in h_in[0])
+    h2d = sum(t.numel() * t.element_size() for t in h_in[0]) + h_pos.numel() * h_pos.element_size()
     d2h = h_out.numel() * h_out.element_size()
+    used_graph = graph is not None
+    del graph
 
     res = {
         "metric": "sparse-attn decode tokens/s (Llama-3-8B shape, 122k ctx)",
@@ -281,7 +365,9 @@ def run_b200(args, world, rank, local):
                           "hbm_peak_gbs": hbm_peak, "hbm_peak_kind": peak_kind, "link_peak_gbs": link_peak},
         "e2e": {"value": tokens / (e2e_step / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
-        "gpu_launches": 8 * args.steps,
+        "kernel_us": kernel_us,
+        "graph": used_graph,
+        "gpu_launches": 6 * args.steps,
         "clocks": clk.summary(),
         "wall_s": t_wall,
     }
@@ -328,11 +414,12 @@ def export_state(layer):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", default="config1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying a CUDA graph")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     args = ap.parse_args()
     if args.impl == "reference":

@@ -232,6 +232,17 @@ typedef struct {
     float scale;        /* softmax scale for scoring and attention, usually 1/sqrt(128) */
 } skv_decode_geom;
 
+/* New-token step (replaces the vllm rotary_embedding call of
+ * models/attention/shadow.py:26 / models/llama.py:149-154 and
+ * ShadowKVCache_CPU.update_kv_cache, models/kvcache/shadow.py:621-633):
+ * q [batch][q_heads][128] and k_new, v_new [batch][kv][128] bf16 of the
+ * generated token, positions [batch] int64.  Writes RoPE(q) to q_out, RoPE(k)
+ * to k_buf row `row` and v to v_buf row `row` of every head.  bf16 op-by-op
+ * RoPE arithmetic; rope_mode / cos_sin as in the geometry. */
+SKV_API int skv_decode_append(const skv_decode_geom *g, const void *q, const void *k_new,
+                              const void *v_new, const int64_t *positions, const void *cos_sin,
+                              void *q_out, void *k_buf, void *v_buf, int row, void *stream);
+
 /* Bytes of caller-provided scratch the selection needs. */
 SKV_API size_t skv_decode_select_workspace(const skv_decode_geom *g);
 

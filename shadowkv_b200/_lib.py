@@ -48,6 +48,7 @@ SIGNATURES = {
     "skv_apply_rotary_pos_emb_push_cache_opt_glm": [P, P, P, P, P] + [c_int] * 19 + [P],
     "skv_batch_gather_gemm": [P, P, P, P, P, P] + [c_int] * 8 + [P, P],
     "skv_batch_gemm_softmax": [P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_float, c_float, P],
+    "skv_decode_append": [ctypes.POINTER(DecodeGeom), P, P, P, P, P, P, P, P, c_int, P],
     "skv_decode_select_workspace": [ctypes.POINTER(DecodeGeom)],
     "skv_decode_select": [ctypes.POINTER(DecodeGeom), P, P, P, P, P, P, P, P, c_size_t, P],
     "skv_decode_gather_values": [ctypes.POINTER(DecodeGeom), P, P, P, P, P, P],

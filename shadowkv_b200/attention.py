@@ -63,8 +63,8 @@ class ShadowAttention:
     def decode_fused(self, query_states, key_states, value_states, position_ids, layer_idx):
         """Same step on the fused kernels (slot-stable reuse cache)."""
         kv = self.kv_cache
-        query_states, key_states = self.apply_rotary_pos_emb(query_states, key_states, position_ids)
-        kv.update_kv_cache(key_states, value_states, layer_idx)
+        query_states = kv.append_fused(layer_idx, query_states.contiguous(), key_states.contiguous(),
+                                       value_states.contiguous(), position_ids.contiguous(), self.cos_sin_cache)
         kv.select_fused(layer_idx, query_states, self.cos_sin_cache)
         curr = torch.cuda.current_stream()
         copy_stream = kv.copy_stream

@@ -2,6 +2,7 @@
 #include "common.cuh"
 
 #include <string.h>
+#include <mutex>
 
 namespace skv {
 
@@ -24,6 +25,39 @@ int check_launch(const char *what)
         set_error("launch of %s failed: %s", what, cudaGetErrorString(e));
         return SKV_ERR_CUDA;
     }
+    return SKV_OK;
+}
+
+int ensure_smem_attr(const void *func, int bytes, const char *name)
+{
+    struct Entry {
+        const void *func;
+        int device;
+        int bytes;
+    };
+    static Entry table[256];
+    static int used = 0;
+    static std::mutex mu;
+    int dev = 0;
+    SKV_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < used; ++i)
+        if (table[i].func == func && table[i].device == dev) {
+            if (table[i].bytes >= bytes) return SKV_OK;
+            cudaError_t e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+            if (e != cudaSuccess) {
+                set_error("cudaFuncSetAttribute(%s, %d bytes) failed: %s", name, bytes, cudaGetErrorString(e));
+                return SKV_ERR_CUDA;
+            }
+            table[i].bytes = bytes;
+            return SKV_OK;
+        }
+    cudaError_t e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) {
+        set_error("cudaFuncSetAttribute(%s, %d bytes) failed: %s", name, bytes, cudaGetErrorString(e));
+        return SKV_ERR_CUDA;
+    }
+    if (used < 256) table[used++] = Entry{func, dev, bytes};
     return SKV_OK;
 }
 

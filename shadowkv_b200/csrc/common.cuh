@@ -46,6 +46,12 @@ void clear_error();
 // Check the launch that was just issued.
 int check_launch(const char *what);
 
+// Raise the dynamic shared-memory limit of `func` to `bytes` on the current
+// device.  Done once per (function, device); later calls only compare, so a
+// launch path makes no CUDA API call beyond the launch itself (safe inside
+// stream capture after the first call).
+int ensure_smem_attr(const void *func, int bytes, const char *name);
+
 // Verify that `p` is page-locked host memory mapped for the current device;
 // on success *dev holds the device-side address of p.
 int host_to_device_ptr(const void *p, const void **dev, const char *name);

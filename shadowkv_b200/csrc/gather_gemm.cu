@@ -212,27 +212,15 @@ static size_t gg_smem_bytes(int rank)
 
 int launch_gather_gemm(const GatherGemmArgs &a, int rope, int nbh, cudaStream_t stream)
 {
-    const size_t smem = gg_smem_bytes(a.rank);
+    const int smem = (int)gg_smem_bytes(a.rank);
     dim3 grid(ceil_div(a.M, GG_CHUNKS), nbh);
-    cudaError_t e = cudaSuccess;
-    switch (rope) {
-    case 0:
-        e = cudaFuncSetAttribute(gather_gemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e == cudaSuccess) gather_gemm_kernel<0><<<grid, GG_THREADS, smem, stream>>>(a);
-        break;
-    case 1:
-        e = cudaFuncSetAttribute(gather_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e == cudaSuccess) gather_gemm_kernel<1><<<grid, GG_THREADS, smem, stream>>>(a);
-        break;
-    default:
-        e = cudaFuncSetAttribute(gather_gemm_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e == cudaSuccess) gather_gemm_kernel<2><<<grid, GG_THREADS, smem, stream>>>(a);
-        break;
-    }
-    if (e != cudaSuccess) {
-        set_error("cudaFuncSetAttribute(gather_gemm_kernel) failed: %s", cudaGetErrorString(e));
-        return SKV_ERR_CUDA;
-    }
+    const void *fn = rope == 0 ? (const void *)gather_gemm_kernel<0>
+                   : rope == 1 ? (const void *)gather_gemm_kernel<1> : (const void *)gather_gemm_kernel<2>;
+    int st = ensure_smem_attr(fn, smem, "gather_gemm_kernel");
+    if (st) return st;
+    if (rope == 0) gather_gemm_kernel<0><<<grid, GG_THREADS, smem, stream>>>(a);
+    else if (rope == 1) gather_gemm_kernel<1><<<grid, GG_THREADS, smem, stream>>>(a);
+    else gather_gemm_kernel<2><<<grid, GG_THREADS, smem, stream>>>(a);
     return check_launch("gather_gemm_kernel");
 }
 

@@ -103,31 +103,44 @@ __global__ void __launch_bounds__(SC_THREADS) score_kernel(
 
     const int r_begin = split * rows_per_split;
     const int r_end = min(L, r_begin + rows_per_split);
-    for (int r0 = r_begin + warp * 16; r0 < r_end; r0 += SC_ROWS_PER_PASS) {
-        const int rowa = r0 + g, rowb = r0 + g + 8;
-        uint4 ra[4], rb[4];
+    // each warp takes two 16-row tiles per pass; all 16 loads are issued before the math
+    for (int r0 = r_begin + warp * 32; r0 < r_end; r0 += 2 * SC_ROWS_PER_PASS) {
+        uint4 ra[2][4], rb[2][4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            ra[i] = rowa < r_end ? ld_stream_v4(lmh + (int64_t)rowa * 128 + (i * 4 + j) * 8) : make_uint4(0, 0, 0, 0);
-            rb[i] = rowb < r_end ? ld_stream_v4(lmh + (int64_t)rowb * 128 + (i * 4 + j) * 8) : make_uint4(0, 0, 0, 0);
+        for (int t = 0; t < 2; ++t) {
+            const int rowa = r0 + 16 * t + g, rowb = rowa + 8;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                ra[t][i] = rowa < r_end ? ld_stream_v4(lmh + (int64_t)rowa * 128 + (i * 4 + j) * 8) : make_uint4(0, 0, 0, 0);
+                rb[t][i] = rowb < r_end ? ld_stream_v4(lmh + (int64_t)rowb * 128 + (i * 4 + j) * 8) : make_uint4(0, 0, 0, 0);
+            }
         }
-        float acc[NT][4];
-        tile_mma<NT>(acc, ra, rb, qf);
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            const int n0 = nt * 8 + 2 * j;
+        for (int t = 0; t < 2; ++t) {
+            const int rowa = r0 + 16 * t + g, rowb = rowa + 8;
+            float acc[NT][4];
+            tile_mma<NT>(acc, ra[t], rb[t], qf);
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                const int row = u ? rowb : rowa;
-                const float x0 = acc[nt][2 * u] * scale, x1 = acc[nt][2 * u + 1] * scale;
-                if (row < r_end) {
-                    if (n0 < G) {
-                        lg[(int64_t)row * G + n0] = x0;
-                        online_update(m[nt][0], s[nt][0], x0);
-                    }
-                    if (n0 + 1 < G) {
-                        lg[(int64_t)row * G + n0 + 1] = x1;
-                        online_update(m[nt][1], s[nt][1], x1);
+            for (int nt = 0; nt < NT; ++nt) {
+                const int n0 = nt * 8 + 2 * j;
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const int row = u ? rowb : rowa;
+                    const float x0 = acc[nt][2 * u] * scale, x1 = acc[nt][2 * u + 1] * scale;
+                    if (row < r_end) {
+                        if (n0 + 1 < G && (G & 1) == 0) {  // 8-byte aligned pair
+                            *reinterpret_cast<float2 *>(lg + (int64_t)row * G + n0) = make_float2(x0, x1);
+                            online_update(m[nt][0], s[nt][0], x0);
+                            online_update(m[nt][1], s[nt][1], x1);
+                        } else if (n0 + 1 < G) {
+                            lg[(int64_t)row * G + n0] = x0;
+                            lg[(int64_t)row * G + n0 + 1] = x1;
+                            online_update(m[nt][0], s[nt][0], x0);
+                            online_update(m[nt][1], s[nt][1], x1);
+                        } else if (n0 < G) {
+                            lg[(int64_t)row * G + n0] = x0;
+                            online_update(m[nt][0], s[nt][0], x0);
+                        }
                     }
                 }
             }
@@ -246,9 +259,17 @@ __global__ void __launch_bounds__(SEL_THREADS) select_kernel(SelectArgs a)
         const int shift = 24 - 8 * pass;
         if (tid < 256) s_hist[tid] = 0;
         __syncthreads();
-        for (int c = tid; c < L; c += SEL_THREADS) {
-            const uint32_t k = keys[c];
-            if ((k & pmask) == prefix) atomicAdd(&s_hist[(k >> shift) & 255], 1);
+        // Scores of one head share their leading bits, so most keys fall in a
+        // few bins: aggregate equal bins across the warp (match_any) and let
+        // one lane per bin add the count, instead of 32 same-address atomics.
+        const int lane = tid & 31;
+        for (int base = 0; base < L; base += SEL_THREADS) {
+            const int c = base + tid;
+            const uint32_t k = c < L ? keys[c] : 0u;
+            const bool part = c < L && (k & pmask) == prefix;
+            const int bin = part ? (int)((k >> shift) & 255) : 256 + lane;
+            const unsigned peers = __match_any_sync(0xffffffffu, bin);
+            if (part && lane == __ffs(peers) - 1) atomicAdd(&s_hist[bin], __popc(peers));
         }
         __syncthreads();
         if (tid < 32) {
@@ -494,11 +515,12 @@ static SelectPlan plan_select(const skv_decode_geom *g)
     SelectPlan p = {};
     const int G = g->q_heads / g->kv_heads;
     const int BH = g->batch * g->kv_heads;
-    const int units = ceil_div(g->num_landmarks, SC_ROWS_PER_PASS);  // 128-row units per head
-    const int target_ctas = 2 * 148;
+    const int unit = 2 * SC_ROWS_PER_PASS;                       // rows of one pass of the CTA
+    const int units = ceil_div(g->num_landmarks, unit);             // per head
+    const int target_ctas = 2 * 148;                                // two resident CTAs per SM
     int per = ceil_div(units * BH, target_ctas);
     if (per < 1) per = 1;
-    p.rows_per_split = per * SC_ROWS_PER_PASS;
+    p.rows_per_split = per * unit;
     p.nsplit = ceil_div(g->num_landmarks, p.rows_per_split);
     const size_t nbw = (size_t)((g->num_chunks + 31) / 32);
     const size_t bitmaps = 2 * nbw * 4;
@@ -581,7 +603,8 @@ int skv_decode_select(const skv_decode_geom *g, const void *q, const void *landm
     a.miss_count = miss_count;
     a.G = G, a.L = g->num_landmarks, a.K = g->select_sets, a.nsplit = p.nsplit;
     a.num_chunks = g->num_chunks;
-    SKV_CUDA(cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.sel_smem));
+    st = ensure_smem_attr((const void *)select_kernel, (int)p.sel_smem, "select_kernel");
+    if (st) return st;
     select_kernel<<<BH, SEL_THREADS, p.sel_smem, s>>>(a);
     return check_launch("select_kernel");
 }

@@ -75,11 +75,27 @@ class DecodeWorkspace:
         if self.select_bytes == 0:
             check(1, "skv_decode_select_workspace (geometry rejected)")
         self.select_ws = torch.empty(self.select_bytes, dtype=torch.uint8, device=device)
-        self.attn_ws = torch.empty(max(self.attn_bytes, 256), dtype=torch.uint8, device=device)
+        # zero-initialised: the attention keeps per-head arrival counters here and
+        # leaves them at zero after every call
+        self.attn_ws = torch.zeros(max(self.attn_bytes, 256), dtype=torch.uint8, device=device)
         bh = geom.batch * geom.kv_heads
         self.miss_slot = torch.zeros(bh, geom.select_sets, dtype=torch.int32, device=device)
         self.miss_chunk = torch.zeros(bh, geom.select_sets, dtype=torch.int32, device=device)
         self.miss_count = torch.zeros(bh, dtype=torch.int32, device=device)
+
+
+def append(geom: Geometry, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, positions: torch.Tensor,
+           cos_sin: torch.Tensor, q_out: torch.Tensor, k_buf: torch.Tensor, v_buf: torch.Tensor, row: int,
+           stream=None) -> torch.Tensor:
+    """RoPE of the new token's q and k, append of k and v at buffer row ``row``; returns ``q_out``."""
+    g = geom.c()
+    check(lib.skv_decode_append(
+        ctypes.byref(g), _req(q, "q", torch.bfloat16), _req(k_new, "k_new", torch.bfloat16),
+        _req(v_new, "v_new", torch.bfloat16), _req(positions, "positions", torch.int64),
+        _req(cos_sin, "cos_sin", torch.bfloat16), _req(q_out, "q_out", torch.bfloat16),
+        _req(k_buf, "k_buf", torch.bfloat16), _req(v_buf, "v_buf", torch.bfloat16), int(row), _stream(stream)),
+        "skv_decode_append")
+    return q_out
 
 
 def select(geom: Geometry, ws: DecodeWorkspace, q: torch.Tensor, landmarks: torch.Tensor,

@@ -304,6 +304,29 @@ class ShadowKVCache_CPU:
             self._fused_ws = fused.DecodeWorkspace(self._fused_geom, self.device)
         return self._fused_geom
 
+    def append_fused(self, layer_idx, query_states, key_states, value_states, positions, cos_sin_cache,
+                     q_out=None):
+        """RoPE of the new token's q/k and append of k/v at ``sparse_end + gen_offset`` (one kernel).
+
+        query_states [B, Hq, 1, D], key/value_states [B, Hkv, 1, D] (pre-RoPE),
+        positions [B] or [B, 1] int64.  Returns the rotated query [B, Hq, 1, D].
+        Same effect as RoPE + ``update_kv_cache`` (shadow.py:621-633).
+        """
+        g = self.fused_geometry(cos_sin_cache)
+        row = self.sparse_end + self.gen_offset
+        if row >= self.buf_len:
+            raise RuntimeError("generated-token region of the K/V buffer is full")
+        B, Hq, Hk, D = self.batch_size, self.num_attention_heads, self.num_key_value_heads, self.head_dim
+        if q_out is None:
+            q_out = torch.empty(B, Hq, 1, D, dtype=self.dtype, device=self.device)
+        fused.append(g, query_states.reshape(B, Hq, D), key_states.reshape(B, Hk, D),
+                     value_states.reshape(B, Hk, D), positions.reshape(B), cos_sin_cache, q_out,
+                     self.k_cache_buffer[layer_idx], self.v_cache_buffer[layer_idx], row)
+        if layer_idx == self.num_layers - 1:
+            self.kv_offset += 1
+            self.gen_offset += 1
+        return q_out
+
     def select_fused(self, layer_idx, query_states, cos_sin_cache):
         """Scoring + top-k + slot-stable reuse diff of one layer (fused kernels)."""
         self.incoming_q_len = query_states.shape[-2]

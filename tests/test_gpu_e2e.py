@@ -1,0 +1,159 @@
+"""GPU: the reference-facing classes end to end (ShadowAttention.decode / decode_fused) vs the oracle."""
+import copy
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import shadowkv_oracle as o
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def f32(t):
+    return t.float().cpu().numpy()
+
+
+def bits(t):
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+@pytest.fixture(scope="module")
+def tiny_layer():
+    from shadowkv_b200 import workload
+    cfg = copy.deepcopy(workload.CONFIGS["tiny"])
+    return workload.Layer(cfg, device=DEV, seed=7)
+
+
+@pytest.mark.parametrize("rope_mode", [0, 1])
+def test_append_kernel(rope_mode):
+    from shadowkv_b200 import decode as fz
+    rng = np.random.default_rng(rope_mode)
+    B, Hq, Hk, buf_len, row = 3, 8, 2, 100, 77
+    width = 128 if rope_mode == 0 else 64
+    cs = o.round_bf16(rng.uniform(-1, 1, (500, width)).astype(np.float32))
+    q = o.round_bf16(rng.standard_normal((B, Hq, 128)).astype(np.float32))
+    k = o.round_bf16(rng.standard_normal((B, Hk, 128)).astype(np.float32))
+    v = o.round_bf16(rng.standard_normal((B, Hk, 128)).astype(np.float32))
+    pos = np.array([3, 499, 250], np.int64)
+    dev = lambda x: torch.from_numpy(o.f32_to_bf16_bits(x).view(np.int16)).view(torch.bfloat16).to(DEV)
+    g = fz.Geometry(batch=B, kv_heads=Hk, q_heads=Hq, rank=64, select_sets=1, num_landmarks=1, num_chunks=1,
+                    ctx_len=8, buf_len=buf_len, sparse_start=0, rope_mode=rope_mode, cos_sin_stride=width,
+                    cos_sin_rows=500)
+    kb = torch.zeros(B, Hk, buf_len, 128, dtype=torch.bfloat16, device=DEV)
+    vb = torch.zeros_like(kb)
+    qo = torch.empty(B, Hq, 128, dtype=torch.bfloat16, device=DEV)
+    fz.append(g, dev(q), dev(k), dev(v), torch.from_numpy(pos).to(DEV), dev(cs), qo, kb, vb, row)
+    c = cs[pos][:, None, :]
+    if rope_mode == 0:
+        eq = o.rope_rotate_half_bf16(q, c[..., :64], c[..., 64:])
+        ek = o.rope_rotate_half_bf16(k, c[..., :64], c[..., 64:])
+    else:
+        eq, ek = o.rope_glm_bf16(q, c), o.rope_glm_bf16(k, c)
+    assert np.array_equal(bits(qo), o.f32_to_bf16_bits(eq))
+    assert np.array_equal(bits(kb[:, :, row]), o.f32_to_bf16_bits(ek))
+    assert np.array_equal(bits(vb[:, :, row]), o.f32_to_bf16_bits(v))
+    assert (f32(kb[:, :, :row]) == 0).all() and (f32(vb[:, :, row + 1:]) == 0).all()
+
+
+def _check_buffers(layer, ids_per_slot, fused):
+    """V rows of every slot equal the host chunk; K rows equal the oracle reconstruction."""
+    c = layer.cache
+    ss = c.sparse_start
+    v_host = bits(c.v_cache_cpu[0])  # [B, H, chunks, 1024]
+    vb = bits(c.v_cache_buffer[0])
+    kb = f32(c.k_cache_buffer[0])
+    U = f32(c.U[0])
+    SVt = f32(c.SV[0])
+    cs = f32(layer.cos_sin)
+    B, H, K = ids_per_slot.shape
+    for b in range(B):
+        for h in range(H):
+            ids = ids_per_slot[b, h]
+            got_v = vb[b, h, ss:ss + 8 * K].reshape(K, 1024)
+            assert np.array_equal(got_v, v_host[b, h, ids]), "V slots"
+            if fused:
+                ek = o.reconstruct_keys_rope(U[b], SVt[b, h], ids, cs)
+            else:
+                x = o.batch_gather_gemm(U[b:b + 1], SVt[b:b + 1, h:h + 1], ids[None, None], np.zeros(1, np.int32))[0, 0]
+                pos = (ids[:, None] * 8 + np.arange(8)).reshape(-1)
+                ek = o.rope_rotate_half_bf16(x, cs[pos][:, :64], cs[pos][:, 64:])
+            np.testing.assert_allclose(kb[b, h, ss:ss + 8 * K], ek, atol=2e-2, rtol=1e-2)
+
+
+def _scores_ok(layer, q_roped, ids_per_slot, rtol):
+    c = layer.cache
+    lm = f32(c.k_landmark[0])
+    lidx = c.k_landmark_idx[0].cpu().numpy()
+    B, H, L, D = lm.shape
+    G = c.num_key_value_groups
+    sc = o.landmark_scores(q_roped.reshape(B, H, G, D), lm)
+    for b in range(B):
+        for h in range(H):
+            order = np.argsort(lidx[b, h])
+            pos = order[np.searchsorted(lidx[b, h][order], np.sort(ids_per_slot[b, h]))]
+            assert o.topk_tie_ok(sc[b, h][None], pos[None], c.select_sets, rtol=rtol)
+
+
+@pytest.mark.parametrize("path", ["fused", "reference"])
+def test_decode_steps_against_oracle(tiny_layer, path):
+    from shadowkv_b200._lib import device_errors
+    layer = tiny_layer
+    c, attn = layer.cache, layer.attn
+    # start from an empty reuse cache: every chunk of the first step is a miss, so every key
+    # in the selected region is a reconstruction (prefill wrote the exact keys of its selection)
+    c.position_ids[0].fill_(-1)
+    c.slots[0].fill_(-1)
+    hits = []
+    for step in range(4):
+        q, k, v = layer.next_inputs()
+        pos = torch.full((c.batch_size, 1), layer.cfg.ctx + step, dtype=torch.int64, device=DEV)
+        c.gen_offset = 0
+        if path == "fused":
+            out = attn.decode_fused(q, k, v, pos, 0)
+            ids = c.slots[0].cpu().numpy()
+            hits.append(c.hit_rate())
+        else:
+            out = attn.decode(q, k, v, pos, 0)
+            ids = c.position_ids[0].cpu().numpy()
+        torch.cuda.synchronize()
+        assert device_errors()[0] == 0
+        # selection: fp32 scores (fused) or the bf16 softmax of the CUTLASS path (reference)
+        qr = attn.apply_rotary_pos_emb(q, k, pos)[0]
+        _scores_ok(layer, f32(qr)[:, :, 0, :], ids, rtol=1e-5 if path == "fused" else 5e-2)
+        _check_buffers(layer, ids, fused=(path == "fused"))
+        seq_len = c.sparse_end + 1
+        ref = o.decode_attention(f32(qr)[:, :, 0, :], f32(c.k_cache_buffer[0]), f32(c.v_cache_buffer[0]), seq_len)
+        np.testing.assert_allclose(f32(out)[:, 0], ref, atol=2e-2, rtol=1e-2)
+    if path == "fused":
+        assert all(0.0 <= h <= 1.0 for h in hits)
+
+
+def test_repeated_query_is_all_hits_on_both_paths(tiny_layer):
+    """The same query twice: the second step serves every chunk from the reuse cache."""
+    layer = tiny_layer
+    c, attn = layer.cache, layer.attn
+    q, k, v = layer.next_inputs()
+    pos = torch.full((c.batch_size, 1), layer.cfg.ctx + 9, dtype=torch.int64, device=DEV)
+    full = c.batch_size * c.num_key_value_heads * c.select_sets
+    c.gen_offset = 0
+    out_ref = attn.decode(q, k, v, pos, 0)
+    c.gen_offset = 0
+    out_ref2 = attn.decode(q, k, v, pos, 0)
+    assert int(c.cnts.sum().item()) == full
+    torch.testing.assert_close(out_ref2, out_ref, atol=0, rtol=0)
+    ref_sets = np.sort(c.position_ids[0].cpu().numpy(), -1)
+    c.sync_slots_from_position_ids(0)
+    c.gen_offset = 0
+    out_f = attn.decode_fused(q, k, v, pos, 0)
+    c.gen_offset = 0
+    out_f2 = attn.decode_fused(q, k, v, pos, 0)
+    assert c.hit_rate() == 1.0
+    torch.testing.assert_close(out_f2, out_f, atol=0, rtol=0)
+    # fp32 (fused) and bf16-rounded (reference) scores select nearly the same chunks
+    f_sets = np.sort(c.slots[0].cpu().numpy(), -1)
+    for b in range(f_sets.shape[0]):
+        for h in range(f_sets.shape[1]):
+            assert len(set(f_sets[b, h]) & set(ref_sets[b, h])) >= 0.85 * f_sets.shape[2]
+    torch.testing.assert_close(out_f.float(), out_ref.float(), atol=5e-2, rtol=5e-2)
