@@ -278,12 +278,16 @@ SKV_API int skv_decode_reconstruct_keys(const skv_decode_geom *g, const void *U,
                                 const int32_t *miss_chunk, const int32_t *miss_count,
                                 void *stream);
 
-/* Bytes of caller-provided scratch the attention needs for seq_len rows. */
+/* Bytes of caller-provided scratch the attention needs for seq_len rows.
+ * Returns 0: the split partials are merged through distributed shared memory
+ * inside one thread-block cluster per head (the function is kept so callers
+ * can size a workspace generically). */
 SKV_API size_t skv_decode_attention_workspace(const skv_decode_geom *g, int seq_len);
 
 /* Split-K GQA decode attention over buffer rows [0, seq_len):
  * q [batch][q_heads][128] bf16, k_buf/v_buf [batch][kv][buf_len][128] bf16
- * -> out [batch][q_heads][128] bf16. */
+ * -> out [batch][q_heads][128] bf16.  One 8-CTA cluster per (b, kv head);
+ * workspace may be NULL. */
 SKV_API int skv_decode_attention(const skv_decode_geom *g, const void *q, const void *k_buf,
                          const void *v_buf, int seq_len, void *out, void *workspace,
                          size_t workspace_bytes, void *stream);

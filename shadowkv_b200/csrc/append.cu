@@ -12,7 +12,8 @@
 
 namespace skv {
 
-// grid = batch, 256 threads: items = (q heads + kv heads) * 64 pairs + kv heads * 16 pieces of v
+// grid = (ceil(items/256), batch), 256 threads, one item per thread:
+// items = (q heads + kv heads) * 64 pairs + kv heads * 16 pieces of v
 __global__ void __launch_bounds__(256) append_kernel(
     const __nv_bfloat16 *__restrict__ q, const __nv_bfloat16 *__restrict__ k_new,
     const __nv_bfloat16 *__restrict__ v_new, const int64_t *__restrict__ positions,
@@ -20,14 +21,14 @@ __global__ void __launch_bounds__(256) append_kernel(
     __nv_bfloat16 *__restrict__ k_buf, __nv_bfloat16 *__restrict__ v_buf, int Hq, int Hkv, int buf_len,
     int row, int rope_mode, int cs_stride, int cs_rows)
 {
-    const int b = blockIdx.x;
+    const int b = blockIdx.y;
     const int64_t pos = positions[b];
     const bool pos_ok = pos >= 0 && pos < cs_rows;
-    if (!pos_ok && threadIdx.x == 0) report_dev_error(DEV_ERR_ROW);
+    if (!pos_ok && threadIdx.x == 0 && blockIdx.x == 0) report_dev_error(DEV_ERR_ROW);
     const __nv_bfloat16 *cs = cos_sin + (pos_ok ? pos : 0) * cs_stride;
     const int rot_items = (Hq + Hkv) * 64;
     const int total = rot_items + Hkv * 16;
-    for (int it = threadIdx.x; it < total; it += blockDim.x) {
+    for (int it = blockIdx.x * blockDim.x + threadIdx.x; it < total; it += gridDim.x * blockDim.x) {
         if (it < rot_items) {
             const int head = it / 64, t = it % 64;
             const __nv_bfloat16 *x;
@@ -82,7 +83,8 @@ int skv_decode_append(const skv_decode_geom *g, const void *q, const void *k_new
     SKV_CHECK_ARG(g->cos_sin_stride >= (g->rope_mode == 0 ? 128 : 64), "cos_sin_stride too small");
     SKV_CHECK_ARG(row >= 0 && row < g->buf_len, "append row %d outside the buffer", row);
     SKV_CHECK_ARG(aligned(v_new, 16) && aligned(v_buf, 16), "v_new and v_buf must be 16-byte aligned");
-    append_kernel<<<g->batch, 256, 0, (cudaStream_t)stream>>>(
+    const int items = (g->q_heads + g->kv_heads) * 64 + g->kv_heads * 16;
+    append_kernel<<<dim3(ceil_div(items, 256), g->batch), 256, 0, (cudaStream_t)stream>>>(
         (const __nv_bfloat16 *)q, (const __nv_bfloat16 *)k_new, (const __nv_bfloat16 *)v_new, positions,
         (const __nv_bfloat16 *)cos_sin, (__nv_bfloat16 *)q_out, (__nv_bfloat16 *)k_buf, (__nv_bfloat16 *)v_buf,
         g->q_heads, g->kv_heads, g->buf_len, row, g->rope_mode, g->cos_sin_stride, g->cos_sin_rows);

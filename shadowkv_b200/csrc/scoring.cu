@@ -12,13 +12,12 @@
 // (head_dim) axis is permuted identically for A and B so that each thread
 // feeds its fragments from four 16-byte loads per row straight from global
 // memory -- no shared-memory staging and fully coalesced 256-byte rows.
-#include "common.cuh"
+#include "select.cuh"
 
 namespace skv {
 
 constexpr int SC_THREADS = 256;   // 8 warps
 constexpr int SC_ROWS_PER_PASS = 16 * (SC_THREADS / 32);
-constexpr int SEL_THREADS = 1024;
 
 // q fragments for one n-tile of 8 query rows: thread (g = lane>>2, j = lane&3)
 // holds row nt*8+g, elements (i*4+j)*8 .. +8 for i = 0..3.
@@ -172,223 +171,6 @@ __global__ void __launch_bounds__(SC_THREADS) score_kernel(
 }
 
 // ---------------------------------------------------------------------------
-// Fused path, kernel 2: per (b,h) top-k over max_g softmax_g, then the
-// slot-stable reuse diff.  One 1024-thread CTA per (b,h).
-// ---------------------------------------------------------------------------
-struct SelectArgs {
-    const float *logits;
-    const float2 *part;
-    uint32_t *gkeys;              // global key scratch (large L) or null
-    const int64_t *landmark_idx;  // [BH][L]
-    int32_t *slots;               // [BH][K] in/out
-    int32_t *miss_slot, *miss_chunk, *miss_count;
-    int G, L, K, nsplit, num_chunks;
-};
-
-__device__ int block_excl_scan_1024(int v, int *total, int *s_warp)
-{
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    int x = v;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, x, o);
-        if (lane >= o) x += y;
-    }
-    if (lane == 31) s_warp[warp] = x;
-    __syncthreads();
-    if (warp == 0) {
-        const int w = s_warp[lane];
-        int wi = w;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, wi, o);
-            if (lane >= o) wi += y;
-        }
-        s_warp[lane] = wi - w;
-        if (lane == 31) s_warp[32] = wi;
-    }
-    __syncthreads();
-    const int r = s_warp[warp] + x - v;
-    *total = s_warp[32];
-    __syncthreads();
-    return r;
-}
-
-__global__ void __launch_bounds__(SEL_THREADS) select_kernel(SelectArgs a)
-{
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    __shared__ float s_M[16], s_invZ[16];
-    __shared__ int s_hist[256];
-    __shared__ int s_warp[33];
-    __shared__ int s_sel[1024];   // selected landmark index, then chunk id
-    __shared__ int s_misssorted[1024];
-    __shared__ int s_cnt, s_digit, s_above;
-
-    const int bh = blockIdx.x, tid = threadIdx.x;
-    const int G = a.G, L = a.L, K = a.K;
-    const int nbw = (a.num_chunks + 31) >> 5;
-    uint32_t *bmA = reinterpret_cast<uint32_t *>(smem_raw);
-    uint32_t *bmB = bmA + nbw;
-    uint32_t *keys = a.gkeys ? a.gkeys + (int64_t)bh * L : (bmB + nbw);
-
-    // 1) softmax normalizers of each query head
-    if (tid < G) {
-        float mm = -INFINITY, ss = 0.f;
-        for (int i = 0; i < a.nsplit; ++i) {
-            const float2 p = a.part[((int64_t)bh * a.nsplit + i) * G + tid];
-            merge_stats(mm, ss, p.x, p.y);
-        }
-        s_M[tid] = mm;
-        s_invZ[tid] = 1.f / ss;
-    }
-    __syncthreads();
-
-    // 2) scores as order-preserving keys (scores are >= 0)
-    const float *lg = a.logits + (int64_t)bh * L * G;
-    for (int c = tid; c < L; c += SEL_THREADS) {
-        float sc = 0.f;
-        for (int gg = 0; gg < G; ++gg) sc = fmaxf(sc, __expf(lg[(int64_t)c * G + gg] - s_M[gg]) * s_invZ[gg]);
-        keys[c] = __float_as_uint(sc);
-    }
-    __syncthreads();
-
-    // 3) radix select of the K-th largest key, 8 bits per pass
-    uint32_t prefix = 0, pmask = 0;
-    int remaining = K;
-    for (int pass = 0; pass < 4; ++pass) {
-        const int shift = 24 - 8 * pass;
-        if (tid < 256) s_hist[tid] = 0;
-        __syncthreads();
-        // Scores of one head share their leading bits, so most keys fall in a
-        // few bins: aggregate equal bins across the warp (match_any) and let
-        // one lane per bin add the count, instead of 32 same-address atomics.
-        const int lane = tid & 31;
-        for (int base = 0; base < L; base += SEL_THREADS) {
-            const int c = base + tid;
-            const uint32_t k = c < L ? keys[c] : 0u;
-            const bool part = c < L && (k & pmask) == prefix;
-            const int bin = part ? (int)((k >> shift) & 255) : 256 + lane;
-            const unsigned peers = __match_any_sync(0xffffffffu, bin);
-            if (part && lane == __ffs(peers) - 1) atomicAdd(&s_hist[bin], __popc(peers));
-        }
-        __syncthreads();
-        if (tid < 32) {
-            // lane l owns digits 255-8l .. 248-8l (descending)
-            int cnt[8], tot = 0;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                cnt[i] = s_hist[255 - 8 * tid - i];
-                tot += cnt[i];
-            }
-            int incl = tot;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int y = __shfl_up_sync(0xffffffffu, incl, o);
-                if (tid >= o) incl += y;
-            }
-            int above = incl - tot;  // count of digits higher than this lane's range
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                if (above < remaining && above + cnt[i] >= remaining) {
-                    s_digit = 255 - 8 * tid - i;
-                    s_above = above;
-                }
-                above += cnt[i];
-            }
-        }
-        __syncthreads();
-        const int d = s_digit;
-        remaining -= s_above;
-        prefix |= (uint32_t)d << shift;
-        pmask |= 255u << shift;
-        __syncthreads();
-    }
-    const uint32_t T = prefix;  // K-th largest key; take `remaining` of the keys equal to T
-
-    // 4) compaction: all keys > T, then the lowest-index `remaining` keys == T
-    if (tid == 0) s_cnt = 0;
-    __syncthreads();
-    for (int c = tid; c < L; c += SEL_THREADS)
-        if (keys[c] > T) s_sel[atomicAdd(&s_cnt, 1)] = c;
-    __syncthreads();
-    const int ngt = s_cnt;
-    int taken = 0;
-    for (int base = 0; base < L && taken < remaining; base += SEL_THREADS) {
-        const int c = base + tid;
-        const int f = (c < L && keys[c] == T) ? 1 : 0;
-        int tot;
-        const int r = block_excl_scan_1024(f, &tot, s_warp);
-        if (f && taken + r < remaining) s_sel[ngt + taken + r] = c;
-        taken += tot;
-    }
-    __syncthreads();
-
-    // 5) landmark index -> chunk id; bitmap A of the new set
-    for (int w = tid; w < 2 * nbw; w += SEL_THREADS) bmA[w] = 0;
-    __syncthreads();
-    const int64_t *lidx = a.landmark_idx + (int64_t)bh * L;
-    for (int jj = tid; jj < K; jj += SEL_THREADS) {
-        const int64_t cid = lidx[s_sel[jj]];
-        int v = -1;
-        if (cid >= 0 && cid < a.num_chunks) {
-            v = (int)cid;
-            atomicOr(&bmA[v >> 5], 1u << (v & 31));
-        } else {
-            report_dev_error(DEV_ERR_HOST_CHUNK);
-        }
-        s_sel[jj] = v;
-    }
-    __syncthreads();
-
-    // 6) classify the cached slots; bitmap B of the cached set
-    int32_t *slots = a.slots + (int64_t)bh * K;
-    const int s = tid;
-    int old = -1, hit = 0;
-    if (s < K) {
-        old = slots[s];
-        if (old >= 0 && old < a.num_chunks) {
-            hit = (bmA[old >> 5] >> (old & 31)) & 1;
-            atomicOr(&bmB[old >> 5], 1u << (old & 31));
-        }
-    }
-    __syncthreads();
-
-    // 7) misses in ascending id order: scan of popcount(A & ~B) over words
-    const int wpt = (nbw + SEL_THREADS - 1) / SEL_THREADS;
-    const int w0 = tid * wpt;
-    int local = 0;
-    for (int w = w0; w < min(nbw, w0 + wpt); ++w) local += __popc(bmA[w] & ~bmB[w]);
-    int nmiss;
-    int rank = block_excl_scan_1024(local, &nmiss, s_warp);
-    for (int w = w0; w < min(nbw, w0 + wpt); ++w) {
-        uint32_t bits = bmA[w] & ~bmB[w];
-        while (bits) {
-            const int bit = __ffs(bits) - 1;
-            bits &= bits - 1;
-            if (rank < 1024) s_misssorted[rank] = w * 32 + bit;
-            ++rank;
-        }
-    }
-    __syncthreads();
-
-    // 8) refill the free slots (ascending) with the misses (ascending)
-    const int is_free = (s < K && !hit) ? 1 : 0;
-    int nfree;
-    const int r = block_excl_scan_1024(is_free, &nfree, s_warp);
-    const int nassign = min(nfree, nmiss);
-    if (is_free && r < nassign) {
-        const int id = s_misssorted[r];
-        slots[s] = id;
-        a.miss_slot[(int64_t)bh * K + r] = s;
-        a.miss_chunk[(int64_t)bh * K + r] = id;
-    }
-    if (tid == 0) {
-        a.miss_count[bh] = nassign;
-        if (nfree != nmiss) report_dev_error(DEV_ERR_SLOT);
-    }
-}
-
-// ---------------------------------------------------------------------------
 // Drop-in batch_gemm_softmax, kernel 1: D, per-256-column partial stats.
 // grid = (ceil(n/256), batch), 256 threads; warp w covers rows 32w..32w+31.
 // ---------------------------------------------------------------------------
@@ -522,11 +304,8 @@ static SelectPlan plan_select(const skv_decode_geom *g)
     if (per < 1) per = 1;
     p.rows_per_split = per * unit;
     p.nsplit = ceil_div(g->num_landmarks, p.rows_per_split);
-    const size_t nbw = (size_t)((g->num_chunks + 31) / 32);
-    const size_t bitmaps = 2 * nbw * 4;
-    const size_t keys_smem = (size_t)g->num_landmarks * 4;
-    p.keys_global = bitmaps + keys_smem > 190 * 1024;
-    p.sel_smem = bitmaps + (p.keys_global ? 0 : keys_smem);
+    p.keys_global = select_smem_bytes(g->num_landmarks, g->num_chunks, false) > 190 * 1024;
+    p.sel_smem = select_smem_bytes(g->num_landmarks, g->num_chunks, p.keys_global);
     auto align = [](size_t x) { return (x + 255) & ~(size_t)255; };
     p.off_logits = 0;
     p.off_part = align((size_t)BH * g->num_landmarks * G * 4);
@@ -544,7 +323,7 @@ static int check_geom(const skv_decode_geom *g)
     SKV_CHECK_SUPPORTED(g->q_heads / g->kv_heads <= 16, "GQA group larger than 16");
     SKV_CHECK_SUPPORTED(g->select_sets >= 1 && g->select_sets <= 1024, "select_sets outside 1..1024");
     SKV_CHECK_ARG(g->num_landmarks >= g->select_sets, "fewer landmarks than selected chunks");
-    SKV_CHECK_ARG(g->num_chunks > 0 && g->num_chunks <= (1 << 22), "num_chunks outside 1..4M");
+    SKV_CHECK_ARG(g->num_chunks > 0 && g->num_chunks <= (1 << 21), "num_chunks outside 1..2M");
     return SKV_OK;
 }
 
@@ -603,10 +382,7 @@ int skv_decode_select(const skv_decode_geom *g, const void *q, const void *landm
     a.miss_count = miss_count;
     a.G = G, a.L = g->num_landmarks, a.K = g->select_sets, a.nsplit = p.nsplit;
     a.num_chunks = g->num_chunks;
-    st = ensure_smem_attr((const void *)select_kernel, (int)p.sel_smem, "select_kernel");
-    if (st) return st;
-    select_kernel<<<BH, SEL_THREADS, p.sel_smem, s>>>(a);
-    return check_launch("select_kernel");
+    return launch_select(a, BH, p.sel_smem, s);
 }
 
 int skv_batch_gemm_softmax(const void *A, const void *B, void *D, float *Norm, float *Sum,

@@ -1,0 +1,26 @@
+// Chunk selection of the fused decode path (shared between scoring.cu and select.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace skv {
+
+constexpr int SEL_CL = 8;    // CTAs per (b, kv head): one thread-block cluster
+constexpr int SEL_T = 512;   // threads per CTA
+
+struct SelectArgs {
+    const float *logits;          // [BH][L][G] scaled logits
+    const float2 *part;           // [BH][nsplit][G] (max, sum-exp) of the scoring splits
+    uint32_t *gkeys;              // [BH][L] key scratch when a slice does not fit in shared memory, else null
+    const int64_t *landmark_idx;  // [BH][L] chunk id of every landmark
+    int32_t *slots;               // [BH][K] in/out slot table
+    int32_t *miss_slot, *miss_chunk, *miss_count;
+    int G, L, K, nsplit, num_chunks;
+};
+
+// Dynamic shared memory of one CTA of the selection kernel.
+size_t select_smem_bytes(int L, int num_chunks, bool keys_global);
+
+int launch_select(const SelectArgs &a, int BH, size_t smem, cudaStream_t stream);
+
+}  // namespace skv
