@@ -201,8 +201,7 @@ def run_b200(args, world, rank, local):
     def step_body(ev=None):
         """One decode step of one layer on the static inputs (appends at row sparse_end)."""
         cache.gen_offset = 0
-        qr = cache.append_fused(0, s_q, s_k, s_v, s_pos, attn.cos_sin_cache, q_out=s_qr)
-        cache.select_fused(0, qr, attn.cos_sin_cache)
+        qr = cache.append_select_fused(0, s_q, s_k, s_v, s_pos, attn.cos_sin_cache, q_out=s_qr)
         cur = torch.cuda.current_stream()
         with torch.cuda.stream(copy_stream):
             copy_stream.wait_stream(cur)
@@ -267,7 +266,7 @@ def run_b200(args, world, rank, local):
 
     # ---- per-kernel times: the same steps launched eagerly, one kernel group at a time,
     # each bracketed by CUDA events on the stream it runs on (L2 flushed before each step)
-    parts = {"append": [], "select": [], "fetch_values": [], "reconstruct_keys": [], "attention": []}
+    parts = {"append_select": [], "fetch_values": [], "reconstruct_keys": [], "attention": []}
     for i in range(args.warmup, min(n, args.warmup + 100)):
         flush.zero_()
         load_inputs(i)
@@ -287,9 +286,8 @@ def run_b200(args, world, rank, local):
             parts[name].append(a.elapsed_time(b))
             return r
 
-        qr = timed("append", lambda: cache.append_fused(0, s_q, s_k, s_v, s_pos, attn.cos_sin_cache, q_out=s_qr),
-                   main)
-        timed("select", lambda: cache.select_fused(0, qr, attn.cos_sin_cache), main)
+        qr = timed("append_select", lambda: cache.append_select_fused(0, s_q, s_k, s_v, s_pos, attn.cos_sin_cache,
+                                                                      q_out=s_qr), main)
         timed("fetch_values", lambda: cache.fetch_values_fused(0, copy_stream), copy_stream)
         timed("reconstruct_keys", lambda: cache.reconstruct_keys_fused(0, attn.cos_sin_cache), main)
         sl = cache.sparse_end + cache._gen_offset(0)
@@ -367,7 +365,7 @@ def run_b200(args, world, rank, local):
                 "d2h_bytes_per_step": d2h},
         "kernel_us": kernel_us,
         "graph": used_graph,
-        "gpu_launches": 6 * args.steps,
+        "gpu_launches": 5 * args.steps,
         "clocks": clk.summary(),
         "wall_s": t_wall,
     }

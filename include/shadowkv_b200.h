@@ -259,6 +259,19 @@ SKV_API int skv_decode_select(const skv_decode_geom *g, const void *q, const voi
                       int32_t *miss_chunk, int32_t *miss_count, void *workspace,
                       size_t workspace_bytes, void *stream);
 
+/* skv_decode_append followed by skv_decode_select in one scoring pass: the
+ * scoring kernel rotates the query rows of each GQA group itself and its
+ * first split per head writes q_out and the new key/value rows.  q is the
+ * pre-RoPE query; the selection uses the rotated query.  Same results as
+ * the two calls in sequence. */
+SKV_API int skv_decode_append_select(const skv_decode_geom *g, const void *q, const void *k_new,
+                                     const void *v_new, const int64_t *positions,
+                                     const void *cos_sin, void *q_out, void *k_buf, void *v_buf,
+                                     int row, const void *landmarks, const int64_t *landmark_idx,
+                                     int32_t *slots, int32_t *miss_slot, int32_t *miss_chunk,
+                                     int32_t *miss_count, void *workspace, size_t workspace_bytes,
+                                     void *stream);
+
 /* Zero-copy fetch of the missed value chunks from page-locked host memory:
  * v_host [batch][kv][num_chunks][8*128] bf16 -> v_buf rows
  * sparse_start + 8*slot of [batch][kv][buf_len][128]. */

@@ -63,9 +63,9 @@ class ShadowAttention:
     def decode_fused(self, query_states, key_states, value_states, position_ids, layer_idx):
         """Same step on the fused kernels (slot-stable reuse cache)."""
         kv = self.kv_cache
-        query_states = kv.append_fused(layer_idx, query_states.contiguous(), key_states.contiguous(),
-                                       value_states.contiguous(), position_ids.contiguous(), self.cos_sin_cache)
-        kv.select_fused(layer_idx, query_states, self.cos_sin_cache)
+        query_states = kv.append_select_fused(layer_idx, query_states.contiguous(), key_states.contiguous(),
+                                              value_states.contiguous(), position_ids.contiguous(),
+                                              self.cos_sin_cache)
         curr = torch.cuda.current_stream()
         copy_stream = kv.copy_stream
         with torch.cuda.stream(copy_stream):

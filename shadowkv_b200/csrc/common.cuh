@@ -62,7 +62,7 @@ inline bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_
 // Device-side error counter: a kernel that finds an index out of range skips
 // the access and records it here (read back by skv_device_errors()).
 // ---------------------------------------------------------------------------
-enum DevErr : uint32_t { DEV_ERR_HOST_CHUNK = 1, DEV_ERR_SLOT = 2, DEV_ERR_ROW = 3 };
+enum DevErr : uint32_t { DEV_ERR_HOST_CHUNK = 1, DEV_ERR_SLOT = 2, DEV_ERR_ROW = 3, DEV_ERR_WAIT = 4 };
 
 extern __device__ unsigned int g_dev_err_count;
 extern __device__ unsigned int g_dev_err_first;
@@ -155,5 +155,65 @@ __device__ __forceinline__ float warp_sum(float v)
 }
 
 __host__ __device__ __forceinline__ int ceil_div(int a, int b) { return (a + b - 1) / b; }
+
+// RoPE of pair t of one 128-dim bf16 row in bf16 op-by-op arithmetic.
+// mode 0: rotate-half, pair (t, t+64), cos = cs[t], sin = cs[t+64], t < 64.
+// mode 1: GLM, pair (2t, 2t+1) with cos = cs[t], sin = cs[t+32] for t < 32;
+//         for 32 <= t < 64 the pass-through dims t+32 and t+64 are copied.
+__device__ __forceinline__ void rope_pair_bf16(const __nv_bfloat16 *x, __nv_bfloat16 *o,
+                                               const __nv_bfloat16 *cs, int t, int mode)
+{
+    if (mode == 0) {
+        const float x1 = bf2f(x[t]), x2 = bf2f(x[t + 64]);
+        const float c = bf2f(cs[t]), s = bf2f(cs[t + 64]);
+        o[t] = f2bf(badd(bmul(x1, c), bmul(-x2, s)));
+        o[t + 64] = f2bf(badd(bmul(x2, c), bmul(x1, s)));
+    } else if (t < 32) {
+        const float xe = bf2f(x[2 * t]), xo = bf2f(x[2 * t + 1]);
+        const float c = bf2f(cs[t]), s = bf2f(cs[t + 32]);
+        o[2 * t] = f2bf(badd(bmul(xe, c), bmul(-xo, s)));
+        o[2 * t + 1] = f2bf(badd(bmul(xo, c), bmul(xe, s)));
+    } else {
+        o[t + 32] = x[t + 32];
+        o[t + 64] = x[t + 64];
+    }
+}
+
+// ---- mbarrier / bulk-copy helpers (sm_90+ PTX) ----
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init()
+{
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, unsigned bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// Bounded wait for the phase with the given parity; false if it did not complete.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity, unsigned max_iter = 1u << 22)
+{
+    const uint32_t a = smem_u32(bar);
+    for (unsigned it = 0; it < max_iter; ++it) {
+        uint32_t done;
+        asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                     : "=r"(done) : "r"(a), "r"(parity) : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+// Bulk (TMA, non-multicast) copy of `bytes` from this GPU's global memory into shared memory.
+__device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *gmem_src, unsigned bytes, uint64_t *bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(smem_dst)), "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
 
 }  // namespace skv

@@ -76,97 +76,207 @@ __device__ __forceinline__ void merge_stats(float &m, float &s, float m2, float 
 // ---------------------------------------------------------------------------
 // Fused path, kernel 1: logits[bh][c][g] = scale * q_g . LM_c and per-split
 // online (max, sum-exp) per query head.
-// grid = (nsplit, B*Hkv), rows [split*rows_per_split, ...).
+//
+// grid = (nsplit, B*Hkv); 8 consumer warps + 1 producer warp.  The producer
+// streams the CTA's landmark rows through a 4-stage ring of 128-row (32 KB)
+// shared-memory tiles with bulk (TMA) copies completed on mbarriers; each
+// consumer warp multiplies 16 rows of a tile per stage on the tensor cores.
+// With APPEND the kernel also performs the new-token step: it rotates the
+// query rows of its GQA group itself, and the split-0 CTA of each head writes
+// the rotated query, the rotated key and the value of the new token.
 // ---------------------------------------------------------------------------
-template <int NT>
-__global__ void __launch_bounds__(SC_THREADS) score_kernel(
-    const __nv_bfloat16 *__restrict__ q, const __nv_bfloat16 *__restrict__ lm,
-    float *__restrict__ logits, float2 *__restrict__ part, int Hkv, int G, int L,
-    int rows_per_split, float scale)
+constexpr int ST_STAGES = 4;
+constexpr int ST_ROWS = 128;
+constexpr int ST_CONSUMERS = 8;
+constexpr int ST_THREADS = (ST_CONSUMERS + 1) * 32;
+constexpr int ST_STAGE_BYTES = ST_ROWS * 256;
+constexpr int ST_SMEM = ST_STAGES * ST_STAGE_BYTES + 16 * 128 * 2 + 1024;  // tiles, q rows, alignment slack
+
+struct ScoreArgs {
+    const __nv_bfloat16 *q;      // [B][Hq][128]: rotated (plain) or pre-RoPE (APPEND)
+    const __nv_bfloat16 *lm;     // [BH][L][128]
+    float *logits;               // [BH][L][G]
+    float2 *part;                // [BH][nsplit][G]
+    int Hkv, G, L, rows_per_split;
+    float scale;
+    // new-token step (APPEND)
+    const __nv_bfloat16 *k_new, *v_new, *cos_sin;
+    const int64_t *positions;
+    __nv_bfloat16 *q_out, *k_buf, *v_buf;
+    int buf_len, row, rope_mode, cs_stride, cs_rows;
+};
+
+template <int NT, bool APPEND>
+__global__ void __launch_bounds__(ST_THREADS) score_tma_kernel(ScoreArgs a)
 {
+    extern __shared__ unsigned char smem_dyn[];
+    unsigned char *smem = reinterpret_cast<unsigned char *>(((uintptr_t)smem_dyn + 1023) & ~(uintptr_t)1023);
+    __nv_bfloat16 *sT = reinterpret_cast<__nv_bfloat16 *>(smem);                       // [STAGES][128][128]
+    __nv_bfloat16 *sQ = reinterpret_cast<__nv_bfloat16 *>(smem + ST_STAGES * ST_STAGE_BYTES);  // [16][128]
+    __shared__ __align__(8) uint64_t full[ST_STAGES], empty[ST_STAGES];
+    __shared__ float2 s_part[ST_CONSUMERS][16];
+    __shared__ int s_abort;
+
     const int bh = blockIdx.y, split = blockIdx.x, nsplit = gridDim.x;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, j = lane & 3;
-    const int b = bh / Hkv, h = bh % Hkv;
-    const __nv_bfloat16 *qrows = q + ((int64_t)b * Hkv * G + (int64_t)h * G) * 128;
-    const __nv_bfloat16 *lmh = lm + (int64_t)bh * L * 128;
-    float *lg = logits + (int64_t)bh * L * G;
+    const int G = a.G, L = a.L;
+    const int b = bh / a.Hkv, h = bh % a.Hkv;
+    const int r_begin = split * a.rows_per_split;
+    const int r_end = min(L, r_begin + a.rows_per_split);
+    const int nst = r_end > r_begin ? (r_end - r_begin + ST_ROWS - 1) / ST_ROWS : 0;
+    const __nv_bfloat16 *lmh = a.lm + (int64_t)bh * L * 128;
 
-    uint4 qf[NT][4];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) load_q_frag(qf[nt], qrows, G, nt, lane);
+    const bool producer = warp == ST_CONSUMERS && lane == 0;
+    if (producer) {
+        for (int s = 0; s < ST_STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], ST_CONSUMERS);
+        }
+        s_abort = 0;
+        mbar_fence_init();
+        // the first tiles go out before the query prologue below
+        for (int i = 0; i < min(nst, ST_STAGES); ++i) {
+            const int r0 = r_begin + i * ST_ROWS;
+            const int nr = min(ST_ROWS, r_end - r0);
+            mbar_arrive_expect_tx(&full[i], (unsigned)nr * 256u);
+            bulk_g2s(sT + (size_t)i * ST_ROWS * 128, lmh + (int64_t)r0 * 128, (unsigned)nr * 256u, &full[i]);
+        }
+    }
+    // query rows of the group in shared memory (rows >= G are zero)
+    const __nv_bfloat16 *qrows = a.q + ((int64_t)b * a.Hkv * G + (int64_t)h * G) * 128;
+    if (APPEND) {
+        const int64_t pos = a.positions[b];
+        const bool ok = pos >= 0 && pos < a.cs_rows;
+        if (!ok && tid == 0 && split == 0) report_dev_error(DEV_ERR_ROW);
+        const __nv_bfloat16 *cs = a.cos_sin + (ok ? pos : 0) * a.cs_stride;
+        for (int it = tid; it < 16 * 64; it += ST_THREADS) {
+            const int r = it >> 6, t = it & 63;
+            if (r < G && ok) rope_pair_bf16(qrows + (int64_t)r * 128, sQ + r * 128, cs, t, a.rope_mode);
+            else if (r >= G) { sQ[r * 128 + t] = f2bf(0.f); sQ[r * 128 + t + 64] = f2bf(0.f); }
+        }
+        if (split == 0 && ok) {
+            // new token: rotated key and value of head h at buffer row `row`
+            const int64_t brow = ((int64_t)bh * a.buf_len + a.row) * 128;
+            if (tid < 64) rope_pair_bf16(a.k_new + (int64_t)bh * 128, a.k_buf + brow, cs, tid, a.rope_mode);
+            else if (tid < 80) st_v4(a.v_buf + brow + (tid - 64) * 8, ld_nc_v4(a.v_new + (int64_t)bh * 128 + (tid - 64) * 8));
+        }
+    } else {
+        for (int it = tid; it < 16 * 16; it += ST_THREADS) {
+            const int r = it >> 4, c = (it & 15) * 8;
+            st_v4(sQ + r * 128 + c, r < G ? ld_nc_v4(qrows + (int64_t)r * 128 + c) : make_uint4(0, 0, 0, 0));
+        }
+    }
+    __syncthreads();
+    if (APPEND && split == 0) {
+        // rotated query rows of the group for the attention
+        for (int it = tid; it < G * 16; it += ST_THREADS) {
+            const int r = it >> 4, c = (it & 15) * 8;
+            st_v4(a.q_out + ((int64_t)b * a.Hkv * G + (int64_t)h * G + r) * 128 + c, ld_v4(sQ + r * 128 + c));
+        }
+    }
 
-    float m[NT][2], s[NT][2];
+    float m[NT][2], sm[NT][2];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) m[nt][0] = m[nt][1] = -INFINITY, s[nt][0] = s[nt][1] = 0.f;
+    for (int nt = 0; nt < NT; ++nt) m[nt][0] = m[nt][1] = -INFINITY, sm[nt][0] = sm[nt][1] = 0.f;
 
-    const int r_begin = split * rows_per_split;
-    const int r_end = min(L, r_begin + rows_per_split);
-    // each warp takes two 16-row tiles per pass; all 16 loads are issued before the math
-    for (int r0 = r_begin + warp * 32; r0 < r_end; r0 += 2 * SC_ROWS_PER_PASS) {
-        uint4 ra[2][4], rb[2][4];
-#pragma unroll
-        for (int t = 0; t < 2; ++t) {
-            const int rowa = r0 + 16 * t + g, rowb = rowa + 8;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                ra[t][i] = rowa < r_end ? ld_stream_v4(lmh + (int64_t)rowa * 128 + (i * 4 + j) * 8) : make_uint4(0, 0, 0, 0);
-                rb[t][i] = rowb < r_end ? ld_stream_v4(lmh + (int64_t)rowb * 128 + (i * 4 + j) * 8) : make_uint4(0, 0, 0, 0);
+    if (warp == ST_CONSUMERS) {
+        // ---- producer: one elected lane streams the row tiles
+        if (lane == 0) {
+            for (int i = ST_STAGES; i < nst; ++i) {
+                const int s = i % ST_STAGES;
+                if (!mbar_wait(&empty[s], ((i / ST_STAGES) - 1) & 1)) {
+                    report_dev_error(DEV_ERR_WAIT);
+                    atomicExch(&s_abort, 1);
+                    break;
+                }
+                const int r0 = r_begin + i * ST_ROWS;
+                const int nr = min(ST_ROWS, r_end - r0);
+                mbar_arrive_expect_tx(&full[s], (unsigned)nr * 256u);
+                bulk_g2s(sT + (size_t)s * ST_ROWS * 128, lmh + (int64_t)r0 * 128, (unsigned)nr * 256u, &full[s]);
             }
         }
+    } else {
+        // ---- consumers
+        uint4 qf[NT][4];
 #pragma unroll
-        for (int t = 0; t < 2; ++t) {
-            const int rowa = r0 + 16 * t + g, rowb = rowa + 8;
+        for (int nt = 0; nt < NT; ++nt) {
+            const int n = nt * 8 + g;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) qf[nt][i] = ld_v4(sQ + n * 128 + (i * 4 + j) * 8);
+        }
+        float *lg = a.logits + (int64_t)bh * L * G;
+        for (int i = 0; i < nst; ++i) {
+            const int s = i % ST_STAGES;
+            if (!mbar_wait(&full[s], (i / ST_STAGES) & 1)) {
+                report_dev_error(DEV_ERR_WAIT);
+                atomicExch(&s_abort, 1);
+                break;
+            }
+            const __nv_bfloat16 *tile = sT + (size_t)s * ST_ROWS * 128;
+            const int lr = warp * 16 + g;  // local rows lr and lr+8
+            uint4 ra[4], rb[4];
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {
+                ra[q4] = ld_v4(tile + lr * 128 + (q4 * 4 + j) * 8);
+                rb[q4] = ld_v4(tile + (lr + 8) * 128 + (q4 * 4 + j) * 8);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);  // the tile's rows are in registers
             float acc[NT][4];
-            tile_mma<NT>(acc, ra[t], rb[t], qf);
+            tile_mma<NT>(acc, ra, rb, qf);
+            const int r0 = r_begin + i * ST_ROWS;
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
                 const int n0 = nt * 8 + 2 * j;
 #pragma unroll
                 for (int u = 0; u < 2; ++u) {
-                    const int row = u ? rowb : rowa;
-                    const float x0 = acc[nt][2 * u] * scale, x1 = acc[nt][2 * u + 1] * scale;
+                    const int row = r0 + lr + 8 * u;
+                    const float x0 = acc[nt][2 * u] * a.scale, x1 = acc[nt][2 * u + 1] * a.scale;
                     if (row < r_end) {
-                        if (n0 + 1 < G && (G & 1) == 0) {  // 8-byte aligned pair
+                        if (n0 + 1 < G && (G & 1) == 0) {
                             *reinterpret_cast<float2 *>(lg + (int64_t)row * G + n0) = make_float2(x0, x1);
-                            online_update(m[nt][0], s[nt][0], x0);
-                            online_update(m[nt][1], s[nt][1], x1);
+                            online_update(m[nt][0], sm[nt][0], x0);
+                            online_update(m[nt][1], sm[nt][1], x1);
                         } else if (n0 + 1 < G) {
                             lg[(int64_t)row * G + n0] = x0;
                             lg[(int64_t)row * G + n0 + 1] = x1;
-                            online_update(m[nt][0], s[nt][0], x0);
-                            online_update(m[nt][1], s[nt][1], x1);
+                            online_update(m[nt][0], sm[nt][0], x0);
+                            online_update(m[nt][1], sm[nt][1], x1);
                         } else if (n0 < G) {
                             lg[(int64_t)row * G + n0] = x0;
-                            online_update(m[nt][0], s[nt][0], x0);
+                            online_update(m[nt][0], sm[nt][0], x0);
                         }
                     }
                 }
             }
         }
-    }
-    // reduce over the 8 lanes sharing j, then over warps
-    __shared__ float2 s_part[SC_THREADS / 32][16];
+        // reduce over the 8 lanes sharing j
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
+        for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            float mm = m[nt][u], ss = s[nt][u];
+            for (int u = 0; u < 2; ++u) {
+                float mm = m[nt][u], ss = sm[nt][u];
 #pragma unroll
-            for (int o = 4; o < 32; o <<= 1) {
-                const float m2 = __shfl_xor_sync(0xffffffffu, mm, o);
-                const float s2 = __shfl_xor_sync(0xffffffffu, ss, o);
-                merge_stats(mm, ss, m2, s2);
+                for (int o = 4; o < 32; o <<= 1) {
+                    const float m2 = __shfl_xor_sync(0xffffffffu, mm, o);
+                    const float s2 = __shfl_xor_sync(0xffffffffu, ss, o);
+                    merge_stats(mm, ss, m2, s2);
+                }
+                const int n = nt * 8 + 2 * j + u;
+                if (g == 0 && n < 16) s_part[warp][n] = make_float2(mm, ss);
             }
-            const int n = nt * 8 + 2 * j + u;
-            if (g == 0 && n < 16) s_part[warp][n] = make_float2(mm, ss);
         }
     }
     __syncthreads();
-    if (threadIdx.x < G) {
+    if (s_abort && warp == ST_CONSUMERS && lane == 0) {
+        // do not leave bulk copies in flight into this CTA's shared memory
+        for (int s = 0; s < ST_STAGES; ++s) mbar_wait(&full[s], 0, 1u << 16), mbar_wait(&full[s], 1, 1u << 16);
+    }
+    if (tid < G) {
         float mm = -INFINITY, ss = 0.f;
-        for (int w = 0; w < SC_THREADS / 32; ++w) merge_stats(mm, ss, s_part[w][threadIdx.x].x, s_part[w][threadIdx.x].y);
-        part[((int64_t)bh * nsplit + split) * G + threadIdx.x] = make_float2(mm, ss);
+        for (int w = 0; w < ST_CONSUMERS; ++w) merge_stats(mm, ss, s_part[w][tid].x, s_part[w][tid].y);
+        a.part[((int64_t)bh * nsplit + split) * G + tid] = make_float2(mm, ss);
     }
 }
 
@@ -297,12 +407,10 @@ static SelectPlan plan_select(const skv_decode_geom *g)
     SelectPlan p = {};
     const int G = g->q_heads / g->kv_heads;
     const int BH = g->batch * g->kv_heads;
-    const int unit = 2 * SC_ROWS_PER_PASS;                       // rows of one pass of the CTA
-    const int units = ceil_div(g->num_landmarks, unit);             // per head
-    const int target_ctas = 2 * 148;                                // two resident CTAs per SM
-    int per = ceil_div(units * BH, target_ctas);
+    const int stages = ceil_div(g->num_landmarks, ST_ROWS);  // 128-row tiles per head
+    int per = ceil_div(stages * BH, 148);                      // about one CTA per SM
     if (per < 1) per = 1;
-    p.rows_per_split = per * unit;
+    p.rows_per_split = per * ST_ROWS;
     p.nsplit = ceil_div(g->num_landmarks, p.rows_per_split);
     p.keys_global = select_smem_bytes(g->num_landmarks, g->num_chunks, false) > 190 * 1024;
     p.sel_smem = select_smem_bytes(g->num_landmarks, g->num_chunks, p.keys_global);
@@ -327,6 +435,53 @@ static int check_geom(const skv_decode_geom *g)
     return SKV_OK;
 }
 
+static int run_select(const skv_decode_geom *g, const ScoreArgs &sa_in, const int64_t *landmark_idx,
+                      int32_t *slots, int32_t *miss_slot, int32_t *miss_chunk, int32_t *miss_count,
+                      void *workspace, size_t workspace_bytes, bool append, cudaStream_t s)
+{
+    const SelectPlan p = plan_select(g);
+    SKV_CHECK_ARG(workspace != nullptr && workspace_bytes >= p.total,
+                  "workspace of %zu bytes needed, %zu given", p.total, workspace_bytes);
+    SKV_CHECK_ARG(aligned(workspace, 256), "workspace must be 256-byte aligned");
+    const int G = g->q_heads / g->kv_heads;
+    const int BH = g->batch * g->kv_heads;
+    unsigned char *ws = reinterpret_cast<unsigned char *>(workspace);
+    ScoreArgs sa = sa_in;
+    sa.logits = reinterpret_cast<float *>(ws + p.off_logits);
+    sa.part = reinterpret_cast<float2 *>(ws + p.off_part);
+    sa.Hkv = g->kv_heads;
+    sa.G = G;
+    sa.L = g->num_landmarks;
+    sa.rows_per_split = p.rows_per_split;
+    sa.scale = g->scale;
+    const void *fn = G <= 8 ? (append ? (const void *)score_tma_kernel<1, true> : (const void *)score_tma_kernel<1, false>)
+                            : (append ? (const void *)score_tma_kernel<2, true> : (const void *)score_tma_kernel<2, false>);
+    int st = ensure_smem_attr(fn, ST_SMEM, "score_tma_kernel");
+    if (st) return st;
+    dim3 grid(p.nsplit, BH);
+    if (G <= 8) {
+        if (append) score_tma_kernel<1, true><<<grid, ST_THREADS, ST_SMEM, s>>>(sa);
+        else score_tma_kernel<1, false><<<grid, ST_THREADS, ST_SMEM, s>>>(sa);
+    } else {
+        if (append) score_tma_kernel<2, true><<<grid, ST_THREADS, ST_SMEM, s>>>(sa);
+        else score_tma_kernel<2, false><<<grid, ST_THREADS, ST_SMEM, s>>>(sa);
+    }
+    st = check_launch("score_tma_kernel");
+    if (st) return st;
+    SelectArgs a = {};
+    a.logits = sa.logits;
+    a.part = sa.part;
+    a.gkeys = p.keys_global ? reinterpret_cast<uint32_t *>(ws + p.off_keys) : nullptr;
+    a.landmark_idx = landmark_idx;
+    a.slots = slots;
+    a.miss_slot = miss_slot;
+    a.miss_chunk = miss_chunk;
+    a.miss_count = miss_count;
+    a.G = G, a.L = g->num_landmarks, a.K = g->select_sets, a.nsplit = p.nsplit;
+    a.num_chunks = g->num_chunks;
+    return launch_select(a, BH, p.sel_smem, s);
+}
+
 }  // namespace skv
 
 using namespace skv;
@@ -349,40 +504,47 @@ int skv_decode_select(const skv_decode_geom *g, const void *q, const void *landm
     SKV_CHECK_ARG(q && landmarks && landmark_idx && slots && miss_slot && miss_chunk && miss_count,
                   "null pointer argument");
     SKV_CHECK_ARG(aligned(q, 16) && aligned(landmarks, 16), "q and landmarks must be 16-byte aligned");
-    const SelectPlan p = plan_select(g);
-    SKV_CHECK_ARG(workspace != nullptr && workspace_bytes >= p.total,
-                  "workspace of %zu bytes needed, %zu given", p.total, workspace_bytes);
-    SKV_CHECK_ARG(aligned(workspace, 256), "workspace must be 256-byte aligned");
-    cudaStream_t s = (cudaStream_t)stream;
-    const int G = g->q_heads / g->kv_heads;
-    const int BH = g->batch * g->kv_heads;
-    unsigned char *ws = reinterpret_cast<unsigned char *>(workspace);
-    float *logits = reinterpret_cast<float *>(ws + p.off_logits);
-    float2 *part = reinterpret_cast<float2 *>(ws + p.off_part);
-    dim3 grid(p.nsplit, BH);
-    if (G <= 8)
-        score_kernel<1><<<grid, SC_THREADS, 0, s>>>((const __nv_bfloat16 *)q, (const __nv_bfloat16 *)landmarks,
-                                                   logits, part, g->kv_heads, G, g->num_landmarks,
-                                                   p.rows_per_split, g->scale);
-    else
-        score_kernel<2><<<grid, SC_THREADS, 0, s>>>((const __nv_bfloat16 *)q, (const __nv_bfloat16 *)landmarks,
-                                                   logits, part, g->kv_heads, G, g->num_landmarks,
-                                                   p.rows_per_split, g->scale);
-    st = check_launch("score_kernel");
-    if (st) return st;
+    ScoreArgs sa = {};
+    sa.q = (const __nv_bfloat16 *)q;
+    sa.lm = (const __nv_bfloat16 *)landmarks;
+    return run_select(g, sa, landmark_idx, slots, miss_slot, miss_chunk, miss_count, workspace, workspace_bytes,
+                      false, (cudaStream_t)stream);
+}
 
-    SelectArgs a = {};
-    a.logits = logits;
-    a.part = part;
-    a.gkeys = p.keys_global ? reinterpret_cast<uint32_t *>(ws + p.off_keys) : nullptr;
-    a.landmark_idx = landmark_idx;
-    a.slots = slots;
-    a.miss_slot = miss_slot;
-    a.miss_chunk = miss_chunk;
-    a.miss_count = miss_count;
-    a.G = G, a.L = g->num_landmarks, a.K = g->select_sets, a.nsplit = p.nsplit;
-    a.num_chunks = g->num_chunks;
-    return launch_select(a, BH, p.sel_smem, s);
+int skv_decode_append_select(const skv_decode_geom *g, const void *q, const void *k_new, const void *v_new,
+                             const int64_t *positions, const void *cos_sin, void *q_out, void *k_buf,
+                             void *v_buf, int row, const void *landmarks, const int64_t *landmark_idx,
+                             int32_t *slots, int32_t *miss_slot, int32_t *miss_chunk, int32_t *miss_count,
+                             void *workspace, size_t workspace_bytes, void *stream)
+{
+    int st = check_geom(g);
+    if (st) return st;
+    SKV_CHECK_ARG(q && k_new && v_new && positions && cos_sin && q_out && k_buf && v_buf && landmarks &&
+                      landmark_idx && slots && miss_slot && miss_chunk && miss_count,
+                  "null pointer argument");
+    SKV_CHECK_SUPPORTED(g->rope_mode == 0 || g->rope_mode == 1, "rope_mode must be 0 or 1");
+    SKV_CHECK_ARG(g->cos_sin_stride >= (g->rope_mode == 0 ? 128 : 64), "cos_sin_stride too small");
+    SKV_CHECK_ARG(row >= 0 && row < g->buf_len, "append row %d outside the buffer", row);
+    SKV_CHECK_ARG(aligned(q, 16) && aligned(landmarks, 16) && aligned(q_out, 16) && aligned(v_new, 16) &&
+                      aligned(v_buf, 16),
+                  "q, q_out, v_new, v_buf and landmarks must be 16-byte aligned");
+    ScoreArgs sa = {};
+    sa.q = (const __nv_bfloat16 *)q;
+    sa.lm = (const __nv_bfloat16 *)landmarks;
+    sa.k_new = (const __nv_bfloat16 *)k_new;
+    sa.v_new = (const __nv_bfloat16 *)v_new;
+    sa.cos_sin = (const __nv_bfloat16 *)cos_sin;
+    sa.positions = positions;
+    sa.q_out = (__nv_bfloat16 *)q_out;
+    sa.k_buf = (__nv_bfloat16 *)k_buf;
+    sa.v_buf = (__nv_bfloat16 *)v_buf;
+    sa.buf_len = g->buf_len;
+    sa.row = row;
+    sa.rope_mode = g->rope_mode;
+    sa.cs_stride = g->cos_sin_stride;
+    sa.cs_rows = g->cos_sin_rows;
+    return run_select(g, sa, landmark_idx, slots, miss_slot, miss_chunk, miss_count, workspace, workspace_bytes,
+                      true, (cudaStream_t)stream);
 }
 
 int skv_batch_gemm_softmax(const void *A, const void *B, void *D, float *Norm, float *Sum,

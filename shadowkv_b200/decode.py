@@ -108,6 +108,24 @@ def select(geom: Geometry, ws: DecodeWorkspace, q: torch.Tensor, landmarks: torc
         ws.select_ws.data_ptr(), ws.select_bytes, _stream(stream)), "skv_decode_select")
 
 
+def append_select(geom: Geometry, ws: DecodeWorkspace, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+                  positions: torch.Tensor, cos_sin: torch.Tensor, q_out: torch.Tensor, k_buf: torch.Tensor,
+                  v_buf: torch.Tensor, row: int, landmarks: torch.Tensor, landmark_idx: torch.Tensor,
+                  slots: torch.Tensor, stream=None) -> torch.Tensor:
+    """``append`` + ``select`` in one scoring pass (q pre-RoPE); returns the rotated query ``q_out``."""
+    g = geom.c()
+    check(lib.skv_decode_append_select(
+        ctypes.byref(g), _req(q, "q", torch.bfloat16), _req(k_new, "k_new", torch.bfloat16),
+        _req(v_new, "v_new", torch.bfloat16), _req(positions, "positions", torch.int64),
+        _req(cos_sin, "cos_sin", torch.bfloat16), _req(q_out, "q_out", torch.bfloat16),
+        _req(k_buf, "k_buf", torch.bfloat16), _req(v_buf, "v_buf", torch.bfloat16), int(row),
+        _req(landmarks, "landmarks", torch.bfloat16), _req(landmark_idx, "landmark_idx", torch.int64),
+        _req(slots, "slots", torch.int32), ws.miss_slot.data_ptr(), ws.miss_chunk.data_ptr(),
+        ws.miss_count.data_ptr(), ws.select_ws.data_ptr(), ws.select_bytes, _stream(stream)),
+        "skv_decode_append_select")
+    return q_out
+
+
 def gather_values(geom: Geometry, ws: DecodeWorkspace, v_host: torch.Tensor, v_buf: torch.Tensor,
                   stream=None) -> None:
     if v_host.is_cuda or not v_host.is_pinned() or v_host.dtype != torch.bfloat16 or not v_host.is_contiguous():

@@ -327,6 +327,26 @@ class ShadowKVCache_CPU:
             self.gen_offset += 1
         return q_out
 
+    def append_select_fused(self, layer_idx, query_states, key_states, value_states, positions, cos_sin_cache,
+                            q_out=None):
+        """``append_fused`` + ``select_fused`` in one scoring pass; returns the rotated query."""
+        g = self.fused_geometry(cos_sin_cache)
+        row = self.sparse_end + self.gen_offset
+        if row >= self.buf_len:
+            raise RuntimeError("generated-token region of the K/V buffer is full")
+        B, Hq, Hk, D = self.batch_size, self.num_attention_heads, self.num_key_value_heads, self.head_dim
+        if q_out is None:
+            q_out = torch.empty(B, Hq, 1, D, dtype=self.dtype, device=self.device)
+        self.incoming_q_len = 1
+        fused.append_select(g, self._fused_ws, query_states.reshape(B, Hq, D), key_states.reshape(B, Hk, D),
+                            value_states.reshape(B, Hk, D), positions.reshape(B), cos_sin_cache, q_out,
+                            self.k_cache_buffer[layer_idx], self.v_cache_buffer[layer_idx], row,
+                            self.k_landmark[layer_idx], self.k_landmark_idx[layer_idx], self.slots[layer_idx])
+        if layer_idx == self.num_layers - 1:
+            self.kv_offset += 1
+            self.gen_offset += 1
+        return q_out
+
     def select_fused(self, layer_idx, query_states, cos_sin_cache):
         """Scoring + top-k + slot-stable reuse diff of one layer (fused kernels)."""
         self.incoming_q_len = query_states.shape[-2]

@@ -157,3 +157,41 @@ def test_repeated_query_is_all_hits_on_both_paths(tiny_layer):
         for h in range(f_sets.shape[1]):
             assert len(set(f_sets[b, h]) & set(ref_sets[b, h])) >= 0.85 * f_sets.shape[2]
     torch.testing.assert_close(out_f.float(), out_ref.float(), atol=5e-2, rtol=5e-2)
+
+
+def test_append_select_equals_append_then_select(tiny_layer):
+    """The fused scoring pass (RoPE + append inside) gives the same q, K/V rows and slots as the two calls."""
+    from shadowkv_b200 import decode as fz
+    layer = tiny_layer
+    c, attn = layer.cache, layer.attn
+    g = c.fused_geometry(layer.cos_sin)
+    q, k, v = layer.next_inputs()
+    pos = torch.full((c.batch_size,), layer.cfg.ctx + 3, dtype=torch.int64, device=DEV)
+    row = c.sparse_end + 5
+    slots0 = c.slots[0].clone()
+    kb0, vb0 = c.k_cache_buffer[0].clone(), c.v_cache_buffer[0].clone()
+    B, Hq, Hk = c.batch_size, c.num_attention_heads, c.num_key_value_heads
+    q1 = torch.empty(B, Hq, 128, dtype=torch.bfloat16, device=DEV)
+    fz.append(g, q.reshape(B, Hq, 128).contiguous(), k.reshape(B, Hk, 128).contiguous(),
+              v.reshape(B, Hk, 128).contiguous(), pos, layer.cos_sin, q1, c.k_cache_buffer[0],
+              c.v_cache_buffer[0], row)
+    fz.select(g, c._fused_ws, q1, c.k_landmark[0], c.k_landmark_idx[0], c.slots[0])
+    s1 = c.slots[0].clone()
+    ms1, mc1, n1 = c._fused_ws.miss_slot.clone(), c._fused_ws.miss_chunk.clone(), c._fused_ws.miss_count.clone()
+    kb1, vb1 = c.k_cache_buffer[0].clone(), c.v_cache_buffer[0].clone()
+    c.slots[0].copy_(slots0)
+    c.k_cache_buffer[0].copy_(kb0)
+    c.v_cache_buffer[0].copy_(vb0)
+    q2 = torch.empty_like(q1)
+    fz.append_select(g, c._fused_ws, q.reshape(B, Hq, 128).contiguous(), k.reshape(B, Hk, 128).contiguous(),
+                     v.reshape(B, Hk, 128).contiguous(), pos, layer.cos_sin, q2, c.k_cache_buffer[0],
+                     c.v_cache_buffer[0], row, c.k_landmark[0], c.k_landmark_idx[0], c.slots[0])
+    torch.cuda.synchronize()
+    assert torch.equal(q1, q2)
+    assert torch.equal(c.slots[0], s1)
+    assert torch.equal(c._fused_ws.miss_count, n1)
+    for b in range(B * Hk):
+        n = int(n1[b])
+        assert torch.equal(c._fused_ws.miss_slot[b, :n], ms1[b, :n])
+        assert torch.equal(c._fused_ws.miss_chunk[b, :n], mc1[b, :n])
+    assert torch.equal(c.k_cache_buffer[0], kb1) and torch.equal(c.v_cache_buffer[0], vb1)
