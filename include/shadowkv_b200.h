@@ -272,6 +272,22 @@ SKV_API int skv_decode_append_select(const skv_decode_geom *g, const void *q, co
                                      int32_t *miss_count, void *workspace, size_t workspace_bytes,
                                      void *stream);
 
+/* Allocation-free skv_decode_select (no counterpart in the reference).
+ * For callers that cannot provide a scratch buffer: an FFI host that owns no
+ * CUDA allocator (it only receives the model-state tensors), or a runtime that
+ * plans all device memory at start-up and forbids allocation on the token
+ * path.  The scratch is a fixed 32 MiB array in the library's device memory,
+ * held on every GPU that loads the library until exit; geometries needing
+ * more (skv_decode_select_workspace) are rejected with SKV_ERR_UNSUPPORTED.
+ * All calls on a device share the array: calls that overlap on the GPU race.
+ * Nothing in it needs clearing (each call writes what it reads).  The first
+ * call on a device looks up the array's address; make it before any stream
+ * capture.  Same outputs as skv_decode_select. */
+SKV_API int skv_decode_select_noalloc(const skv_decode_geom *g, const void *q, const void *landmarks,
+                                      const int64_t *landmark_idx, int32_t *slots,
+                                      int32_t *miss_slot, int32_t *miss_chunk,
+                                      int32_t *miss_count, void *stream);
+
 /* Zero-copy fetch of the missed value chunks from page-locked host memory:
  * v_host [batch][kv][num_chunks][8*128] bf16 -> v_buf rows
  * sparse_start + 8*slot of [batch][kv][buf_len][128]. */

@@ -52,6 +52,7 @@ SIGNATURES = {
     "skv_decode_select_workspace": [ctypes.POINTER(DecodeGeom)],
     "skv_decode_select": [ctypes.POINTER(DecodeGeom), P, P, P, P, P, P, P, P, c_size_t, P],
     "skv_decode_append_select": [ctypes.POINTER(DecodeGeom)] + [P] * 8 + [c_int] + [P] * 7 + [c_size_t, P],
+    "skv_decode_select_noalloc": [ctypes.POINTER(DecodeGeom), P, P, P, P, P, P, P, P],
     "skv_decode_gather_values": [ctypes.POINTER(DecodeGeom), P, P, P, P, P, P],
     "skv_decode_reconstruct_keys": [ctypes.POINTER(DecodeGeom), P, P, P, P, P, P, P, P],
     "skv_decode_attention_workspace": [ctypes.POINTER(DecodeGeom), c_int],
