@@ -143,28 +143,42 @@ __global__ void __launch_bounds__(ST_THREADS) score_tma_kernel(ScoreArgs a)
             bulk_g2s(sT + (size_t)i * ST_ROWS * 128, lmh + (int64_t)r0 * 128, (unsigned)nr * 256u, &full[i]);
         }
     }
-    // query rows of the group in shared memory (rows >= G are zero)
+    // query rows of the group in shared memory (rows >= G are zero).  The raw
+    // rows (and the cos/sin row) are loaded in one parallel round first, so the
+    // prologue costs one memory latency, not one per loop trip.
     const __nv_bfloat16 *qrows = a.q + ((int64_t)b * a.Hkv * G + (int64_t)h * G) * 128;
+    __shared__ __align__(16) __nv_bfloat16 s_raw[18 * 128];  // q rows, then k row, then cos/sin row
+    int64_t pos = 0;
+    bool pos_ok = true;
     if (APPEND) {
-        const int64_t pos = a.positions[b];
-        const bool ok = pos >= 0 && pos < a.cs_rows;
-        if (!ok && tid == 0 && split == 0) report_dev_error(DEV_ERR_ROW);
-        const __nv_bfloat16 *cs = a.cos_sin + (ok ? pos : 0) * a.cs_stride;
+        pos = a.positions[b];
+        pos_ok = pos >= 0 && pos < a.cs_rows;
+        if (!pos_ok && tid == 0 && split == 0) report_dev_error(DEV_ERR_ROW);
+    }
+    const int nrows = APPEND ? 18 : 16;  // q rows (16) [+ new key row, cos/sin row]
+    for (int it = tid; it < nrows * 16; it += ST_THREADS) {
+        const int r = it >> 4, c = (it & 15) * 8;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (r < G) v = ld_nc_v4(qrows + (int64_t)r * 128 + c);
+        else if (APPEND && r == 16) v = ld_nc_v4(a.k_new + (int64_t)bh * 128 + c);
+        else if (APPEND && r == 17 && pos_ok && c < a.cs_stride) v = ld_nc_v4(a.cos_sin + pos * a.cs_stride + c);
+        st_v4((APPEND ? s_raw : sQ) + r * 128 + c, v);
+    }
+    uint4 vnew = make_uint4(0, 0, 0, 0);
+    if (APPEND && split == 0 && tid >= 64 && tid < 80) vnew = ld_nc_v4(a.v_new + (int64_t)bh * 128 + (tid - 64) * 8);
+    __syncthreads();
+    if (APPEND) {
+        const __nv_bfloat16 *cs = s_raw + 17 * 128;
         for (int it = tid; it < 16 * 64; it += ST_THREADS) {
             const int r = it >> 6, t = it & 63;
-            if (r < G && ok) rope_pair_bf16(qrows + (int64_t)r * 128, sQ + r * 128, cs, t, a.rope_mode);
+            if (r < G && pos_ok) rope_pair_bf16(s_raw + r * 128, sQ + r * 128, cs, t, a.rope_mode);
             else if (r >= G) { sQ[r * 128 + t] = f2bf(0.f); sQ[r * 128 + t + 64] = f2bf(0.f); }
         }
-        if (split == 0 && ok) {
+        if (split == 0 && pos_ok) {
             // new token: rotated key and value of head h at buffer row `row`
             const int64_t brow = ((int64_t)bh * a.buf_len + a.row) * 128;
-            if (tid < 64) rope_pair_bf16(a.k_new + (int64_t)bh * 128, a.k_buf + brow, cs, tid, a.rope_mode);
-            else if (tid < 80) st_v4(a.v_buf + brow + (tid - 64) * 8, ld_nc_v4(a.v_new + (int64_t)bh * 128 + (tid - 64) * 8));
-        }
-    } else {
-        for (int it = tid; it < 16 * 16; it += ST_THREADS) {
-            const int r = it >> 4, c = (it & 15) * 8;
-            st_v4(sQ + r * 128 + c, r < G ? ld_nc_v4(qrows + (int64_t)r * 128 + c) : make_uint4(0, 0, 0, 0));
+            if (tid < 64) rope_pair_bf16(s_raw + 16 * 128, a.k_buf + brow, cs, tid, a.rope_mode);
+            else if (tid < 80) st_v4(a.v_buf + brow + (tid - 64) * 8, vnew);
         }
     }
     __syncthreads();
@@ -175,7 +189,6 @@ __global__ void __launch_bounds__(ST_THREADS) score_tma_kernel(ScoreArgs a)
             st_v4(a.q_out + ((int64_t)b * a.Hkv * G + (int64_t)h * G + r) * 128 + c, ld_v4(sQ + r * 128 + c));
         }
     }
-
     float m[NT][2], sm[NT][2];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) m[nt][0] = m[nt][1] = -INFINITY, sm[nt][0] = sm[nt][1] = 0.f;
@@ -526,8 +539,8 @@ int skv_decode_append_select(const skv_decode_geom *g, const void *q, const void
     SKV_CHECK_ARG(g->cos_sin_stride >= (g->rope_mode == 0 ? 128 : 64), "cos_sin_stride too small");
     SKV_CHECK_ARG(row >= 0 && row < g->buf_len, "append row %d outside the buffer", row);
     SKV_CHECK_ARG(aligned(q, 16) && aligned(landmarks, 16) && aligned(q_out, 16) && aligned(v_new, 16) &&
-                      aligned(v_buf, 16),
-                  "q, q_out, v_new, v_buf and landmarks must be 16-byte aligned");
+                      aligned(v_buf, 16) && aligned(k_new, 16) && aligned(cos_sin, 16) && g->cos_sin_stride % 8 == 0,
+                  "q, q_out, k_new, v_new, v_buf, landmarks and cos_sin rows must be 16-byte aligned");
     ScoreArgs sa = {};
     sa.q = (const __nv_bfloat16 *)q;
     sa.lm = (const __nv_bfloat16 *)landmarks;

@@ -53,6 +53,8 @@ __device__ __forceinline__ void merge_ms(float &m, float &s, float m2, float s2)
     m = mm;
 }
 
+__device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
+
 // Exclusive prefix sum over the CTA (SEL_T threads).
 __device__ int cta_excl_scan(int v, int *total, int *s_warp)
 {
@@ -111,15 +113,25 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
 
     if (tid == 0) s_cnt = 0;
 
-    // 1) softmax normalisers of each query head of the group
-    if (tid < G) {
+    // 1) softmax normalisers of each query head of the group: warp w merges the
+    //    split partials of head w (lanes load in parallel, then a shuffle merge)
+    if (warp_id() < G) {
+        const int gg = warp_id();
         float mm = -INFINITY, ss = 0.f;
-        for (int i = 0; i < a.nsplit; ++i) {
-            const float2 p = a.part[((int64_t)bh * a.nsplit + i) * G + tid];
+        for (int i = lane; i < a.nsplit; i += 32) {
+            const float2 p = a.part[((int64_t)bh * a.nsplit + i) * G + gg];
             merge_ms(mm, ss, p.x, p.y);
         }
-        s_M[tid] = mm;
-        s_invZ[tid] = 1.f / ss;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float m2 = __shfl_xor_sync(0xffffffffu, mm, o);
+            const float s2 = __shfl_xor_sync(0xffffffffu, ss, o);
+            merge_ms(mm, ss, m2, s2);
+        }
+        if (lane == 0) {
+            s_M[gg] = mm;
+            s_invZ[gg] = 1.f / ss;
+        }
     }
     __syncthreads();
 
