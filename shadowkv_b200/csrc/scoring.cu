@@ -86,6 +86,7 @@ __device__ __forceinline__ void merge_stats(float &m, float &s, float m2, float 
 // the rotated query, the rotated key and the value of the new token.
 // ---------------------------------------------------------------------------
 constexpr int ST_STAGES = 4;
+constexpr int ST_PRE = 1;     // stages issued before the query prologue
 constexpr int ST_ROWS = 128;
 constexpr int ST_CONSUMERS = 8;
 constexpr int ST_THREADS = (ST_CONSUMERS + 1) * 32;
@@ -127,6 +128,7 @@ __global__ void __launch_bounds__(ST_THREADS) score_tma_kernel(ScoreArgs a)
     const int nst = r_end > r_begin ? (r_end - r_begin + ST_ROWS - 1) / ST_ROWS : 0;
     const __nv_bfloat16 *lmh = a.lm + (int64_t)bh * L * 128;
 
+    pdl_launch_dependents();  // the selection kernel may be scheduled early (it waits for this grid)
     const bool producer = warp == ST_CONSUMERS && lane == 0;
     if (producer) {
         for (int s = 0; s < ST_STAGES; ++s) {
@@ -135,8 +137,10 @@ __global__ void __launch_bounds__(ST_THREADS) score_tma_kernel(ScoreArgs a)
         }
         s_abort = 0;
         mbar_fence_init();
-        // the first tiles go out before the query prologue below
-        for (int i = 0; i < min(nst, ST_STAGES); ++i) {
+        // the first tile goes out before the query prologue below; the other
+        // stages follow once the prologue's own loads are back, so they do
+        // not queue behind a burst of tile traffic
+        for (int i = 0; i < min(nst, ST_PRE); ++i) {
             const int r0 = r_begin + i * ST_ROWS;
             const int nr = min(ST_ROWS, r_end - r0);
             mbar_arrive_expect_tx(&full[i], (unsigned)nr * 256u);
@@ -196,9 +200,9 @@ __global__ void __launch_bounds__(ST_THREADS) score_tma_kernel(ScoreArgs a)
     if (warp == ST_CONSUMERS) {
         // ---- producer: one elected lane streams the row tiles
         if (lane == 0) {
-            for (int i = ST_STAGES; i < nst; ++i) {
+            for (int i = ST_PRE; i < nst; ++i) {
                 const int s = i % ST_STAGES;
-                if (!mbar_wait(&empty[s], ((i / ST_STAGES) - 1) & 1)) {
+                if (i >= ST_STAGES && !mbar_wait(&empty[s], ((i / ST_STAGES) - 1) & 1)) {
                     report_dev_error(DEV_ERR_WAIT);
                     atomicExch(&s_abort, 1);
                     break;
@@ -425,7 +429,7 @@ static SelectPlan plan_select(const skv_decode_geom *g)
     if (per < 1) per = 1;
     p.rows_per_split = per * ST_ROWS;
     p.nsplit = ceil_div(g->num_landmarks, p.rows_per_split);
-    p.keys_global = select_smem_bytes(g->num_landmarks, g->num_chunks, false) > 190 * 1024;
+    p.keys_global = select_smem_bytes(g->num_landmarks, g->num_chunks, false) > 150 * 1024;
     p.sel_smem = select_smem_bytes(g->num_landmarks, g->num_chunks, p.keys_global);
     auto align = [](size_t x) { return (x + 255) & ~(size_t)255; };
     p.off_logits = 0;

@@ -6,13 +6,17 @@
 //
 // One 8-CTA thread-block cluster per (b, kv head).  Every CTA turns its
 // eighth of the landmarks into order-preserving keys (max over the group of
-// the softmax-normalised score), then the cluster runs a 4-pass radix select
-// (8 bits per pass): each CTA builds a private histogram, the cluster barrier
-// publishes it, and every CTA sums the eight histograms through distributed
-// shared memory.  Selected landmarks are appended to rank 0's list with
-// cluster-scope shared-memory atomics (one per warp); when the k-th score is
-// tied the lowest landmark indices win.  Rank 0 then maps landmarks to chunk
-// ids and computes the slot-stable diff with two shared-memory bitmaps.
+// the softmax-normalised score) and builds a 2048-bin histogram of their top
+// bits.  After one cluster barrier every CTA sums the eight histograms through
+// distributed shared memory and finds the bin that holds the K-th largest key.
+// Keys above that bin are selected outright: their chunk ids are set in rank
+// 0's bitmap of the new set with cluster-scope shared-memory atomics.  Keys in
+// the bin (a few dozen for softmax scores) are appended to rank 0's candidate
+// list, which rank 0 ranks exactly -- key descending, landmark index
+// ascending, so that when the K-th score is tied the lowest landmark indices
+// win.  Should more than SEL_CAND keys share the bin, the cluster falls back
+// to an exact 4-pass radix select (8 bits per pass) with the same tie rule.
+// Rank 0 then computes the slot-stable diff from the two bitmaps.
 #include "select.cuh"
 
 namespace skv {
@@ -86,17 +90,33 @@ __device__ int cta_excl_scan(int v, int *total, int *s_warp)
     return r;
 }
 
+__device__ __forceinline__ void atom_or_dsmem_u32(uint32_t addr, uint32_t v)
+{
+    asm volatile("red.shared::cluster.or.b32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint4 ld_dsmem_v4(uint32_t addr)
+{
+    uint4 v;
+    asm volatile("ld.shared::cluster.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr) : "memory");
+    return v;
+}
+
 __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
 {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     __shared__ float s_M[16], s_invZ[16];
-    __shared__ unsigned s_hist[2][256];
+    __shared__ __align__(16) unsigned s_h1[SEL_BINS];  // first-pass histogram (DSMEM-read)
+    __shared__ unsigned s_hist[2][256];                // exact fallback: 8-bit pass histograms
     __shared__ unsigned s_tot[256];
     __shared__ int s_warp[33];
-    __shared__ int s_sel[1024];        // rank 0: selected landmark index, then chunk id
-    __shared__ int s_misssorted[1024]; // rank 0: missed chunk ids, ascending
-    __shared__ unsigned s_cnt;         // rank 0: append position of the selected list
-    __shared__ int s_digit, s_above;
+    __shared__ uint32_t s_ckey[SEL_CAND];              // rank 0: boundary-bin candidates (key,
+    __shared__ int s_clm[SEL_CAND], s_cchunk[SEL_CAND]; //   landmark index, chunk id)
+    __shared__ int s_misssorted[1024];                 // rank 0: missed chunk ids, ascending
+    __shared__ unsigned s_ncand, s_nloc, s_cbase;
+    __shared__ uint32_t s_lkey[SEL_CAND];              // this CTA's candidates before the push
+    __shared__ int s_llm[SEL_CAND], s_lchunk[SEL_CAND];
+    __shared__ int s_digit, s_above, s_bin, s_bin_above, s_bin_cnt;
     __shared__ unsigned s_eq_rank[SEL_CL];
 
     const unsigned rank = blockIdx.x;
@@ -108,10 +128,37 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
     const int nbw = (a.num_chunks + 31) >> 5;
     uint32_t *dyn = reinterpret_cast<uint32_t *>(smem_raw);
     uint32_t *keys = a.gkeys ? a.gkeys + (int64_t)bh * L + c0 : dyn;
-    uint32_t *bmA = a.gkeys ? dyn : dyn + slice;
+    int *lidx_s = a.gkeys ? nullptr : reinterpret_cast<int *>(dyn + slice);
+    uint32_t *bmA = a.gkeys ? dyn : dyn + 2 * slice;
     uint32_t *bmB = bmA + nbw;
+    const int64_t *lidx = a.landmark_idx + (int64_t)bh * L + c0;
+    int32_t *slots = a.slots + (int64_t)bh * K;
 
-    if (tid == 0) s_cnt = 0;
+    // 0) loads that do not depend on the scores: the cached slots (rank 0,
+    //    thread t owns slots 2t, 2t+1) and the chunk ids of this slice
+    int old[2] = {-1, -1};
+    if (rank == 0) {
+        for (int w = tid; w < 2 * nbw; w += SEL_T) bmA[w] = 0;  // bmA and bmB are contiguous
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int sl = 2 * tid + u;
+            if (sl < K) old[u] = slots[sl];
+        }
+    }
+    if (lidx_s) {
+        for (int cb = tid; cb < n; cb += 4 * SEL_T) {
+            int64_t v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u] = cb + u * SEL_T < n ? __ldg(lidx + cb + u * SEL_T) : -1;
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (cb + u * SEL_T < n) lidx_s[cb + u * SEL_T] = (v[u] >= 0 && v[u] < a.num_chunks) ? (int)v[u] : -1;
+        }
+    }
+    for (int i = tid; i < SEL_BINS; i += SEL_T) s_h1[i] = 0;
+    if (tid == 0) s_ncand = s_nloc = 0;
+
+    pdl_wait();  // the scoring kernel's logits and partials are complete from here on
 
     // 1) softmax normalisers of each query head of the group: warp w merges the
     //    split partials of head w (lanes load in parallel, then a shuffle merge)
@@ -134,184 +181,267 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
         }
     }
     __syncthreads();
+    bool hit[2] = {false, false};
+    if (rank == 0) {
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+            if (old[u] >= 0 && old[u] < a.num_chunks) atomicOr(&bmB[old[u] >> 5], 1u << (old[u] & 31));
+    }
 
-    // 2) keys of this CTA's landmarks: bits of max_g softmax_g (>= 0, so the
-    //    unsigned order of the bits is the order of the scores)
+    // 2) keys of this CTA's landmarks -- the bits of max_g softmax_g, which is
+    //    >= 0, so the unsigned order of the bits is the order of the scores --
+    //    and their first-pass histogram over bits 30..20.  Warp-uniform loop:
+    //    lane l of warp w handles landmark 32w + l + 512j.
     const float *lg = a.logits + ((int64_t)bh * L + c0) * G;
-    if ((G & 3) == 0) {
-        constexpr int U = 4;
-        const int G4 = G >> 2;
-        for (int base = tid; base < n; base += U * SEL_T) {
-            float4 v[U][4];
+    constexpr int U = 4;
+    for (int base = (tid & ~31); base < n; base += U * SEL_T) {
+        float4 v[U][4];
+        const int G4 = (G & 3) == 0 ? G >> 2 : 0;
 #pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int c = base + u * SEL_T;
+        for (int u = 0; u < U; ++u) {
+            const int c = base + lane + u * SEL_T;
 #pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4)
-                    if (q4 < G4 && c < n) v[u][q4] = __ldcg(reinterpret_cast<const float4 *>(lg + (int64_t)c * G) + q4);
-            }
+            for (int q4 = 0; q4 < 4; ++q4)
+                if (q4 < G4 && c < n) v[u][q4] = __ldcg(reinterpret_cast<const float4 *>(lg + (int64_t)c * G) + q4);
+        }
 #pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int c = base + u * SEL_T;
-                if (c >= n) continue;
-                float sc = 0.f;
+        for (int u = 0; u < U; ++u) {
+            const int c = base + lane + u * SEL_T;
+            float sc = 0.f;
+            if (c < n) {
+                if (G4) {
 #pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4) {
-                    if (q4 < G4) {
-                        sc = fmaxf(sc, __expf(v[u][q4].x - s_M[4 * q4 + 0]) * s_invZ[4 * q4 + 0]);
-                        sc = fmaxf(sc, __expf(v[u][q4].y - s_M[4 * q4 + 1]) * s_invZ[4 * q4 + 1]);
-                        sc = fmaxf(sc, __expf(v[u][q4].z - s_M[4 * q4 + 2]) * s_invZ[4 * q4 + 2]);
-                        sc = fmaxf(sc, __expf(v[u][q4].w - s_M[4 * q4 + 3]) * s_invZ[4 * q4 + 3]);
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        if (q4 < G4) {
+                            sc = fmaxf(sc, __expf(v[u][q4].x - s_M[4 * q4 + 0]) * s_invZ[4 * q4 + 0]);
+                            sc = fmaxf(sc, __expf(v[u][q4].y - s_M[4 * q4 + 1]) * s_invZ[4 * q4 + 1]);
+                            sc = fmaxf(sc, __expf(v[u][q4].z - s_M[4 * q4 + 2]) * s_invZ[4 * q4 + 2]);
+                            sc = fmaxf(sc, __expf(v[u][q4].w - s_M[4 * q4 + 3]) * s_invZ[4 * q4 + 3]);
+                        }
                     }
+                } else {
+                    for (int gg = 0; gg < G; ++gg)
+                        sc = fmaxf(sc, __expf(lg[(int64_t)c * G + gg] - s_M[gg]) * s_invZ[gg]);
                 }
                 keys[c] = __float_as_uint(sc);
             }
+            const int bin = c < n ? (int)(__float_as_uint(sc) >> (31 - SEL_BITS1)) : SEL_BINS + lane;
+            const unsigned peers = __match_any_sync(0xffffffffu, bin);
+            if (c < n && lane == __ffs(peers) - 1) atomicAdd(&s_h1[bin], (unsigned)__popc(peers));
+        }
+    }
+    cluster_sync();  // every CTA's first-pass histogram is complete; rank 0's bitmaps are zero
+
+    // 3) every CTA sums the eight histograms (thread t: bins 2047-4t .. 2044-4t,
+    //    descending) and finds the bin holding the K-th largest key
+    {
+        const int b0 = SEL_BINS - 4 - 4 * tid;
+        uint4 part[SEL_CL];
+        const uint32_t la = (uint32_t)__cvta_generic_to_shared(&s_h1[b0]);
+#pragma unroll
+        for (unsigned r = 0; r < SEL_CL; ++r) {
+            uint32_t ra;
+            asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(la), "r"(r));
+            part[r] = ld_dsmem_v4(ra);
+        }
+        int cnt[4] = {0, 0, 0, 0};  // cnt[i]: bin b0 + 3 - i
+#pragma unroll
+        for (unsigned r = 0; r < SEL_CL; ++r) {
+            cnt[0] += (int)part[r].w;
+            cnt[1] += (int)part[r].z;
+            cnt[2] += (int)part[r].y;
+            cnt[3] += (int)part[r].x;
+        }
+        int total;
+        int above = cta_excl_scan(cnt[0] + cnt[1] + cnt[2] + cnt[3], &total, s_warp);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if (above < K && above + cnt[i] >= K) {
+                s_bin = b0 + 3 - i;
+                s_bin_above = above;
+                s_bin_cnt = cnt[i];
+            }
+            above += cnt[i];
+        }
+        __syncthreads();
+    }
+    const int bstar = s_bin, bin_above = s_bin_above, bin_cnt = s_bin_cnt;
+    const uint32_t bmA0 = dsmem_addr(bmA, 0);
+    auto chunk_of = [&](int c) -> int {
+        if (lidx_s) return lidx_s[c];
+        const int64_t v = lidx[c];
+        return (v >= 0 && v < a.num_chunks) ? (int)v : -1;
+    };
+    auto mark = [&](int cid) {  // set the chunk in rank 0's bitmap of the new set
+        if (cid >= 0) atom_or_dsmem_u32(bmA0 + 4u * (uint32_t)(cid >> 5), 1u << (cid & 31));
+        else report_dev_error(DEV_ERR_HOST_CHUNK);
+    };
+
+    if (bin_cnt <= SEL_CAND) {
+        // 4) keys above the boundary bin are selected; the keys inside it are
+        //    the candidates: compacted locally, then pushed to rank 0's list
+        //    at an offset taken with one cluster-scope atomic per CTA
+        for (int base = (tid & ~31); base < n; base += SEL_T) {
+            const int c = base + lane;
+            const uint32_t k = c < n ? keys[c] : 0u;
+            const int bin = (int)(k >> (31 - SEL_BITS1));
+            if (c < n && bin > bstar) mark(chunk_of(c));
+            const bool cand = c < n && bin == bstar;
+            const unsigned ballot = __ballot_sync(0xffffffffu, cand);
+            if (ballot) {
+                unsigned pos0 = 0;
+                if (lane == 0) pos0 = atomicAdd(&s_nloc, (unsigned)__popc(ballot));
+                pos0 = __shfl_sync(0xffffffffu, pos0, 0);
+                if (cand) {
+                    const unsigned pos = pos0 + __popc(ballot & ((1u << lane) - 1u));
+                    s_lkey[pos] = k;
+                    s_llm[pos] = c0 + c;
+                    s_lchunk[pos] = chunk_of(c);
+                }
+            }
+        }
+        __syncthreads();
+        const int nloc = (int)s_nloc;
+        if (tid == 0 && nloc > 0) s_cbase = atom_add_dsmem_u32(dsmem_addr(&s_ncand, 0), (unsigned)nloc);
+        __syncthreads();
+        if (nloc > 0) {
+            const uint32_t ckey0 = dsmem_addr(s_ckey, 0), clm0 = dsmem_addr(s_clm, 0), cch0 = dsmem_addr(s_cchunk, 0);
+            for (int i = tid; i < nloc; i += SEL_T) {
+                const uint32_t off = 4u * (s_cbase + (unsigned)i);
+                st_dsmem_u32(ckey0 + off, s_lkey[i]);
+                st_dsmem_u32(clm0 + off, (uint32_t)s_llm[i]);
+                st_dsmem_u32(cch0 + off, (uint32_t)s_lchunk[i]);
+            }
+        }
+        cluster_sync();  // rank 0 holds the candidates and the bits of the keys above them
+        if (rank != 0) return;
+        // 5) exact order among the candidates (key descending, landmark index
+        //    ascending); the first K - bin_above of them are selected.  Warp w
+        //    ranks candidates w, w + 16, ...; its lanes split the comparisons.
+        const int nc = (int)s_ncand, need = K - bin_above;
+        for (int i = warp_id(); i < nc; i += SEL_T / 32) {
+            const uint32_t ki = s_ckey[i];
+            const int li = s_clm[i];
+            unsigned before = 0;
+            for (int j = lane; j < nc; j += 32) {
+                const uint32_t kj = s_ckey[j];
+                const int lj = s_clm[j];
+                before += (kj > ki || (kj == ki && lj < li)) ? 1u : 0u;
+            }
+            before = __reduce_add_sync(0xffffffffu, before);
+            if (lane == 0 && (int)before < need) {
+                const int cid = s_cchunk[i];
+                if (cid >= 0) atomicOr(&bmA[cid >> 5], 1u << (cid & 31));
+                else report_dev_error(DEV_ERR_HOST_CHUNK);
+            }
         }
     } else {
-        for (int c = tid; c < n; c += SEL_T) {
-            float sc = 0.f;
-            for (int gg = 0; gg < G; ++gg) sc = fmaxf(sc, __expf(lg[(int64_t)c * G + gg] - s_M[gg]) * s_invZ[gg]);
-            keys[c] = __float_as_uint(sc);
-        }
-    }
-
-    // 3) cluster-wide radix select of the K-th largest key
-    uint32_t prefix = 0, pmask = 0;
-    int remaining = K, n_equal = 0;
-    for (int pass = 0; pass < 4; ++pass) {
-        const int shift = 24 - 8 * pass;
-        unsigned *h = s_hist[pass & 1];
-        if (tid < 256) h[tid] = 0;
-        __syncthreads();
-        for (int base = 0; base < n; base += SEL_T) {
-            const int c = base + tid;
-            const uint32_t k = c < n ? keys[c] : 0u;
-            const bool part = c < n && (k & pmask) == prefix;
-            const int bin = part ? (int)((k >> shift) & 255) : 256 + lane;
-            const unsigned peers = __match_any_sync(0xffffffffu, bin);
-            if (part && lane == __ffs(peers) - 1) atomicAdd(&h[bin], (unsigned)__popc(peers));
-        }
-        cluster_sync();  // every CTA's histogram of this pass is complete
-        if (tid < 256) {
-            unsigned t = 0;
-#pragma unroll
-            for (unsigned r = 0; r < SEL_CL; ++r) t += ld_dsmem_u32(dsmem_addr(&h[tid], r));
-            s_tot[tid] = t;
-        }
-        __syncthreads();
-        if (tid < 32) {
-            // lane l owns digits 255-8l .. 248-8l (descending)
-            int cnt[8], tot = 0;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                cnt[i] = (int)s_tot[255 - 8 * tid - i];
-                tot += cnt[i];
+        // 4') more than SEL_CAND keys share the boundary bin (e.g. many equal
+        //     scores): exact cluster-wide radix select, 4 passes of 8 bits
+        uint32_t prefix = 0, pmask = 0;
+        int remaining = K, n_equal = 0;
+        for (int pass = 0; pass < 4; ++pass) {
+            const int shift = 24 - 8 * pass;
+            unsigned *h = s_hist[pass & 1];
+            if (tid < 256) h[tid] = 0;
+            __syncthreads();
+            for (int base = (tid & ~31); base < n; base += SEL_T) {
+                const int c = base + lane;
+                const uint32_t k = c < n ? keys[c] : 0u;
+                const bool part = c < n && (k & pmask) == prefix;
+                const int bin = part ? (int)((k >> shift) & 255) : 256 + lane;
+                const unsigned peers = __match_any_sync(0xffffffffu, bin);
+                if (part && lane == __ffs(peers) - 1) atomicAdd(&h[bin], (unsigned)__popc(peers));
             }
-            int incl = tot;
+            cluster_sync();  // every CTA's histogram of this pass is complete
+            if (tid < 256) {
+                unsigned t = 0;
 #pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int y = __shfl_up_sync(0xffffffffu, incl, o);
-                if (tid >= o) incl += y;
+                for (unsigned r = 0; r < SEL_CL; ++r) t += ld_dsmem_u32(dsmem_addr(&h[tid], r));
+                s_tot[tid] = t;
             }
-            int above = incl - tot;
+            __syncthreads();
+            if (tid < 32) {
+                // lane l owns digits 255-8l .. 248-8l (descending)
+                int cnt[8], tot = 0;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                if (above < remaining && above + cnt[i] >= remaining) {
-                    s_digit = 255 - 8 * tid - i;
-                    s_above = above;
+                for (int i = 0; i < 8; ++i) {
+                    cnt[i] = (int)s_tot[255 - 8 * tid - i];
+                    tot += cnt[i];
                 }
-                above += cnt[i];
-            }
-        }
-        __syncthreads();
-        const int d = s_digit;
-        remaining -= s_above;
-        prefix |= (uint32_t)d << shift;
-        pmask |= 255u << shift;
-        if (pass == 3) {
-            n_equal = (int)s_tot[d];
-            if (tid < SEL_CL) s_eq_rank[tid] = ld_dsmem_u32(dsmem_addr(&h[d], tid));
-        }
-        __syncthreads();
-    }
-    const uint32_t T = prefix;     // the K-th largest key
-    const int ngt = K - remaining;  // keys strictly above T
-
-    // 4) append the selected landmarks to rank 0's list
-    const bool take_all_equal = n_equal == remaining;
-    const uint32_t cnt_addr = dsmem_addr(&s_cnt, 0);
-    const uint32_t sel_addr = dsmem_addr(&s_sel[0], 0);
-    for (int base = 0; base < n; base += SEL_T) {
-        const int c = base + tid;
-        const uint32_t k = c < n ? keys[c] : 0u;
-        const bool take = c < n && (k > T || (take_all_equal && k == T));
-        const unsigned ballot = __ballot_sync(0xffffffffu, take);
-        if (ballot) {
-            unsigned pos0 = 0;
-            if (lane == 0) pos0 = atom_add_dsmem_u32(cnt_addr, (unsigned)__popc(ballot));
-            pos0 = __shfl_sync(0xffffffffu, pos0, 0);
-            if (take) st_dsmem_u32(sel_addr + 4u * (pos0 + __popc(ballot & ((1u << lane) - 1u))), (uint32_t)(c0 + c));
-        }
-    }
-    if (!take_all_equal) {
-        // ties at the threshold: lowest landmark index first, ranks in index order
-        int before = 0;
-        for (unsigned r = 0; r < rank; ++r) before += (int)s_eq_rank[r];
-        const int quota = max(0, min(remaining - before, (int)s_eq_rank[rank]));
-        int taken = 0;
-        for (int base = 0; base < n && taken < quota; base += SEL_T) {
-            const int c = base + tid;
-            const int f = (c < n && keys[c] == T) ? 1 : 0;
-            int tot;
-            const int r = cta_excl_scan(f, &tot, s_warp);
-            if (f && taken + r < quota) st_dsmem_u32(sel_addr + 4u * (ngt + before + taken + r), (uint32_t)(c0 + c));
-            taken += tot;
-        }
-    }
-    cluster_sync();  // rank 0 holds the complete selection
-    if (rank != 0) return;
-
-    // 5) landmark -> chunk id; bitmap A of the new set
-    for (int w = tid; w < 2 * nbw; w += SEL_T) bmA[w] = 0;  // bmA and bmB are contiguous
-    __syncthreads();
-    const int64_t *lidx = a.landmark_idx + (int64_t)bh * L;
-    for (int jj = tid; jj < K; jj += SEL_T) {
-        const int lm = s_sel[jj];
-        const int64_t cid = (lm >= 0 && lm < L) ? lidx[lm] : -1;
-        int v = -1;
-        if (cid >= 0 && cid < a.num_chunks) {
-            v = (int)cid;
-            atomicOr(&bmA[v >> 5], 1u << (v & 31));
-        } else {
-            report_dev_error(DEV_ERR_HOST_CHUNK);
-        }
-        s_sel[jj] = v;
-    }
-    __syncthreads();
-
-    // 6) classify the cached slots (thread t owns slots 2t, 2t+1); bitmap B of the cached set
-    int32_t *slots = a.slots + (int64_t)bh * K;
-    int hit[2] = {0, 0};
+                int incl = tot;
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-        const int s = 2 * tid + u;
-        if (s < K) {
-            const int old = slots[s];
-            if (old >= 0 && old < a.num_chunks) {
-                hit[u] = (bmA[old >> 5] >> (old & 31)) & 1;
-                atomicOr(&bmB[old >> 5], 1u << (old & 31));
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (tid >= o) incl += y;
+                }
+                int above = incl - tot;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    if (above < remaining && above + cnt[i] >= remaining) {
+                        s_digit = 255 - 8 * tid - i;
+                        s_above = above;
+                    }
+                    above += cnt[i];
+                }
+            }
+            __syncthreads();
+            const int d = s_digit;
+            remaining -= s_above;
+            prefix |= (uint32_t)d << shift;
+            pmask |= 255u << shift;
+            if (pass == 3) {
+                n_equal = (int)s_tot[d];
+                if (tid < SEL_CL) s_eq_rank[tid] = ld_dsmem_u32(dsmem_addr(&h[d], tid));
+            }
+            __syncthreads();
+        }
+        const uint32_t T = prefix;  // the K-th largest key
+        const bool take_all_equal = n_equal == remaining;
+        for (int base = (tid & ~31); base < n; base += SEL_T) {
+            const int c = base + lane;
+            if (c < n) {
+                const uint32_t k = keys[c];
+                if (k > T || (take_all_equal && k == T)) mark(chunk_of(c));
             }
         }
+        if (!take_all_equal) {
+            // ties at the threshold: lowest landmark index first, ranks in index order
+            int before = 0;
+            for (unsigned r = 0; r < rank; ++r) before += (int)s_eq_rank[r];
+            const int quota = max(0, min(remaining - before, (int)s_eq_rank[rank]));
+            int taken = 0;
+            for (int base = 0; base < n && taken < quota; base += SEL_T) {
+                const int c = base + tid;
+                const int f = (c < n && keys[c] == T) ? 1 : 0;
+                int tot;
+                const int r = cta_excl_scan(f, &tot, s_warp);
+                if (f && taken + r < quota) mark(chunk_of(c));
+                taken += tot;
+            }
+        }
+        cluster_sync();  // rank 0's bitmap holds the complete selection
+        if (rank != 0) return;
     }
     __syncthreads();
 
-    // 7) missed ids (in A, not in B) in ascending order
+    // 6) classify the cached slots against the new set; count the missed ids
+    //    (in A, not in B) of this thread's bitmap words; one scan gives both
+    //    the miss ranks (high half) and the free-slot ranks (low half)
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+        if (old[u] >= 0 && old[u] < a.num_chunks) hit[u] = (bmA[old[u] >> 5] >> (old[u] & 31)) & 1;
     const int wpt = (nbw + SEL_T - 1) / SEL_T;
     const int w0 = tid * wpt;
     int local = 0;
     for (int w = w0; w < min(nbw, w0 + wpt); ++w) local += __popc(bmA[w] & ~bmB[w]);
-    int nmiss;
-    int rk = cta_excl_scan(local, &nmiss, s_warp);
+    const int f0 = (2 * tid < K && !hit[0]) ? 1 : 0;
+    const int f1 = (2 * tid + 1 < K && !hit[1]) ? 1 : 0;
+    int tot;
+    const int packed = cta_excl_scan((local << 16) | (f0 + f1), &tot, s_warp);
+    const int nmiss = tot >> 16, nfree = tot & 0xffff;
+    int rk = packed >> 16;
+    const int r0 = packed & 0xffff;
     for (int w = w0; w < min(nbw, w0 + wpt); ++w) {
         uint32_t bits = bmA[w] & ~bmB[w];
         while (bits) {
@@ -323,21 +453,17 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
     }
     __syncthreads();
 
-    // 8) refill the free slots (ascending) with the misses (ascending)
-    const int f0 = (2 * tid < K && !hit[0]) ? 1 : 0;
-    const int f1 = (2 * tid + 1 < K && !hit[1]) ? 1 : 0;
-    int nfree;
-    const int r0 = cta_excl_scan(f0 + f1, &nfree, s_warp);
+    // 7) refill the free slots (ascending) with the misses (ascending)
     const int nassign = min(nfree, nmiss);
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
         const int f = u == 0 ? f0 : f1;
         const int r = u == 0 ? r0 : r0 + f0;
-        const int s = 2 * tid + u;
+        const int sl = 2 * tid + u;
         if (f && r < nassign) {
             const int id = s_misssorted[r];
-            slots[s] = id;
-            a.miss_slot[(int64_t)bh * K + r] = s;
+            slots[sl] = id;
+            a.miss_slot[(int64_t)bh * K + r] = sl;
             a.miss_chunk[(int64_t)bh * K + r] = id;
         }
     }
@@ -351,7 +477,7 @@ size_t select_smem_bytes(int L, int num_chunks, bool keys_global)
 {
     const size_t slice = (size_t)((L + SEL_CL - 1) / SEL_CL);
     const size_t nbw = (size_t)((num_chunks + 31) / 32);
-    return (keys_global ? 0 : slice * 4) + 2 * nbw * 4;
+    return (keys_global ? 0 : slice * 8) + 2 * nbw * 4;  // keys + chunk ids of the slice, bitmaps
 }
 
 int launch_select(const SelectArgs &a, int BH, size_t smem, cudaStream_t stream)
@@ -363,13 +489,16 @@ int launch_select(const SelectArgs &a, int BH, size_t smem, cudaStream_t stream)
     cfg.blockDim = dim3(SEL_T, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = SEL_CL;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    // may start while the scoring kernel drains; it reads the scores only after pdl_wait()
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     cudaError_t e = cudaLaunchKernelEx(&cfg, select_cluster_kernel, a);
     if (e != cudaSuccess) {
         cudaGetLastError();

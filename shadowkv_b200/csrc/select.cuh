@@ -7,6 +7,9 @@ namespace skv {
 
 constexpr int SEL_CL = 8;    // CTAs per (b, kv head): one thread-block cluster
 constexpr int SEL_T = 512;   // threads per CTA
+constexpr int SEL_BITS1 = 11;              // first-pass digit: key bits 30..20
+constexpr int SEL_BINS = 1 << SEL_BITS1;   // = 4 * SEL_T (each thread sums 4 bins)
+constexpr int SEL_CAND = 1024;             // candidate capacity of the exact stage
 
 struct SelectArgs {
     const float *logits;          // [BH][L][G] scaled logits

@@ -148,6 +148,43 @@ def test_select_topk_and_slot_update(G, L, K, H):
         assert np.array_equal(new[0, h, ms[h, :n]], mch[h, :n])
 
 
+@pytest.mark.parametrize("n_top,n_next,L", [(50, 600, 3000), (100, 2900, 3000), (0, 3000, 3000), (7, 1200, 9000)])
+def test_select_ties_lowest_landmark_first(n_top, n_next, L):
+    """Tied scores at the K-th place: the lowest landmark indices win.
+
+    Landmark rows are copies of three vectors, so their scores are bitwise
+    equal; (50, 600) resolves the ties among the candidates of the boundary
+    bin, (100, 2900) and (0, 3000) put more than 1024 keys in that bin and go
+    through the exact radix fallback.
+    """
+    from shadowkv_b200 import decode as fz
+    rng = np.random.default_rng(n_top + 7 * n_next)
+    H, G, K = 2, 4, 256
+    q = o.round_bf16(rng.standard_normal((1, H * G, 128)).astype(np.float32))
+    base = o.round_bf16(rng.standard_normal((3, 128)).astype(np.float32))
+    s3 = o.landmark_scores(q.reshape(1, H, G, 128), np.broadcast_to(base, (1, H, 3, 128)))
+    lm = np.empty((1, H, L, 128), np.float32)
+    for h in range(H):
+        order = np.argsort(-s3[0, h], kind="stable")  # best, next, worst vector for this head
+        kind = np.full(L, order[2])
+        pos = rng.permutation(L)
+        kind[pos[:n_top]] = order[0]
+        kind[pos[n_top:n_top + n_next]] = order[1]
+        lm[0, h] = base[kind]
+    lidx = torch.arange(L, dtype=torch.int64, device=DEV).repeat(1, H, 1).contiguous()
+    g = make_geom(batch=1, kv_heads=H, q_heads=H * G, rank=64, select_sets=K, num_landmarks=L, num_chunks=L,
+                  ctx_len=L * 8, buf_len=K * 8, sparse_start=0)
+    ws = fz.DecodeWorkspace(g, DEV)
+    slots = torch.full((1, H, K), -1, dtype=torch.int32, device=DEV)
+    fz.select(g, ws, to_bf16_dev(q), to_bf16_dev(lm), lidx, slots)
+    torch.cuda.synchronize()
+    assert no_device_errors()
+    sc = o.landmark_scores(q.reshape(1, H, G, 128), lm)
+    for h in range(H):
+        expect = np.sort(np.argsort(-sc[0, h], kind="stable")[:K])
+        assert np.array_equal(np.sort(slots[0, h].cpu().numpy()), expect)
+
+
 def test_select_repeated_query_is_all_hits():
     from shadowkv_b200 import decode as fz
     rng = np.random.default_rng(0)
