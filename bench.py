@@ -198,22 +198,21 @@ def run_b200(args, world, rank, local):
         s_v.copy_(v)
         s_pos.fill_(pos0 + i)
 
-    def step_body(ev=None):
+    def step_body():
         """One decode step of one layer on the static inputs (appends at row sparse_end)."""
         cache.gen_offset = 0
         qr = cache.append_select_fused(0, s_q, s_k, s_v, s_pos, attn.cos_sin_cache, q_out=s_qr)
-        cur = torch.cuda.current_stream()
-        with torch.cuda.stream(copy_stream):
-            copy_stream.wait_stream(cur)
-            if ev is not None:
-                ev[0].record(copy_stream)
-            cache.fetch_values_fused(0, copy_stream)
-            if ev is not None:
-                ev[1].record(copy_stream)
-        cache.reconstruct_keys_fused(0, attn.cos_sin_cache)
-        cur.wait_stream(copy_stream)
         seq_len = cache.sparse_end + cache._gen_offset(0)
-        cache.attention(0, qr, seq_len, out=s_out)
+        if args.split:
+            cur = torch.cuda.current_stream()
+            with torch.cuda.stream(copy_stream):
+                copy_stream.wait_stream(cur)
+                cache.fetch_values_fused(0, copy_stream)
+            cache.reconstruct_keys_fused(0, attn.cos_sin_cache)
+            cur.wait_stream(copy_stream)
+            cache.attention(0, qr, seq_len, out=s_out)
+        else:
+            cache.sparse_attention_fused(0, qr, seq_len, attn.cos_sin_cache, out=s_out)
         cache.gen_offset = 0
         return seq_len
 
@@ -266,7 +265,9 @@ def run_b200(args, world, rank, local):
 
     # ---- per-kernel times: the same steps launched eagerly, one kernel group at a time,
     # each bracketed by CUDA events on the stream it runs on (L2 flushed before each step)
-    parts = {"append_select": [], "fetch_values": [], "reconstruct_keys": [], "attention": []}
+    names = (["append_select", "fetch_values", "reconstruct_keys", "attention"] if args.split
+             else ["append_select", "sparse_attention"])
+    parts = {k: [] for k in names}
     for i in range(args.warmup, min(n, args.warmup + 100)):
         flush.zero_()
         load_inputs(i)
@@ -288,13 +289,17 @@ def run_b200(args, world, rank, local):
 
         qr = timed("append_select", lambda: cache.append_select_fused(0, s_q, s_k, s_v, s_pos, attn.cos_sin_cache,
                                                                       q_out=s_qr), main)
-        timed("fetch_values", lambda: cache.fetch_values_fused(0, copy_stream), copy_stream)
-        timed("reconstruct_keys", lambda: cache.reconstruct_keys_fused(0, attn.cos_sin_cache), main)
         sl = cache.sparse_end + cache._gen_offset(0)
-        timed("attention", lambda: cache.attention(0, qr, sl, out=s_out), main)
+        if args.split:
+            timed("fetch_values", lambda: cache.fetch_values_fused(0, copy_stream), copy_stream)
+            timed("reconstruct_keys", lambda: cache.reconstruct_keys_fused(0, attn.cos_sin_cache), main)
+            timed("attention", lambda: cache.attention(0, qr, sl, out=s_out), main)
+        else:
+            timed("sparse_attention", lambda: cache.sparse_attention_fused(0, qr, sl, attn.cos_sin_cache, out=s_out),
+                  main)
         misses_all.append(int(cache._fused_ws.miss_count.sum().item()))
         cache.gen_offset = 0
-    fetch_ms = parts["fetch_values"]
+    fetch_ms = parts["fetch_values" if args.split else "sparse_attention"]
     kernel_us = {k: 1e3 * statistics.mean(v) for k, v in parts.items() if v}
 
     ms_step = sum(per_step) / len(per_step)
@@ -354,7 +359,9 @@ def run_b200(args, world, rank, local):
                                f"budget {cfg.budget}, rank {cfg.rank}, V in pinned host memory",
                    "global_batch": B * world, "seq_len": cfg.ctx, "parallelism": f"batch-sharded x{world}",
                    "l2": "flushed between timed steps (256 MB write)", "hit_rate": hit_rate},
-        "roofline": {"kernel": "fetch_misses_kernel (zero-copy V gather)", "bound": "host_link",
+        "roofline": {"kernel": ("fetch_misses_kernel (zero-copy V gather)" if args.split else
+                                "sparse_attend_kernel (zero-copy V gather + key reconstruction + attention)"),
+                     "bound": "host_link",
                      "achieved": link_achieved, "peak": link_peak, "unit": "GB/s",
                      "frac": link_achieved / link_peak if link_peak else None, "traffic": None,
                      "peak_kind": "measured in-run: pinned H2D copy-engine bandwidth"},
@@ -365,7 +372,7 @@ def run_b200(args, world, rank, local):
                 "d2h_bytes_per_step": d2h},
         "kernel_us": kernel_us,
         "graph": used_graph,
-        "gpu_launches": 5 * args.steps,
+        "gpu_launches": (5 if args.split else 3) * args.steps,
         "clocks": clk.summary(),
         "wall_s": t_wall,
     }
@@ -419,6 +426,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying a CUDA graph")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--split", action="store_true",
+                    help="fetch / reconstruction / attention as three launches instead of the fused kernel")
     args = ap.parse_args()
     if args.impl == "reference":
         # the CPU reference arm runs on rank 0 only; other ranks exit without work

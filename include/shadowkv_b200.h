@@ -321,6 +321,32 @@ SKV_API int skv_decode_attention(const skv_decode_geom *g, const void *q, const 
                          const void *v_buf, int seq_len, void *out, void *workspace,
                          size_t workspace_bytes, void *stream);
 
+/* Bytes of caller-provided scratch skv_decode_sparse_attention needs for
+ * seq_len rows: per-CTA partials plus one ticket per (b, kv head).  The
+ * scratch must be zero-filled before its first use (the kernel leaves the
+ * tickets at zero when it completes); it must not be shared by launches that
+ * can run at the same time. */
+SKV_API size_t skv_decode_sparse_attention_workspace(const skv_decode_geom *g, int seq_len);
+
+/* One launch for value fetch + key reconstruction + attention of a decode
+ * step, after skv_decode_select / skv_decode_append_select:
+ *   - the missed chunks of the miss lists are fetched from page-locked
+ *     v_host into v_buf (as skv_decode_gather_values),
+ *   - their keys are reconstructed from U and SV^T with RoPE into k_buf (as
+ *     skv_decode_reconstruct_keys),
+ *   - out = GQA attention of q over buffer rows [0, seq_len) (as
+ *     skv_decode_attention; per-CTA partials merged by the last CTA).
+ * seq_len must cover the selected rows (>= sparse_start + 8*select_sets).
+ * No counterpart in the reference, which runs these as separate kernels
+ * (kernels/gather_copy.cu, kernels/batch_gather_gemm.cu + kernels/rope_new.cu,
+ * flash_attn_with_kvcache in models/attention/shadow.py:48). */
+SKV_API int skv_decode_sparse_attention(const skv_decode_geom *g, const void *q, const void *U,
+                                        const void *SVt, const void *cos_sin, const void *v_host,
+                                        void *k_buf, void *v_buf, const int32_t *miss_slot,
+                                        const int32_t *miss_chunk, const int32_t *miss_count,
+                                        int seq_len, void *out, void *workspace,
+                                        size_t workspace_bytes, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -57,9 +57,11 @@ SIGNATURES = {
     "skv_decode_reconstruct_keys": [ctypes.POINTER(DecodeGeom), P, P, P, P, P, P, P, P],
     "skv_decode_attention_workspace": [ctypes.POINTER(DecodeGeom), c_int],
     "skv_decode_attention": [ctypes.POINTER(DecodeGeom), P, P, P, c_int, P, P, c_size_t, P],
+    "skv_decode_sparse_attention_workspace": [ctypes.POINTER(DecodeGeom), c_int],
+    "skv_decode_sparse_attention": [ctypes.POINTER(DecodeGeom)] + [P] * 10 + [c_int, P, P, c_size_t, P],
 }
 _RET = {"skv_last_error": c_char_p, "skv_decode_select_workspace": c_size_t,
-        "skv_decode_attention_workspace": c_size_t}
+        "skv_decode_attention_workspace": c_size_t, "skv_decode_sparse_attention_workspace": c_size_t}
 
 
 def _load():

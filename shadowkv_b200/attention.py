@@ -61,7 +61,19 @@ class ShadowAttention:
         return out.view(out.shape[0], 1, out.shape[1], out.shape[2])
 
     def decode_fused(self, query_states, key_states, value_states, position_ids, layer_idx):
-        """Same step on the fused kernels (slot-stable reuse cache)."""
+        """Same step on the fused kernels (slot-stable reuse cache): scoring +
+        selection, then one launch for value fetch, key reconstruction and attention."""
+        kv = self.kv_cache
+        query_states = kv.append_select_fused(layer_idx, query_states.contiguous(), key_states.contiguous(),
+                                              value_states.contiguous(), position_ids.contiguous(),
+                                              self.cos_sin_cache)
+        seq_len = kv.sparse_end + kv._gen_offset(layer_idx)
+        out = kv.sparse_attention_fused(layer_idx, query_states, seq_len, self.cos_sin_cache)
+        return out.view(out.shape[0], 1, out.shape[1], out.shape[2])
+
+    def decode_fused_split(self, query_states, key_states, value_states, position_ids, layer_idx):
+        """decode_fused with fetch, reconstruction and attention as three launches
+        (fetch on the copy stream, overlapping the reconstruction)."""
         kv = self.kv_cache
         query_states = kv.append_select_fused(layer_idx, query_states.contiguous(), key_states.contiguous(),
                                               value_states.contiguous(), position_ids.contiguous(),

@@ -197,7 +197,6 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar)
 {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
-// Bounded wait for the phase with the given parity; false if it did not complete.
 // Programmatic dependent launch (sm_90+).  A kernel launched with the
 // programmatic-serialization attribute may start while the previous kernel of
 // its stream still runs; pdl_wait() blocks until that kernel has completed and
@@ -205,6 +204,7 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar)
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Bounded wait for the phase with the given parity; false if it did not complete.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity, unsigned max_iter = 1u << 22)
 {
     const uint32_t a = smem_u32(bar);

@@ -6,8 +6,8 @@
 //
 // One 8-CTA thread-block cluster per (b, kv head).  Every CTA turns its
 // eighth of the landmarks into order-preserving keys (max over the group of
-// the softmax-normalised score) and builds a 2048-bin histogram of their top
-// bits.  After one cluster barrier every CTA sums the eight histograms through
+// the softmax-normalised score) and builds a 256-bin histogram of their top
+// bits (exponent and three mantissa bits).  After one cluster barrier every CTA sums the eight histograms through
 // distributed shared memory and finds the bin that holds the K-th largest key.
 // Keys above that bin are selected outright: their chunk ids are set in rank
 // 0's bitmap of the new set with cluster-scope shared-memory atomics.  Keys in
@@ -134,6 +134,10 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
     const int64_t *lidx = a.landmark_idx + (int64_t)bh * L + c0;
     int32_t *slots = a.slots + (int64_t)bh * K;
 
+    // No early trigger for the kernel that follows: launched while this grid
+    // runs, its CTAs would crowd onto the SMs this grid leaves free, and the
+    // zero-copy fetch it issues needs the load slots of every SM.
+
     // 0) loads that do not depend on the scores: the cached slots (rank 0,
     //    thread t owns slots 2t, 2t+1) and the chunk ids of this slice
     int old[2] = {-1, -1};
@@ -159,6 +163,24 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
     if (tid == 0) s_ncand = s_nloc = 0;
 
     pdl_wait();  // the scoring kernel's logits and partials are complete from here on
+
+    // the first batch of this CTA's logits goes out before the partials are
+    // merged (two independent loads, one memory latency)
+    const float *lg = a.logits + ((int64_t)bh * L + c0) * G;
+    constexpr int U = 4;
+    const int G4 = (G & 3) == 0 ? G >> 2 : 0;
+    float4 v[U][4];
+    auto load_batch = [&](int base) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int c = base + lane + u * SEL_T;
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4)
+                if (q4 < G4 && c < n) v[u][q4] = __ldcg(reinterpret_cast<const float4 *>(lg + (int64_t)c * G) + q4);
+        }
+    };
+    const int base0 = tid & ~31;
+    if (base0 < n) load_batch(base0);
 
     // 1) softmax normalisers of each query head of the group: warp w merges the
     //    split partials of head w (lanes load in parallel, then a shuffle merge)
@@ -190,20 +212,10 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
 
     // 2) keys of this CTA's landmarks -- the bits of max_g softmax_g, which is
     //    >= 0, so the unsigned order of the bits is the order of the scores --
-    //    and their first-pass histogram over bits 30..20.  Warp-uniform loop:
-    //    lane l of warp w handles landmark 32w + l + 512j.
-    const float *lg = a.logits + ((int64_t)bh * L + c0) * G;
-    constexpr int U = 4;
-    for (int base = (tid & ~31); base < n; base += U * SEL_T) {
-        float4 v[U][4];
-        const int G4 = (G & 3) == 0 ? G >> 2 : 0;
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int c = base + lane + u * SEL_T;
-#pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4)
-                if (q4 < G4 && c < n) v[u][q4] = __ldcg(reinterpret_cast<const float4 *>(lg + (int64_t)c * G) + q4);
-        }
+    //    and their first-pass histogram.  Warp-uniform loop: lane l of warp w
+    //    handles landmark 32w + l + 512j.
+    for (int base = base0; base < n; base += U * SEL_T) {
+        if (base != base0) load_batch(base);
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int c = base + lane + u * SEL_T;
@@ -225,46 +237,59 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
                 }
                 keys[c] = __float_as_uint(sc);
             }
-            const int bin = c < n ? (int)(__float_as_uint(sc) >> (31 - SEL_BITS1)) : SEL_BINS + lane;
+            const int bin = c < n ? sel_key_bin(__float_as_uint(sc)) : SEL_BINS + lane;
             const unsigned peers = __match_any_sync(0xffffffffu, bin);
             if (c < n && lane == __ffs(peers) - 1) atomicAdd(&s_h1[bin], (unsigned)__popc(peers));
         }
     }
     cluster_sync();  // every CTA's first-pass histogram is complete; rank 0's bitmaps are zero
 
-    // 3) every CTA sums the eight histograms (thread t: bins 2047-4t .. 2044-4t,
-    //    descending) and finds the bin holding the K-th largest key
-    {
-        const int b0 = SEL_BINS - 4 - 4 * tid;
-        uint4 part[SEL_CL];
+    // 3) every CTA sums the eight histograms and finds the bin holding the
+    //    K-th largest key: warp 0, lane l owns bins 255-8l .. 248-8l
+    if (warp_id() == 0) {
+        const int b0 = SEL_BINS - 8 - 8 * lane;
+        uint4 lo[SEL_CL], hi[SEL_CL];
         const uint32_t la = (uint32_t)__cvta_generic_to_shared(&s_h1[b0]);
 #pragma unroll
         for (unsigned r = 0; r < SEL_CL; ++r) {
             uint32_t ra;
             asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(la), "r"(r));
-            part[r] = ld_dsmem_v4(ra);
+            lo[r] = ld_dsmem_v4(ra);
+            hi[r] = ld_dsmem_v4(ra + 16u);
         }
-        int cnt[4] = {0, 0, 0, 0};  // cnt[i]: bin b0 + 3 - i
+        int cnt[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // cnt[i]: bin b0 + 7 - i
 #pragma unroll
         for (unsigned r = 0; r < SEL_CL; ++r) {
-            cnt[0] += (int)part[r].w;
-            cnt[1] += (int)part[r].z;
-            cnt[2] += (int)part[r].y;
-            cnt[3] += (int)part[r].x;
+            cnt[0] += (int)hi[r].w;
+            cnt[1] += (int)hi[r].z;
+            cnt[2] += (int)hi[r].y;
+            cnt[3] += (int)hi[r].x;
+            cnt[4] += (int)lo[r].w;
+            cnt[5] += (int)lo[r].z;
+            cnt[6] += (int)lo[r].y;
+            cnt[7] += (int)lo[r].x;
         }
-        int total;
-        int above = cta_excl_scan(cnt[0] + cnt[1] + cnt[2] + cnt[3], &total, s_warp);
+        int tot = 0;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < 8; ++i) tot += cnt[i];
+        int incl = tot;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        int above = incl - tot;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
             if (above < K && above + cnt[i] >= K) {
-                s_bin = b0 + 3 - i;
+                s_bin = b0 + 7 - i;
                 s_bin_above = above;
                 s_bin_cnt = cnt[i];
             }
             above += cnt[i];
         }
-        __syncthreads();
     }
+    __syncthreads();
     const int bstar = s_bin, bin_above = s_bin_above, bin_cnt = s_bin_cnt;
     const uint32_t bmA0 = dsmem_addr(bmA, 0);
     auto chunk_of = [&](int c) -> int {
@@ -284,7 +309,7 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
         for (int base = (tid & ~31); base < n; base += SEL_T) {
             const int c = base + lane;
             const uint32_t k = c < n ? keys[c] : 0u;
-            const int bin = (int)(k >> (31 - SEL_BITS1));
+            const int bin = sel_key_bin(k);
             if (c < n && bin > bstar) mark(chunk_of(c));
             const bool cand = c < n && bin == bstar;
             const unsigned ballot = __ballot_sync(0xffffffffu, cand);

@@ -7,9 +7,18 @@ namespace skv {
 
 constexpr int SEL_CL = 8;    // CTAs per (b, kv head): one thread-block cluster
 constexpr int SEL_T = 512;   // threads per CTA
-constexpr int SEL_BITS1 = 11;              // first-pass digit: key bits 30..20
-constexpr int SEL_BINS = 1 << SEL_BITS1;   // = 4 * SEL_T (each thread sums 4 bins)
-constexpr int SEL_CAND = 1024;             // candidate capacity of the exact stage
+// First pass: a 256-bin histogram of key bits 30..20 (exponent and 3
+// mantissa bits).  Keys are probabilities in [0, 1] (bits 30..20 <= 1016);
+// bins 1..255 hold bits 769..1023, bin 0 every key below 2^-31.
+constexpr int SEL_BIN_LO = 768;
+constexpr int SEL_BINS = 256;
+constexpr int SEL_CAND = 1024;  // candidate capacity of the exact stage
+
+__device__ __forceinline__ int sel_key_bin(uint32_t k)
+{
+    const int t = (int)(k >> 20);
+    return t > SEL_BIN_LO ? t - SEL_BIN_LO : 0;
+}
 
 struct SelectArgs {
     const float *logits;          // [BH][L][G] scaled logits

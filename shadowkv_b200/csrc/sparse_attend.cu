@@ -1,0 +1,578 @@
+// Fused value fetch + key reconstruction + decode attention of the fused
+// decode path (one launch after the selection).
+//
+// Replaces, for one step, the three launches
+//   gather of the missed value chunks from pinned host memory
+//     (kernels/gather_copy.cu:193-253, gather_copy_with_offsets),
+//   low-rank reconstruction of the missed keys with RoPE
+//     (kernels/batch_gather_gemm.cu:136-213 + kernels/rope_new.cu:224-374),
+//   GQA decode attention over the budget
+//     (models/attention/shadow.py:48, flash_attn_with_kvcache, q_len = 1),
+// and leaves the same state behind: the missed rows of k_buf / v_buf hold the
+// reconstructed keys and the fetched values, as the separate kernels write them.
+//
+// Grid: ceil(seq_len / 128) * B * Hkv CTAs; CTA (b, h, j) owns buffer rows
+// [128 j, 128 j + 128): sixteen 8-row groups, each either a group of buffer
+// rows (prefix, cached slot, generated token) or a missed slot.  A CTA
+//   1. waits for the selection (programmatic dependent launch: the CTA may
+//      be resident before the selection kernel ends),
+//   2. reads the miss list, issues the zero-copy loads of its missed value
+//      chunks into registers, then bulk-copies SV^T, the U and cos/sin rows
+//      of those chunks and the buffer rows of the other groups,
+//   3. reconstructs the missed keys on the tensor cores (RoPE on the fp32
+//      accumulators, one rounding) while the values cross the host link --
+//      device-memory rows come in through bulk copies, which do not queue
+//      behind the zero-copy loads, and global stores wait until the values
+//      are in,
+//   4. computes S = K q^T and the softmax of its 128 keys for the G query
+//      heads of the group, then, once the values are in, O = P V,
+//   5. writes its partial (max, sum, O) and takes a ticket; the last CTA of
+//      the head merges the partials into the output.
+// The host link is the bound of the step; everything but the final P V and
+// the merge overlaps the value transfer.
+#include "common.cuh"
+
+namespace skv {
+
+constexpr int SA_THREADS = 256;  // 8 warps
+constexpr int SA_ROWS = 128;     // rows per CTA
+constexpr int SA_GROUPS = SA_ROWS / 8;
+constexpr int SA_PITCH = 136;    // K / V tile row pitch (bf16)
+
+struct SparseAttendArgs {
+    const __nv_bfloat16 *q;        // [B][Hq][128] rotated queries
+    const __nv_bfloat16 *U;        // [B][ctx][rank]
+    const __nv_bfloat16 *SVt;      // [B][Hkv][128][rank]
+    const __nv_bfloat16 *cos_sin;  // [cs_rows][cs_stride]
+    const uint4 *v_host;           // device view of the pinned values [B*Hkv][num_chunks][8 rows][128]
+    __nv_bfloat16 *k_buf, *v_buf;  // [B*Hkv][buf_len][128]
+    const int32_t *miss_slot, *miss_chunk, *miss_count;  // [BH][K], [BH][K], [BH]
+    float *part_o;                 // [BH][nblk][G][128]
+    float2 *part_ml;               // [BH][nblk][G] (max, sum)
+    unsigned *ticket;              // [BH], zero between launches
+    __nv_bfloat16 *out;            // [B][Hq][128]
+    int Hkv, G, K, rank, ctx, num_chunks, buf_len, sparse_start, seq_len, nblk;
+    int rope_mode, cs_stride, cs_rows;
+    float scale;
+};
+
+__device__ __forceinline__ void sa_ldsm(uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3, const void *p)
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void sa_ldsm_t(uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3, const void *p)
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(smem_u32(p)));
+}
+
+// NT: n-tiles of query heads in S = K q^T (1: G <= 8, 2: G <= 16)
+template <int NT>
+__global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAttendArgs a)
+{
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int KP = a.rank + 8;         // row pitch of SV^T (conflict-free ldmatrix)
+    const int KT = max(KP, SA_PITCH);  // row pitch of the U rows (rank wide) / keys (128 wide)
+    __nv_bfloat16 *sK = reinterpret_cast<__nv_bfloat16 *>(smem_raw);  // [128][KT]: U rows, then keys
+    __nv_bfloat16 *sB = sK + SA_ROWS * KT;                              // [128][KP]: SV^T of the head
+    __nv_bfloat16 *sV = sB + 128 * KP;                                  // [128][SA_PITCH]: values
+    __nv_bfloat16 *sQ = sV + SA_ROWS * SA_PITCH;                        // [16][SA_PITCH]
+    __nv_bfloat16 *sP = sQ + 16 * SA_PITCH;                             // [16][SA_PITCH] probabilities
+    float *sS = reinterpret_cast<float *>(sP + 16 * SA_PITCH);         // [128][16] logits
+    __nv_bfloat16 *sCS = reinterpret_cast<__nv_bfloat16 *>(sS + SA_ROWS * 16);  // [128][SA_PITCH] cos/sin rows
+    __shared__ int s_kind[SA_GROUPS];   // 0: buffer rows, 1: missed slot
+    __shared__ int s_chunk[SA_GROUPS];  // chunk id of a missed slot
+    __shared__ int s_any_miss;
+    __shared__ float s_m[16], s_l[16];
+    __shared__ unsigned s_last;
+    __shared__ __align__(8) uint64_t s_bar;  // completion of the bulk copies of the device-memory rows
+
+    // 1-D grid, the blocks that hold selected slots first: with more blocks
+    // than SMs, the blocks left for a second wave are the light ones (prefix
+    // and generated rows only), not ones that wait on the host link
+    int blk, bh;
+    {
+        const int blo = a.sparse_start / SA_ROWS;
+        const int nheavy = min(a.nblk, ceil_div(a.sparse_start + 8 * a.K, SA_ROWS)) - blo;
+        const int nlight = a.nblk - nheavy;
+        const int L = blockIdx.x;
+        const int BHn = gridDim.x / a.nblk;
+        if (L < BHn * nheavy) {
+            bh = L / nheavy;
+            blk = blo + L % nheavy;
+        } else {
+            const int L2 = L - BHn * nheavy;
+            bh = L2 / nlight;
+            const int j = L2 % nlight;
+            blk = j < blo ? j : j + nheavy;
+        }
+    }
+    const int b = bh / a.Hkv;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int G = a.G;
+    const int row0 = blk * SA_ROWS;
+    const int nrows = min(SA_ROWS, a.seq_len - row0);
+    const int sparse_end = a.sparse_start + 8 * a.K;
+    const bool has_slots = row0 < sparse_end && row0 + SA_ROWS > a.sparse_start;
+    const int ppr = a.rank / 8;  // 16-byte pieces per U / SV^T row
+
+    if (tid == 0) {
+        mbar_init(&s_bar, 1);
+        mbar_fence_init();
+    }
+    if (tid < SA_GROUPS) {
+        s_kind[tid] = 0;
+        s_chunk[tid] = -1;
+    }
+    if (tid == 0) s_any_miss = 0;
+    pdl_wait();  // the selection (and the scoring before it) are complete from here on
+    __syncthreads();
+
+    // 2) missed slots of this CTA: every thread checks its entries of the miss list
+    if (has_slots) {
+        const int nmiss = min(max(a.miss_count[bh], 0), a.K);
+        for (int t = tid; t < nmiss; t += SA_THREADS) {
+            const int s = a.miss_slot[(int64_t)bh * a.K + t];
+            const int gi = (a.sparse_start + 8 * s - row0) >> 3;
+            if (s >= 0 && s < a.K && a.sparse_start + 8 * s >= row0 && gi < SA_GROUPS) {
+                const int c = a.miss_chunk[(int64_t)bh * a.K + t];
+                if (c >= 0 && c < a.num_chunks && (int64_t)c * 8 + 8 <= a.ctx) {
+                    s_chunk[gi] = c;
+                    s_kind[gi] = 1;
+                    s_any_miss = 1;
+                } else {
+                    report_dev_error(DEV_ERR_HOST_CHUNK);
+                }
+            }
+        }
+    }
+    // query rows of the group (rows >= G are zero)
+    {
+        const __nv_bfloat16 *qrows = a.q + (int64_t)bh * G * 128;
+        for (int p = tid; p < 16 * 16; p += SA_THREADS) {
+            const int r = p >> 4, c = (p & 15) * 8;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (r < G) v = ld_nc_v4(qrows + (int64_t)r * 128 + c);
+            st_v4(sQ + r * SA_PITCH + c, v);
+        }
+    }
+    __syncthreads();
+    const bool any_miss = s_any_miss != 0;
+
+    // 3) zero-copy loads of the missed value chunks (2 KiB each), issued
+    //    first -- the host link is the bound of the step -- and kept in
+    //    registers until the end: element p = tid + 256 u is piece p & 127 of group p >> 7
+    uint4 vreg[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+        const int p = tid + SA_THREADS * u;
+        const int gi = p >> 7;
+        vreg[u] = make_uint4(0, 0, 0, 0);
+        if (s_kind[gi] == 1)
+            vreg[u] = ld_stream_v4(a.v_host + ((int64_t)bh * a.num_chunks + s_chunk[gi]) * 128 + (p & 127));
+    }
+
+    // 4) device-memory rows as bulk (TMA) copies: SV^T of the head, U and
+    //    cos/sin rows of the missed groups, K and V rows of the buffer groups.
+    //    They do not go through the load path the zero-copy loads above
+    //    occupy, so they land while the values are still crossing the link.
+    //    Rows past seq_len are zero.
+    const unsigned ub = (unsigned)a.rank * 2u, csb = a.rope_mode == 0 ? 256u : 128u;
+    if (tid == 0) {
+        unsigned total = has_slots && any_miss ? 128u * ub : 0u;
+        for (int gi = 0; gi < SA_GROUPS; ++gi) {
+            const int k = s_kind[gi];
+            for (int i = 0; i < 8; ++i) {
+                const int r = gi * 8 + i;
+                if (k == 1) {
+                    total += ub;
+                    if ((int64_t)s_chunk[gi] * 8 + i < a.cs_rows) total += csb;
+                } else if (r < nrows) {
+                    total += 512u;
+                }
+            }
+        }
+        mbar_arrive_expect_tx(&s_bar, total);
+    }
+    __syncthreads();
+    {
+        if (has_slots && any_miss && tid < 128) {
+            const __nv_bfloat16 *Bb = a.SVt + (int64_t)bh * 128 * a.rank;
+            bulk_g2s(sB + tid * KP, Bb + (int64_t)tid * a.rank, ub, &s_bar);
+        }
+        const __nv_bfloat16 *Ub = a.U + (int64_t)b * a.ctx * a.rank;
+        const __nv_bfloat16 *kb = a.k_buf + ((int64_t)bh * a.buf_len + row0) * 128;
+        const __nv_bfloat16 *vb = a.v_buf + ((int64_t)bh * a.buf_len + row0) * 128;
+        const int r = tid & (SA_ROWS - 1);
+        const int gi = r >> 3;
+        if (tid < SA_ROWS) {
+            if (s_kind[gi] == 1) {
+                bulk_g2s(sK + r * KT, Ub + ((int64_t)s_chunk[gi] * 8 + (r & 7)) * a.rank, ub, &s_bar);
+            } else if (r < nrows) {
+                bulk_g2s(sK + r * KT, kb + (int64_t)r * 128, 256u, &s_bar);
+            }
+        } else {
+            if (s_kind[gi] == 1) {
+                const int64_t pos = (int64_t)s_chunk[gi] * 8 + (r & 7);
+                if (pos < a.cs_rows) bulk_g2s(sCS + r * SA_PITCH, a.cos_sin + pos * a.cs_stride, csb, &s_bar);
+            } else if (r < nrows) {
+                bulk_g2s(sV + r * SA_PITCH, vb + (int64_t)r * 128, 256u, &s_bar);
+            }
+        }
+    }
+    for (int p = tid; p < SA_ROWS * 16; p += SA_THREADS) {
+        const int r = p >> 4, c = (p & 15) * 8;
+        if (r >= nrows && s_kind[r >> 3] == 0) {
+            st_v4(sK + r * KT + c, make_uint4(0, 0, 0, 0));
+            st_v4(sV + r * SA_PITCH + c, make_uint4(0, 0, 0, 0));
+        }
+    }
+    // bounded waits: a copy that never lands is reported, it does not hang the GPU
+    if (!mbar_wait(&s_bar, 0)) {
+        if (lane == 0) report_dev_error(DEV_ERR_WAIT);
+    }
+    __syncthreads();
+
+    // 5) key reconstruction of the missed groups: U rows x SV^T, RoPE at the
+    //    original positions on the fp32 accumulators, one rounding to bf16.
+    //    Warp w owns rows 16w .. 16w+15: it reads only its own U rows, so it
+    //    overwrites them with its keys once both column halves are done.
+    if (any_miss && (s_kind[2 * warp] == 1 || s_kind[2 * warp + 1] == 1)) {
+        const int g = lane >> 2, t4 = lane & 3;
+        const __nv_bfloat16 *aRow = sK + (warp * 16 + (lane & 15)) * KT + (lane >> 4) * 8;
+        const int bColOff = ((lane >> 3) & 1) * 8;
+        uint32_t kres[2][16];  // packed bf16 keys: [half][row g / g+8][8 n-tiles]
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+            // n-tiles {4h .. 4h+3} and {8+4h .. 8+4h+3}: the rotate-half pairs
+            // (t, t+64) of a row stay in one thread
+            float acc[8][4];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+            for (int k0 = 0; k0 < a.rank; k0 += 16) {
+                uint32_t a0, a1, a2, a3;
+                sa_ldsm(a0, a1, a2, a3, aRow + k0);
+#pragma unroll
+                for (int pr = 0; pr < 4; ++pr) {
+                    // one x4 ldmatrix: SV^T rows of n-tile (4h + pr) for lanes 0-15 and of
+                    // n-tile (8 + 4h + pr) for lanes 16-31, k halves by lane bit 3
+                    const int ntA = 4 * half + pr, ntB = 8 + 4 * half + pr;
+                    const int rsel = (lane & 7) + ((lane >> 4) ? ntB * 8 : ntA * 8);
+                    uint32_t b0, b1, b2, b3;
+                    sa_ldsm(b0, b1, b2, b3, sB + rsel * KP + k0 + bColOff);
+                    mma_bf16_16816(acc[pr], a0, a1, a2, a3, b0, b1);
+                    mma_bf16_16816(acc[4 + pr], a0, a1, a2, a3, b2, b3);
+                }
+            }
+            // epilogue of this half: acc[pr] is n-tile 4h + pr, acc[4 + pr] is 8 + 4h + pr
+#pragma unroll
+            for (int hr = 0; hr < 2; ++hr) {
+                const int r = warp * 16 + g + 8 * hr;
+                const int gi = r >> 3;
+                float v[8][2];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    v[i][0] = acc[i][2 * hr];
+                    v[i][1] = acc[i][2 * hr + 1];
+                }
+                if (s_kind[gi] == 1) {
+                    const int64_t pos = (int64_t)s_chunk[gi] * 8 + (r & 7);
+                    if (pos >= a.cs_rows) {
+                        if (t4 == 0) report_dev_error(DEV_ERR_ROW);
+                    } else {
+                        const __nv_bfloat16 *cs = sCS + r * SA_PITCH;
+                        if (a.rope_mode == 0) {
+#pragma unroll
+                            for (int pr = 0; pr < 4; ++pr) {
+#pragma unroll
+                                for (int u = 0; u < 2; ++u) {
+                                    const int t = (4 * half + pr) * 8 + t4 * 2 + u;  // < 64
+                                    const float cc = bf2f(cs[t]), ss = bf2f(cs[t + 64]);
+                                    const float x1 = v[pr][u], x2 = v[4 + pr][u];
+                                    v[pr][u] = x1 * cc - x2 * ss;
+                                    v[4 + pr][u] = x2 * cc + x1 * ss;
+                                }
+                            }
+                        } else {
+                            // GLM: pairs (2i, 2i+1) of the first 64 dims, both in one thread
+#pragma unroll
+                            for (int pr = 0; pr < 4; ++pr) {
+                                const int tp = ((4 * half + pr) * 8 + t4 * 2) >> 1;  // pair index < 32
+                                const float cc = bf2f(cs[tp]), ss = bf2f(cs[tp + 32]);
+                                const float xe = v[pr][0], xo = v[pr][1];
+                                v[pr][0] = xe * cc - xo * ss;
+                                v[pr][1] = xo * cc + xe * ss;
+                            }
+                        }
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < 8; ++i) kres[half][hr * 8 + i] = pack_bf2(v[i][0], v[i][1]);
+            }
+        }
+        __syncwarp();  // every lane is done reading this warp's U rows
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+#pragma unroll
+            for (int hr = 0; hr < 2; ++hr) {
+                const int r = warp * 16 + g + 8 * hr;
+                if (s_kind[r >> 3] != 1) continue;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int nt = i < 4 ? 4 * half + i : 8 + 4 * half + (i - 4);
+                    *reinterpret_cast<uint32_t *>(sK + r * KT + nt * 8 + t4 * 2) = kres[half][hr * 8 + i];
+                }
+            }
+        }
+    }
+    __syncthreads();
+
+    // 6) S = K q^T: warp w scores keys 16w .. 16w+15
+    {
+        float sc[NT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+        const __nv_bfloat16 *aRow = sK + (warp * 16 + (lane & 15)) * KT + (lane >> 4) * 8;
+        const int bRow = (lane & 7) + ((lane >> 4) << 3);
+        const int bCol = ((lane >> 3) & 1) * 8;
+#pragma unroll
+        for (int kk = 0; kk < 128; kk += 16) {
+            uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+            sa_ldsm(a0, a1, a2, a3, aRow + kk);
+            sa_ldsm(b0, b1, b2, b3, sQ + bRow * SA_PITCH + kk + bCol);
+            mma_bf16_16816(sc[0], a0, a1, a2, a3, b0, b1);
+            if (NT == 2) mma_bf16_16816(sc[NT - 1], a0, a1, a2, a3, b2, b3);
+        }
+        const int g = lane >> 2, t4 = lane & 3;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const int r0 = warp * 16 + g, r1 = r0 + 8;
+            const int n0 = nt * 8 + 2 * t4;
+            sS[r0 * 16 + n0] = r0 < nrows ? sc[nt][0] * a.scale : -INFINITY;
+            sS[r0 * 16 + n0 + 1] = r0 < nrows ? sc[nt][1] * a.scale : -INFINITY;
+            sS[r1 * 16 + n0] = r1 < nrows ? sc[nt][2] * a.scale : -INFINITY;
+            sS[r1 * 16 + n0 + 1] = r1 < nrows ? sc[nt][3] * a.scale : -INFINITY;
+        }
+    }
+    __syncthreads();
+    // softmax of the tile: warp w handles heads w and w+8 (128 keys, 4 per lane)
+    for (int gg = warp; gg < 16; gg += 8) {
+        if (gg < G) {
+            float x[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) x[u] = sS[(lane + 32 * u) * 16 + gg];
+            const float m = warp_max(fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3])));  // finite: nrows >= 1
+            float psum = 0.f;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const float p = x[u] == -INFINITY ? 0.f : __expf(x[u] - m);
+                const __nv_bfloat16 pb = f2bf(p);
+                sP[gg * SA_PITCH + lane + 32 * u] = pb;
+                psum += bf2f(pb);  // the sum uses the same rounded weights as P V
+            }
+            psum = warp_sum(psum);
+            if (lane == 0) {
+                s_m[gg] = m;
+                s_l[gg] = psum;
+            }
+        } else {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) sP[gg * SA_PITCH + lane + 32 * u] = f2bf(0.f);
+        }
+    }
+
+    // 7) the fetched values: into the V tile and back to the slot in v_buf.
+    //    Global stores come only now: issued earlier, they would queue behind
+    //    the zero-copy loads.  The reconstructed keys go back to k_buf here too
+    //    (the slot keeps them for later hits).
+    if (any_miss) {
+        __nv_bfloat16 *kdst = a.k_buf + ((int64_t)bh * a.buf_len + row0) * 128;
+        for (int p = tid; p < SA_ROWS * 16; p += SA_THREADS) {
+            const int r = p >> 4, c = (p & 15) * 8;
+            if (s_kind[r >> 3] == 1) st_v4(kdst + (int64_t)r * 128 + c, ld_v4(sK + r * KT + c));
+        }
+        __nv_bfloat16 *vdst = a.v_buf + ((int64_t)bh * a.buf_len + row0) * 128;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int p = tid + SA_THREADS * u;
+            const int gi = p >> 7;
+            if (s_kind[gi] == 1) {
+                const int r = gi * 8 + ((p & 127) >> 4), c = (p & 15) * 8;
+                st_v4(sV + r * SA_PITCH + c, vreg[u]);
+                __stcg(reinterpret_cast<uint4 *>(vdst + (int64_t)r * 128 + c), vreg[u]);
+            }
+        }
+    }
+    __syncthreads();
+
+    // 8) O = P V: warp w computes dims 16w .. 16w+15 for the 16 head rows
+    float o[2][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    {
+        const __nv_bfloat16 *aRow = sP + (lane & 15) * SA_PITCH + (lane >> 4) * 8;
+        const int vRow = (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int vCol = warp * 16 + (lane >> 4) * 8;
+#pragma unroll
+        for (int kk = 0; kk < SA_ROWS; kk += 16) {
+            uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+            sa_ldsm(a0, a1, a2, a3, aRow + kk);
+            sa_ldsm_t(b0, b1, b2, b3, sV + (kk + vRow) * SA_PITCH + vCol);
+            mma_bf16_16816(o[0], a0, a1, a2, a3, b0, b1);
+            mma_bf16_16816(o[1], a0, a1, a2, a3, b2, b3);
+        }
+    }
+
+    // 9) partial of this CTA, then the last CTA of the head merges
+    {
+        const int g = lane >> 2, t4 = lane & 3;
+        float *po = a.part_o + ((int64_t)bh * a.nblk + blk) * G * 128;
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int d = warp * 16 + i * 8 + 2 * t4;
+            if (g < G) *reinterpret_cast<float2 *>(po + g * 128 + d) = make_float2(o[i][0], o[i][1]);
+            if (g + 8 < G) *reinterpret_cast<float2 *>(po + (g + 8) * 128 + d) = make_float2(o[i][2], o[i][3]);
+        }
+        if (tid < G) a.part_ml[((int64_t)bh * a.nblk + blk) * G + tid] = make_float2(s_m[tid], s_l[tid]);
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(&a.ticket[bh], 1u) == (unsigned)(a.nblk - 1) ? 1u : 0u;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int p = tid; p < G * 128; p += SA_THREADS) {
+        const int gg = p >> 7, d = p & 127;
+        const float2 *ml = a.part_ml + (int64_t)bh * a.nblk * G + gg;
+        const float *po = a.part_o + (int64_t)bh * a.nblk * G * 128 + gg * 128 + d;
+        float M = -INFINITY;
+        for (int j = 0; j < a.nblk; ++j) M = fmaxf(M, __ldcg(&ml[j * G].x));
+        float L = 0.f, acc = 0.f;
+        for (int j = 0; j < a.nblk; ++j) {
+            const float2 v = __ldcg(&ml[j * G]);
+            const float w = __expf(v.x - M);
+            L += v.y * w;
+            acc += __ldcg(&po[(int64_t)j * G * 128]) * w;
+        }
+        a.out[((int64_t)bh * G + gg) * 128 + d] = f2bf(acc / L);
+    }
+    if (tid == 0) a.ticket[bh] = 0;  // ready for the next launch
+}
+
+static size_t sa_smem_bytes(int rank)
+{
+    const size_t KP = (size_t)rank + 8, KT = KP > (size_t)SA_PITCH ? KP : (size_t)SA_PITCH;
+    return (SA_ROWS * KT + 128 * KP + 2 * SA_ROWS * SA_PITCH + 2 * 16 * SA_PITCH) * 2 + SA_ROWS * 16 * 4;
+}
+
+}  // namespace skv
+
+using namespace skv;
+
+extern "C" {
+
+size_t skv_decode_sparse_attention_workspace(const skv_decode_geom *g, int seq_len)
+{
+    if (!g || g->batch <= 0 || g->kv_heads <= 0 || g->q_heads % g->kv_heads != 0 || seq_len <= 0) return 0;
+    const size_t BH = (size_t)g->batch * g->kv_heads, G = (size_t)(g->q_heads / g->kv_heads);
+    const size_t nblk = (size_t)ceil_div(seq_len, SA_ROWS);
+    const size_t o = BH * nblk * G * 128 * 4, ml = BH * nblk * G * 8, tk = BH * 4;
+    return ((o + 255) & ~(size_t)255) + ((ml + 255) & ~(size_t)255) + ((tk + 255) & ~(size_t)255);
+}
+
+int skv_decode_sparse_attention(const skv_decode_geom *g, const void *q, const void *U, const void *SVt,
+                                const void *cos_sin, const void *v_host, void *k_buf, void *v_buf,
+                                const int32_t *miss_slot, const int32_t *miss_chunk,
+                                const int32_t *miss_count, int seq_len, void *out, void *workspace,
+                                size_t workspace_bytes, void *stream)
+{
+    SKV_CHECK_ARG(g && q && U && SVt && cos_sin && k_buf && v_buf && miss_slot && miss_chunk && miss_count && out &&
+                      workspace,
+                  "null pointer argument");
+    SKV_CHECK_ARG(g->batch > 0 && g->kv_heads > 0 && g->q_heads % g->kv_heads == 0, "bad head counts");
+    SKV_CHECK_SUPPORTED(g->head_dim == 128 && g->chunk_size == 8, "head_dim 128 and chunk 8 only");
+    const int G = g->q_heads / g->kv_heads;
+    SKV_CHECK_SUPPORTED(G <= 16, "GQA group larger than 16");
+    SKV_CHECK_SUPPORTED(g->rank % 16 == 0 && g->rank >= 16 && g->rank <= 256, "rank must be a multiple of 16 in 16..256");
+    SKV_CHECK_SUPPORTED(g->rope_mode == 0 || g->rope_mode == 1, "rope_mode must be 0 or 1");
+    SKV_CHECK_ARG(g->cos_sin_stride >= (g->rope_mode == 0 ? 128 : 64), "cos_sin_stride too small");
+    SKV_CHECK_ARG(g->select_sets >= 1 && g->sparse_start >= 0 && g->sparse_start % 8 == 0 &&
+                      g->sparse_start + 8 * (int64_t)g->select_sets <= g->buf_len,
+                  "selected rows exceed buf_len (or sparse_start not a multiple of 8)");
+    SKV_CHECK_ARG(seq_len >= g->sparse_start + 8 * g->select_sets && seq_len <= g->buf_len,
+                  "seq_len %d must cover the selected rows and fit in buf_len", seq_len);
+    SKV_CHECK_ARG(aligned(q, 16) && aligned(U, 16) && aligned(SVt, 16) && aligned(cos_sin, 16) && aligned(k_buf, 16) &&
+                      aligned(v_buf, 16) && aligned(workspace, 256),
+                  "operands must be 16-byte aligned (workspace 256)");
+    SKV_CHECK_ARG(g->cos_sin_stride % 8 == 0, "cos_sin_stride must be a multiple of 8 (16-byte rows)");
+    const size_t need = skv_decode_sparse_attention_workspace(g, seq_len);
+    SKV_CHECK_ARG(workspace_bytes >= need, "workspace too small: %zu < %zu bytes", workspace_bytes, need);
+    const void *hdev = nullptr;
+    int st = host_to_device_ptr(v_host, &hdev, "v_host");
+    if (st != SKV_OK) return st;
+    SKV_CHECK_ARG(aligned(hdev, 16), "v_host must be 16-byte aligned");
+
+    const int BH = g->batch * g->kv_heads;
+    const int nblk = ceil_div(seq_len, SA_ROWS);
+    const size_t o_bytes = (size_t)BH * nblk * G * 128 * 4, ml_bytes = (size_t)BH * nblk * G * 8;
+    unsigned char *ws = static_cast<unsigned char *>(workspace);
+    SparseAttendArgs a = {};
+    a.q = (const __nv_bfloat16 *)q;
+    a.U = (const __nv_bfloat16 *)U;
+    a.SVt = (const __nv_bfloat16 *)SVt;
+    a.cos_sin = (const __nv_bfloat16 *)cos_sin;
+    a.v_host = (const uint4 *)hdev;
+    a.k_buf = (__nv_bfloat16 *)k_buf;
+    a.v_buf = (__nv_bfloat16 *)v_buf;
+    a.miss_slot = miss_slot;
+    a.miss_chunk = miss_chunk;
+    a.miss_count = miss_count;
+    // tickets first: their offset must not depend on seq_len (they stay zero between launches)
+    const size_t tk_bytes = ((size_t)BH * 4 + 255) & ~(size_t)255;
+    a.ticket = reinterpret_cast<unsigned *>(ws);
+    a.part_ml = reinterpret_cast<float2 *>(ws + tk_bytes);
+    a.part_o = reinterpret_cast<float *>(ws + tk_bytes + ((ml_bytes + 255) & ~(size_t)255));
+    (void)o_bytes;
+    a.out = (__nv_bfloat16 *)out;
+    a.Hkv = g->kv_heads;
+    a.G = G;
+    a.K = g->select_sets;
+    a.rank = g->rank;
+    a.ctx = g->ctx_len;
+    a.num_chunks = g->num_chunks;
+    a.buf_len = g->buf_len;
+    a.sparse_start = g->sparse_start;
+    a.seq_len = seq_len;
+    a.nblk = nblk;
+    a.rope_mode = g->rope_mode;
+    a.cs_stride = g->cos_sin_stride;
+    a.cs_rows = g->cos_sin_rows;
+    a.scale = g->scale;
+
+    const int smem = (int)sa_smem_bytes(g->rank);
+    const void *fn = G <= 8 ? (const void *)sparse_attend_kernel<1> : (const void *)sparse_attend_kernel<2>;
+    st = ensure_smem_attr(fn, smem, "sparse_attend_kernel");
+    if (st) return st;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(nblk * BH, 1, 1);
+    cfg.blockDim = dim3(SA_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attr[1];
+    // may start while the selection drains: only SV^T is read before pdl_wait()
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = G <= 8 ? cudaLaunchKernelEx(&cfg, sparse_attend_kernel<1>, a)
+                           : cudaLaunchKernelEx(&cfg, sparse_attend_kernel<2>, a);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        set_error("launch of sparse_attend_kernel failed: %s", cudaGetErrorString(e));
+        return SKV_ERR_CUDA;
+    }
+    return SKV_OK;
+}
+
+}  // extern "C"

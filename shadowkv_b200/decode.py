@@ -78,6 +78,10 @@ class DecodeWorkspace:
         # zero-initialised: the attention keeps per-head arrival counters here and
         # leaves them at zero after every call
         self.attn_ws = torch.zeros(max(self.attn_bytes, 256), dtype=torch.uint8, device=device)
+        # fused fetch + reconstruction + attention: partials and per-head
+        # tickets, zero-filled once (the kernel leaves the tickets at zero)
+        self.sparse_bytes = int(lib.skv_decode_sparse_attention_workspace(ctypes.byref(g), geom.buf_len))
+        self.sparse_ws = torch.zeros(max(self.sparse_bytes, 256), dtype=torch.uint8, device=device)
         bh = geom.batch * geom.kv_heads
         self.miss_slot = torch.zeros(bh, geom.select_sets, dtype=torch.int32, device=device)
         self.miss_chunk = torch.zeros(bh, geom.select_sets, dtype=torch.int32, device=device)
@@ -154,4 +158,20 @@ def attention(geom: Geometry, ws: DecodeWorkspace, q: torch.Tensor, k_buf: torch
         ctypes.byref(g), _req(q, "q", torch.bfloat16), _req(k_buf, "k_buf", torch.bfloat16),
         _req(v_buf, "v_buf", torch.bfloat16), int(seq_len), _req(out, "out", torch.bfloat16),
         ws.attn_ws.data_ptr(), ws.attn_bytes, _stream(stream)), "skv_decode_attention")
+    return out
+
+
+def sparse_attention(geom: Geometry, ws: DecodeWorkspace, q: torch.Tensor, U: torch.Tensor, SVt: torch.Tensor,
+                     cos_sin: torch.Tensor, v_host: torch.Tensor, k_buf: torch.Tensor, v_buf: torch.Tensor,
+                     seq_len: int, out: torch.Tensor, stream=None) -> torch.Tensor:
+    """``gather_values`` + ``reconstruct_keys`` + ``attention`` in one launch (after a selection)."""
+    if v_host.is_cuda or not v_host.is_pinned() or v_host.dtype != torch.bfloat16 or not v_host.is_contiguous():
+        raise RuntimeError("v_host must be a contiguous pinned CPU bf16 tensor")
+    g = geom.c()
+    check(lib.skv_decode_sparse_attention(
+        ctypes.byref(g), _req(q, "q", torch.bfloat16), _req(U, "U", torch.bfloat16), _req(SVt, "SVt", torch.bfloat16),
+        _req(cos_sin, "cos_sin", torch.bfloat16), v_host.data_ptr(), _req(k_buf, "k_buf", torch.bfloat16),
+        _req(v_buf, "v_buf", torch.bfloat16), ws.miss_slot.data_ptr(), ws.miss_chunk.data_ptr(),
+        ws.miss_count.data_ptr(), int(seq_len), _req(out, "out", torch.bfloat16), ws.sparse_ws.data_ptr(),
+        ws.sparse_bytes, _stream(stream)), "skv_decode_sparse_attention")
     return out

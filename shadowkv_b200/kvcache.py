@@ -363,6 +363,15 @@ class ShadowKVCache_CPU:
         fused.reconstruct_keys(self._fused_geom, self._fused_ws, self.U[layer_idx], self.SV[layer_idx], cos_sin_cache,
                                self.k_cache_buffer[layer_idx], stream)
 
+    def sparse_attention_fused(self, layer_idx, query_states, seq_len, cos_sin_cache, out=None):
+        """Fetch of the missed values + reconstruction of the missed keys + attention, one launch."""
+        q = query_states.reshape(self.batch_size, self.num_attention_heads, self.head_dim)
+        if out is None:
+            out = torch.empty_like(q)
+        return fused.sparse_attention(self._fused_geom, self._fused_ws, q, self.U[layer_idx], self.SV[layer_idx],
+                                      cos_sin_cache, self.v_cache_cpu[layer_idx], self.k_cache_buffer[layer_idx],
+                                      self.v_cache_buffer[layer_idx], seq_len, out)
+
     def attention(self, layer_idx, query_states, seq_len, out=None):
         """GQA decode attention over buffer rows [0, seq_len) -> [B, Hq, D]."""
         g = self._fused_geom if self._fused_geom is not None else fused.Geometry(

@@ -96,7 +96,7 @@ def _scores_ok(layer, q_roped, ids_per_slot, rtol):
             assert o.topk_tie_ok(sc[b, h][None], pos[None], c.select_sets, rtol=rtol)
 
 
-@pytest.mark.parametrize("path", ["fused", "reference"])
+@pytest.mark.parametrize("path", ["fused", "fused_split", "reference"])
 def test_decode_steps_against_oracle(tiny_layer, path):
     from shadowkv_b200._lib import device_errors
     layer = tiny_layer
@@ -110,8 +110,8 @@ def test_decode_steps_against_oracle(tiny_layer, path):
         q, k, v = layer.next_inputs()
         pos = torch.full((c.batch_size, 1), layer.cfg.ctx + step, dtype=torch.int64, device=DEV)
         c.gen_offset = 0
-        if path == "fused":
-            out = attn.decode_fused(q, k, v, pos, 0)
+        if path in ("fused", "fused_split"):
+            out = (attn.decode_fused if path == "fused" else attn.decode_fused_split)(q, k, v, pos, 0)
             ids = c.slots[0].cpu().numpy()
             hits.append(c.hit_rate())
         else:
@@ -121,12 +121,12 @@ def test_decode_steps_against_oracle(tiny_layer, path):
         assert device_errors()[0] == 0
         # selection: fp32 scores (fused) or the bf16 softmax of the CUTLASS path (reference)
         qr = attn.apply_rotary_pos_emb(q, k, pos)[0]
-        _scores_ok(layer, f32(qr)[:, :, 0, :], ids, rtol=1e-5 if path == "fused" else 5e-2)
-        _check_buffers(layer, ids, fused=(path == "fused"))
+        _scores_ok(layer, f32(qr)[:, :, 0, :], ids, rtol=5e-2 if path == "reference" else 1e-5)
+        _check_buffers(layer, ids, fused=(path != "reference"))
         seq_len = c.sparse_end + 1
         ref = o.decode_attention(f32(qr)[:, :, 0, :], f32(c.k_cache_buffer[0]), f32(c.v_cache_buffer[0]), seq_len)
         np.testing.assert_allclose(f32(out)[:, 0], ref, atol=2e-2, rtol=1e-2)
-    if path == "fused":
+    if path != "reference":
         assert all(0.0 <= h <= 1.0 for h in hits)
 
 

@@ -290,3 +290,75 @@ def test_attention(B, Hq, Hkv, S):
     fz.attention(g, ws, to_bf16_dev(q), to_bf16_dev(k), to_bf16_dev(v), S, out)
     ref = o.decode_attention(q, k, v, S)
     np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=2e-2, rtol=1e-2)
+
+
+@pytest.mark.parametrize("B,Hkv,G,rank,K,ss,extra,rope_mode,pattern", [
+    (1, 2, 4, 64, 64, 40, 1, 0, "mixed"),
+    (2, 2, 16, 160, 128, 32, 5, 0, "all"),
+    (1, 3, 8, 96, 256, 416, 130, 1, "mixed"),
+    (1, 2, 4, 160, 256, 416, 1, 0, "none"),
+    (1, 1, 1, 32, 16, 8, 1, 0, "all"),
+])
+def test_sparse_attention_fetch_reconstruct_attend(B, Hkv, G, rank, K, ss, extra, rope_mode, pattern):
+    """One launch = gather_values + reconstruct_keys + attention: buffers and output vs the oracle."""
+    from shadowkv_b200 import decode as fz
+    rng = np.random.default_rng(K + rank + extra)
+    T = 4096
+    chunks = T // 8
+    width = 128 if rope_mode == 0 else 64
+    se = ss + 8 * K
+    seq_len = se + extra
+    buf_len = seq_len + 3
+    Hq = Hkv * G
+    U = o.round_bf16((rng.standard_normal((B, T, rank)) / 8).astype(np.float32))
+    SVt = o.round_bf16(rng.standard_normal((B, Hkv, 128, rank)).astype(np.float32))
+    cs = o.round_bf16(rng.uniform(-1, 1, (T + 64, width)).astype(np.float32))
+    host = o.round_bf16(rng.standard_normal((B, Hkv, chunks, 1024)).astype(np.float32))
+    host_t = torch.from_numpy(o.f32_to_bf16_bits(host).view(np.int16)).view(torch.bfloat16).pin_memory()
+    kb0 = o.round_bf16(rng.standard_normal((B, Hkv, buf_len, 128)).astype(np.float32))
+    vb0 = o.round_bf16(rng.standard_normal((B, Hkv, buf_len, 128)).astype(np.float32))
+    q = o.round_bf16(rng.standard_normal((B, Hq, 128)).astype(np.float32))
+    g = make_geom(batch=B, kv_heads=Hkv, q_heads=Hq, rank=rank, select_sets=K, num_landmarks=K, num_chunks=chunks,
+                  ctx_len=T, buf_len=buf_len, sparse_start=ss, rope_mode=rope_mode, cos_sin_stride=width,
+                  cos_sin_rows=T + 64)
+    ws = fz.DecodeWorkspace(g, DEV)
+    ms = np.zeros((B * Hkv, K), np.int32)
+    mc = np.zeros((B * Hkv, K), np.int32)
+    cnt = np.zeros(B * Hkv, np.int32)
+    for i in range(B * Hkv):
+        n = {"all": K, "none": 0, "mixed": int(rng.integers(1, K))}[pattern]
+        cnt[i] = n
+        ms[i, :n] = np.sort(rng.permutation(K)[:n])
+        mc[i, :n] = rng.permutation(chunks)[:n]
+    ws.miss_slot.copy_(torch.from_numpy(ms))
+    ws.miss_chunk.copy_(torch.from_numpy(mc))
+    ws.miss_count.copy_(torch.from_numpy(cnt))
+    kbuf, vbuf = to_bf16_dev(kb0), to_bf16_dev(vb0)
+    out = torch.empty(B, Hq, 128, dtype=torch.bfloat16, device=DEV)
+    args = (g, ws, to_bf16_dev(q), to_bf16_dev(U), to_bf16_dev(SVt), to_bf16_dev(cs), host_t, kbuf, vbuf, seq_len)
+    fz.sparse_attention(*args, out)
+    torch.cuda.synchronize()
+    assert no_device_errors()
+    ek, ev = kb0.copy(), vb0.copy()
+    for i in range(B * Hkv):
+        b, h = divmod(i, Hkv)
+        n = cnt[i]
+        if n == 0:
+            continue
+        rot = o.reconstruct_keys_rope(U[b], SVt[b, h], mc[i, :n], cs, glm=rope_mode == 1)
+        for j in range(n):
+            r0 = ss + 8 * ms[i, j]
+            ek[b, h, r0:r0 + 8] = rot[8 * j:8 * j + 8]
+            ev[b, h, r0:r0 + 8] = host[b, h, mc[i, j]].reshape(8, 128)
+    gk = kbuf.float().cpu().numpy()
+    assert np.array_equal(vbuf.float().cpu().numpy(), ev), "fetched values"
+    untouched = ek == kb0
+    assert np.array_equal(gk[untouched], ek[untouched])
+    np.testing.assert_allclose(gk, ek, atol=2e-2, rtol=1e-2)
+    ref = o.decode_attention(q, gk, ev, seq_len)
+    np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=2e-2, rtol=1e-2)
+    # the per-head tickets are back at zero: a second launch gives the same output
+    out2 = torch.empty_like(out)
+    fz.sparse_attention(*args, out2)
+    torch.cuda.synchronize()
+    assert torch.equal(out, out2)
