@@ -416,6 +416,7 @@ struct SelectPlan {
     int nsplit, rows_per_split;
     size_t off_logits, off_part, off_keys, total;
     bool keys_global;
+    int cl;  // CTAs per selection cluster
     size_t sel_smem;
 };
 
@@ -429,13 +430,22 @@ static SelectPlan plan_select(const skv_decode_geom *g)
     if (per < 1) per = 1;
     p.rows_per_split = per * ST_ROWS;
     p.nsplit = ceil_div(g->num_landmarks, p.rows_per_split);
-    p.keys_global = select_smem_bytes(g->num_landmarks, g->num_chunks, false) > 150 * 1024;
-    p.sel_smem = select_smem_bytes(g->num_landmarks, g->num_chunks, p.keys_global);
+    // 16-CTA clusters for very long contexts (more than 4096 landmarks per CTA at 8)
+    p.cl = 8;
+    if (g->num_landmarks > 8 * 4096) {
+        const size_t s16 = select_smem_bytes(g->num_landmarks, g->num_chunks, false, 16);
+        if (s16 <= 150 * 1024 && select_cluster16_ok(s16)) p.cl = 16;
+    }
+    p.keys_global = select_smem_bytes(g->num_landmarks, g->num_chunks, false, p.cl) > 150 * 1024;
+    p.sel_smem = select_smem_bytes(g->num_landmarks, g->num_chunks, p.keys_global, p.cl);
     auto align = [](size_t x) { return (x + 255) & ~(size_t)255; };
     p.off_logits = 0;
     p.off_part = align((size_t)BH * g->num_landmarks * G * 4);
     p.off_keys = p.off_part + align((size_t)BH * p.nsplit * G * 8);
-    p.total = p.off_keys + (p.keys_global ? align((size_t)BH * g->num_landmarks * 4) : 0);
+    // sized for the 8-CTA plan, whose key scratch is the larger: the size does
+    // not depend on which cluster size the device allows
+    const bool keys_global8 = select_smem_bytes(g->num_landmarks, g->num_chunks, false, 8) > 150 * 1024;
+    p.total = p.off_keys + (keys_global8 ? align((size_t)BH * g->num_landmarks * 4) : 0);
     return p;
 }
 
@@ -496,7 +506,7 @@ static int run_select(const skv_decode_geom *g, const ScoreArgs &sa_in, const in
     a.miss_count = miss_count;
     a.G = G, a.L = g->num_landmarks, a.K = g->select_sets, a.nsplit = p.nsplit;
     a.num_chunks = g->num_chunks;
-    return launch_select(a, BH, p.sel_smem, s);
+    return launch_select(a, BH, p.sel_smem, p.cl, s);
 }
 
 }  // namespace skv

@@ -14,7 +14,7 @@
 // the bin (a few dozen for softmax scores) are appended to rank 0's candidate
 // list, which rank 0 ranks exactly -- key descending, landmark index
 // ascending, so that when the K-th score is tied the lowest landmark indices
-// win.  Should more than SEL_CAND keys share the bin, the cluster falls back
+// win.  Should more than SEL_REGION keys share the bin, the cluster falls back
 // to an exact 4-pass radix select (8 bits per pass) with the same tie rule.
 // Rank 0 then computes the slot-stable diff from the two bitmaps.
 #include "select.cuh"
@@ -36,12 +36,6 @@ __device__ __forceinline__ uint32_t ld_dsmem_u32(uint32_t addr)
 __device__ __forceinline__ void st_dsmem_u32(uint32_t addr, uint32_t v)
 {
     asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t atom_add_dsmem_u32(uint32_t addr, uint32_t v)
-{
-    uint32_t old;
-    asm volatile("atom.shared::cluster.add.u32 %0, [%1], %2;" : "=r"(old) : "r"(addr), "r"(v) : "memory");
-    return old;
 }
 __device__ __forceinline__ void cluster_sync()
 {
@@ -94,6 +88,10 @@ __device__ __forceinline__ void atom_or_dsmem_u32(uint32_t addr, uint32_t v)
 {
     asm volatile("red.shared::cluster.or.b32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
 }
+__device__ __forceinline__ void red_add_dsmem_u32(uint32_t addr, uint32_t v)
+{
+    asm volatile("red.shared::cluster.add.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
 __device__ __forceinline__ uint4 ld_dsmem_v4(uint32_t addr)
 {
     uint4 v;
@@ -102,8 +100,10 @@ __device__ __forceinline__ uint4 ld_dsmem_v4(uint32_t addr)
     return v;
 }
 
+template <int CL>
 __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
 {
+    constexpr int REGION = SEL_CAND / CL;  // candidates a CTA may push on the fast path
     extern __shared__ __align__(16) unsigned char smem_raw[];
     __shared__ float s_M[16], s_invZ[16];
     __shared__ __align__(16) unsigned s_h1[SEL_BINS];  // first-pass histogram (DSMEM-read)
@@ -111,18 +111,20 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
     __shared__ unsigned s_tot[256];
     __shared__ int s_warp[33];
     __shared__ uint32_t s_ckey[SEL_CAND];              // rank 0: boundary-bin candidates (key,
-    __shared__ int s_clm[SEL_CAND], s_cchunk[SEL_CAND]; //   landmark index, chunk id)
+    __shared__ int s_clm[SEL_CAND], s_cchunk[SEL_CAND]; //   landmark index, chunk id), region r from CTA r
+    __shared__ unsigned s_ccnt[CL];                // rank 0: candidates pushed by CTA r
+    __shared__ int s_pre[CL + 1];                  // rank 0: their exclusive prefix
     __shared__ int s_misssorted[1024];                 // rank 0: missed chunk ids, ascending
-    __shared__ unsigned s_ncand, s_nloc, s_cbase;
-    __shared__ uint32_t s_lkey[SEL_CAND];              // this CTA's candidates before the push
-    __shared__ int s_llm[SEL_CAND], s_lchunk[SEL_CAND];
+    __shared__ unsigned s_nloc;                        // candidates this CTA pushed so far
+    __shared__ uint32_t s_lkey[SEL_REGION];            // rank 0: the candidates, compacted
+    __shared__ int s_llm[SEL_REGION], s_lchunk[SEL_REGION];
     __shared__ int s_digit, s_above, s_bin, s_bin_above, s_bin_cnt;
-    __shared__ unsigned s_eq_rank[SEL_CL];
+    __shared__ unsigned s_eq_rank[CL];
 
     const unsigned rank = blockIdx.x;
     const int bh = blockIdx.y, tid = threadIdx.x, lane = tid & 31;
     const int G = a.G, L = a.L, K = a.K;
-    const int slice = (L + SEL_CL - 1) / SEL_CL;
+    const int slice = (L + CL - 1) / CL;
     const int c0 = (int)rank * slice;
     const int n = max(0, min(L, c0 + slice) - c0);
     const int nbw = (a.num_chunks + 31) >> 5;
@@ -160,7 +162,8 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
         }
     }
     for (int i = tid; i < SEL_BINS; i += SEL_T) s_h1[i] = 0;
-    if (tid == 0) s_ncand = s_nloc = 0;
+    if (tid == 0) s_nloc = 0;
+    if (tid < CL) s_ccnt[tid] = 0;
 
     pdl_wait();  // the scoring kernel's logits and partials are complete from here on
 
@@ -248,10 +251,10 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
     //    K-th largest key: warp 0, lane l owns bins 255-8l .. 248-8l
     if (warp_id() == 0) {
         const int b0 = SEL_BINS - 8 - 8 * lane;
-        uint4 lo[SEL_CL], hi[SEL_CL];
+        uint4 lo[CL], hi[CL];
         const uint32_t la = (uint32_t)__cvta_generic_to_shared(&s_h1[b0]);
 #pragma unroll
-        for (unsigned r = 0; r < SEL_CL; ++r) {
+        for (unsigned r = 0; r < CL; ++r) {
             uint32_t ra;
             asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(la), "r"(r));
             lo[r] = ld_dsmem_v4(ra);
@@ -259,7 +262,7 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
         }
         int cnt[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // cnt[i]: bin b0 + 7 - i
 #pragma unroll
-        for (unsigned r = 0; r < SEL_CL; ++r) {
+        for (unsigned r = 0; r < CL; ++r) {
             cnt[0] += (int)hi[r].w;
             cnt[1] += (int)hi[r].z;
             cnt[2] += (int)hi[r].y;
@@ -302,10 +305,14 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
         else report_dev_error(DEV_ERR_HOST_CHUNK);
     };
 
-    if (bin_cnt <= SEL_CAND) {
+    if (bin_cnt <= REGION) {
         // 4) keys above the boundary bin are selected; the keys inside it are
-        //    the candidates: compacted locally, then pushed to rank 0's list
-        //    at an offset taken with one cluster-scope atomic per CTA
+        //    the candidates.  CTA r pushes its candidates into region r of rank
+        //    0's store and adds their count to rank 0's s_ccnt[r]: only
+        //    fire-and-forget remote writes, no round trip.
+        const uint32_t reg0 = (uint32_t)rank * REGION;
+        const uint32_t ckey0 = dsmem_addr(s_ckey, 0), clm0 = dsmem_addr(s_clm, 0), cch0 = dsmem_addr(s_cchunk, 0);
+        const uint32_t ccnt0 = dsmem_addr(&s_ccnt[rank], 0);
         for (int base = (tid & ~31); base < n; base += SEL_T) {
             const int c = base + lane;
             const uint32_t k = c < n ? keys[c] : 0u;
@@ -315,53 +322,62 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
             const unsigned ballot = __ballot_sync(0xffffffffu, cand);
             if (ballot) {
                 unsigned pos0 = 0;
-                if (lane == 0) pos0 = atomicAdd(&s_nloc, (unsigned)__popc(ballot));
+                if (lane == 0) {
+                    pos0 = atomicAdd(&s_nloc, (unsigned)__popc(ballot));
+                    red_add_dsmem_u32(ccnt0, (unsigned)__popc(ballot));
+                }
                 pos0 = __shfl_sync(0xffffffffu, pos0, 0);
                 if (cand) {
-                    const unsigned pos = pos0 + __popc(ballot & ((1u << lane) - 1u));
-                    s_lkey[pos] = k;
-                    s_llm[pos] = c0 + c;
-                    s_lchunk[pos] = chunk_of(c);
+                    const uint32_t off = 4u * (reg0 + pos0 + __popc(ballot & ((1u << lane) - 1u)));
+                    st_dsmem_u32(ckey0 + off, k);
+                    st_dsmem_u32(clm0 + off, (uint32_t)(c0 + c));
+                    st_dsmem_u32(cch0 + off, (uint32_t)chunk_of(c));
                 }
-            }
-        }
-        __syncthreads();
-        const int nloc = (int)s_nloc;
-        if (tid == 0 && nloc > 0) s_cbase = atom_add_dsmem_u32(dsmem_addr(&s_ncand, 0), (unsigned)nloc);
-        __syncthreads();
-        if (nloc > 0) {
-            const uint32_t ckey0 = dsmem_addr(s_ckey, 0), clm0 = dsmem_addr(s_clm, 0), cch0 = dsmem_addr(s_cchunk, 0);
-            for (int i = tid; i < nloc; i += SEL_T) {
-                const uint32_t off = 4u * (s_cbase + (unsigned)i);
-                st_dsmem_u32(ckey0 + off, s_lkey[i]);
-                st_dsmem_u32(clm0 + off, (uint32_t)s_llm[i]);
-                st_dsmem_u32(cch0 + off, (uint32_t)s_lchunk[i]);
             }
         }
         cluster_sync();  // rank 0 holds the candidates and the bits of the keys above them
         if (rank != 0) return;
+        // the regions, compacted
+        if (tid == 0) {
+            int acc = 0;
+            for (int r = 0; r < CL; ++r) {
+                s_pre[r] = acc;
+                acc += (int)s_ccnt[r];
+            }
+            s_pre[CL] = acc;
+        }
+        __syncthreads();
+        for (int t = tid; t < SEL_CAND; t += SEL_T) {
+            const int r = t / REGION, o = t % REGION;
+            if (o < (int)s_ccnt[r]) {
+                s_lkey[s_pre[r] + o] = s_ckey[t];
+                s_llm[s_pre[r] + o] = s_clm[t];
+                s_lchunk[s_pre[r] + o] = s_cchunk[t];
+            }
+        }
+        __syncthreads();
         // 5) exact order among the candidates (key descending, landmark index
         //    ascending); the first K - bin_above of them are selected.  Warp w
         //    ranks candidates w, w + 16, ...; its lanes split the comparisons.
-        const int nc = (int)s_ncand, need = K - bin_above;
+        const int nc = s_pre[CL], need = K - bin_above;
         for (int i = warp_id(); i < nc; i += SEL_T / 32) {
-            const uint32_t ki = s_ckey[i];
-            const int li = s_clm[i];
+            const uint32_t ki = s_lkey[i];
+            const int li = s_llm[i];
             unsigned before = 0;
             for (int j = lane; j < nc; j += 32) {
-                const uint32_t kj = s_ckey[j];
-                const int lj = s_clm[j];
+                const uint32_t kj = s_lkey[j];
+                const int lj = s_llm[j];
                 before += (kj > ki || (kj == ki && lj < li)) ? 1u : 0u;
             }
             before = __reduce_add_sync(0xffffffffu, before);
             if (lane == 0 && (int)before < need) {
-                const int cid = s_cchunk[i];
+                const int cid = s_lchunk[i];
                 if (cid >= 0) atomicOr(&bmA[cid >> 5], 1u << (cid & 31));
                 else report_dev_error(DEV_ERR_HOST_CHUNK);
             }
         }
     } else {
-        // 4') more than SEL_CAND keys share the boundary bin (e.g. many equal
+        // 4') more than REGION keys share the boundary bin (e.g. many equal
         //     scores): exact cluster-wide radix select, 4 passes of 8 bits
         uint32_t prefix = 0, pmask = 0;
         int remaining = K, n_equal = 0;
@@ -382,7 +398,7 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
             if (tid < 256) {
                 unsigned t = 0;
 #pragma unroll
-                for (unsigned r = 0; r < SEL_CL; ++r) t += ld_dsmem_u32(dsmem_addr(&h[tid], r));
+                for (unsigned r = 0; r < CL; ++r) t += ld_dsmem_u32(dsmem_addr(&h[tid], r));
                 s_tot[tid] = t;
             }
             __syncthreads();
@@ -417,7 +433,7 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
             pmask |= 255u << shift;
             if (pass == 3) {
                 n_equal = (int)s_tot[d];
-                if (tid < SEL_CL) s_eq_rank[tid] = ld_dsmem_u32(dsmem_addr(&h[d], tid));
+                if (tid < CL) s_eq_rank[tid] = ld_dsmem_u32(dsmem_addr(&h[d], tid));
             }
             __syncthreads();
         }
@@ -498,25 +514,65 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
     }
 }
 
-size_t select_smem_bytes(int L, int num_chunks, bool keys_global)
+size_t select_smem_bytes(int L, int num_chunks, bool keys_global, int cl)
 {
-    const size_t slice = (size_t)((L + SEL_CL - 1) / SEL_CL);
+    const size_t slice = (size_t)((L + cl - 1) / cl);
     const size_t nbw = (size_t)((num_chunks + 31) / 32);
     return (keys_global ? 0 : slice * 8) + 2 * nbw * 4;  // keys + chunk ids of the slice, bitmaps
 }
 
-int launch_select(const SelectArgs &a, int BH, size_t smem, cudaStream_t stream)
+// Whether this device can schedule 16-CTA clusters of the selection kernel
+// (a non-portable cluster size), decided once per device.
+bool select_cluster16_ok(size_t smem)
 {
-    int st = ensure_smem_attr((const void *)select_cluster_kernel, (int)smem, "select_cluster_kernel");
+    static int cached[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        return false;
+    }
+    if (cached[dev]) return cached[dev] > 0;
+    int ok = -1;
+    const void *fn = (const void *)select_cluster_kernel<16>;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess &&
+        ensure_smem_attr(fn, (int)smem, "select_cluster_kernel<16>") == SKV_OK) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(16, 1, 1);
+        cfg.blockDim = dim3(SEL_T, 1, 1);
+        cfg.dynamicSmemBytes = smem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 16;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) == cudaSuccess && n >= 1) ok = 1;
+    }
+    cudaGetLastError();
+    cached[dev] = ok;
+    return ok > 0;
+}
+
+int launch_select(const SelectArgs &a, int BH, size_t smem, int cl, cudaStream_t stream)
+{
+    const void *fn = cl == 16 ? (const void *)select_cluster_kernel<16> : (const void *)select_cluster_kernel<8>;
+    int st = ensure_smem_attr(fn, (int)smem, "select_cluster_kernel");
     if (st) return st;
+    if (cl == 16 && cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+        cudaGetLastError();
+        set_error("16-CTA clusters not available for select_cluster_kernel");
+        return SKV_ERR_CUDA;
+    }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(SEL_CL, BH, 1);
+    cfg.gridDim = dim3(cl, BH, 1);
     cfg.blockDim = dim3(SEL_T, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = SEL_CL;
+    attr[0].val.clusterDim.x = cl;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     // may start while the scoring kernel drains; it reads the scores only after pdl_wait()
@@ -524,7 +580,8 @@ int launch_select(const SelectArgs &a, int BH, size_t smem, cudaStream_t stream)
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, select_cluster_kernel, a);
+    cudaError_t e = cl == 16 ? cudaLaunchKernelEx(&cfg, select_cluster_kernel<16>, a)
+                             : cudaLaunchKernelEx(&cfg, select_cluster_kernel<8>, a);
     if (e != cudaSuccess) {
         cudaGetLastError();
         set_error("launch of select_cluster_kernel failed: %s", cudaGetErrorString(e));

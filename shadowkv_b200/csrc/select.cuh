@@ -5,14 +5,15 @@
 
 namespace skv {
 
-constexpr int SEL_CL = 8;    // CTAs per (b, kv head): one thread-block cluster
+constexpr int SEL_CL = 8;    // CTAs per (b, kv head): one thread-block cluster (16 for very long contexts)
 constexpr int SEL_T = 512;   // threads per CTA
 // First pass: a 256-bin histogram of key bits 30..20 (exponent and 3
 // mantissa bits).  Keys are probabilities in [0, 1] (bits 30..20 <= 1016);
 // bins 1..255 hold bits 769..1023, bin 0 every key below 2^-31.
 constexpr int SEL_BIN_LO = 768;
 constexpr int SEL_BINS = 256;
-constexpr int SEL_CAND = 1024;  // candidate capacity of the exact stage
+constexpr int SEL_CAND = 2048;                 // rank 0's candidate store: one region per CTA
+constexpr int SEL_REGION = SEL_CAND / SEL_CL;  // largest per-CTA candidate region (8-CTA clusters)
 
 __device__ __forceinline__ int sel_key_bin(uint32_t k)
 {
@@ -30,9 +31,12 @@ struct SelectArgs {
     int G, L, K, nsplit, num_chunks;
 };
 
-// Dynamic shared memory of one CTA of the selection kernel.
-size_t select_smem_bytes(int L, int num_chunks, bool keys_global);
+// Dynamic shared memory of one CTA of the selection kernel (cl CTAs per cluster).
+size_t select_smem_bytes(int L, int num_chunks, bool keys_global, int cl);
 
-int launch_select(const SelectArgs &a, int BH, size_t smem, cudaStream_t stream);
+// Whether 16-CTA clusters of the selection kernel can be scheduled on this device.
+bool select_cluster16_ok(size_t smem);
+
+int launch_select(const SelectArgs &a, int BH, size_t smem, int cl, cudaStream_t stream);
 
 }  // namespace skv
