@@ -3,9 +3,11 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config config1]
 
 One step = one decode step of one layer through ``ShadowAttention.decode_fused``:
-RoPE of the new q/k, append, landmark scoring + top-k + reuse diff, zero-copy
-fetch of the missed value chunks from pinned host memory (copy stream),
-tensor-core key reconstruction + RoPE (main stream), split-K GQA attention.
+RoPE of the new q/k, append, landmark scoring + top-k + reuse diff (two
+launches), then one launch that fetches the missed value chunks from pinned
+host memory (zero-copy), reconstructs the missed keys on the tensor cores
+with RoPE and computes the GQA attention (``--split``: the last three stages
+as separate launches, the fetch on a copy stream).
 The workload is BASELINE configs[1] (Llama-3-8B shape, 122880 context, budget
 2048, rank 160) with seeded synthetic inputs; every rank runs its own
 sequence (batch-sharded weak scaling, no collective on the data path).
@@ -363,7 +365,11 @@ def run_b200(args, world, rank, local):
                                 "sparse_attend_kernel (zero-copy V gather + key reconstruction + attention)"),
                      "bound": "host_link",
                      "achieved": link_achieved, "peak": link_peak, "unit": "GB/s",
-                     "frac": link_achieved / link_peak if link_peak else None, "traffic": None,
+                     "frac": link_achieved / link_peak if link_peak else None,
+                     # sysmem bytes read per launch in the ncu capture of this workload
+                     # (profiles/sparse_attend_kernel_config1.md): equal to the missed bytes
+                     "traffic": (4.098e6 if cfg.name == "config1" and not args.split else None),
+                     "traffic_kind": "sysmem (host link) bytes read per launch, ncu",
                      "peak_kind": "measured in-run: pinned H2D copy-engine bandwidth"},
         "step_roofline": {"t_roof_us": t_roof * 1e6, "t_step_us": ms_step * 1e3,
                           "frac": t_roof / (ms_step * 1e-3), "hbm_bytes": hbm_b, "host_bytes": host_b,
