@@ -216,7 +216,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity, unsign
     }
     return false;
 }
-// Bulk (TMA, non-multicast) copy of `bytes` from this GPU's global memory into shared memory.
+// Bulk (TMA) copy of `bytes` from this GPU's global memory into this CTA's shared memory only.
 __device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *gmem_src, unsigned bytes, uint64_t *bar)
 {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
