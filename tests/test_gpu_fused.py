@@ -234,11 +234,11 @@ def test_gather_values_exact():
     assert np.array_equal(bits(buf), expect)
 
 
-@pytest.mark.parametrize("rope_mode", [0, 1])
-def test_reconstruct_keys_with_rope(rope_mode):
+@pytest.mark.parametrize("rope_mode,rank", [(0, 160), (1, 160), (0, 64), (1, 16), (0, 256)])
+def test_reconstruct_keys_with_rope(rope_mode, rank):
     from shadowkv_b200 import decode as fz
-    rng = np.random.default_rng(rope_mode + 3)
-    B, H, K, T, rank = 1, 4, 256, 16384, 160
+    rng = np.random.default_rng(rope_mode + 3 + rank)
+    B, H, K, T = 1, 4, 256, 16384
     chunks = T // 8
     width = 128 if rope_mode == 0 else 64
     U = o.round_bf16((rng.standard_normal((B, T, rank)) / 8).astype(np.float32))
