@@ -20,6 +20,7 @@ host memory and the attention output copied back every step.
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import json
 import math
 import os
@@ -170,6 +171,13 @@ def run_b200(args, world, rank, local):
         from shadowkv_b200 import numa
         numa.bind_to_gpu_numa(local)
     cfg = workload.CONFIGS[args.config]
+    heads_sharded = args.shard == "heads" and world > 1
+    if heads_sharded:
+        # rank r owns kv heads [r*Hkv/N, (r+1)*Hkv/N) and their GQA groups; the attention
+        # outputs are all-gathered (NCCL over NVLink) inside the step, before o_proj
+        from shadowkv_b200 import sharding
+        k0, kn, q0, qn = sharding.head_range(cfg.kv_heads, cfg.q_heads, world, rank)
+        cfg = dataclasses.replace(cfg, kv_heads=kn, q_heads=qn)
     torch.manual_seed(0)
     layer = workload.Layer(cfg, device=f"cuda:{local}", seed=1000 + rank)
     cache, attn = layer.cache, layer.attn
@@ -190,6 +198,8 @@ def run_b200(args, world, rank, local):
     s_v = torch.empty_like(inputs[0][2])
     s_pos = torch.full((B, 1), pos0, dtype=torch.int64, device="cuda")
     s_out = torch.empty(B, Hq, 128, dtype=torch.bfloat16, device="cuda")
+    # heads sharded: every rank ends the step with the attention output of all heads
+    s_full = torch.empty(world * B * Hq, 128, dtype=torch.bfloat16, device="cuda") if heads_sharded else None
     s_qr = torch.empty(B, Hq, 1, 128, dtype=torch.bfloat16, device="cuda")
     cache.fused_geometry(attn.cos_sin_cache)
 
@@ -215,6 +225,8 @@ def run_b200(args, world, rank, local):
             cache.attention(0, qr, seq_len, out=s_out)
         else:
             cache.sparse_attention_fused(0, qr, seq_len, attn.cos_sin_cache, out=s_out)
+        if heads_sharded:
+            torch.distributed.all_gather_into_tensor(s_full, s_out.view(B * Hq, 128))
         cache.gen_offset = 0
         return seq_len
 
@@ -306,7 +318,7 @@ def run_b200(args, world, rank, local):
 
     ms_step = sum(per_step) / len(per_step)
     ms_step_max = max_over_ranks(ms_step, world)
-    tokens = B * world
+    tokens = B if heads_sharded else B * world
     value = tokens / (ms_step_max / 1e3)
     misses = statistics.mean(misses_all)
     hit_rate = 1.0 - misses / (B * Hkv * cache.select_sets)
@@ -318,7 +330,7 @@ def run_b200(args, world, rank, local):
     # ---- e2e: inputs copied from pinned host memory, the output copied back, every step
     h_in = [tuple(t.cpu().pin_memory() for t in inp) for inp in inputs]
     h_pos = torch.empty(B, 1, dtype=torch.int64).pin_memory()
-    h_out = torch.empty(B, Hq, 128, dtype=torch.bfloat16).pin_memory()
+    h_out = torch.empty(*(s_full.shape if heads_sharded else (B, Hq, 128)), dtype=torch.bfloat16).pin_memory()
     nin = len(inputs)
     e2e_ms = []
     for i in range(args.warmup, n):
@@ -334,7 +346,7 @@ def run_b200(args, world, rank, local):
             graph.replay()
         else:
             step_body()
-        h_out.copy_(s_out, non_blocking=True)
+        h_out.copy_(s_full if heads_sharded else s_out, non_blocking=True)
         e.record(main)
         e.synchronize()
         e2e_ms.append(s.elapsed_time(e))
@@ -353,13 +365,16 @@ def run_b200(args, world, rank, local):
         "warmup": args.warmup,
         "ms_per_step": ms_step_max,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if heads_sharded else "weak",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded; BASELINE configs[1] shapes and distributions)",
-        "config": {"workload": f"{cfg.name}: one decode layer, B={B}/GPU, {Hq}q/{Hkv}kv heads, ctx {cfg.ctx}, "
+        "config": {"workload": f"{cfg.name}: one decode layer, B={B}/GPU, {Hq}q/{Hkv}kv heads"
+                               f"{' per GPU' if heads_sharded else ''}, ctx {cfg.ctx}, "
                                f"budget {cfg.budget}, rank {cfg.rank}, V in pinned host memory",
-                   "global_batch": B * world, "seq_len": cfg.ctx, "parallelism": f"batch-sharded x{world}",
+                   "global_batch": tokens, "seq_len": cfg.ctx,
+                   "parallelism": (f"kv-head-sharded x{world} (NCCL all-gather of the attention output)"
+                                   if heads_sharded else f"batch-sharded x{world}"),
                    "l2": "flushed between timed steps (256 MB write)", "hit_rate": hit_rate},
         "roofline": {"kernel": ("fetch_misses_kernel (zero-copy V gather)" if args.split else
                                 "sparse_attend_kernel (zero-copy V gather + key reconstruction + attention)"),
@@ -432,6 +447,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying a CUDA graph")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--shard", default="batch", choices=["batch", "heads"],
+                    help="multi-GPU partition: one sequence per rank (weak scaling) or the kv heads of one "
+                         "sequence split over the ranks with an NCCL all-gather of the outputs (strong scaling)")
     ap.add_argument("--split", action="store_true",
                     help="fetch / reconstruction / attention as three launches instead of the fused kernel")
     args = ap.parse_args()
