@@ -78,14 +78,14 @@ __device__ __forceinline__ void merge_stats(float &m, float &s, float m2, float 
 // online (max, sum-exp) per query head.
 //
 // grid = (nsplit, B*Hkv); 8 consumer warps + 1 producer warp.  The producer
-// streams the CTA's landmark rows through a 4-stage ring of 128-row (32 KB)
+// streams the CTA's landmark rows through a 3-stage ring of 128-row (32 KB)
 // shared-memory tiles with bulk (TMA) copies completed on mbarriers; each
 // consumer warp multiplies 16 rows of a tile per stage on the tensor cores.
 // With APPEND the kernel also performs the new-token step: it rotates the
 // query rows of its GQA group itself, and the split-0 CTA of each head writes
 // the rotated query, the rotated key and the value of the new token.
 // ---------------------------------------------------------------------------
-constexpr int ST_STAGES = 4;
+constexpr int ST_STAGES = 3;   // 3 x 32 KB tiles: two CTAs per SM
 constexpr int ST_PRE = 1;     // stages issued before the query prologue
 constexpr int ST_ROWS = 128;
 constexpr int ST_CONSUMERS = 8;
@@ -426,7 +426,7 @@ static SelectPlan plan_select(const skv_decode_geom *g)
     const int G = g->q_heads / g->kv_heads;
     const int BH = g->batch * g->kv_heads;
     const int stages = ceil_div(g->num_landmarks, ST_ROWS);  // 128-row tiles per head
-    int per = ceil_div(stages * BH, 148);                      // about one CTA per SM
+    int per = ceil_div(stages * BH, 2 * 148);                  // about two CTAs per SM
     if (per < 1) per = 1;
     p.rows_per_split = per * ST_ROWS;
     p.nsplit = ceil_div(g->num_landmarks, p.rows_per_split);
