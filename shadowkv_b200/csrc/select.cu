@@ -100,6 +100,112 @@ __device__ __forceinline__ uint4 ld_dsmem_v4(uint32_t addr)
     return v;
 }
 
+// Exact cluster-wide radix select (4 passes of 8 bits) of the K largest keys,
+// for the rare case of more boundary-bin candidates than a CTA's region holds
+// (e.g. many equal scores); ties at the K-th key go to the lowest landmark
+// indices (ranks in index order).  Sets the chunks in rank 0's bitmap (bmA0).
+// Kept out of line so that the common path stays compact in the instruction cache.
+template <int CL>
+__device__ __noinline__ void select_radix_fallback(const uint32_t *keys, int n, int K, int c0, unsigned rank,
+                                                   const int *lidx_s, const int64_t *lidx, int num_chunks,
+                                                   uint32_t bmA0, unsigned (*s_hist)[256], unsigned *s_tot,
+                                                   int *s_warp, unsigned *s_eq_rank)
+{
+    __shared__ int s_digit, s_above;
+    const int tid = threadIdx.x, lane = tid & 31;
+    auto chunk_of = [&](int c) -> int {
+        if (lidx_s) return lidx_s[c];
+        const int64_t v = lidx[c];
+        return (v >= 0 && v < num_chunks) ? (int)v : -1;
+    };
+    auto mark = [&](int cid) {
+        if (cid >= 0) atom_or_dsmem_u32(bmA0 + 4u * (uint32_t)(cid >> 5), 1u << (cid & 31));
+        else report_dev_error(DEV_ERR_HOST_CHUNK);
+    };
+    (void)c0;
+    uint32_t prefix = 0, pmask = 0;
+    int remaining = K, n_equal = 0;
+    for (int pass = 0; pass < 4; ++pass) {
+        const int shift = 24 - 8 * pass;
+        unsigned *h = s_hist[pass & 1];
+        if (tid < 256) h[tid] = 0;
+        __syncthreads();
+        for (int base = (tid & ~31); base < n; base += SEL_T) {
+            const int c = base + lane;
+            const uint32_t k = c < n ? keys[c] : 0u;
+            const bool part = c < n && (k & pmask) == prefix;
+            const int bin = part ? (int)((k >> shift) & 255) : 256 + lane;
+            const unsigned peers = __match_any_sync(0xffffffffu, bin);
+            if (part && lane == __ffs(peers) - 1) atomicAdd(&h[bin], (unsigned)__popc(peers));
+        }
+        cluster_sync();  // every CTA's histogram of this pass is complete
+        if (tid < 256) {
+            unsigned t = 0;
+            for (unsigned r = 0; r < CL; ++r) t += ld_dsmem_u32(dsmem_addr(&h[tid], r));
+            s_tot[tid] = t;
+        }
+        __syncthreads();
+        if (tid < 32) {
+            // lane l owns digits 255-8l .. 248-8l (descending)
+            int cnt[8], tot = 0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                cnt[i] = (int)s_tot[255 - 8 * tid - i];
+                tot += cnt[i];
+            }
+            int incl = tot;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (tid >= o) incl += y;
+            }
+            int above = incl - tot;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                if (above < remaining && above + cnt[i] >= remaining) {
+                    s_digit = 255 - 8 * tid - i;
+                    s_above = above;
+                }
+                above += cnt[i];
+            }
+        }
+        __syncthreads();
+        const int d = s_digit;
+        remaining -= s_above;
+        prefix |= (uint32_t)d << shift;
+        pmask |= 255u << shift;
+        if (pass == 3) {
+            n_equal = (int)s_tot[d];
+            if (tid < CL) s_eq_rank[tid] = ld_dsmem_u32(dsmem_addr(&h[d], tid));
+        }
+        __syncthreads();
+    }
+    const uint32_t T = prefix;  // the K-th largest key
+    const bool take_all_equal = n_equal == remaining;
+    for (int base = (tid & ~31); base < n; base += SEL_T) {
+        const int c = base + lane;
+        if (c < n) {
+            const uint32_t k = keys[c];
+            if (k > T || (take_all_equal && k == T)) mark(chunk_of(c));
+        }
+    }
+    if (!take_all_equal) {
+        // ties at the threshold: lowest landmark index first, ranks in index order
+        int before = 0;
+        for (unsigned r = 0; r < rank; ++r) before += (int)s_eq_rank[r];
+        const int quota = max(0, min(remaining - before, (int)s_eq_rank[rank]));
+        int taken = 0;
+        for (int base = 0; base < n && taken < quota; base += SEL_T) {
+            const int c = base + tid;
+            const int f = (c < n && keys[c] == T) ? 1 : 0;
+            int tot;
+            const int r = cta_excl_scan(f, &tot, s_warp);
+            if (f && taken + r < quota) mark(chunk_of(c));
+            taken += tot;
+        }
+    }
+}
+
 template <int CL>
 __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
 {
@@ -118,7 +224,7 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
     __shared__ unsigned s_nloc;                        // candidates this CTA pushed so far
     __shared__ uint32_t s_lkey[SEL_REGION];            // rank 0: the candidates, compacted
     __shared__ int s_llm[SEL_REGION], s_lchunk[SEL_REGION];
-    __shared__ int s_digit, s_above, s_bin, s_bin_above, s_bin_cnt;
+    __shared__ int s_bin, s_bin_above, s_bin_cnt;
     __shared__ unsigned s_eq_rank[CL];
 
     const unsigned rank = blockIdx.x;
@@ -170,7 +276,7 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
     // the first batch of this CTA's logits goes out before the partials are
     // merged (two independent loads, one memory latency)
     const float *lg = a.logits + ((int64_t)bh * L + c0) * G;
-    constexpr int U = 4;
+    constexpr int U = 1;  // one landmark per lane per loop trip: compact code (executed once per step, cold)
     const int G4 = (G & 3) == 0 ? G >> 2 : 0;
     float4 v[U][4];
     auto load_batch = [&](int base) {
@@ -378,89 +484,9 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
         }
     } else {
         // 4') more than REGION keys share the boundary bin (e.g. many equal
-        //     scores): exact cluster-wide radix select, 4 passes of 8 bits
-        uint32_t prefix = 0, pmask = 0;
-        int remaining = K, n_equal = 0;
-        for (int pass = 0; pass < 4; ++pass) {
-            const int shift = 24 - 8 * pass;
-            unsigned *h = s_hist[pass & 1];
-            if (tid < 256) h[tid] = 0;
-            __syncthreads();
-            for (int base = (tid & ~31); base < n; base += SEL_T) {
-                const int c = base + lane;
-                const uint32_t k = c < n ? keys[c] : 0u;
-                const bool part = c < n && (k & pmask) == prefix;
-                const int bin = part ? (int)((k >> shift) & 255) : 256 + lane;
-                const unsigned peers = __match_any_sync(0xffffffffu, bin);
-                if (part && lane == __ffs(peers) - 1) atomicAdd(&h[bin], (unsigned)__popc(peers));
-            }
-            cluster_sync();  // every CTA's histogram of this pass is complete
-            if (tid < 256) {
-                unsigned t = 0;
-#pragma unroll
-                for (unsigned r = 0; r < CL; ++r) t += ld_dsmem_u32(dsmem_addr(&h[tid], r));
-                s_tot[tid] = t;
-            }
-            __syncthreads();
-            if (tid < 32) {
-                // lane l owns digits 255-8l .. 248-8l (descending)
-                int cnt[8], tot = 0;
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    cnt[i] = (int)s_tot[255 - 8 * tid - i];
-                    tot += cnt[i];
-                }
-                int incl = tot;
-#pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const int y = __shfl_up_sync(0xffffffffu, incl, o);
-                    if (tid >= o) incl += y;
-                }
-                int above = incl - tot;
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    if (above < remaining && above + cnt[i] >= remaining) {
-                        s_digit = 255 - 8 * tid - i;
-                        s_above = above;
-                    }
-                    above += cnt[i];
-                }
-            }
-            __syncthreads();
-            const int d = s_digit;
-            remaining -= s_above;
-            prefix |= (uint32_t)d << shift;
-            pmask |= 255u << shift;
-            if (pass == 3) {
-                n_equal = (int)s_tot[d];
-                if (tid < CL) s_eq_rank[tid] = ld_dsmem_u32(dsmem_addr(&h[d], tid));
-            }
-            __syncthreads();
-        }
-        const uint32_t T = prefix;  // the K-th largest key
-        const bool take_all_equal = n_equal == remaining;
-        for (int base = (tid & ~31); base < n; base += SEL_T) {
-            const int c = base + lane;
-            if (c < n) {
-                const uint32_t k = keys[c];
-                if (k > T || (take_all_equal && k == T)) mark(chunk_of(c));
-            }
-        }
-        if (!take_all_equal) {
-            // ties at the threshold: lowest landmark index first, ranks in index order
-            int before = 0;
-            for (unsigned r = 0; r < rank; ++r) before += (int)s_eq_rank[r];
-            const int quota = max(0, min(remaining - before, (int)s_eq_rank[rank]));
-            int taken = 0;
-            for (int base = 0; base < n && taken < quota; base += SEL_T) {
-                const int c = base + tid;
-                const int f = (c < n && keys[c] == T) ? 1 : 0;
-                int tot;
-                const int r = cta_excl_scan(f, &tot, s_warp);
-                if (f && taken + r < quota) mark(chunk_of(c));
-                taken += tot;
-            }
-        }
+        //     scores): exact cluster-wide radix select, out of line
+        select_radix_fallback<CL>(keys, n, K, c0, rank, lidx_s, lidx, a.num_chunks, bmA0, s_hist, s_tot, s_warp,
+                                  s_eq_rank);
         cluster_sync();  // rank 0's bitmap holds the complete selection
         if (rank != 0) return;
     }
