@@ -129,25 +129,9 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
     pdl_wait();  // the selection (and the scoring before it) are complete from here on
     __syncthreads();
 
-    // 2) missed slots of this CTA: every thread checks its entries of the miss list
-    if (has_slots) {
-        const int nmiss = min(max(a.miss_count[bh], 0), a.K);
-        for (int t = tid; t < nmiss; t += SA_THREADS) {
-            const int s = a.miss_slot[(int64_t)bh * a.K + t];
-            const int gi = (a.sparse_start + 8 * s - row0) >> 3;
-            if (s >= 0 && s < a.K && a.sparse_start + 8 * s >= row0 && gi < SA_GROUPS) {
-                const int c = a.miss_chunk[(int64_t)bh * a.K + t];
-                if (c >= 0 && c < a.num_chunks && (int64_t)c * 8 + 8 <= a.ctx) {
-                    s_chunk[gi] = c;
-                    s_kind[gi] = 1;
-                    s_any_miss = 1;
-                } else {
-                    report_dev_error(DEV_ERR_HOST_CHUNK);
-                }
-            }
-        }
-    }
-    // query rows of the group (rows >= G are zero)
+    // 2) query rows of the group (rows >= G are zero) and the missed slots of
+    //    this CTA; every load of this phase is issued in one round: the miss
+    //    count, slots and chunk ids are read together (K <= 4 * SA_THREADS)
     {
         const __nv_bfloat16 *qrows = a.q + (int64_t)bh * G * 128;
         for (int p = tid; p < 16 * 16; p += SA_THREADS) {
@@ -155,6 +139,34 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
             uint4 v = make_uint4(0, 0, 0, 0);
             if (r < G) v = ld_nc_v4(qrows + (int64_t)r * 128 + c);
             st_v4(sQ + r * SA_PITCH + c, v);
+        }
+    }
+    if (has_slots) {
+        const int32_t *msl = a.miss_slot + (int64_t)bh * a.K, *mch = a.miss_chunk + (int64_t)bh * a.K;
+        const int nm_raw = a.miss_count[bh];
+        int sv[4], cv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int t = tid + SA_THREADS * u;
+            sv[u] = t < a.K ? msl[t] : -1;
+            cv[u] = t < a.K ? mch[t] : -1;
+        }
+        const int nmiss = min(max(nm_raw, 0), a.K);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int t = tid + SA_THREADS * u;
+            const int s = sv[u];
+            if (t >= nmiss || s < 0 || s >= a.K || a.sparse_start + 8 * s < row0) continue;
+            const int gi = (a.sparse_start + 8 * s - row0) >> 3;
+            if (gi >= SA_GROUPS) continue;
+            const int c = cv[u];
+            if (c >= 0 && c < a.num_chunks && (int64_t)c * 8 + 8 <= a.ctx) {
+                s_chunk[gi] = c;
+                s_kind[gi] = 1;
+                s_any_miss = 1;
+            } else {
+                report_dev_error(DEV_ERR_HOST_CHUNK);
+            }
         }
     }
     __syncthreads();
@@ -497,6 +509,7 @@ int skv_decode_sparse_attention(const skv_decode_geom *g, const void *q, const v
     SKV_CHECK_SUPPORTED(g->rank % 16 == 0 && g->rank >= 16 && g->rank <= 256, "rank must be a multiple of 16 in 16..256");
     SKV_CHECK_SUPPORTED(g->rope_mode == 0 || g->rope_mode == 1, "rope_mode must be 0 or 1");
     SKV_CHECK_ARG(g->cos_sin_stride >= (g->rope_mode == 0 ? 128 : 64), "cos_sin_stride too small");
+    SKV_CHECK_SUPPORTED(g->select_sets <= 4 * SA_THREADS, "select_sets above %d", 4 * SA_THREADS);
     SKV_CHECK_ARG(g->select_sets >= 1 && g->sparse_start >= 0 && g->sparse_start % 8 == 0 &&
                       g->sparse_start + 8 * (int64_t)g->select_sets <= g->buf_len,
                   "selected rows exceed buf_len (or sparse_start not a multiple of 8)");
