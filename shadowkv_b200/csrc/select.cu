@@ -242,9 +242,9 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
     const int64_t *lidx = a.landmark_idx + (int64_t)bh * L + c0;
     int32_t *slots = a.slots + (int64_t)bh * K;
 
-    // No early trigger for the kernel that follows: launched while this grid
-    // runs, its CTAs would crowd onto the SMs this grid leaves free, and the
-    // zero-copy fetch it issues needs the load slots of every SM.
+    // The fused attention that follows (one CTA per SM) may become resident on
+    // the SMs this grid leaves free; it waits for this grid before reading.
+    pdl_launch_dependents();
 
     // 0) loads that do not depend on the scores: the cached slots (rank 0,
     //    thread t owns slots 2t, 2t+1) and the chunk ids of this slice
