@@ -17,8 +17,10 @@ constexpr int SEL_REGION = SEL_CAND / SEL_CL;  // largest per-CTA candidate regi
 
 __device__ __forceinline__ int sel_key_bin(uint32_t k)
 {
+    // finite softmax keys are <= 1.0 (bits 30..20 <= 1016); a non-finite key
+    // (inf or nan scores from non-finite inputs) is clamped into the last bin
     const int t = (int)(k >> 20);
-    return t > SEL_BIN_LO ? t - SEL_BIN_LO : 0;
+    return t > SEL_BIN_LO ? min(t - SEL_BIN_LO, SEL_BINS - 1) : 0;
 }
 
 struct SelectArgs {

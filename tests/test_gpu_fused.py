@@ -363,3 +363,23 @@ def test_sparse_attention_fetch_reconstruct_attend(B, Hkv, G, rank, K, ss, extra
     fz.sparse_attention(*args, out2)
     torch.cuda.synchronize()
     assert torch.equal(out, out2)
+
+
+def test_select_non_finite_query_does_not_fault():
+    """Scores from a query with inf entries give non-finite keys; the selection
+    still completes with an in-range slot table (which chunks it picks is unspecified)."""
+    from shadowkv_b200 import decode as fz
+    rng = np.random.default_rng(11)
+    H, G, L, K = 2, 4, 3000, 128
+    q = rng.standard_normal((1, H * G, 128)).astype(np.float32)
+    q[0, 0, :4] = np.inf
+    lm = to_bf16_dev(rng.standard_normal((1, H, L, 128)))
+    lidx = torch.arange(L, dtype=torch.int64, device=DEV).repeat(1, H, 1).contiguous()
+    g = make_geom(batch=1, kv_heads=H, q_heads=H * G, rank=64, select_sets=K, num_landmarks=L, num_chunks=L,
+                  ctx_len=L * 8, buf_len=K * 8, sparse_start=0)
+    ws = fz.DecodeWorkspace(g, DEV)
+    slots = torch.full((1, H, K), -1, dtype=torch.int32, device=DEV)
+    fz.select(g, ws, to_bf16_dev(q), lm, lidx, slots)
+    torch.cuda.synchronize()
+    s = slots.cpu().numpy()
+    assert ((s >= 0) & (s < L)).all()
