@@ -433,18 +433,19 @@ static SelectPlan plan_select(const skv_decode_geom *g)
     // 16-CTA clusters for very long contexts (more than 4096 landmarks per CTA at 8)
     p.cl = 8;
     if (g->num_landmarks > 8 * 4096) {
-        const size_t s16 = select_smem_bytes(g->num_landmarks, g->num_chunks, false, 16);
-        if (s16 <= 150 * 1024 && select_cluster16_ok(s16)) p.cl = 16;
+        const bool kg16 = select_smem_bytes(g->num_landmarks, g->num_chunks, G, false, 16) > SEL_SMEM_CAP;
+        const size_t s16 = select_smem_bytes(g->num_landmarks, g->num_chunks, G, kg16, 16);
+        if (s16 <= SEL_SMEM_CAP && select_cluster16_ok(s16)) p.cl = 16;
     }
-    p.keys_global = select_smem_bytes(g->num_landmarks, g->num_chunks, false, p.cl) > 150 * 1024;
-    p.sel_smem = select_smem_bytes(g->num_landmarks, g->num_chunks, p.keys_global, p.cl);
+    p.keys_global = select_smem_bytes(g->num_landmarks, g->num_chunks, G, false, p.cl) > SEL_SMEM_CAP;
+    p.sel_smem = select_smem_bytes(g->num_landmarks, g->num_chunks, G, p.keys_global, p.cl);
     auto align = [](size_t x) { return (x + 255) & ~(size_t)255; };
     p.off_logits = 0;
     p.off_part = align((size_t)BH * g->num_landmarks * G * 4);
     p.off_keys = p.off_part + align((size_t)BH * p.nsplit * G * 8);
     // sized for the 8-CTA plan, whose key scratch is the larger: the size does
     // not depend on which cluster size the device allows
-    const bool keys_global8 = select_smem_bytes(g->num_landmarks, g->num_chunks, false, 8) > 150 * 1024;
+    const bool keys_global8 = select_smem_bytes(g->num_landmarks, g->num_chunks, G, false, 8) > SEL_SMEM_CAP;
     p.total = p.off_keys + (keys_global8 ? align((size_t)BH * g->num_landmarks * 4) : 0);
     return p;
 }

@@ -105,6 +105,50 @@ __device__ __forceinline__ uint4 ld_dsmem_v4(uint32_t addr)
 // (e.g. many equal scores); ties at the K-th key go to the lowest landmark
 // indices (ranks in index order).  Sets the chunks in rank 0's bitmap (bmA0).
 // Kept out of line so that the common path stays compact in the instruction cache.
+// Keys of the landmarks of one logits tile in shared memory (cnt landmarks,
+// rows of G = 4Q floats; the first is landmark k0 of the CTA) and their
+// first-pass histogram.  The key of landmark c is
+//     max_g softmax_g(c) = exp(max_g (logit_g(c) - C_g)),  C_g = M_g + ln Z_g,
+// one exponential per landmark (exp is increasing, so the max moves inside).
+// A warp takes 32 landmarks in Q reads of 32 consecutive 16-byte words (no
+// bank conflicts): lane l holds heads 4(l%Q)..4(l%Q)+3 of one landmark, the Q
+// lanes of a landmark reduce their maxima by shuffles, and the maximum moves
+// to the landmark's lane.  The Q reads are independent (unrolled) chains.
+template <int Q>
+__device__ __forceinline__ void ring_tile_keys(const float4 *tile, int k0, int cnt, const float *s_C,
+                                               uint32_t *keys, unsigned *s_hw)
+{
+    constexpr int LPL = 32 / Q;  // landmarks per read
+    const int lane = threadIdx.x & 31, g0 = (lane & (Q - 1)) * 4;
+    const float4 Cg = make_float4(s_C[g0], s_C[g0 + 1], s_C[g0 + 2], s_C[g0 + 3]);
+    for (int base = threadIdx.x & ~31; base < cnt; base += SEL_T) {
+        float m[Q];
+#pragma unroll
+        for (int j = 0; j < Q; ++j) {
+            m[j] = -INFINITY;
+            if (base + j * LPL + lane / Q < cnt) {
+                const float4 v = tile[(base + j * LPL) * Q + lane];
+                m[j] = fmaxf(fmaxf(m[j], v.x - Cg.x), v.y - Cg.y);
+                m[j] = fmaxf(fmaxf(m[j], v.z - Cg.z), v.w - Cg.w);
+            }
+        }
+#pragma unroll
+        for (int o = 1; o < Q; o <<= 1)
+#pragma unroll
+            for (int j = 0; j < Q; ++j) m[j] = fmaxf(m[j], __shfl_xor_sync(0xffffffffu, m[j], o));
+        float d = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < Q; ++j) {
+            const float v2 = __shfl_sync(0xffffffffu, m[j], (lane % LPL) * Q);
+            if (lane / LPL == j) d = v2;
+        }
+        const float sc = __expf(d);
+        const bool valid = base + lane < cnt;
+        if (valid) keys[k0 + base + lane] = __float_as_uint(sc);
+        if (valid) atomicAdd(&s_hw[sel_key_bin(__float_as_uint(sc))], 1u);
+    }
+}
+
 template <int CL>
 __device__ __noinline__ void select_radix_fallback(const uint32_t *keys, int n, int K, int c0, unsigned rank,
                                                    const int *lidx_s, const int64_t *lidx, int num_chunks,
@@ -211,7 +255,7 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
 {
     constexpr int REGION = SEL_CAND / CL;  // candidates a CTA may push on the fast path
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    __shared__ float s_M[16], s_invZ[16];
+    __shared__ float s_C[16];  // M_g + ln Z_g of each query head of the group
     __shared__ __align__(16) unsigned s_h1[SEL_BINS];  // first-pass histogram (DSMEM-read)
     __shared__ unsigned s_hist[2][256];                // exact fallback: 8-bit pass histograms
     __shared__ unsigned s_tot[256];
@@ -239,6 +283,12 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
     int *lidx_s = a.gkeys ? nullptr : reinterpret_cast<int *>(dyn + slice);
     uint32_t *bmA = a.gkeys ? dyn : dyn + 2 * slice;
     uint32_t *bmB = bmA + nbw;
+    // per-warp first-pass histograms and the ring of logits tiles, after the
+    // keys, chunk ids and bitmaps (128-byte aligned)
+    unsigned (*s_hw)[SEL_BINS] = reinterpret_cast<unsigned (*)[SEL_BINS]>(
+        smem_raw + ((select_base_bytes(L, a.num_chunks, a.gkeys != nullptr, CL) + 127) & ~(size_t)127));
+    float *ring = reinterpret_cast<float *>(&s_hw[SEL_T / 32][0]);
+    __shared__ __align__(8) uint64_t s_full[SEL_RING];
     const int64_t *lidx = a.landmark_idx + (int64_t)bh * L + c0;
     int32_t *slots = a.slots + (int64_t)bh * K;
 
@@ -268,28 +318,31 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
         }
     }
     for (int i = tid; i < SEL_BINS; i += SEL_T) s_h1[i] = 0;
+    for (int i = tid; i < (SEL_T / 32) * SEL_BINS; i += SEL_T) (&s_hw[0][0])[i] = 0;
     if (tid == 0) s_nloc = 0;
     if (tid < CL) s_ccnt[tid] = 0;
 
     pdl_wait();  // the scoring kernel's logits and partials are complete from here on
 
-    // the first batch of this CTA's logits goes out before the partials are
-    // merged (two independent loads, one memory latency)
+    // the logits of this CTA's landmarks come in through bulk (TMA) copies,
+    // SEL_RING tiles in flight, issued before the split partials are merged;
+    // for G = 4, 8 or 16 (a landmark row of 1, 2 or 4 16-byte words);
+    // other group sizes read them directly
     const float *lg = a.logits + ((int64_t)bh * L + c0) * G;
-    constexpr int U = 1;  // one landmark per lane per loop trip: compact code (executed once per step, cold)
-    const int G4 = (G & 3) == 0 ? G >> 2 : 0;
-    float4 v[U][4];
-    auto load_batch = [&](int base) {
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int c = base + lane + u * SEL_T;
-#pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4)
-                if (q4 < G4 && c < n) v[u][q4] = __ldcg(reinterpret_cast<const float4 *>(lg + (int64_t)c * G) + q4);
-        }
+    const bool use_ring = G == 4 || G == 8 || G == 16;
+    const int kps = use_ring ? (SEL_RSTAGE / (G * 4)) & ~31 : 0;  // landmarks per tile
+    const int ntile = use_ring ? (n + kps - 1) / kps : 0;
+    auto issue_tile = [&](int i) {
+        const int cnt = min(kps, n - i * kps);
+        const unsigned bytes = (unsigned)cnt * (unsigned)G * 4u;
+        mbar_arrive_expect_tx(&s_full[i % SEL_RING], bytes);
+        bulk_g2s(ring + (size_t)(i % SEL_RING) * (SEL_RSTAGE / 4), lg + (int64_t)i * kps * G, bytes, &s_full[i % SEL_RING]);
     };
-    const int base0 = tid & ~31;
-    if (base0 < n) load_batch(base0);
+    if (use_ring && tid == 0) {
+        for (int i = 0; i < SEL_RING; ++i) mbar_init(&s_full[i], 1);
+        mbar_fence_init();
+        for (int i = 0; i < min(ntile, SEL_RING); ++i) issue_tile(i);
+    }
 
     // 1) softmax normalisers of each query head of the group: warp w merges the
     //    split partials of head w (lanes load in parallel, then a shuffle merge)
@@ -307,8 +360,7 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
             merge_ms(mm, ss, m2, s2);
         }
         if (lane == 0) {
-            s_M[gg] = mm;
-            s_invZ[gg] = 1.f / ss;
+            s_C[gg] = mm + logf(ss);
         }
     }
     __syncthreads();
@@ -319,37 +371,48 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
             if (old[u] >= 0 && old[u] < a.num_chunks) atomicOr(&bmB[old[u] >> 5], 1u << (old[u] & 31));
     }
 
-    // 2) keys of this CTA's landmarks -- the bits of max_g softmax_g, which is
-    //    >= 0, so the unsigned order of the bits is the order of the scores --
-    //    and their first-pass histogram.  Warp-uniform loop: lane l of warp w
-    //    handles landmark 32w + l + 512j.
-    for (int base = base0; base < n; base += U * SEL_T) {
-        if (base != base0) load_batch(base);
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int c = base + lane + u * SEL_T;
-            float sc = 0.f;
-            if (c < n) {
-                if (G4) {
-#pragma unroll
-                    for (int q4 = 0; q4 < 4; ++q4) {
-                        if (q4 < G4) {
-                            sc = fmaxf(sc, __expf(v[u][q4].x - s_M[4 * q4 + 0]) * s_invZ[4 * q4 + 0]);
-                            sc = fmaxf(sc, __expf(v[u][q4].y - s_M[4 * q4 + 1]) * s_invZ[4 * q4 + 1]);
-                            sc = fmaxf(sc, __expf(v[u][q4].z - s_M[4 * q4 + 2]) * s_invZ[4 * q4 + 2]);
-                            sc = fmaxf(sc, __expf(v[u][q4].w - s_M[4 * q4 + 3]) * s_invZ[4 * q4 + 3]);
-                        }
-                    }
-                } else {
-                    for (int gg = 0; gg < G; ++gg)
-                        sc = fmaxf(sc, __expf(lg[(int64_t)c * G + gg] - s_M[gg]) * s_invZ[gg]);
-                }
-                keys[c] = __float_as_uint(sc);
+    // 2) keys of this CTA's landmarks -- the bits of max_g softmax_g =
+    //    exp(max_g (logit_g - C_g)), which is >= 0, so the unsigned order of
+    //    the bits is the order of the scores -- and their first-pass
+    //    histogram.  Warp-uniform loops (compact code: it runs once per step, cold).
+    auto key_of = [&](const float *row) -> float {
+        float d = -INFINITY;
+        for (int gg = 0; gg < G; ++gg) d = fmaxf(d, row[gg] - s_C[gg]);
+        return __expf(d);
+    };
+    auto add_key = [&](int c, bool valid, float sc) {
+        if (valid) keys[c] = __float_as_uint(sc);
+        if (valid) atomicAdd(&s_hw[warp_id()][sel_key_bin(__float_as_uint(sc))], 1u);
+    };
+    if (use_ring) {
+        for (int i = 0; i < ntile; ++i) {
+            if (!mbar_wait(&s_full[i % SEL_RING], (i / SEL_RING) & 1)) {
+                if (tid == 0) report_dev_error(DEV_ERR_WAIT);
+                mbar_wait(&s_full[i % SEL_RING], (i / SEL_RING) & 1);  // the tile must land before it is reused
             }
-            const int bin = c < n ? sel_key_bin(__float_as_uint(sc)) : SEL_BINS + lane;
-            const unsigned peers = __match_any_sync(0xffffffffu, bin);
-            if (c < n && lane == __ffs(peers) - 1) atomicAdd(&s_h1[bin], (unsigned)__popc(peers));
+            const float4 *tile = reinterpret_cast<const float4 *>(ring + (size_t)(i % SEL_RING) * (SEL_RSTAGE / 4));
+            const int k0 = i * kps, cnt = min(kps, n - k0);
+            switch (G) {
+            case 4: ring_tile_keys<1>(tile, k0, cnt, s_C, keys, s_hw[warp_id()]); break;
+            case 8: ring_tile_keys<2>(tile, k0, cnt, s_C, keys, s_hw[warp_id()]); break;
+            default: ring_tile_keys<4>(tile, k0, cnt, s_C, keys, s_hw[warp_id()]); break;
+            }
+            __syncthreads();  // every thread is done with this tile: its slot takes the next one
+            if (tid == 0 && i + SEL_RING < ntile) issue_tile(i + SEL_RING);
         }
+    } else {
+        for (int base = (tid & ~31); base < n; base += SEL_T) {
+            const int c = base + lane;
+            const float sc = c < n ? key_of(lg + (int64_t)c * G) : 0.f;
+            add_key(c, c < n, sc);
+        }
+    }
+    __syncthreads();
+    for (int t = tid; t < SEL_BINS; t += SEL_T) {
+        unsigned h = 0;
+#pragma unroll
+        for (int w = 0; w < SEL_T / 32; ++w) h += s_hw[w][t];
+        s_h1[t] = h;
     }
     cluster_sync();  // every CTA's first-pass histogram is complete; rank 0's bitmaps are zero
 
@@ -540,11 +603,12 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
     }
 }
 
-size_t select_smem_bytes(int L, int num_chunks, bool keys_global, int cl)
+size_t select_smem_bytes(int L, int num_chunks, int G, bool keys_global, int cl)
 {
-    const size_t slice = (size_t)((L + cl - 1) / cl);
-    const size_t nbw = (size_t)((num_chunks + 31) / 32);
-    return (keys_global ? 0 : slice * 8) + 2 * nbw * 4;  // keys + chunk ids of the slice, bitmaps
+    // keys + chunk ids of the slice and bitmaps, then (128-byte aligned) the
+    // per-warp histograms and the logits ring
+    return ((select_base_bytes(L, num_chunks, keys_global, cl) + 127) & ~(size_t)127) +
+           (size_t)(SEL_T / 32) * SEL_BINS * 4 + select_ring_bytes(L, G, cl);
 }
 
 // Whether this device can schedule 16-CTA clusters of the selection kernel

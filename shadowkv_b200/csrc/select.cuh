@@ -33,8 +33,32 @@ struct SelectArgs {
     int G, L, K, nsplit, num_chunks;
 };
 
+constexpr int SEL_RING = 2;              // logits tiles in flight per CTA
+constexpr size_t SEL_SMEM_CAP = 188 * 1024;  // dynamic shared memory of a selection CTA (static ~37 KB)
+constexpr int SEL_RSTAGE = 32 * 1024;    // bytes per logits tile
+
+// Keys + chunk ids of a CTA's slice and the two bitmaps (bytes).
+__host__ __device__ inline size_t select_base_bytes(int L, int num_chunks, bool keys_global, int cl)
+{
+    const size_t slice = (size_t)((L + cl - 1) / cl);
+    const size_t nbw = (size_t)((num_chunks + 31) / 32);
+    return (keys_global ? 0 : slice * 8) + 2 * nbw * 4;
+}
+
+// Logits ring of one selection CTA (bytes): one tile when the slice fits in
+// one, else SEL_RING full tiles; none for group sizes read directly.
+__host__ __device__ inline size_t select_ring_bytes(int L, int G, int cl)
+{
+    if (!(G == 4 || G == 8 || G == 16)) return 0;
+    const size_t slice_bytes = (size_t)((L + cl - 1) / cl) * G * 4;
+    const size_t kps_bytes = (size_t)((SEL_RSTAGE / (G * 4)) & ~31) * G * 4;
+    if (slice_bytes <= kps_bytes) return (slice_bytes + 127) & ~(size_t)127;
+    const size_t ntile = (slice_bytes + kps_bytes - 1) / kps_bytes;
+    return (size_t)(ntile < SEL_RING ? ntile : SEL_RING) * SEL_RSTAGE;
+}
+
 // Dynamic shared memory of one CTA of the selection kernel (cl CTAs per cluster).
-size_t select_smem_bytes(int L, int num_chunks, bool keys_global, int cl);
+size_t select_smem_bytes(int L, int num_chunks, int G, bool keys_global, int cl);
 
 // Whether 16-CTA clusters of the selection kernel can be scheduled on this device.
 bool select_cluster16_ok(size_t smem);
