@@ -266,8 +266,10 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
     __shared__ int s_pre[CL + 1];                  // rank 0: their exclusive prefix
     __shared__ int s_misssorted[1024];                 // rank 0: missed chunk ids, ascending
     __shared__ unsigned s_nloc;                        // candidates this CTA pushed so far
-    __shared__ uint32_t s_lkey[SEL_REGION];            // rank 0: the candidates, compacted
-    __shared__ int s_llm[SEL_REGION], s_lchunk[SEL_REGION];
+    // rank 0: the candidates, compacted; order word = key << 32 | ~landmark
+    // (larger word = earlier in the selection order)
+    __shared__ uint64_t s_lord[SEL_REGION];
+    __shared__ int s_lchunk[SEL_REGION];
     __shared__ int s_bin, s_bin_above, s_bin_cnt;
     __shared__ unsigned s_eq_rank[CL];
 
@@ -416,18 +418,24 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
     }
     cluster_sync();  // every CTA's first-pass histogram is complete; rank 0's bitmaps are zero
 
-    // 3) every CTA sums the eight histograms and finds the bin holding the
-    //    K-th largest key: warp 0, lane l owns bins 255-8l .. 248-8l
+    // 3) every CTA sums the CL histograms and finds the bin holding the K-th
+    //    largest key.  Warp r copies CTA r's histogram into row r of this
+    //    CTA's (now free) per-warp histograms, all CL remote reads at once;
+    //    then warp 0, lane l summing bins 255-8l .. 248-8l, scans.
+    if (warp_id() < CL) {
+        const uint32_t ra = dsmem_addr(&s_h1[lane * 8], (unsigned)warp_id());
+        const uint4 x = ld_dsmem_v4(ra), y = ld_dsmem_v4(ra + 16u);
+        st_v4(&s_hw[warp_id()][lane * 8], x);
+        st_v4(&s_hw[warp_id()][lane * 8 + 4], y);
+    }
+    __syncthreads();
     if (warp_id() == 0) {
         const int b0 = SEL_BINS - 8 - 8 * lane;
         uint4 lo[CL], hi[CL];
-        const uint32_t la = (uint32_t)__cvta_generic_to_shared(&s_h1[b0]);
 #pragma unroll
         for (unsigned r = 0; r < CL; ++r) {
-            uint32_t ra;
-            asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(la), "r"(r));
-            lo[r] = ld_dsmem_v4(ra);
-            hi[r] = ld_dsmem_v4(ra + 16u);
+            lo[r] = ld_v4(&s_hw[r][b0]);
+            hi[r] = ld_v4(&s_hw[r][b0 + 4]);
         }
         int cnt[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // cnt[i]: bin b0 + 7 - i
 #pragma unroll
@@ -519,27 +527,25 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
         for (int t = tid; t < SEL_CAND; t += SEL_T) {
             const int r = t / REGION, o = t % REGION;
             if (o < (int)s_ccnt[r]) {
-                s_lkey[s_pre[r] + o] = s_ckey[t];
-                s_llm[s_pre[r] + o] = s_clm[t];
+                s_lord[s_pre[r] + o] = ((uint64_t)s_ckey[t] << 32) | (uint32_t)~s_clm[t];
                 s_lchunk[s_pre[r] + o] = s_cchunk[t];
             }
         }
         __syncthreads();
         // 5) exact order among the candidates (key descending, landmark index
-        //    ascending); the first K - bin_above of them are selected.  Warp w
-        //    ranks candidates w, w + 16, ...; its lanes split the comparisons.
+        //    ascending); the first K - bin_above of them are selected.  Two
+        //    threads per candidate (nc <= REGION <= SEL_T / 2) count the
+        //    order words above its own, each over half of the candidates.
         const int nc = s_pre[CL], need = K - bin_above;
-        for (int i = warp_id(); i < nc; i += SEL_T / 32) {
-            const uint32_t ki = s_lkey[i];
-            const int li = s_llm[i];
+        {
+            const int i = tid >> 1;
             unsigned before = 0;
-            for (int j = lane; j < nc; j += 32) {
-                const uint32_t kj = s_lkey[j];
-                const int lj = s_llm[j];
-                before += (kj > ki || (kj == ki && lj < li)) ? 1u : 0u;
+            if (i < nc) {
+                const uint64_t oi = s_lord[i];
+                for (int j = tid & 1; j < nc; j += 2) before += s_lord[j] > oi ? 1u : 0u;
             }
-            before = __reduce_add_sync(0xffffffffu, before);
-            if (lane == 0 && (int)before < need) {
+            before += __shfl_xor_sync(0xffffffffu, before, 1);
+            if (i < nc && (tid & 1) == 0 && (int)before < need) {
                 const int cid = s_lchunk[i];
                 if (cid >= 0) atomicOr(&bmA[cid >> 5], 1u << (cid & 31));
                 else report_dev_error(DEV_ERR_HOST_CHUNK);
