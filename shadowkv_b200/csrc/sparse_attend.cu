@@ -454,20 +454,45 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    for (int p = tid; p < G * 128; p += SA_THREADS) {
-        const int gg = p >> 7, d = p & 127;
-        const float2 *ml = a.part_ml + (int64_t)bh * a.nblk * G + gg;
-        const float *po = a.part_o + (int64_t)bh * a.nblk * G * 128 + gg * 128 + d;
-        float M = -INFINITY;
-        for (int j = 0; j < a.nblk; ++j) M = fmaxf(M, __ldcg(&ml[j * G].x));
-        float L = 0.f, acc = 0.f;
-        for (int j = 0; j < a.nblk; ++j) {
-            const float2 v = __ldcg(&ml[j * G]);
-            const float w = __expf(v.x - M);
-            L += v.y * w;
-            acc += __ldcg(&po[(int64_t)j * G * 128]) * w;
+    // merge of the head's nblk partial outputs: all (m, l) pairs come in
+    // one round of loads; warp w turns those of heads w, w + 8 into weights
+    // w_j = exp(m_j - M) / L; then each thread sums 4 columns of one query
+    // row over the partials, loads unrolled (the tiles' shared memory is free)
+    {
+        const int nml = a.nblk * G;
+        float2 *s_ml = reinterpret_cast<float2 *>(smem_raw);  // [nblk][G]
+        float *s_w = reinterpret_cast<float *>(s_ml + nml);  // [nblk][G]
+        const float2 *ml = a.part_ml + (int64_t)bh * nml;
+        for (int t = tid; t < nml; t += SA_THREADS) s_ml[t] = __ldcg(&ml[t]);
+        __syncthreads();
+        for (int gg = warp; gg < G; gg += SA_THREADS / 32) {
+            float M = -INFINITY, L = 0.f;
+            for (int j = lane; j < a.nblk; j += 32) M = fmaxf(M, s_ml[j * G + gg].x);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+            for (int j = lane; j < a.nblk; j += 32) L += s_ml[j * G + gg].y * __expf(s_ml[j * G + gg].x - M);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+            const float inv = 1.f / L;
+            for (int j = lane; j < a.nblk; j += 32) s_w[j * G + gg] = __expf(s_ml[j * G + gg].x - M) * inv;
         }
-        a.out[((int64_t)bh * G + gg) * 128 + d] = f2bf(acc / L);
+        __syncthreads();
+        for (int p = tid; p < G * 32; p += SA_THREADS) {
+            const int gg = p >> 5, d = (p & 31) * 4;
+            const float *po = a.part_o + (int64_t)bh * a.nblk * G * 128 + gg * 128 + d;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+            for (int j = 0; j < a.nblk; ++j) {
+                const float4 v = __ldcg(reinterpret_cast<const float4 *>(po + (int64_t)j * G * 128));
+                const float w = s_w[j * G + gg];
+                acc.x += v.x * w, acc.y += v.y * w, acc.z += v.z * w, acc.w += v.w * w;
+            }
+            __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+            uint2 pk;
+            pk.x = *reinterpret_cast<uint32_t *>(&lo);
+            pk.y = *reinterpret_cast<uint32_t *>(&hi);
+            *reinterpret_cast<uint2 *>(a.out + ((int64_t)bh * G + gg) * 128 + d) = pk;
+        }
     }
     if (tid == 0) a.ticket[bh] = 0;  // ready for the next launch
 }
@@ -564,6 +589,7 @@ int skv_decode_sparse_attention(const skv_decode_geom *g, const void *q, const v
     a.scale = g->scale;
 
     const int smem = (int)sa_smem_bytes(g->rank);
+    SKV_CHECK_SUPPORTED((size_t)nblk * G * 12 <= (size_t)smem, "seq_len %d too long for the merge of the partials", seq_len);
     const void *fn = G <= 8 ? (const void *)sparse_attend_kernel<1> : (const void *)sparse_attend_kernel<2>;
     st = ensure_smem_attr(fn, smem, "sparse_attend_kernel");
     if (st) return st;
