@@ -171,7 +171,12 @@ def run_b200(args, world, rank, local):
         from shadowkv_b200 import numa
         numa.bind_to_gpu_numa(local)
     cfg = workload.CONFIGS[args.config]
+    NL = args.layers
+    if NL > 1:
+        cfg = dataclasses.replace(cfg, layers=NL)
     heads_sharded = args.shard == "heads" and world > 1
+    if heads_sharded and NL > 1:
+        raise SystemExit("--layers > 1 runs with --shard batch")
     if heads_sharded:
         # rank r owns kv heads [r*Hkv/N, (r+1)*Hkv/N) and their GQA groups; the attention
         # outputs are all-gathered (NCCL over NVLink) inside the step, before o_proj
@@ -213,6 +218,9 @@ def run_b200(args, world, rank, local):
     # heads sharded: every rank ends the step with the attention output of all heads
     s_full = torch.empty(world * B * Hq, 128, dtype=torch.bfloat16, device="cuda") if heads_sharded else None
     s_qr = torch.empty(B, Hq, 1, 128, dtype=torch.bfloat16, device="cuda")
+    # several layers: layer l + 1 takes layer l's attention output as its query
+    # (a real data dependency between the layers, as in the model)
+    s_mid = [torch.empty(B, Hq, 128, dtype=torch.bfloat16, device="cuda") for _ in range(2)]
     cache.fused_geometry(attn.cos_sin_cache)
 
     def load_inputs(i):
@@ -223,20 +231,23 @@ def run_b200(args, world, rank, local):
         s_pos.fill_(pos0 + i)
 
     def step_body():
-        """One decode step of one layer on the static inputs (appends at row sparse_end)."""
+        """One decode step of NL layers on the static inputs (appends at row sparse_end)."""
         cache.gen_offset = 0
-        qr = cache.append_select_fused(0, s_q, s_k, s_v, s_pos, attn.cos_sin_cache, q_out=s_qr)
-        seq_len = cache.sparse_end + cache._gen_offset(0)
-        if args.split:
-            cur = torch.cuda.current_stream()
-            with torch.cuda.stream(copy_stream):
-                copy_stream.wait_stream(cur)
-                cache.fetch_values_fused(0, copy_stream)
-            cache.reconstruct_keys_fused(0, attn.cos_sin_cache)
-            cur.wait_stream(copy_stream)
-            cache.attention(0, qr, seq_len, out=s_out)
-        else:
-            cache.sparse_attention_fused(0, qr, seq_len, attn.cos_sin_cache, out=s_out)
+        for li in range(NL):
+            q_in = s_q if li == 0 else s_mid[(li - 1) % 2]
+            out = s_out if li == NL - 1 else s_mid[li % 2]
+            qr = cache.append_select_fused(li, q_in, s_k, s_v, s_pos, attn.cos_sin_cache, q_out=s_qr)
+            seq_len = cache.sparse_end + cache._gen_offset(li)
+            if args.split:
+                cur = torch.cuda.current_stream()
+                with torch.cuda.stream(copy_stream):
+                    copy_stream.wait_stream(cur)
+                    cache.fetch_values_fused(li, copy_stream)
+                cache.reconstruct_keys_fused(li, attn.cos_sin_cache)
+                cur.wait_stream(copy_stream)
+                cache.attention(li, qr, seq_len, out=out)
+            else:
+                cache.sparse_attention_fused(li, qr, seq_len, attn.cos_sin_cache, out=out)
         if heads_sharded:
             torch.distributed.all_gather_into_tensor(s_full, s_out.view(B * Hq, 128))
         cache.gen_offset = 0
@@ -335,6 +346,7 @@ def run_b200(args, world, rank, local):
     misses = statistics.mean(misses_all)
     hit_rate = 1.0 - misses / (B * Hkv * cache.select_sets)
     hbm_b, host_b = algorithmic_bytes(cache, misses, statistics.mean(seqlens))
+    hbm_b, host_b = hbm_b * NL, host_b * NL  # the misses of the last layer stand for every layer
     t_roof = max(hbm_b / (hbm_peak * 1e9), host_b / (link_peak * 1e9))
     fetch_avg = statistics.mean(fetch_ms)
     link_achieved = host_b / (fetch_avg * 1e-3) / 1e9 if fetch_avg > 0 else 0.0
@@ -373,7 +385,8 @@ def run_b200(args, world, rank, local):
     del graph
 
     res = {
-        "metric": "sparse-attn decode tokens/s (Llama-3-8B shape, 122k ctx)",
+        "metric": ("sparse-attn decode tokens/s (Llama-3-8B shape, 122k ctx)" if NL == 1 else
+                   f"sparse-attn decode tokens/s ({NL} attention layers, Llama-3-8B shape, 122k ctx)"),
         "value": value,
         "unit": "tokens/s",
         "n_gpus": world,
@@ -385,7 +398,8 @@ def run_b200(args, world, rank, local):
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded; BASELINE configs[1] shapes and distributions)",
-        "config": {"workload": f"{cfg.name}: one decode layer, B={B}/GPU, {Hq}q/{Hkv}kv heads"
+        "config": {"workload": f"{cfg.name}: {'one decode layer' if NL == 1 else f'{NL} chained decode layers'}"
+                               f", B={B}/GPU, {Hq}q/{Hkv}kv heads"
                                f"{' per GPU' if heads_sharded else ''}, ctx {cfg.ctx}, "
                                f"budget {cfg.budget}, rank {cfg.rank}, V in pinned host memory",
                    "global_batch": tokens, "seq_len": cfg.ctx,
@@ -409,16 +423,16 @@ def run_b200(args, world, rank, local):
                 "d2h_bytes_per_step": d2h},
         "kernel_us": kernel_us,
         "graph": used_graph,
-        "gpu_launches": (5 if args.split else 3) * args.steps,
+        "gpu_launches": (5 if args.split else 3) * NL * args.steps,
         "clocks": clk.summary(),
         "wall_s": t_wall,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        res["cpu_baseline"] = cpu_baseline(layer, inputs, seconds=args.cpu_seconds)
+        res["cpu_baseline"] = cpu_baseline(layer, inputs, seconds=args.cpu_seconds, layers=NL)
     return res
 
 
-def cpu_baseline(layer, inputs, seconds=15.0):
+def cpu_baseline(layer, inputs, seconds=15.0, layers=1):
     """The oracle port of the reference's torch-eager decode step, timed on the host cores."""
     import numpy as np
     from oracle import shadowkv_oracle as o
@@ -434,8 +448,9 @@ def cpu_baseline(layer, inputs, seconds=15.0):
         times.append(time.perf_counter() - t0)
         i += 1
     med = statistics.median(times)
-    return {"value": layer.cfg.batch / med, "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"{len(times)} full config1 decode steps of the numpy port (median)"}
+    return {"value": layer.cfg.batch / (med * layers), "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{len(times)} full config1 decode steps of the numpy port (median)"
+                      + (f", one layer's time x {layers} layers" if layers > 1 else "")}
 
 
 def export_state(layer):
@@ -462,6 +477,8 @@ def main():
     ap.add_argument("--config", default="config1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying a CUDA graph")
+    ap.add_argument("--layers", type=int, default=1,
+                    help="decode layers per step (chained: each layer's output is the next one's query)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--shard", default="batch", choices=["batch", "heads"],
                     help="multi-GPU partition: one sequence per rank (weak scaling) or the kv heads of one "
