@@ -15,7 +15,9 @@ sequence (batch-sharded weak scaling, no collective on the data path).
 Printed: one JSON line (rank 0).  ``value`` = tokens/s of the whole job with
 inputs resident (device-timed, CUDA events, max over ranks); ``e2e`` = the
 same through the host API with the query/new-token inputs copied from pinned
-host memory and the attention output copied back every step.
+host memory and the attention output brought back every step (the fused
+step writes it straight into pinned host memory; the split and head-sharded
+steps copy it back).
 """
 from __future__ import annotations
 
@@ -230,12 +232,12 @@ def run_b200(args, world, rank, local):
         s_v.copy_(v)
         s_pos.fill_(pos0 + i)
 
-    def step_body():
+    def step_body(final_out=None):
         """One decode step of NL layers on the static inputs (appends at row sparse_end)."""
         cache.gen_offset = 0
         for li in range(NL):
             q_in = s_q if li == 0 else s_mid[(li - 1) % 2]
-            out = s_out if li == NL - 1 else s_mid[li % 2]
+            out = (s_out if final_out is None else final_out) if li == NL - 1 else s_mid[li % 2]
             qr = cache.append_select_fused(li, q_in, s_k, s_v, s_pos, attn.cos_sin_cache, q_out=s_qr)
             seq_len = cache.sparse_end + cache._gen_offset(li)
             if args.split:
@@ -351,7 +353,7 @@ def run_b200(args, world, rank, local):
     fetch_avg = statistics.mean(fetch_ms)
     link_achieved = host_b / (fetch_avg * 1e-3) / 1e9 if fetch_avg > 0 else 0.0
 
-    # ---- e2e: inputs copied from pinned host memory, the output copied back, every step
+    # ---- e2e: inputs copied from pinned host memory, the output brought back, every step
     # per step: the inputs packed in one pinned host buffer (q, k, v, position)
     h_in = []
     for j, inp in enumerate(inputs):
@@ -360,6 +362,16 @@ def run_b200(args, world, rank, local):
             dst.copy_(src.cpu())
         h_in.append(hb)
     h_out = torch.empty(*(s_full.shape if heads_sharded else (B, Hq, 128)), dtype=torch.bfloat16).pin_memory()
+    # the fused step writes its output straight into the page-locked host buffer
+    # (the merge stores it over the link: no separate device-to-host copy)
+    out_direct = not heads_sharded and not args.split
+    graph_e2e = None
+    if out_direct and graph is not None:
+        torch.cuda.synchronize()
+        graph_e2e = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph_e2e):
+            step_body(h_out)
+        torch.cuda.synchronize()
     nin = len(inputs)
     e2e_ms = []
     for i in range(args.warmup, n):
@@ -370,11 +382,17 @@ def run_b200(args, world, rank, local):
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record(main)
         d_in.copy_(hb, non_blocking=True)  # the step's packed inputs, pinned host -> device
-        if graph is not None:
-            graph.replay()
+        if out_direct:
+            if graph_e2e is not None:
+                graph_e2e.replay()
+            else:
+                step_body(h_out)
         else:
-            step_body()
-        h_out.copy_(s_full if heads_sharded else s_out, non_blocking=True)
+            if graph is not None:
+                graph.replay()
+            else:
+                step_body()
+            h_out.copy_(s_full if heads_sharded else s_out, non_blocking=True)
         e.record(main)
         e.synchronize()
         e2e_ms.append(s.elapsed_time(e))
@@ -382,7 +400,7 @@ def run_b200(args, world, rank, local):
     h2d = nbytes
     d2h = h_out.numel() * h_out.element_size()
     used_graph = graph is not None
-    del graph
+    del graph, graph_e2e
 
     res = {
         "metric": ("sparse-attn decode tokens/s (Llama-3-8B shape, 122k ctx)" if NL == 1 else

@@ -337,6 +337,9 @@ SKV_API size_t skv_decode_sparse_attention_workspace(const skv_decode_geom *g, i
  *   - out = GQA attention of q over buffer rows [0, seq_len) (as
  *     skv_decode_attention; per-CTA partials merged by the last CTA).
  * seq_len must cover the selected rows (>= sparse_start + 8*select_sets).
+ * out may be device memory or page-locked host memory: the last CTA of each
+ * head then writes its rows over the host link, with no separate
+ * device-to-host copy after the launch.
  * No counterpart in the reference, which runs these as separate kernels
  * (kernels/gather_copy.cu, kernels/batch_gather_gemm.cu + kernels/rope_new.cu,
  * flash_attn_with_kvcache in models/attention/shadow.py:48). */

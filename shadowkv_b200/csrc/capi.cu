@@ -88,6 +88,29 @@ int host_to_device_ptr(const void *p, const void **dev, const char *name)
     return SKV_OK;
 }
 
+int out_to_device_ptr(void *p, void **dev, const char *name)
+{
+    if (p == nullptr) {
+        set_error("%s is null", name);
+        return SKV_ERR_INVALID_ARGUMENT;
+    }
+    cudaPointerAttributes attr;
+    if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+        cudaGetLastError();
+        attr.type = cudaMemoryTypeUnregistered;
+    }
+    if (attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged) {
+        *dev = p;
+        return SKV_OK;
+    }
+    if (attr.type == cudaMemoryTypeHost && attr.devicePointer != nullptr) {
+        *dev = attr.devicePointer;
+        return SKV_OK;
+    }
+    set_error("%s must be device memory or page-locked host memory mapped for the device", name);
+    return SKV_ERR_INVALID_ARGUMENT;
+}
+
 __device__ unsigned int g_dev_err_count = 0;
 __device__ unsigned int g_dev_err_first = 0;
 

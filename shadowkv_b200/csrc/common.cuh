@@ -55,6 +55,9 @@ int ensure_smem_attr(const void *func, int bytes, const char *name);
 // Verify that `p` is page-locked host memory mapped for the current device;
 // on success *dev holds the device-side address of p.
 int host_to_device_ptr(const void *p, const void **dev, const char *name);
+// Device address of an output that is device memory or page-locked host
+// memory (the kernel then writes it over the host link).
+int out_to_device_ptr(void *p, void **dev, const char *name);
 
 inline bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 

@@ -550,6 +550,10 @@ int skv_decode_sparse_attention(const skv_decode_geom *g, const void *q, const v
     int st = host_to_device_ptr(v_host, &hdev, "v_host");
     if (st != SKV_OK) return st;
     SKV_CHECK_ARG(aligned(hdev, 16), "v_host must be 16-byte aligned");
+    void *dout = nullptr;
+    st = out_to_device_ptr(out, &dout, "out");
+    if (st != SKV_OK) return st;
+    SKV_CHECK_ARG(aligned(dout, 8), "out must be 8-byte aligned");
 
     const int BH = g->batch * g->kv_heads;
     const int nblk = ceil_div(seq_len, SA_ROWS);
@@ -572,7 +576,7 @@ int skv_decode_sparse_attention(const skv_decode_geom *g, const void *q, const v
     a.part_ml = reinterpret_cast<float2 *>(ws + tk_bytes);
     a.part_o = reinterpret_cast<float *>(ws + tk_bytes + ((ml_bytes + 255) & ~(size_t)255));
     (void)o_bytes;
-    a.out = (__nv_bfloat16 *)out;
+    a.out = (__nv_bfloat16 *)dout;
     a.Hkv = g->kv_heads;
     a.G = G;
     a.K = g->select_sets;

@@ -55,6 +55,15 @@ def _stream(stream=None) -> int:
     return s.cuda_stream
 
 
+def _req_out(t: torch.Tensor):
+    """An output that is a CUDA tensor or a page-locked CPU tensor (written over the host link)."""
+    if t.is_cuda:
+        return _req(t, "out", torch.bfloat16)
+    if not t.is_pinned() or t.dtype != torch.bfloat16 or not t.is_contiguous():
+        raise RuntimeError("out must be a contiguous bf16 CUDA tensor or a page-locked CPU tensor")
+    return t.data_ptr()
+
+
 def _req(t: torch.Tensor, name: str, dtype, shape=None):
     if not t.is_cuda or t.dtype != dtype or not t.is_contiguous():
         raise RuntimeError(f"{name} must be a contiguous CUDA {dtype} tensor "
@@ -164,7 +173,10 @@ def attention(geom: Geometry, ws: DecodeWorkspace, q: torch.Tensor, k_buf: torch
 def sparse_attention(geom: Geometry, ws: DecodeWorkspace, q: torch.Tensor, U: torch.Tensor, SVt: torch.Tensor,
                      cos_sin: torch.Tensor, v_host: torch.Tensor, k_buf: torch.Tensor, v_buf: torch.Tensor,
                      seq_len: int, out: torch.Tensor, stream=None) -> torch.Tensor:
-    """``gather_values`` + ``reconstruct_keys`` + ``attention`` in one launch (after a selection)."""
+    """``gather_values`` + ``reconstruct_keys`` + ``attention`` in one launch (after a selection).
+
+    ``out`` may be a page-locked CPU tensor: the kernel writes the output over
+    the host link (no device-to-host copy after the launch)."""
     if v_host.is_cuda or not v_host.is_pinned() or v_host.dtype != torch.bfloat16 or not v_host.is_contiguous():
         raise RuntimeError("v_host must be a contiguous pinned CPU bf16 tensor")
     g = geom.c()
@@ -172,6 +184,6 @@ def sparse_attention(geom: Geometry, ws: DecodeWorkspace, q: torch.Tensor, U: to
         ctypes.byref(g), _req(q, "q", torch.bfloat16), _req(U, "U", torch.bfloat16), _req(SVt, "SVt", torch.bfloat16),
         _req(cos_sin, "cos_sin", torch.bfloat16), v_host.data_ptr(), _req(k_buf, "k_buf", torch.bfloat16),
         _req(v_buf, "v_buf", torch.bfloat16), ws.miss_slot.data_ptr(), ws.miss_chunk.data_ptr(),
-        ws.miss_count.data_ptr(), int(seq_len), _req(out, "out", torch.bfloat16), ws.sparse_ws.data_ptr(),
+        ws.miss_count.data_ptr(), int(seq_len), _req_out(out), ws.sparse_ws.data_ptr(),
         ws.sparse_bytes, _stream(stream)), "skv_decode_sparse_attention")
     return out

@@ -263,3 +263,29 @@ def test_chained_layers_overlap_matches_synchronized():
                 assert np.array_equal(x, y), mode
         for x, y in zip(res["sync"][1], res[mode][1]):
             assert np.array_equal(x, y), mode
+
+
+def test_sparse_attention_output_into_pinned_host_memory():
+    """The fused step with a page-locked CPU output (written over the host
+    link by the kernel) gives the same bits as with a device output."""
+    from shadowkv_b200 import workload
+    cfg = copy.deepcopy(workload.CONFIGS["tiny"])
+    outs = []
+    for where in ("device", "host"):
+        layer = workload.Layer(cfg, device=DEV, seed=13)
+        c, attn = layer.cache, layer.attn
+        torch.manual_seed(3)
+        q, k, v = layer.next_inputs()
+        pos = torch.full((cfg.batch, 1), c.sparse_end + 500, dtype=torch.int64, device=DEV)
+        out = (torch.empty(cfg.batch, cfg.q_heads, 128, dtype=torch.bfloat16, device=DEV) if where == "device"
+               else torch.empty(cfg.batch, cfg.q_heads, 128, dtype=torch.bfloat16).pin_memory())
+        c.fused_geometry(attn.cos_sin_cache)
+        qr = c.append_select_fused(0, q, k, v, pos, attn.cos_sin_cache)
+        c.sparse_attention_fused(0, qr, c.sparse_end + c._gen_offset(0), attn.cos_sin_cache, out=out)
+        torch.cuda.synchronize()
+        outs.append(bits(out))
+        del layer
+    assert np.array_equal(outs[0], outs[1])
+    with pytest.raises(RuntimeError):
+        from shadowkv_b200 import decode as fz
+        fz._req_out(torch.empty(4, dtype=torch.bfloat16))  # pageable host memory is refused
