@@ -179,12 +179,16 @@ def run_b200(args, world, rank, local):
     heads_sharded = args.shard == "heads" and world > 1
     if heads_sharded and NL > 1:
         raise SystemExit("--layers > 1 runs with --shard batch")
+    full_cfg = cfg
     if heads_sharded:
-        # rank r owns kv heads [r*Hkv/N, (r+1)*Hkv/N) and their GQA groups; the attention
-        # outputs are all-gathered (NCCL over NVLink) inside the step, before o_proj
+        # rank r owns kv heads [r*Hkv/N, (r+1)*Hkv/N) and their GQA groups; inside the step
+        # every rank ends with the attention rows of all heads (o_proj's input): written to
+        # every rank's memory over NVLink by the attention kernel itself (--gather peer),
+        # or all-gathered by NCCL after it (--gather nccl)
         from shadowkv_b200 import sharding
         k0, kn, q0, qn = sharding.head_range(cfg.kv_heads, cfg.q_heads, world, rank)
         cfg = dataclasses.replace(cfg, kv_heads=kn, q_heads=qn)
+    peer_out = None
     torch.manual_seed(0)
     layer = workload.Layer(cfg, device=f"cuda:{local}", seed=1000 + rank)
     cache, attn = layer.cache, layer.attn
@@ -218,7 +222,13 @@ def run_b200(args, world, rank, local):
     s_pos.fill_(pos0)
     s_out = torch.empty(B, Hq, 128, dtype=torch.bfloat16, device="cuda")
     # heads sharded: every rank ends the step with the attention output of all heads
-    s_full = torch.empty(world * B * Hq, 128, dtype=torch.bfloat16, device="cuda") if heads_sharded else None
+    s_full = None
+    if heads_sharded and args.gather == "peer" and not args.split:
+        from shadowkv_b200.peer import PeerOutput
+        peer_out = PeerOutput.create(B, full_cfg.q_heads, q0, B * full_cfg.kv_heads)
+        s_full = torch.empty(B, full_cfg.q_heads, 128, dtype=torch.bfloat16, device="cuda")
+    elif heads_sharded:
+        s_full = torch.empty(world * B * Hq, 128, dtype=torch.bfloat16, device="cuda")
     s_qr = torch.empty(B, Hq, 1, 128, dtype=torch.bfloat16, device="cuda")
     # several layers: layer l + 1 takes layer l's attention output as its query
     # (a real data dependency between the layers, as in the model)
@@ -248,9 +258,12 @@ def run_b200(args, world, rank, local):
                 cache.reconstruct_keys_fused(li, attn.cos_sin_cache)
                 cur.wait_stream(copy_stream)
                 cache.attention(li, qr, seq_len, out=out)
+            elif peer_out is not None:
+                cache.sparse_attention_gather(li, qr, seq_len, attn.cos_sin_cache, peer_out)
+                peer_out.finish(s_full)
             else:
                 cache.sparse_attention_fused(li, qr, seq_len, attn.cos_sin_cache, out=out)
-        if heads_sharded:
+        if heads_sharded and peer_out is None:
             torch.distributed.all_gather_into_tensor(s_full, s_out.view(B * Hq, 128))
         cache.gen_offset = 0
         return seq_len
@@ -421,7 +434,9 @@ def run_b200(args, world, rank, local):
                                f"{' per GPU' if heads_sharded else ''}, ctx {cfg.ctx}, "
                                f"budget {cfg.budget}, rank {cfg.rank}, V in pinned host memory",
                    "global_batch": tokens, "seq_len": cfg.ctx,
-                   "parallelism": (f"kv-head-sharded x{world} (NCCL all-gather of the attention output)"
+                   "parallelism": ((f"kv-head-sharded x{world} (attention rows written to every rank over "
+                                    f"NVLink peer memory by the attention kernel)" if peer_out is not None else
+                                    f"kv-head-sharded x{world} (NCCL all-gather of the attention output)")
                                    if heads_sharded else f"batch-sharded x{world}"),
                    "l2": "flushed between timed steps (256 MB write)", "hit_rate": hit_rate},
         "roofline": {"kernel": ("fetch_misses_kernel (zero-copy V gather)" if args.split else
@@ -445,6 +460,10 @@ def run_b200(args, world, rank, local):
         "clocks": clk.summary(),
         "wall_s": t_wall,
     }
+    if peer_out is not None:
+        torch.cuda.synchronize()
+        torch.distributed.barrier()  # every rank is done writing into the others' blocks
+        peer_out.close()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline(layer, inputs, seconds=args.cpu_seconds, layers=NL)
     return res
@@ -495,6 +514,8 @@ def main():
     ap.add_argument("--config", default="config1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying a CUDA graph")
+    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
+                    help="--shard heads: how every rank gets all heads' attention rows")
     ap.add_argument("--layers", type=int, default=1,
                     help="decode layers per step (chained: each layer's output is the next one's query)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)

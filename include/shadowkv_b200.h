@@ -350,6 +350,55 @@ SKV_API int skv_decode_sparse_attention(const skv_decode_geom *g, const void *q,
                                         int seq_len, void *out, void *workspace,
                                         size_t workspace_bytes, void *stream);
 
+/* ---- attention output gathered over peer memory (kv heads split over ranks)
+ *
+ * With the kv heads of a sequence split over `world` GPUs (one process per
+ * GPU), o_proj needs every rank's attention rows.  The reference would
+ * all-gather them after the attention (NCCL, one collective per layer);
+ * here the attention kernel's merge writes its rows straight into every
+ * rank's landing buffer over NVLink and bumps every rank's arrival counter,
+ * and skv_peer_gather_finish waits for the counter and copies the full
+ * output out of the landing buffer.  Each rank owns one peer block
+ * (skv_peer_block_bytes): [arrival counter | epoch | landing buffer
+ * [2][batch][q_heads_total][128] bf16]; the landing half used by a step is
+ * epoch & 1, so a rank one step ahead never writes the half a slower rank
+ * still reads.  Blocks are shared through CUDA IPC handles (64 bytes). */
+#define SKV_MAX_PEERS 8
+typedef struct {
+    int world;            /* ranks sharing the output, 1..SKV_MAX_PEERS */
+    int rank;             /* this rank */
+    int q_head0;          /* first query head of this rank in the full output */
+    int q_heads_total;    /* query heads of the full output */
+    int merges_per_step;  /* (sequence, kv head) units of one step summed over all ranks */
+    void *block[SKV_MAX_PEERS];  /* every rank's peer block, as addressed from this GPU */
+} skv_peer_gather;
+
+SKV_API size_t skv_peer_block_bytes(int batch, int q_heads_total);
+/* cudaMalloc'd, zero-filled block of `bytes`. */
+SKV_API int skv_peer_alloc(size_t bytes, void **block);
+SKV_API int skv_peer_free(void *block);
+/* CUDA IPC handle (64 bytes) of a block, and its mapping in another process
+ * (peer access enabled on first use); skv_peer_close unmaps it. */
+SKV_API int skv_peer_export(const void *block, void *handle64);
+SKV_API int skv_peer_import(const void *handle64, void **block);
+SKV_API int skv_peer_close(void *block);
+
+/* skv_decode_sparse_attention with the output written to every rank's
+ * landing buffer (rows q_head0 .. q_head0 + q_heads of the full output). */
+SKV_API int skv_decode_sparse_attention_gather(const skv_decode_geom *g, const void *q, const void *U,
+                                               const void *SVt, const void *cos_sin, const void *v_host,
+                                               void *k_buf, void *v_buf, const int32_t *miss_slot,
+                                               const int32_t *miss_chunk, const int32_t *miss_count,
+                                               int seq_len, const skv_peer_gather *pg, void *workspace,
+                                               size_t workspace_bytes, void *stream);
+
+/* Waits (bounded; a timeout is counted in skv_device_errors) until every
+ * rank's rows of this step have arrived, copies the full output
+ * [batch][q_heads_total][128] into `out` (device memory) and advances the
+ * epoch.  One call per step, after skv_decode_sparse_attention_gather, on
+ * the same stream. */
+SKV_API int skv_peer_gather_finish(const skv_peer_gather *pg, int batch, void *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

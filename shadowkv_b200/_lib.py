@@ -31,6 +31,18 @@ class DecodeGeom(ctypes.Structure):
     ]
 
 
+SKV_MAX_PEERS = 8
+
+
+class PeerGather(ctypes.Structure):
+    """``skv_peer_gather`` of include/shadowkv_b200.h."""
+
+    _fields_ = [
+        ("world", c_int), ("rank", c_int), ("q_head0", c_int), ("q_heads_total", c_int),
+        ("merges_per_step", c_int), ("block", c_void_p * SKV_MAX_PEERS),
+    ]
+
+
 # name -> argument types (every function returns int status unless listed in _RET)
 SIGNATURES = {
     "skv_last_error": [],
@@ -59,9 +71,19 @@ SIGNATURES = {
     "skv_decode_attention": [ctypes.POINTER(DecodeGeom), P, P, P, c_int, P, P, c_size_t, P],
     "skv_decode_sparse_attention_workspace": [ctypes.POINTER(DecodeGeom), c_int],
     "skv_decode_sparse_attention": [ctypes.POINTER(DecodeGeom)] + [P] * 10 + [c_int, P, P, c_size_t, P],
+    "skv_decode_sparse_attention_gather": [ctypes.POINTER(DecodeGeom)] + [P] * 10
+                                          + [c_int, ctypes.POINTER(PeerGather), P, c_size_t, P],
+    "skv_peer_block_bytes": [c_int, c_int],
+    "skv_peer_alloc": [c_size_t, ctypes.POINTER(c_void_p)],
+    "skv_peer_free": [P],
+    "skv_peer_export": [P, P],
+    "skv_peer_import": [P, ctypes.POINTER(c_void_p)],
+    "skv_peer_close": [P],
+    "skv_peer_gather_finish": [ctypes.POINTER(PeerGather), c_int, P, P],
 }
 _RET = {"skv_last_error": c_char_p, "skv_decode_select_workspace": c_size_t,
-        "skv_decode_attention_workspace": c_size_t, "skv_decode_sparse_attention_workspace": c_size_t}
+        "skv_decode_attention_workspace": c_size_t, "skv_decode_sparse_attention_workspace": c_size_t,
+        "skv_peer_block_bytes": c_size_t}
 
 
 def _load():

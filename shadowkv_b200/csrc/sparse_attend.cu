@@ -30,6 +30,8 @@
 //      the head merges the partials into the output.
 // The host link is the bound of the step; everything but the final P V and
 // the merge overlaps the value transfer.
+#include <string.h>
+
 #include "common.cuh"
 
 namespace skv {
@@ -50,10 +52,17 @@ struct SparseAttendArgs {
     float *part_o;                 // [BH][nblk][G][128]
     float2 *part_ml;               // [BH][nblk][G] (max, sum)
     unsigned *ticket;              // [BH], zero between launches
-    __nv_bfloat16 *out;            // [B][Hq][128]
+    __nv_bfloat16 *out;            // [B][Hq][128] (world == 0)
     int Hkv, G, K, rank, ctx, num_chunks, buf_len, sparse_start, seq_len, nblk;
     int rope_mode, cs_stride, cs_rows;
     float scale;
+    // world > 0: the output rows go to every rank's landing buffer
+    // [2][B][q_heads_total][128] (half epoch & 1) over peer memory, then one
+    // system-scope increment of every rank's arrival counter per (b, kv head)
+    int world, q_head0, q_heads_total;
+    __nv_bfloat16 *landing[SKV_MAX_PEERS];
+    unsigned *counter[SKV_MAX_PEERS];
+    const unsigned *epoch;
 };
 
 __device__ __forceinline__ void sa_ldsm(uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3, const void *p)
@@ -491,10 +500,66 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
             uint2 pk;
             pk.x = *reinterpret_cast<uint32_t *>(&lo);
             pk.y = *reinterpret_cast<uint32_t *>(&hi);
-            *reinterpret_cast<uint2 *>(a.out + ((int64_t)bh * G + gg) * 128 + d) = pk;
+            if (a.world == 0) {
+                *reinterpret_cast<uint2 *>(a.out + ((int64_t)bh * G + gg) * 128 + d) = pk;
+            } else {
+                const int b = bh / a.Hkv, h = bh % a.Hkv;
+                const int64_t o = (((int64_t)(*a.epoch & 1u) * (gridDim.x / a.nblk / a.Hkv) + b) * a.q_heads_total +
+                                   a.q_head0 + h * G + gg) * 128 + d;
+                for (int r = 0; r < a.world; ++r) *reinterpret_cast<uint2 *>(a.landing[r] + o) = pk;
+            }
         }
     }
+    if (a.world > 0) {
+        // the rows are in every rank's memory before any counter moves
+        __threadfence_system();
+        __syncthreads();
+        if (tid == 0)
+            for (int r = 0; r < a.world; ++r) atomicAdd_system(a.counter[r], 1u);
+    }
     if (tid == 0) a.ticket[bh] = 0;  // ready for the next launch
+}
+
+// Peer block layout: arrival counter, this rank's epoch, landing buffer.
+constexpr size_t PEER_COUNTER_OFF = 0, PEER_EPOCH_OFF = 128, PEER_LANDING_OFF = 256;
+
+struct PeerFinishArgs {
+    const unsigned *counter;  // arrivals of (sequence, kv head) rows from every rank
+    unsigned *epoch;          // steps completed by this rank
+    const uint4 *landing;     // [2][n16] 16-byte words
+    uint4 *out;               // [n16]
+    int64_t n16;
+    unsigned merges;          // arrivals per step
+};
+
+// One CTA: a bounded wait until every rank's rows of this step have arrived
+// (counter >= (epoch + 1) * merges; a timeout is counted as a device error
+// and the copy goes ahead), the copy of the landing half epoch & 1, and the
+// epoch advance.
+__global__ void __launch_bounds__(256) peer_gather_finish_kernel(PeerFinishArgs f)
+{
+    __shared__ unsigned s_e;
+    if (threadIdx.x == 0) {
+        const unsigned e = *f.epoch;
+        const unsigned target = (e + 1u) * f.merges;
+        bool ok = false;
+        for (unsigned it = 0; it < (1u << 22); ++it) {
+            unsigned v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f.counter) : "memory");
+            if ((int)(v - target) >= 0) {
+                ok = true;
+                break;
+            }
+            __nanosleep(64);
+        }
+        if (!ok) report_dev_error(DEV_ERR_WAIT);
+        s_e = e;
+    }
+    __syncthreads();
+    const uint4 *src = f.landing + (int64_t)(s_e & 1u) * f.n16;
+    for (int64_t i = threadIdx.x; i < f.n16; i += blockDim.x) f.out[i] = __ldcg(src + i);
+    __syncthreads();
+    if (threadIdx.x == 0) *f.epoch = s_e + 1u;
 }
 
 static size_t sa_smem_bytes(int rank)
@@ -518,14 +583,17 @@ size_t skv_decode_sparse_attention_workspace(const skv_decode_geom *g, int seq_l
     return ((o + 255) & ~(size_t)255) + ((ml + 255) & ~(size_t)255) + ((tk + 255) & ~(size_t)255);
 }
 
-int skv_decode_sparse_attention(const skv_decode_geom *g, const void *q, const void *U, const void *SVt,
-                                const void *cos_sin, const void *v_host, void *k_buf, void *v_buf,
-                                const int32_t *miss_slot, const int32_t *miss_chunk,
-                                const int32_t *miss_count, int seq_len, void *out, void *workspace,
-                                size_t workspace_bytes, void *stream)
+}  // extern "C"
+
+static int launch_sparse_attention(const skv_decode_geom *g, const void *q, const void *U, const void *SVt,
+                                   const void *cos_sin, const void *v_host, void *k_buf, void *v_buf,
+                                   const int32_t *miss_slot, const int32_t *miss_chunk,
+                                   const int32_t *miss_count, int seq_len, void *out,
+                                   const skv_peer_gather *pg, void *workspace, size_t workspace_bytes,
+                                   void *stream)
 {
-    SKV_CHECK_ARG(g && q && U && SVt && cos_sin && k_buf && v_buf && miss_slot && miss_chunk && miss_count && out &&
-                      workspace,
+    SKV_CHECK_ARG(g && q && U && SVt && cos_sin && k_buf && v_buf && miss_slot && miss_chunk && miss_count &&
+                      (out || pg) && workspace,
                   "null pointer argument");
     SKV_CHECK_ARG(g->batch > 0 && g->kv_heads > 0 && g->q_heads % g->kv_heads == 0, "bad head counts");
     SKV_CHECK_SUPPORTED(g->head_dim == 128 && g->chunk_size == 8, "head_dim 128 and chunk 8 only");
@@ -551,9 +619,20 @@ int skv_decode_sparse_attention(const skv_decode_geom *g, const void *q, const v
     if (st != SKV_OK) return st;
     SKV_CHECK_ARG(aligned(hdev, 16), "v_host must be 16-byte aligned");
     void *dout = nullptr;
-    st = out_to_device_ptr(out, &dout, "out");
-    if (st != SKV_OK) return st;
-    SKV_CHECK_ARG(aligned(dout, 8), "out must be 8-byte aligned");
+    if (!pg) {
+        st = out_to_device_ptr(out, &dout, "out");
+        if (st != SKV_OK) return st;
+        SKV_CHECK_ARG(aligned(dout, 8), "out must be 8-byte aligned");
+    } else {
+        SKV_CHECK_ARG(pg->world >= 1 && pg->world <= SKV_MAX_PEERS && pg->rank >= 0 && pg->rank < pg->world,
+                      "peer gather: world must be 1..%d and rank in [0, world)", SKV_MAX_PEERS);
+        SKV_CHECK_ARG(pg->q_head0 >= 0 && pg->q_head0 + g->q_heads <= pg->q_heads_total,
+                      "peer gather: query heads [%d, %d) outside the %d of the full output", pg->q_head0,
+                      pg->q_head0 + g->q_heads, pg->q_heads_total);
+        SKV_CHECK_ARG(pg->merges_per_step >= g->batch * g->kv_heads, "peer gather: merges_per_step too small");
+        for (int r = 0; r < pg->world; ++r)
+            SKV_CHECK_ARG(pg->block[r] && aligned(pg->block[r], 256), "peer gather: block %d null or unaligned", r);
+    }
 
     const int BH = g->batch * g->kv_heads;
     const int nblk = ceil_div(seq_len, SA_ROWS);
@@ -577,6 +656,17 @@ int skv_decode_sparse_attention(const skv_decode_geom *g, const void *q, const v
     a.part_o = reinterpret_cast<float *>(ws + tk_bytes + ((ml_bytes + 255) & ~(size_t)255));
     (void)o_bytes;
     a.out = (__nv_bfloat16 *)dout;
+    if (pg) {
+        a.world = pg->world;
+        a.q_head0 = pg->q_head0;
+        a.q_heads_total = pg->q_heads_total;
+        for (int r = 0; r < pg->world; ++r) {
+            unsigned char *blk = static_cast<unsigned char *>(pg->block[r]);
+            a.counter[r] = reinterpret_cast<unsigned *>(blk + PEER_COUNTER_OFF);
+            a.landing[r] = reinterpret_cast<__nv_bfloat16 *>(blk + PEER_LANDING_OFF);
+        }
+        a.epoch = reinterpret_cast<const unsigned *>(static_cast<unsigned char *>(pg->block[pg->rank]) + PEER_EPOCH_OFF);
+    }
     a.Hkv = g->kv_heads;
     a.G = G;
     a.K = g->select_sets;
@@ -616,6 +706,125 @@ int skv_decode_sparse_attention(const skv_decode_geom *g, const void *q, const v
         return SKV_ERR_CUDA;
     }
     return SKV_OK;
+}
+
+extern "C" {
+
+int skv_decode_sparse_attention(const skv_decode_geom *g, const void *q, const void *U, const void *SVt,
+                                const void *cos_sin, const void *v_host, void *k_buf, void *v_buf,
+                                const int32_t *miss_slot, const int32_t *miss_chunk,
+                                const int32_t *miss_count, int seq_len, void *out, void *workspace,
+                                size_t workspace_bytes, void *stream)
+{
+    SKV_CHECK_ARG(out != nullptr, "null pointer argument");
+    return launch_sparse_attention(g, q, U, SVt, cos_sin, v_host, k_buf, v_buf, miss_slot, miss_chunk, miss_count,
+                                   seq_len, out, nullptr, workspace, workspace_bytes, stream);
+}
+
+int skv_decode_sparse_attention_gather(const skv_decode_geom *g, const void *q, const void *U, const void *SVt,
+                                       const void *cos_sin, const void *v_host, void *k_buf, void *v_buf,
+                                       const int32_t *miss_slot, const int32_t *miss_chunk,
+                                       const int32_t *miss_count, int seq_len, const skv_peer_gather *pg,
+                                       void *workspace, size_t workspace_bytes, void *stream)
+{
+    SKV_CHECK_ARG(pg != nullptr, "null pointer argument");
+    return launch_sparse_attention(g, q, U, SVt, cos_sin, v_host, k_buf, v_buf, miss_slot, miss_chunk, miss_count,
+                                   seq_len, nullptr, pg, workspace, workspace_bytes, stream);
+}
+
+size_t skv_peer_block_bytes(int batch, int q_heads_total)
+{
+    if (batch <= 0 || q_heads_total <= 0) return 0;
+    return PEER_LANDING_OFF + (size_t)2 * batch * q_heads_total * 128 * 2;
+}
+
+int skv_peer_alloc(size_t bytes, void **block)
+{
+    SKV_CHECK_ARG(block != nullptr && bytes >= PEER_LANDING_OFF, "bad peer block request");
+    *block = nullptr;
+    cudaError_t e = cudaMalloc(block, bytes);
+    if (e == cudaSuccess) e = cudaMemset(*block, 0, bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        if (*block) cudaFree(*block);
+        *block = nullptr;
+        set_error("peer block of %zu bytes: %s", bytes, cudaGetErrorString(e));
+        return SKV_ERR_CUDA;
+    }
+    return SKV_OK;
+}
+
+int skv_peer_free(void *block)
+{
+    if (!block) return SKV_OK;
+    cudaError_t e = cudaFree(block);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        set_error("cudaFree of a peer block: %s", cudaGetErrorString(e));
+        return SKV_ERR_CUDA;
+    }
+    return SKV_OK;
+}
+
+int skv_peer_export(const void *block, void *handle64)
+{
+    SKV_CHECK_ARG(block && handle64, "null pointer argument");
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void *>(block));
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        set_error("cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+        return SKV_ERR_CUDA;
+    }
+    memcpy(handle64, &h, sizeof(h));
+    return SKV_OK;
+}
+
+int skv_peer_import(const void *handle64, void **block)
+{
+    SKV_CHECK_ARG(handle64 && block, "null pointer argument");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle64, sizeof(h));
+    cudaError_t e = cudaIpcOpenMemHandle(block, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        set_error("cudaIpcOpenMemHandle: %s", cudaGetErrorString(e));
+        return SKV_ERR_CUDA;
+    }
+    return SKV_OK;
+}
+
+int skv_peer_close(void *block)
+{
+    SKV_CHECK_ARG(block != nullptr, "null pointer argument");
+    cudaError_t e = cudaIpcCloseMemHandle(block);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        set_error("cudaIpcCloseMemHandle: %s", cudaGetErrorString(e));
+        return SKV_ERR_CUDA;
+    }
+    return SKV_OK;
+}
+
+int skv_peer_gather_finish(const skv_peer_gather *pg, int batch, void *out, void *stream)
+{
+    SKV_CHECK_ARG(pg && out && batch > 0, "null pointer argument or batch <= 0");
+    SKV_CHECK_ARG(pg->world >= 1 && pg->world <= SKV_MAX_PEERS && pg->rank >= 0 && pg->rank < pg->world &&
+                      pg->q_heads_total > 0 && pg->merges_per_step > 0,
+                  "bad peer gather description");
+    SKV_CHECK_ARG(pg->block[pg->rank] && aligned(pg->block[pg->rank], 256) && aligned(out, 16),
+                  "peer block or output unaligned");
+    unsigned char *blk = static_cast<unsigned char *>(pg->block[pg->rank]);
+    PeerFinishArgs f;
+    f.counter = reinterpret_cast<const unsigned *>(blk + PEER_COUNTER_OFF);
+    f.epoch = reinterpret_cast<unsigned *>(blk + PEER_EPOCH_OFF);
+    f.landing = reinterpret_cast<const uint4 *>(blk + PEER_LANDING_OFF);
+    f.out = static_cast<uint4 *>(out);
+    f.n16 = (int64_t)batch * pg->q_heads_total * 128 * 2 / 16;
+    f.merges = (unsigned)pg->merges_per_step;
+    peer_gather_finish_kernel<<<1, 256, 0, (cudaStream_t)stream>>>(f);
+    return check_launch("peer_gather_finish_kernel");
 }
 
 }  // extern "C"

@@ -372,6 +372,14 @@ class ShadowKVCache_CPU:
                                       cos_sin_cache, self.v_cache_cpu[layer_idx], self.k_cache_buffer[layer_idx],
                                       self.v_cache_buffer[layer_idx], seq_len, out)
 
+    def sparse_attention_gather(self, layer_idx, query_states, seq_len, cos_sin_cache, peer):
+        """``sparse_attention_fused`` with the output rows sent to every rank's landing buffer
+        (kv heads split over ranks; ``peer`` is a ``peer.PeerOutput``, ``peer.finish`` ends the step)."""
+        q = query_states.reshape(self.batch_size, self.num_attention_heads, self.head_dim)
+        peer.attention(self._fused_geom, self._fused_ws, q, self.U[layer_idx], self.SV[layer_idx], cos_sin_cache,
+                       self.v_cache_cpu[layer_idx], self.k_cache_buffer[layer_idx], self.v_cache_buffer[layer_idx],
+                       seq_len)
+
     def attention(self, layer_idx, query_states, seq_len, out=None):
         """GQA decode attention over buffer rows [0, seq_len) -> [B, Hq, D]."""
         g = self._fused_geom if self._fused_geom is not None else fused.Geometry(
