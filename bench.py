@@ -469,6 +469,55 @@ def run_b200(args, world, rank, local):
     return res
 
 
+def run_prefill(args):
+    """Prefill state build of one layer (config1 shapes, B=1): torch restatement vs skv_prefill_build.
+
+    Both include the 252 MB device-to-host copy of the values into the page-locked
+    chunk store (the reference's prefill does it too); the SVD is not part of either."""
+    import types
+    from shadowkv_b200 import workload
+    from shadowkv_b200.kvcache import ShadowKVCache_CPU
+    cfg = workload.CONFIGS[args.config]
+    T, Hk, Hq, D = cfg.ctx, cfg.kv_heads, cfg.q_heads, 128
+    g = torch.Generator(device="cuda").manual_seed(0)
+    k_roped = torch.randn(1, Hk, T, D, generator=g, device="cuda").to(torch.bfloat16)
+    v = torch.randn(1, Hk, T, D, generator=g, device="cuda").to(torch.bfloat16)
+    q_last = torch.randn(1, Hq, 1, D, generator=g, device="cuda").to(torch.bfloat16)
+    conf = types.SimpleNamespace(num_attention_heads=Hq, num_key_value_heads=Hk, hidden_size=Hq * D,
+                                 num_hidden_layers=1)
+    cache = ShadowKVCache_CPU(conf, batch_size=1, max_length=T, device="cuda", sparse_budget=cfg.budget,
+                              rank=cfg.rank, local_chunk=cfg.local_chunk, outlier_chunk=cfg.outliers,
+                              gen_len=cfg.gen_len, geometry=cfg.geometry)
+    times = {"torch": [], "native": [], "build": []}
+    for i in range(args.warmup + args.steps):
+        for kind in ("torch", "native"):
+            cache.prefilled_batch, cache.kv_offset = 0, 0
+            torch.cuda.synchronize()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            if kind == "torch":
+                cache.prefill_kv_cache(v, 0, k_roped, q_last)
+            else:
+                cache.prefill_kv_cache_native(v, 0, k_roped, q_last, build_events=(b0, b1))
+            e.record()
+            e.synchronize()
+            if i >= args.warmup:
+                times[kind].append(s.elapsed_time(e))
+                if kind == "native":
+                    times["build"].append(b0.elapsed_time(b1))
+    tn, tt, tb = (statistics.median(times[k]) for k in ("native", "torch", "build"))
+    host_bytes = (T // 8) * 8 * D * 2 * Hk
+    return {"metric": f"prefill state build ms ({cfg.name} shapes, one layer)", "value": tn, "unit": "ms",
+            "higher_is_better": False, "steps": args.steps, "warmup": args.warmup,
+            "torch_path_ms": tt, "speedup_vs_torch_path": tt / tn,
+            "device_state_kernels_ms": tb, "host_store_bytes": host_bytes,
+            "host_store_gbs": host_bytes / (tn * 1e-3) / 1e9,
+            "config": {"workload": f"{cfg.name}: B=1, {Hq}q/{Hk}kv heads, T {T}, {cfg.outliers} outliers, "
+                                   f"budget {cfg.budget}; includes the device-to-host copy of the values"},
+            "data": "synthetic (seeded normal keys/values)"}
+
+
 def cpu_baseline(layer, inputs, seconds=15.0, layers=1):
     """The oracle port of the reference's torch-eager decode step, timed on the host cores."""
     import numpy as np
@@ -514,6 +563,8 @@ def main():
     ap.add_argument("--config", default="config1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying a CUDA graph")
+    ap.add_argument("--prefill", action="store_true",
+                    help="time the prefill state build of one layer (torch path vs skv_prefill_build)")
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
                     help="--shard heads: how every rank gets all heads' attention rows")
     ap.add_argument("--layers", type=int, default=1,
@@ -534,6 +585,9 @@ def main():
         from oracle import cpu_reference
         res = cpu_reference.run(args, world, rank)
         print(json.dumps(res), flush=True)
+        return
+    if args.prefill:
+        print(json.dumps(run_prefill(args)), flush=True)
         return
     world, rank, local = dist_setup()
     res = run_b200(args, world, rank, local)

@@ -350,6 +350,45 @@ SKV_API int skv_decode_sparse_attention(const skv_decode_geom *g, const void *q,
                                         int seq_len, void *out, void *workspace,
                                         size_t workspace_bytes, void *stream);
 
+/* ---- prefill state builder (ShadowKVCache_CPU.prefill_kv_cache,
+ * models/kvcache/shadow.py:463-544) for one layer of `batch` sequences. */
+typedef struct {
+    int batch, kv_heads, q_heads;
+    int tokens;         /* prompt length T */
+    int chunks;         /* landmark candidates per head: T/8 - local_chunk (rounded down
+                           to a multiple of 8 for the CPU-class geometry); the last
+                           T - 8*chunks tokens are the local window */
+    int outlier_chunk;  /* chunks of lowest key similarity kept in the buffer (<= 256) */
+    int select_sets;    /* chunks of the first selection */
+    int buf_len;        /* rows of each K/V buffer per head */
+    int host_chunks;    /* chunk slots per head of the host value store (>= T/8) */
+} skv_prefill_geom;
+
+SKV_API size_t skv_prefill_workspace(const skv_prefill_geom *p);
+
+/* The prompt's values v [batch][kv][T][128] bf16 into the page-locked host
+ * store v_host [batch][kv][host_chunks][8*128], chunks 0 .. T/8-1 (one
+ * strided device-to-host copy; give it a stream of its own to overlap
+ * skv_prefill_build). */
+SKV_API int skv_prefill_store_values(const skv_prefill_geom *p, const void *v, void *v_host, void *stream);
+
+/* k_roped, v [batch][kv][T][128] bf16 (post-RoPE keys, values), q_last
+ * [batch][q_heads][128] bf16 (post-RoPE last prompt query).  Writes
+ *   k_buf, v_buf [batch][kv][buf_len][128] rows 0 .. sparse_end-1: local
+ *     window, the outlier chunks (ascending minimum similarity, ties to the
+ *     lower chunk id), the selected chunks in slot order;
+ *   landmarks [batch][kv][chunks-outlier_chunk][128] bf16 and landmark_idx
+ *     (int64): means of the non-outlier chunks in chunk order;
+ *   slots (int32) and position_ids (int64) [batch][kv][select_sets]: the
+ *     first selection (scores of q_last against the landmarks; ascending
+ *     chunk id in slot order).
+ * Mean and cosine similarity are computed op by op in bf16 like the torch
+ * ops they replace; the selection uses fp32 scores (the reference rounds
+ * them to bf16 and leaves ties to torch.topk). */
+SKV_API int skv_prefill_build(const skv_prefill_geom *p, const void *k_roped, const void *v, const void *q_last,
+                              void *k_buf, void *v_buf, void *landmarks, int64_t *landmark_idx, int32_t *slots,
+                              int64_t *position_ids, void *workspace, size_t workspace_bytes, void *stream);
+
 /* ---- attention output gathered over peer memory (kv heads split over ranks)
  *
  * With the kv heads of a sequence split over `world` GPUs (one process per

@@ -31,6 +31,15 @@ class DecodeGeom(ctypes.Structure):
     ]
 
 
+class PrefillGeom(ctypes.Structure):
+    """``skv_prefill_geom`` of include/shadowkv_b200.h."""
+
+    _fields_ = [
+        ("batch", c_int), ("kv_heads", c_int), ("q_heads", c_int), ("tokens", c_int), ("chunks", c_int),
+        ("outlier_chunk", c_int), ("select_sets", c_int), ("buf_len", c_int), ("host_chunks", c_int),
+    ]
+
+
 SKV_MAX_PEERS = 8
 
 
@@ -73,6 +82,9 @@ SIGNATURES = {
     "skv_decode_sparse_attention": [ctypes.POINTER(DecodeGeom)] + [P] * 10 + [c_int, P, P, c_size_t, P],
     "skv_decode_sparse_attention_gather": [ctypes.POINTER(DecodeGeom)] + [P] * 10
                                           + [c_int, ctypes.POINTER(PeerGather), P, c_size_t, P],
+    "skv_prefill_workspace": [ctypes.POINTER(PrefillGeom)],
+    "skv_prefill_store_values": [ctypes.POINTER(PrefillGeom), P, P, P],
+    "skv_prefill_build": [ctypes.POINTER(PrefillGeom)] + [P] * 10 + [c_size_t, P],
     "skv_peer_block_bytes": [c_int, c_int],
     "skv_peer_alloc": [c_size_t, ctypes.POINTER(c_void_p)],
     "skv_peer_free": [P],
@@ -83,7 +95,7 @@ SIGNATURES = {
 }
 _RET = {"skv_last_error": c_char_p, "skv_decode_select_workspace": c_size_t,
         "skv_decode_attention_workspace": c_size_t, "skv_decode_sparse_attention_workspace": c_size_t,
-        "skv_peer_block_bytes": c_size_t}
+        "skv_peer_block_bytes": c_size_t, "skv_prefill_workspace": c_size_t}
 
 
 def _load():

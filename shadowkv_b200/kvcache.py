@@ -217,6 +217,87 @@ class ShadowKVCache_CPU:
             if self.prefilled_batch == self.batch_size:
                 self.kv_offset += incoming
 
+    def prefill_kv_cache_native(self, new_v_cache: torch.Tensor, layer_idx: int, key_states_roped: torch.Tensor,
+                                last_query_states: torch.Tensor, build_events=None):
+        """``prefill_kv_cache`` as GPU kernels (``skv_prefill_build``): host value store,
+        landmarks and outliers (bf16 op by op like the torch ops), first selection with
+        fp32 scores, buffer rows.  Same state layout; outliers listed by (similarity,
+        chunk id), the first selection in ascending chunk id per slot.  ``build_events``
+        (two CUDA events) bracket the device-state kernels on the current stream, the
+        host-store copy running beside them on the copy stream."""
+        import ctypes
+        from ._lib import PrefillGeom, check, lib
+        bsz, H, incoming, D = new_v_cache.shape
+        c = self.chunk_size
+        if incoming // c > self.host_chunks:
+            raise RuntimeError(f"prompt of {incoming} tokens exceeds max_length {self.max_length}")
+        chunks = incoming // c - self.local_chunk
+        if self.geometry == "cpu":
+            chunks = chunks - chunks % 8
+        prefill_local = incoming - chunks * c
+        sparse_start = prefill_local + self.outlier_chunk * c
+        if sparse_start + self.sparse_budget + self.gen_len > self.buf_len:
+            raise RuntimeError("K/V buffer too small for the prefill geometry")
+        num_landmarks = chunks - self.outlier_chunk
+        if self.k_landmark is None:
+            G = self.num_key_value_groups
+            self.k_landmark = torch.zeros(self.num_layers, self.batch_size, H, num_landmarks, D, dtype=self.dtype,
+                                          device=self.device)
+            self.k_landmark_idx = torch.zeros(self.num_layers, self.batch_size, H, num_landmarks, dtype=torch.long,
+                                              device=self.device)
+            nblk = (num_landmarks + 255) // 256
+            self.gemm_o = torch.zeros(self.batch_size, H, G, num_landmarks, dtype=torch.bfloat16, device=self.device)
+            self.softmax_o = torch.zeros_like(self.gemm_o)
+            self.norm = torch.zeros(self.batch_size * H, G, nblk, dtype=torch.float32, device=self.device)
+            self.sum = torch.zeros_like(self.norm)
+        if self.k_landmark.shape[-2] != num_landmarks:
+            raise RuntimeError("every layer and sequence of one cache must have the same prompt geometry")
+        pb = self.prefilled_batch
+        pg = PrefillGeom(batch=bsz, kv_heads=H, q_heads=self.num_attention_heads, tokens=incoming, chunks=chunks,
+                         outlier_chunk=self.outlier_chunk, select_sets=self.select_sets, buf_len=self.buf_len,
+                         host_chunks=self.host_chunks)
+        nbytes = int(lib.skv_prefill_workspace(ctypes.byref(pg)))
+        if nbytes == 0:
+            raise RuntimeError("prefill geometry rejected: " + (lib.skv_last_error() or b"").decode())
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+        k = key_states_roped.contiguous()
+        v = new_v_cache.contiguous()
+        q = last_query_states.reshape(bsz, self.num_attention_heads, D).to(self.dtype).contiguous()
+        for t in (k, v, q):
+            if not t.is_cuda or t.dtype != self.dtype:
+                raise RuntimeError("prefill inputs must be bf16 CUDA tensors")
+        cur = torch.cuda.current_stream(self.device)
+        # the 8 MB-per-head copy into the host store runs on the copy stream, beside the kernels
+        self.copy_stream.wait_stream(cur)
+        check(lib.skv_prefill_store_values(ctypes.byref(pg), v.data_ptr(),
+                                           self.v_cache_cpu[layer_idx][pb:pb + bsz].data_ptr(),
+                                           self.copy_stream.cuda_stream), "skv_prefill_store_values")
+        if build_events is not None:
+            build_events[0].record(cur)
+        check(lib.skv_prefill_build(
+            ctypes.byref(pg), k.data_ptr(), v.data_ptr(), q.data_ptr(),
+            self.k_cache_buffer[layer_idx][pb:pb + bsz].data_ptr(), self.v_cache_buffer[layer_idx][pb:pb + bsz].data_ptr(),
+            self.k_landmark[layer_idx][pb:pb + bsz].data_ptr(), self.k_landmark_idx[layer_idx][pb:pb + bsz].data_ptr(),
+            self.slots[layer_idx][pb:pb + bsz].data_ptr(), self.position_ids[layer_idx][pb:pb + bsz].data_ptr(),
+            ws.data_ptr(), nbytes, cur.cuda_stream), "skv_prefill_build")
+        if build_events is not None:
+            build_events[1].record(cur)
+        cur.wait_stream(self.copy_stream)
+        v.record_stream(self.copy_stream)
+        self.prefill = incoming
+        self.max_ctx_chunks_len = (incoming // c) * c
+        self.chunks = chunks
+        self.prefill_local = prefill_local
+        self.sparse_start = sparse_start
+        self.sparse_end = sparse_start + self.sparse_budget
+        self.kernel_offset = self.sparse_start * D
+        self.kernel_stride = self.buf_len * D
+        if layer_idx == self.num_layers - 1:
+            self.prefilled_batch += bsz
+            if self.prefilled_batch == self.batch_size:
+                self.kv_offset += incoming
+        return ws  # keep the scratch alive until the stream is past the launch
+
     def H2D(self):
         """The state already lives on the device; kept for API parity (shadow.py:599-619)."""
         torch.cuda.synchronize(self.device)
