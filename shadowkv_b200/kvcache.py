@@ -17,9 +17,9 @@ pre-RoPE factors.  Two decode paths share the state:
 ``sync_slots_from_position_ids`` / ``sync_position_ids_from_slots`` convert
 between the two slot orders, so one cache can be driven by either.
 
-Prefill (``get_svd``, ``prefill_kv_cache``) builds the state in torch on the
-GPU with the reference's algorithm (shadow.py:411-544); it is outside the
-accelerated decode path.
+Prefill builds the state with the reference's algorithm (shadow.py:411-544):
+``get_svd`` and ``prefill_kv_cache`` in torch on the GPU (the torch path),
+``prefill_kv_cache_native`` with the library's prefill kernels.
 """
 from __future__ import annotations
 
