@@ -36,12 +36,18 @@ class ShadowAttention:
         pk = position_ids.view(B, 1, S).expand(B, Hk, S)
         return apply_rotary_pos_emb_cuda(q, self.cos_sin_cache, pq), apply_rotary_pos_emb_cuda(k, self.cos_sin_cache, pk)
 
-    def prefill(self, query_states, key_states, value_states, position_ids, layer_idx):
-        """Build the cache state of one layer (pre-RoPE k -> SVD; post-RoPE k -> landmarks)."""
+    def prefill(self, query_states, key_states, value_states, position_ids, layer_idx, native=False):
+        """Build the cache state of one layer (pre-RoPE k -> SVD; post-RoPE k -> landmarks).
+
+        ``native=True`` builds the landmarks, outliers, host store, first selection and
+        buffer rows with the library's prefill kernels instead of the torch ops."""
         kv = self.kv_cache
         kv.get_svd(key_states, layer_idx=layer_idx)
         q, k = self.apply_rotary_pos_emb(query_states, key_states, position_ids)
-        kv.prefill_kv_cache(value_states, layer_idx, k, q[:, :, -1:])
+        if native:
+            kv.prefill_kv_cache_native(value_states, layer_idx, k, q[:, :, -1:])
+        else:
+            kv.prefill_kv_cache(value_states, layer_idx, k, q[:, :, -1:])
 
     def decode(self, query_states, key_states, value_states, position_ids, layer_idx):
         """models/attention/shadow.py:22-48 -> attention output [B, 1, Hq, D]."""
