@@ -8,8 +8,9 @@ The attention is the library's split-K GQA kernel instead of
 instead of vllm's ``rotary_embedding`` custom op (llama.py:149-154).
 ``decode_fused`` runs the same step on the fused slot-stable kernels.
 
-Prefill is outside the accelerated path; ``prefill`` builds the cache state
-with torch (SVD, landmarks, outliers) and returns no attention output.
+``prefill`` builds the cache state (SVD in torch; landmarks, outliers, host
+store and first selection in torch or, with ``native=True``, with the
+library's prefill kernels) and returns no attention output.
 """
 from __future__ import annotations
 
