@@ -77,3 +77,30 @@ def test_ctypes_signatures_match_header_parameter_counts():
         params = params.strip()
         n = 0 if params in ("", "void") else params.count(",") + 1
         assert len(_lib.SIGNATURES[name]) == n, f"{name}: header {n} params, ctypes {len(_lib.SIGNATURES[name])}"
+
+
+def test_peer_gather_struct_and_block_size_match_the_header():
+    from shadowkv_b200 import _lib
+    # int world, rank, q_head0, q_heads_total, merges_per_step; void *block[8]
+    assert ctypes.sizeof(_lib.PeerGather) == 24 + 8 * _lib.SKV_MAX_PEERS
+    assert _lib.PeerGather.block.offset == 24
+    src = open(os.path.join(ROOT, "include", "shadowkv_b200.h")).read()
+    assert re.search(r"#define SKV_MAX_PEERS\s+%d\b" % _lib.SKV_MAX_PEERS, src)
+    # counter | epoch | landing [2][batch][q_heads_total][128] bf16
+    assert _lib.lib.skv_peer_block_bytes(1, 32) == 256 + 2 * 32 * 128 * 2
+    assert _lib.lib.skv_peer_block_bytes(0, 32) == 0 and _lib.lib.skv_peer_block_bytes(2, 0) == 0
+
+
+def test_prefill_geometry_checks_are_pure_host():
+    from shadowkv_b200 import _lib
+    ok = dict(batch=1, kv_heads=2, q_heads=8, tokens=2048, chunks=252, outlier_chunk=8, select_sets=32,
+              buf_len=2048, host_chunks=256)
+    assert _lib.lib.skv_prefill_workspace(ctypes.byref(_lib.PrefillGeom(**ok))) > 0
+    for bad in (dict(chunks=300),            # chunks exceed the prompt
+                dict(outlier_chunk=300),     # more outliers than supported
+                dict(select_sets=250),       # fewer landmarks than selected chunks
+                dict(buf_len=100),           # buffer too small for local + outlier + selected rows
+                dict(host_chunks=10),        # host store smaller than the prompt
+                dict(q_heads=7)):            # q heads not a multiple of kv heads
+        g = dict(ok, **bad)
+        assert _lib.lib.skv_prefill_workspace(ctypes.byref(_lib.PrefillGeom(**g))) == 0, bad
