@@ -351,9 +351,17 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
     if (warp_id() < G) {
         const int gg = warp_id();
         float mm = -INFINITY, ss = 0.f;
-        for (int i = lane; i < a.nsplit; i += 32) {
-            const float2 p = a.part[((int64_t)bh * a.nsplit + i) * G + gg];
-            merge_ms(mm, ss, p.x, p.y);
+        // four loads in flight per lane before they are merged (long contexts
+        // have a hundred or more splits per head)
+        for (int i0 = lane; i0 < a.nsplit; i0 += 4 * 32) {
+            float2 p[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int i = i0 + 32 * u;
+                p[u] = i < a.nsplit ? a.part[((int64_t)bh * a.nsplit + i) * G + gg] : make_float2(-INFINITY, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) merge_ms(mm, ss, p[u].x, p[u].y);
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
