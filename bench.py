@@ -176,6 +176,8 @@ def run_b200(args, world, rank, local):
     NL = args.layers
     if NL > 1:
         cfg = dataclasses.replace(cfg, layers=NL)
+    if args.batch:
+        cfg = dataclasses.replace(cfg, batch=args.batch)
     heads_sharded = args.shard == "heads" and world > 1
     if heads_sharded and NL > 1:
         raise SystemExit("--layers > 1 runs with --shard batch")
@@ -567,6 +569,7 @@ def main():
                     help="time the prefill state build of one layer (torch path vs skv_prefill_build)")
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
                     help="--shard heads: how every rank gets all heads' attention rows")
+    ap.add_argument("--batch", type=int, default=0, help="sequences per GPU (default: the config's, 1)")
     ap.add_argument("--layers", type=int, default=1,
                     help="decode layers per step (chained: each layer's output is the next one's query)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
