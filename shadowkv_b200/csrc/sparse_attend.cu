@@ -463,15 +463,25 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    // merge of the head's nblk partial outputs: all (m, l) pairs come in
-    // one round of loads; warp w turns those of heads w, w + 8 into weights
-    // w_j = exp(m_j - M) / L; then each thread sums 4 columns of one query
-    // row over the partials, loads unrolled (the tiles' shared memory is free)
+    // merge of the head's nblk partial outputs: each thread sums 4 columns of
+    // one query row over the partials.  Its first row's partials (up to
+    // SA_MERGE_REGS of them) and all (m, l) pairs are loaded in one round;
+    // warp w turns the pairs of heads w, w + 8 into weights
+    // w_j = exp(m_j - M) / L meanwhile (the tiles' shared memory is free).
     {
+        constexpr int SA_MERGE_REGS = 24;
         const int nml = a.nblk * G;
         float2 *s_ml = reinterpret_cast<float2 *>(smem_raw);  // [nblk][G]
         float *s_w = reinterpret_cast<float *>(s_ml + nml);  // [nblk][G]
         const float2 *ml = a.part_ml + (int64_t)bh * nml;
+        const float *po_head = a.part_o + (int64_t)bh * a.nblk * G * 128;
+        float4 pre[SA_MERGE_REGS];
+        if (tid < G * 32) {
+            const float *po = po_head + (tid >> 5) * 128 + (tid & 31) * 4;
+#pragma unroll
+            for (int j = 0; j < SA_MERGE_REGS; ++j)
+                if (j < a.nblk) pre[j] = __ldcg(reinterpret_cast<const float4 *>(po + (int64_t)j * G * 128));
+        }
         for (int t = tid; t < nml; t += SA_THREADS) s_ml[t] = __ldcg(&ml[t]);
         __syncthreads();
         for (int gg = warp; gg < G; gg += SA_THREADS / 32) {
@@ -488,10 +498,20 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
         __syncthreads();
         for (int p = tid; p < G * 32; p += SA_THREADS) {
             const int gg = p >> 5, d = (p & 31) * 4;
-            const float *po = a.part_o + (int64_t)bh * a.nblk * G * 128 + gg * 128 + d;
+            const float *po = po_head + gg * 128 + d;
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            int j0 = 0;
+            if (p == tid) {  // the first row: partials already in registers
+#pragma unroll
+                for (int j = 0; j < SA_MERGE_REGS; ++j)
+                    if (j < a.nblk) {
+                        const float w = s_w[j * G + gg];
+                        acc.x += pre[j].x * w, acc.y += pre[j].y * w, acc.z += pre[j].z * w, acc.w += pre[j].w * w;
+                    }
+                j0 = min(a.nblk, SA_MERGE_REGS);
+            }
 #pragma unroll 8
-            for (int j = 0; j < a.nblk; ++j) {
+            for (int j = j0; j < a.nblk; ++j) {
                 const float4 v = __ldcg(reinterpret_cast<const float4 *>(po + (int64_t)j * G * 128));
                 const float w = s_w[j * G + gg];
                 acc.x += v.x * w, acc.y += v.y * w, acc.z += v.z * w, acc.w += v.w * w;
