@@ -165,6 +165,13 @@ def algorithmic_bytes(cache, misses: int, seq_len: int):
     return hbm, host
 
 
+def select_kernels(cache):
+    """Kernels of one fused append+select call (2, or 3 with the keys kernel of long contexts)."""
+    import ctypes
+    from shadowkv_b200._lib import lib
+    return int(lib.skv_decode_select_kernels(ctypes.byref(cache._fused_geom.c())))
+
+
 def run_b200(args, world, rank, local):
     from shadowkv_b200 import workload
     from shadowkv_b200._lib import device_errors
@@ -458,7 +465,7 @@ def run_b200(args, world, rank, local):
                 "d2h_bytes_per_step": d2h},
         "kernel_us": kernel_us,
         "graph": used_graph,
-        "gpu_launches": (5 if args.split else 3) * NL * args.steps,
+        "gpu_launches": select_kernels(cache) * NL * args.steps + (3 if args.split else 1) * NL * args.steps,
         "clocks": clk.summary(),
         "wall_s": t_wall,
     }

@@ -246,6 +246,12 @@ SKV_API int skv_decode_append(const skv_decode_geom *g, const void *q, const voi
 /* Bytes of caller-provided scratch the selection needs. */
 SKV_API size_t skv_decode_select_workspace(const skv_decode_geom *g);
 
+/* Kernels one skv_decode_select / skv_decode_append_select launches: 2
+ * (scoring, selection), or 3 for more than 32768 landmarks per head, where a
+ * keys kernel between them computes the selection keys on the whole GPU
+ * (0 for a rejected geometry). */
+SKV_API int skv_decode_select_kernels(const skv_decode_geom *g);
+
 /* Landmark scoring + top-k + slot-stable reuse-cache diff for one layer.
  * q [batch][q_heads][128] bf16 (post-RoPE), landmarks [batch][kv][L][128]
  * bf16, landmark_idx [batch][kv][L] int64 chunk ids, slots

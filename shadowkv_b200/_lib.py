@@ -71,6 +71,7 @@ SIGNATURES = {
     "skv_batch_gemm_softmax": [P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_float, c_float, P],
     "skv_decode_append": [ctypes.POINTER(DecodeGeom), P, P, P, P, P, P, P, P, c_int, P],
     "skv_decode_select_workspace": [ctypes.POINTER(DecodeGeom)],
+    "skv_decode_select_kernels": [ctypes.POINTER(DecodeGeom)],
     "skv_decode_select": [ctypes.POINTER(DecodeGeom), P, P, P, P, P, P, P, P, c_size_t, P],
     "skv_decode_append_select": [ctypes.POINTER(DecodeGeom)] + [P] * 8 + [c_int] + [P] * 7 + [c_size_t, P],
     "skv_decode_select_noalloc": [ctypes.POINTER(DecodeGeom), P, P, P, P, P, P, P, P],

@@ -97,7 +97,7 @@ struct ScoreArgs {
     const __nv_bfloat16 *q;      // [B][Hq][128]: rotated (plain) or pre-RoPE (APPEND)
     const __nv_bfloat16 *lm;     // [BH][L][128]
     float *logits;               // [BH][L][G]
-    float2 *part;                // [BH][nsplit][G]
+    float2 *part;                // [BH][G][nsplit]
     int Hkv, G, L, rows_per_split;
     float scale;
     // new-token step (APPEND)
@@ -293,7 +293,7 @@ __global__ void __launch_bounds__(ST_THREADS) score_tma_kernel(ScoreArgs a)
     if (tid < G) {
         float mm = -INFINITY, ss = 0.f;
         for (int w = 0; w < ST_CONSUMERS; ++w) merge_stats(mm, ss, s_part[w][tid].x, s_part[w][tid].y);
-        a.part[((int64_t)bh * nsplit + split) * G + tid] = make_float2(mm, ss);
+        a.part[((int64_t)bh * G + tid) * nsplit + split] = make_float2(mm, ss);  // [BH][G][nsplit]
     }
 }
 
@@ -414,9 +414,11 @@ __global__ void __launch_bounds__(256) bgs_softmax_kernel(const __nv_bfloat16 *_
 // ---------------------------------------------------------------------------
 struct SelectPlan {
     int nsplit, rows_per_split;
-    size_t off_logits, off_part, off_keys, total;
+    size_t off_logits, off_part, off_keys, off_kin, total;
     bool keys_global;
-    int cl;  // CTAs per selection cluster
+    bool keys_pre;  // long contexts: keys_kernel computes the keys on the whole GPU first
+    int keys_rows;  // landmarks per keys_kernel CTA
+    int cl;         // CTAs per selection cluster
     size_t sel_smem;
 };
 
@@ -430,23 +432,30 @@ static SelectPlan plan_select(const skv_decode_geom *g)
     if (per < 1) per = 1;
     p.rows_per_split = per * ST_ROWS;
     p.nsplit = ceil_div(g->num_landmarks, p.rows_per_split);
-    // 16-CTA clusters for very long contexts (more than 4096 landmarks per CTA at 8)
+    // very long contexts (more than 4096 landmarks per CTA at 8): the keys are
+    // computed by keys_kernel on the whole GPU (the selection's clusters would
+    // spend long reading the logits) and the selection uses 16-CTA clusters
+    const int L = g->num_landmarks;
+    p.keys_pre = L > 8 * 4096;
+    const int64_t kr = ((int64_t)L * BH + 2 * 148 - 1) / (2 * 148);  // about two CTAs per SM
+    p.keys_rows = kr < 512 ? 512 : (int)kr;
     p.cl = 8;
-    if (g->num_landmarks > 8 * 4096) {
-        const bool kg16 = select_smem_bytes(g->num_landmarks, g->num_chunks, G, false, 16) > SEL_SMEM_CAP;
-        const size_t s16 = select_smem_bytes(g->num_landmarks, g->num_chunks, G, kg16, 16);
+    if (p.keys_pre) {
+        const bool kg16 = select_smem_bytes(L, g->num_chunks, G, false, 16, true) > SEL_SMEM_CAP;
+        const size_t s16 = select_smem_bytes(L, g->num_chunks, G, kg16, 16, true);
         if (s16 <= SEL_SMEM_CAP && select_cluster16_ok(s16)) p.cl = 16;
     }
-    p.keys_global = select_smem_bytes(g->num_landmarks, g->num_chunks, G, false, p.cl) > SEL_SMEM_CAP;
-    p.sel_smem = select_smem_bytes(g->num_landmarks, g->num_chunks, G, p.keys_global, p.cl);
+    p.keys_global = select_smem_bytes(L, g->num_chunks, G, false, p.cl, p.keys_pre) > SEL_SMEM_CAP;
+    p.sel_smem = select_smem_bytes(L, g->num_chunks, G, p.keys_global, p.cl, p.keys_pre);
     auto align = [](size_t x) { return (x + 255) & ~(size_t)255; };
     p.off_logits = 0;
-    p.off_part = align((size_t)BH * g->num_landmarks * G * 4);
+    p.off_part = align((size_t)BH * L * G * 4);
     p.off_keys = p.off_part + align((size_t)BH * p.nsplit * G * 8);
     // sized for the 8-CTA plan, whose key scratch is the larger: the size does
     // not depend on which cluster size the device allows
-    const bool keys_global8 = select_smem_bytes(g->num_landmarks, g->num_chunks, G, false, 8) > SEL_SMEM_CAP;
-    p.total = p.off_keys + (keys_global8 ? align((size_t)BH * g->num_landmarks * 4) : 0);
+    const bool keys_global8 = select_smem_bytes(L, g->num_chunks, G, false, 8, p.keys_pre) > SEL_SMEM_CAP;
+    p.off_kin = p.off_keys + (keys_global8 ? align((size_t)BH * L * 4) : 0);
+    p.total = p.off_kin + (p.keys_pre ? align((size_t)BH * L * 4) : 0);
     return p;
 }
 
@@ -507,6 +516,16 @@ static int run_select(const skv_decode_geom *g, const ScoreArgs &sa_in, const in
     a.miss_count = miss_count;
     a.G = G, a.L = g->num_landmarks, a.K = g->select_sets, a.nsplit = p.nsplit;
     a.num_chunks = g->num_chunks;
+    if (p.keys_pre) {
+        KeysArgs k;
+        k.logits = sa.logits;
+        k.part = sa.part;
+        k.keys = reinterpret_cast<uint32_t *>(ws + p.off_kin);
+        k.G = G, k.L = g->num_landmarks, k.nsplit = p.nsplit, k.rows = p.keys_rows;
+        st = launch_keys(k, BH, s);
+        if (st) return st;
+        a.keys_in = k.keys;
+    }
     return launch_select(a, BH, p.sel_smem, p.cl, s);
 }
 
@@ -520,6 +539,12 @@ size_t skv_decode_select_workspace(const skv_decode_geom *g)
 {
     if (check_geom(g) != SKV_OK) return 0;
     return plan_select(g).total;
+}
+
+int skv_decode_select_kernels(const skv_decode_geom *g)
+{
+    if (check_geom(g) != SKV_OK) return 0;
+    return plan_select(g).keys_pre ? 3 : 2;
 }
 
 int skv_decode_select(const skv_decode_geom *g, const void *q, const void *landmarks,

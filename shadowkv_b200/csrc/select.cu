@@ -105,6 +105,35 @@ __device__ __forceinline__ uint4 ld_dsmem_v4(uint32_t addr)
 // (e.g. many equal scores); ties at the K-th key go to the lowest landmark
 // indices (ranks in index order).  Sets the chunks in rank 0's bitmap (bmA0).
 // Kept out of line so that the common path stays compact in the instruction cache.
+// C_g = M_g + ln Z_g of query head gg from the scoring splits' (max, sum-exp)
+// partials of head bh; one warp, the result in every lane.  The selection and
+// keys_kernel both use it, so their keys are the same bits.
+__device__ __forceinline__ float merge_partials(const float2 *part, int bh, int nsplit, int G, int gg, int lane)
+{
+    float mm = -INFINITY, ss = 0.f;
+    // part is [BH][G][nsplit]: a warp's loads are contiguous; eight in flight
+    // per lane before they are merged (long contexts have a hundred or more
+    // splits per head)
+    const float2 *ph = part + ((int64_t)bh * G + gg) * nsplit;
+    for (int i0 = lane; i0 < nsplit; i0 += 8 * 32) {
+        float2 p[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = i0 + 32 * u;
+            p[u] = i < nsplit ? ph[i] : make_float2(-INFINITY, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) merge_ms(mm, ss, p[u].x, p[u].y);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, mm, o);
+        const float s2 = __shfl_xor_sync(0xffffffffu, ss, o);
+        merge_ms(mm, ss, m2, s2);
+    }
+    return mm + logf(ss);
+}
+
 // Keys of the landmarks of one logits tile in shared memory (cnt landmarks,
 // rows of G = 4Q floats; the first is landmark k0 of the CTA) and their
 // first-pass histogram.  The key of landmark c is
@@ -331,7 +360,7 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
     // for G = 4, 8 or 16 (a landmark row of 1, 2 or 4 16-byte words);
     // other group sizes read them directly
     const float *lg = a.logits + ((int64_t)bh * L + c0) * G;
-    const bool use_ring = G == 4 || G == 8 || G == 16;
+    const bool use_ring = !a.keys_in && (G == 4 || G == 8 || G == 16);
     const int kps = use_ring ? (SEL_RSTAGE / (G * 4)) & ~31 : 0;  // landmarks per tile
     const int ntile = use_ring ? (n + kps - 1) / kps : 0;
     auto issue_tile = [&](int i) {
@@ -348,30 +377,9 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
 
     // 1) softmax normalisers of each query head of the group: warp w merges the
     //    split partials of head w (lanes load in parallel, then a shuffle merge)
-    if (warp_id() < G) {
-        const int gg = warp_id();
-        float mm = -INFINITY, ss = 0.f;
-        // four loads in flight per lane before they are merged (long contexts
-        // have a hundred or more splits per head)
-        for (int i0 = lane; i0 < a.nsplit; i0 += 4 * 32) {
-            float2 p[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int i = i0 + 32 * u;
-                p[u] = i < a.nsplit ? a.part[((int64_t)bh * a.nsplit + i) * G + gg] : make_float2(-INFINITY, 0.f);
-            }
-#pragma unroll
-            for (int u = 0; u < 4; ++u) merge_ms(mm, ss, p[u].x, p[u].y);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float m2 = __shfl_xor_sync(0xffffffffu, mm, o);
-            const float s2 = __shfl_xor_sync(0xffffffffu, ss, o);
-            merge_ms(mm, ss, m2, s2);
-        }
-        if (lane == 0) {
-            s_C[gg] = mm + logf(ss);
-        }
+    if (!a.keys_in && warp_id() < G) {
+        const float C = merge_partials(a.part, bh, a.nsplit, G, warp_id(), lane);
+        if (lane == 0) s_C[warp_id()] = C;
     }
     __syncthreads();
     bool hit[2] = {false, false};
@@ -394,7 +402,22 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
         if (valid) keys[c] = __float_as_uint(sc);
         if (valid) atomicAdd(&s_hw[warp_id()][sel_key_bin(__float_as_uint(sc))], 1u);
     };
-    if (use_ring) {
+    if (a.keys_in) {
+        // keys computed by keys_kernel: copied into this CTA's slice, eight
+        // loads in flight per thread, and counted
+        const uint32_t *kin = a.keys_in + (int64_t)bh * L + c0;
+        for (int cb = tid; cb < n; cb += 8 * SEL_T) {
+            uint32_t kk[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) kk[u] = cb + u * SEL_T < n ? __ldg(kin + cb + u * SEL_T) : 0u;
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (cb + u * SEL_T < n) {
+                    keys[cb + u * SEL_T] = kk[u];
+                    atomicAdd(&s_hw[warp_id()][sel_key_bin(kk[u])], 1u);
+                }
+        }
+    } else if (use_ring) {
         for (int i = 0; i < ntile; ++i) {
             if (!mbar_wait(&s_full[i % SEL_RING], (i / SEL_RING) & 1)) {
                 if (tid == 0) report_dev_error(DEV_ERR_WAIT);
@@ -617,12 +640,78 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
     }
 }
 
-size_t select_smem_bytes(int L, int num_chunks, int G, bool keys_global, int cl)
+size_t select_smem_bytes(int L, int num_chunks, int G, bool keys_global, int cl, bool keys_pre)
 {
     // keys + chunk ids of the slice and bitmaps, then (128-byte aligned) the
-    // per-warp histograms and the logits ring
+    // per-warp histograms and the logits ring (none when the keys come ready)
     return ((select_base_bytes(L, num_chunks, keys_global, cl) + 127) & ~(size_t)127) +
-           (size_t)(SEL_T / 32) * SEL_BINS * 4 + select_ring_bytes(L, G, cl);
+           (size_t)(SEL_T / 32) * SEL_BINS * 4 + (keys_pre ? 0 : select_ring_bytes(L, G, cl));
+}
+
+// Keys of landmarks [r0, r1) of head bh, one thread per landmark, G = 4Q logits per row.
+template <int Q>
+__device__ __forceinline__ void keys_rows(const KeysArgs &k, int bh, int r0, int r1, const float *s_C)
+{
+    for (int c = r0 + (int)threadIdx.x; c < r1; c += KEYS_T) {
+        const float4 *row = reinterpret_cast<const float4 *>(k.logits + ((int64_t)bh * k.L + c) * (4 * Q));
+        float4 v[Q];
+#pragma unroll
+        for (int q = 0; q < Q; ++q) v[q] = row[q];
+        float d = -INFINITY;
+#pragma unroll
+        for (int q = 0; q < Q; ++q) {
+            d = fmaxf(fmaxf(d, v[q].x - s_C[4 * q]), v[q].y - s_C[4 * q + 1]);
+            d = fmaxf(fmaxf(d, v[q].z - s_C[4 * q + 2]), v[q].w - s_C[4 * q + 3]);
+        }
+        k.keys[(int64_t)bh * k.L + c] = __float_as_uint(__expf(d));
+    }
+}
+
+__global__ void __launch_bounds__(KEYS_T) keys_kernel(KeysArgs k)
+{
+    __shared__ float s_C[16];
+    const int bh = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int G = k.G, L = k.L;
+    pdl_launch_dependents();  // the selection may become resident; it waits for this grid
+    pdl_wait();               // the scoring kernel's logits and partials are complete
+    for (int gg = warp; gg < G; gg += KEYS_T / 32) {
+        const float C = merge_partials(k.part, bh, k.nsplit, G, gg, lane);
+        if (lane == 0) s_C[gg] = C;
+    }
+    __syncthreads();
+    const int r0 = blockIdx.x * k.rows, r1 = min(L, r0 + k.rows);
+    switch (G) {  // a row's 16-byte words all in flight at once
+    case 4: keys_rows<1>(k, bh, r0, r1, s_C); break;
+    case 8: keys_rows<2>(k, bh, r0, r1, s_C); break;
+    case 16: keys_rows<4>(k, bh, r0, r1, s_C); break;
+    default:
+        for (int c = r0 + tid; c < r1; c += KEYS_T) {
+            const float *row = k.logits + ((int64_t)bh * L + c) * G;
+            float d = -INFINITY;
+            for (int gg = 0; gg < G; ++gg) d = fmaxf(d, row[gg] - s_C[gg]);
+            k.keys[(int64_t)bh * L + c] = __float_as_uint(__expf(d));
+        }
+    }
+}
+
+int launch_keys(const KeysArgs &k, int BH, cudaStream_t stream)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((k.L + k.rows - 1) / k.rows, BH, 1);
+    cfg.blockDim = dim3(KEYS_T, 1, 1);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, keys_kernel, k);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        set_error("launch of keys_kernel failed: %s", cudaGetErrorString(e));
+        return SKV_ERR_CUDA;
+    }
+    return SKV_OK;
 }
 
 // Whether this device can schedule 16-CTA clusters of the selection kernel

@@ -25,13 +25,29 @@ __device__ __forceinline__ int sel_key_bin(uint32_t k)
 
 struct SelectArgs {
     const float *logits;          // [BH][L][G] scaled logits
-    const float2 *part;           // [BH][nsplit][G] (max, sum-exp) of the scoring splits
+    const float2 *part;           // [BH][G][nsplit] (max, sum-exp) of the scoring splits
     uint32_t *gkeys;              // [BH][L] key scratch when a slice does not fit in shared memory, else null
     const int64_t *landmark_idx;  // [BH][L] chunk id of every landmark
     int32_t *slots;               // [BH][K] in/out slot table
     int32_t *miss_slot, *miss_chunk, *miss_count;
     int G, L, K, nsplit, num_chunks;
+    // [BH][L] keys already computed by keys_kernel (long contexts), or null:
+    // the selection then computes them from the logits itself
+    const uint32_t *keys_in;
 };
+
+// keys_kernel: the selection keys of every landmark from the scoring
+// kernel's logits and split partials, spread over the whole GPU (long
+// contexts, where the selection's clusters alone would take long to read the
+// logits).  grid = (ceil(L / rows), BH), KEYS_T threads.
+constexpr int KEYS_T = 512;  // 16 warps: one per query head of a group when the partials are merged
+struct KeysArgs {
+    const float *logits;   // [BH][L][G]
+    const float2 *part;    // [BH][G][nsplit]
+    uint32_t *keys;        // [BH][L]
+    int G, L, nsplit, rows;
+};
+int launch_keys(const KeysArgs &k, int BH, cudaStream_t stream);
 
 constexpr int SEL_RING = 2;              // logits tiles in flight per CTA
 constexpr size_t SEL_SMEM_CAP = 188 * 1024;  // dynamic shared memory of a selection CTA (static ~37 KB)
@@ -58,7 +74,7 @@ __host__ __device__ inline size_t select_ring_bytes(int L, int G, int cl)
 }
 
 // Dynamic shared memory of one CTA of the selection kernel (cl CTAs per cluster).
-size_t select_smem_bytes(int L, int num_chunks, int G, bool keys_global, int cl);
+size_t select_smem_bytes(int L, int num_chunks, int G, bool keys_global, int cl, bool keys_pre = false);
 
 // Whether 16-CTA clusters of the selection kernel can be scheduled on this device.
 bool select_cluster16_ok(size_t smem);
