@@ -114,7 +114,10 @@ def test_fused_step_matches_reference_torch_class(fix):
 # ------------------------------------------------------------------ kernels one by one
 
 @pytest.mark.parametrize("G,L,K,H", [(4, 15308, 256, 3), (16, 6000, 256, 2), (1, 700, 64, 2), (4, 2000, 1000, 1),
-                                     (4, 40000, 256, 2), (16, 131072, 256, 1)])
+                                     (4, 40000, 256, 2), (16, 131072, 256, 1),
+                                     # long contexts through the keys kernel: G = 8 and a G that is
+                                     # not a multiple of 4 (scalar logit loads)
+                                     (8, 50000, 512, 2), (6, 40000, 256, 2)])
 def test_select_topk_and_slot_update(G, L, K, H):
     from shadowkv_b200 import decode as fz
     rng = np.random.default_rng(G * 1000 + L)
