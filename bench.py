@@ -257,6 +257,11 @@ def run_b200(args, world, rank, local):
         for li in range(NL):
             q_in = s_q if li == 0 else s_mid[(li - 1) % 2]
             out = (s_out if final_out is None else final_out) if li == NL - 1 else s_mid[li % 2]
+            if args.microbatch > 1 and not args.split and not heads_sharded:
+                seq_len = cache.sparse_end + cache.gen_offset + 1
+                cache.decode_step_microbatched(li, q_in, s_k, s_v, s_pos, attn.cos_sin_cache, out,
+                                               args.microbatch, q_out=s_qr, max_ctas=args.fetch_ctas)
+                continue
             qr = cache.append_select_fused(li, q_in, s_k, s_v, s_pos, attn.cos_sin_cache, q_out=s_qr)
             seq_len = cache.sparse_end + cache._gen_offset(li)
             if args.split:
@@ -447,7 +452,8 @@ def run_b200(args, world, rank, local):
                                     f"NVLink peer memory by the attention kernel)" if peer_out is not None else
                                     f"kv-head-sharded x{world} (NCCL all-gather of the attention output)")
                                    if heads_sharded else f"batch-sharded x{world}"),
-                   "l2": "flushed between timed steps (256 MB write)", "hit_rate": hit_rate},
+                   "l2": "flushed between timed steps (256 MB write)", "hit_rate": hit_rate,
+                   "microbatch": args.microbatch, "fetch_ctas": args.fetch_ctas if args.microbatch > 1 else None},
         "roofline": {"kernel": ("fetch_misses_kernel (zero-copy V gather)" if args.split else
                                 "sparse_attend_kernel (zero-copy V gather + key reconstruction + attention)"),
                      "bound": "host_link",
@@ -465,7 +471,8 @@ def run_b200(args, world, rank, local):
                 "d2h_bytes_per_step": d2h},
         "kernel_us": kernel_us,
         "graph": used_graph,
-        "gpu_launches": select_kernels(cache) * NL * args.steps + (3 if args.split else 1) * NL * args.steps,
+        "gpu_launches": (select_kernels(cache) + (3 if args.split else 1)) * NL * args.steps
+                        * (args.microbatch if args.microbatch > 1 and not args.split and not heads_sharded else 1),
         "clocks": clk.summary(),
         "wall_s": t_wall,
     }
@@ -577,6 +584,10 @@ def main():
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
                     help="--shard heads: how every rank gets all heads' attention rows")
     ap.add_argument("--batch", type=int, default=0, help="sequences per GPU (default: the config's, 1)")
+    ap.add_argument("--microbatch", type=int, default=1,
+                    help="batch slices whose selection overlaps the previous slice's value fetch")
+    ap.add_argument("--fetch-ctas", type=int, default=64,
+                    help="--microbatch: CTAs of each slice's fetch + attention (the rest run the next selection)")
     ap.add_argument("--layers", type=int, default=1,
                     help="decode layers per step (chained: each layer's output is the next one's query)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)

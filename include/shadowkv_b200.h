@@ -395,6 +395,18 @@ SKV_API int skv_prefill_build(const skv_prefill_geom *p, const void *k_roped, co
                               void *k_buf, void *v_buf, void *landmarks, int64_t *landmark_idx, int32_t *slots,
                               int64_t *position_ids, void *workspace, size_t workspace_bytes, void *stream);
 
+/* skv_decode_sparse_attention on at most max_ctas CTAs (one per SM), each
+ * taking (kv head, 128-row block) work items in strides.  With many sequences
+ * the host link stays saturated by far fewer SMs than the GPU has; the SMs
+ * left free run the next batch slice's scoring and selection meanwhile (on
+ * another, higher-priority stream). */
+SKV_API int skv_decode_sparse_attention_ctas(const skv_decode_geom *g, const void *q, const void *U,
+                                             const void *SVt, const void *cos_sin, const void *v_host,
+                                             void *k_buf, void *v_buf, const int32_t *miss_slot,
+                                             const int32_t *miss_chunk, const int32_t *miss_count,
+                                             int seq_len, void *out, int max_ctas, void *workspace,
+                                             size_t workspace_bytes, void *stream);
+
 /* ---- attention output gathered over peer memory (kv heads split over ranks)
  *
  * With the kv heads of a sequence split over `world` GPUs (one process per

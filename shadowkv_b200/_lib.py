@@ -81,6 +81,7 @@ SIGNATURES = {
     "skv_decode_attention": [ctypes.POINTER(DecodeGeom), P, P, P, c_int, P, P, c_size_t, P],
     "skv_decode_sparse_attention_workspace": [ctypes.POINTER(DecodeGeom), c_int],
     "skv_decode_sparse_attention": [ctypes.POINTER(DecodeGeom)] + [P] * 10 + [c_int, P, P, c_size_t, P],
+    "skv_decode_sparse_attention_ctas": [ctypes.POINTER(DecodeGeom)] + [P] * 10 + [c_int, P, c_int, P, c_size_t, P],
     "skv_decode_sparse_attention_gather": [ctypes.POINTER(DecodeGeom)] + [P] * 10
                                           + [c_int, ctypes.POINTER(PeerGather), P, c_size_t, P],
     "skv_prefill_workspace": [ctypes.POINTER(PrefillGeom)],

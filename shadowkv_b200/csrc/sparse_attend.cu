@@ -54,6 +54,7 @@ struct SparseAttendArgs {
     unsigned *ticket;              // [BH], zero between launches
     __nv_bfloat16 *out;            // [B][Hq][128] (world == 0)
     int Hkv, G, K, rank, ctx, num_chunks, buf_len, sparse_start, seq_len, nblk;
+    int total;                     // work items: nblk * B * Hkv
     int rope_mode, cs_stride, cs_rows;
     float scale;
     // world > 0: the output rows go to every rank's landing buffer
@@ -97,16 +98,27 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
     __shared__ unsigned s_last;
     __shared__ __align__(8) uint64_t s_bar;  // completion of the bulk copies of the device-memory rows
 
-    // 1-D grid, the blocks that hold selected slots first: with more blocks
-    // than SMs, the blocks left for a second wave are the light ones (prefix
-    // and generated rows only), not ones that wait on the host link
+    if (threadIdx.x == 0) {
+        mbar_init(&s_bar, 1);
+        mbar_fence_init();
+    }
+    pdl_wait();  // the selection (and the scoring before it) are complete from here on
+
+    // Work items: (kv head, 128-row block), the blocks that hold selected slots
+    // first -- with more items than CTAs the ones left for later are the light
+    // ones (prefix and generated rows only), not ones that wait on the host
+    // link.  One item per CTA for a full grid; a grid of fewer CTAs (leaving
+    // SMs to other work while the link is busy) walks the items in strides.
+    unsigned iter = 0;
+    for (int item = blockIdx.x; item < a.total; item += gridDim.x, ++iter) {
+    __syncthreads();  // the previous item's shared memory is no longer read
     int blk, bh;
     {
         const int blo = a.sparse_start / SA_ROWS;
         const int nheavy = min(a.nblk, ceil_div(a.sparse_start + 8 * a.K, SA_ROWS)) - blo;
         const int nlight = a.nblk - nheavy;
-        const int L = blockIdx.x;
-        const int BHn = gridDim.x / a.nblk;
+        const int L = item;
+        const int BHn = a.total / a.nblk;
         if (L < BHn * nheavy) {
             bh = L / nheavy;
             blk = blo + L % nheavy;
@@ -126,16 +138,11 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
     const bool has_slots = row0 < sparse_end && row0 + SA_ROWS > a.sparse_start;
     const int ppr = a.rank / 8;  // 16-byte pieces per U / SV^T row
 
-    if (tid == 0) {
-        mbar_init(&s_bar, 1);
-        mbar_fence_init();
-    }
     if (tid < SA_GROUPS) {
         s_kind[tid] = 0;
         s_chunk[tid] = -1;
     }
     if (tid == 0) s_any_miss = 0;
-    pdl_wait();  // the selection (and the scoring before it) are complete from here on
     __syncthreads();
 
     // 2) query rows of the group (rows >= G are zero) and the missed slots of
@@ -250,7 +257,7 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
         }
     }
     // bounded waits: a copy that never lands is reported, it does not hang the GPU
-    if (!mbar_wait(&s_bar, 0)) {
+    if (!mbar_wait(&s_bar, iter & 1u)) {
         if (lane == 0) report_dev_error(DEV_ERR_WAIT);
     }
     __syncthreads();
@@ -461,7 +468,7 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
     __syncthreads();
     if (tid == 0) s_last = atomicAdd(&a.ticket[bh], 1u) == (unsigned)(a.nblk - 1) ? 1u : 0u;
     __syncthreads();
-    if (!s_last) return;
+    if (s_last) {
     __threadfence();
     // merge of the head's nblk partial outputs: each thread sums 4 columns of
     // one query row over the partials.  Its first row's partials (up to
@@ -469,7 +476,7 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
     // warp w turns the pairs of heads w, w + 8 into weights
     // w_j = exp(m_j - M) / L meanwhile (the tiles' shared memory is free).
     {
-        constexpr int SA_MERGE_REGS = 24;
+        constexpr int SA_MERGE_REGS = 16;
         const int nml = a.nblk * G;
         float2 *s_ml = reinterpret_cast<float2 *>(smem_raw);  // [nblk][G]
         float *s_w = reinterpret_cast<float *>(s_ml + nml);  // [nblk][G]
@@ -524,7 +531,7 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
                 *reinterpret_cast<uint2 *>(a.out + ((int64_t)bh * G + gg) * 128 + d) = pk;
             } else {
                 const int b = bh / a.Hkv, h = bh % a.Hkv;
-                const int64_t o = (((int64_t)(*a.epoch & 1u) * (gridDim.x / a.nblk / a.Hkv) + b) * a.q_heads_total +
+                const int64_t o = (((int64_t)(*a.epoch & 1u) * (a.total / a.nblk / a.Hkv) + b) * a.q_heads_total +
                                    a.q_head0 + h * G + gg) * 128 + d;
                 for (int r = 0; r < a.world; ++r) *reinterpret_cast<uint2 *>(a.landing[r] + o) = pk;
             }
@@ -538,6 +545,8 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
             for (int r = 0; r < a.world; ++r) atomicAdd_system(a.counter[r], 1u);
     }
     if (tid == 0) a.ticket[bh] = 0;  // ready for the next launch
+    }  // the head's last block
+    }  // work items
 }
 
 // Peer block layout: arrival counter, this rank's epoch, landing buffer.
@@ -610,7 +619,7 @@ static int launch_sparse_attention(const skv_decode_geom *g, const void *q, cons
                                    const int32_t *miss_slot, const int32_t *miss_chunk,
                                    const int32_t *miss_count, int seq_len, void *out,
                                    const skv_peer_gather *pg, void *workspace, size_t workspace_bytes,
-                                   void *stream)
+                                   void *stream, int max_ctas = 0)
 {
     SKV_CHECK_ARG(g && q && U && SVt && cos_sin && k_buf && v_buf && miss_slot && miss_chunk && miss_count &&
                       (out || pg) && workspace,
@@ -697,6 +706,7 @@ static int launch_sparse_attention(const skv_decode_geom *g, const void *q, cons
     a.sparse_start = g->sparse_start;
     a.seq_len = seq_len;
     a.nblk = nblk;
+    a.total = nblk * BH;
     a.rope_mode = g->rope_mode;
     a.cs_stride = g->cos_sin_stride;
     a.cs_rows = g->cos_sin_rows;
@@ -708,7 +718,7 @@ static int launch_sparse_attention(const skv_decode_geom *g, const void *q, cons
     st = ensure_smem_attr(fn, smem, "sparse_attend_kernel");
     if (st) return st;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(nblk * BH, 1, 1);
+    cfg.gridDim = dim3(max_ctas > 0 && max_ctas < nblk * BH ? max_ctas : nblk * BH, 1, 1);
     cfg.blockDim = dim3(SA_THREADS, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = (cudaStream_t)stream;
@@ -739,6 +749,17 @@ int skv_decode_sparse_attention(const skv_decode_geom *g, const void *q, const v
     SKV_CHECK_ARG(out != nullptr, "null pointer argument");
     return launch_sparse_attention(g, q, U, SVt, cos_sin, v_host, k_buf, v_buf, miss_slot, miss_chunk, miss_count,
                                    seq_len, out, nullptr, workspace, workspace_bytes, stream);
+}
+
+int skv_decode_sparse_attention_ctas(const skv_decode_geom *g, const void *q, const void *U, const void *SVt,
+                                     const void *cos_sin, const void *v_host, void *k_buf, void *v_buf,
+                                     const int32_t *miss_slot, const int32_t *miss_chunk,
+                                     const int32_t *miss_count, int seq_len, void *out, int max_ctas,
+                                     void *workspace, size_t workspace_bytes, void *stream)
+{
+    SKV_CHECK_ARG(out != nullptr && max_ctas >= 1, "null output or max_ctas < 1");
+    return launch_sparse_attention(g, q, U, SVt, cos_sin, v_host, k_buf, v_buf, miss_slot, miss_chunk, miss_count,
+                                   seq_len, out, nullptr, workspace, workspace_bytes, stream, max_ctas);
 }
 
 int skv_decode_sparse_attention_gather(const skv_decode_geom *g, const void *q, const void *U, const void *SVt,

@@ -172,18 +172,22 @@ def attention(geom: Geometry, ws: DecodeWorkspace, q: torch.Tensor, k_buf: torch
 
 def sparse_attention(geom: Geometry, ws: DecodeWorkspace, q: torch.Tensor, U: torch.Tensor, SVt: torch.Tensor,
                      cos_sin: torch.Tensor, v_host: torch.Tensor, k_buf: torch.Tensor, v_buf: torch.Tensor,
-                     seq_len: int, out: torch.Tensor, stream=None) -> torch.Tensor:
-    """``gather_values`` + ``reconstruct_keys`` + ``attention`` in one launch (after a selection).
+                     seq_len: int, out: torch.Tensor, stream=None, max_ctas: int = 0) -> torch.Tensor:
+    """``gather_values`` + ``reconstruct_keys`` + ``attention`` in one launch (after a selection);
+    ``max_ctas`` > 0 caps the grid (work items walked in strides).
 
     ``out`` may be a page-locked CPU tensor: the kernel writes the output over
     the host link (no device-to-host copy after the launch)."""
     if v_host.is_cuda or not v_host.is_pinned() or v_host.dtype != torch.bfloat16 or not v_host.is_contiguous():
         raise RuntimeError("v_host must be a contiguous pinned CPU bf16 tensor")
     g = geom.c()
-    check(lib.skv_decode_sparse_attention(
-        ctypes.byref(g), _req(q, "q", torch.bfloat16), _req(U, "U", torch.bfloat16), _req(SVt, "SVt", torch.bfloat16),
-        _req(cos_sin, "cos_sin", torch.bfloat16), v_host.data_ptr(), _req(k_buf, "k_buf", torch.bfloat16),
-        _req(v_buf, "v_buf", torch.bfloat16), ws.miss_slot.data_ptr(), ws.miss_chunk.data_ptr(),
-        ws.miss_count.data_ptr(), int(seq_len), _req_out(out), ws.sparse_ws.data_ptr(),
-        ws.sparse_bytes, _stream(stream)), "skv_decode_sparse_attention")
+    args = [ctypes.byref(g), _req(q, "q", torch.bfloat16), _req(U, "U", torch.bfloat16),
+            _req(SVt, "SVt", torch.bfloat16), _req(cos_sin, "cos_sin", torch.bfloat16), v_host.data_ptr(),
+            _req(k_buf, "k_buf", torch.bfloat16), _req(v_buf, "v_buf", torch.bfloat16), ws.miss_slot.data_ptr(),
+            ws.miss_chunk.data_ptr(), ws.miss_count.data_ptr(), int(seq_len), _req_out(out)]
+    tail = [ws.sparse_ws.data_ptr(), ws.sparse_bytes, _stream(stream)]
+    if max_ctas:
+        check(lib.skv_decode_sparse_attention_ctas(*args, int(max_ctas), *tail), "skv_decode_sparse_attention_ctas")
+    else:
+        check(lib.skv_decode_sparse_attention(*args, *tail), "skv_decode_sparse_attention")
     return out

@@ -453,6 +453,68 @@ class ShadowKVCache_CPU:
                                       cos_sin_cache, self.v_cache_cpu[layer_idx], self.k_cache_buffer[layer_idx],
                                       self.v_cache_buffer[layer_idx], seq_len, out)
 
+    def decode_step_microbatched(self, layer_idx, query_states, key_states, value_states, positions, cos_sin_cache,
+                                 out, parts: int, q_out=None, max_ctas: int = 64):
+        """The fused step (``append_select_fused`` + ``sparse_attention_fused``) in ``parts`` slices of
+        the batch: slice i's scoring and selection run on a high-priority stream while slice i-1's
+        value fetch, capped at ``max_ctas`` CTAs (plenty to keep the host link busy), holds the
+        others -- the link no longer waits for the whole batch's selection.  The fetches of
+        consecutive slices alternate between two streams, so one's tail overlaps the next one's
+        start.  ``out`` [B, Hq, D]."""
+        B, Hq, Hk, D = self.batch_size, self.num_attention_heads, self.num_key_value_heads, self.head_dim
+        if parts < 1 or B % parts:
+            raise RuntimeError(f"batch {B} does not split into {parts} equal parts")
+        g = self.fused_geometry(cos_sin_cache)
+        row = self.sparse_end + self.gen_offset
+        if row >= self.buf_len:
+            raise RuntimeError("generated-token region of the K/V buffer is full")
+        mb = B // parts
+        key = (parts, mb)
+        if getattr(self, "_mb_state", None) is None or self._mb_state[0] != key:
+            import dataclasses
+            gp = dataclasses.replace(g, batch=mb)
+            self._mb_state = (key, gp, [fused.DecodeWorkspace(gp, self.device) for _ in range(parts)],
+                              torch.cuda.Stream(device=self.device, priority=-1),
+                              [torch.cuda.Stream(device=self.device, priority=0) for _ in range(2)])
+        _, gp, wss, hi, los = self._mb_state
+        if q_out is None:
+            q_out = torch.empty(B, Hq, 1, D, dtype=self.dtype, device=self.device)
+        q = query_states.reshape(B, Hq, D)
+        k = key_states.reshape(B, Hk, D)
+        v = value_states.reshape(B, Hk, D)
+        pos = positions.reshape(B)
+        qo = q_out.reshape(B, Hq, D)
+        last = layer_idx == self.num_layers - 1
+        seq_len = self.sparse_end + (self.gen_offset + 1)
+        cur = torch.cuda.current_stream(self.device)
+        hi.wait_stream(cur)
+        for lo in los:
+            lo.wait_stream(cur)
+        for i in range(parts):
+            sl = slice(i * mb, (i + 1) * mb)
+            lo = los[i % 2]  # consecutive slices' fetches may overlap: the link never waits for a tail
+            with torch.cuda.stream(hi):
+                fused.append_select(gp, wss[i], q[sl], k[sl], v[sl], pos[sl], cos_sin_cache, qo[sl],
+                                    self.k_cache_buffer[layer_idx][sl], self.v_cache_buffer[layer_idx][sl], row,
+                                    self.k_landmark[layer_idx][sl], self.k_landmark_idx[layer_idx][sl],
+                                    self.slots[layer_idx][sl], stream=hi)
+                ev = torch.cuda.Event()
+                ev.record(hi)
+            with torch.cuda.stream(lo):
+                lo.wait_event(ev)
+                fused.sparse_attention(gp, wss[i], qo[sl], self.U[layer_idx][sl], self.SV[layer_idx][sl],
+                                       cos_sin_cache, self.v_cache_cpu[layer_idx][sl],
+                                       self.k_cache_buffer[layer_idx][sl], self.v_cache_buffer[layer_idx][sl],
+                                       seq_len, out[sl], stream=lo, max_ctas=max_ctas)
+        cur.wait_stream(hi)
+        for lo in los:
+            cur.wait_stream(lo)
+        self.incoming_q_len = 1
+        if last:
+            self.kv_offset += 1
+            self.gen_offset += 1
+        return out
+
     def sparse_attention_gather(self, layer_idx, query_states, seq_len, cos_sin_cache, peer):
         """``sparse_attention_fused`` with the output rows sent to every rank's landing buffer
         (kv heads split over ranks; ``peer`` is a ``peer.PeerOutput``, ``peer.finish`` ends the step)."""

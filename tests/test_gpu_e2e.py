@@ -289,3 +289,58 @@ def test_sparse_attention_output_into_pinned_host_memory():
     with pytest.raises(RuntimeError):
         from shadowkv_b200 import decode as fz
         fz._req_out(torch.empty(4, dtype=torch.bfloat16))  # pageable host memory is refused
+
+
+def _tiny_batch_layer(seed, batch=4):
+    from shadowkv_b200 import workload
+    cfg = copy.deepcopy(workload.CONFIGS["tiny"])
+    cfg.batch = batch
+    return workload.Layer(cfg, device=DEV, seed=seed)
+
+
+def test_sparse_attention_on_fewer_ctas_matches_full_grid():
+    """The fused attention with its grid capped (CTAs walking the work items in
+    strides) gives the same bits as one CTA per item."""
+    outs = []
+    for ctas in (0, 3):
+        layer = _tiny_batch_layer(17)
+        c, attn = layer.cache, layer.attn
+        torch.manual_seed(4)
+        q, k, v = layer.next_inputs()
+        pos = torch.full((4, 1), c.sparse_end + 300, dtype=torch.int64, device=DEV)
+        g = c.fused_geometry(attn.cos_sin_cache)
+        qr = c.append_select_fused(0, q, k, v, pos, attn.cos_sin_cache)
+        from shadowkv_b200 import decode as fz
+        out = torch.empty(4, g.q_heads, 128, dtype=torch.bfloat16, device=DEV)
+        fz.sparse_attention(g, c._fused_ws, qr.reshape(4, g.q_heads, 128), c.U[0], c.SV[0], attn.cos_sin_cache,
+                            c.v_cache_cpu[0], c.k_cache_buffer[0], c.v_cache_buffer[0], c.sparse_end + 1, out,
+                            max_ctas=ctas)
+        torch.cuda.synchronize()
+        outs.append((bits(out), bits(c.k_cache_buffer[0]), bits(c.v_cache_buffer[0])))
+        del layer
+    for x, y in zip(*outs):
+        assert np.array_equal(x, y)
+
+
+def test_microbatched_step_matches_whole_batch():
+    """The step in batch slices (selection of slice i on a high-priority stream
+    beside slice i-1's capped fetch) equals the whole-batch step."""
+    res = []
+    for parts in (1, 2):
+        layer = _tiny_batch_layer(23)
+        c, attn = layer.cache, layer.attn
+        torch.manual_seed(6)
+        q, k, v = layer.next_inputs()
+        pos = torch.full((4, 1), c.sparse_end + 200, dtype=torch.int64, device=DEV)
+        out = torch.empty(4, c.num_attention_heads, 128, dtype=torch.bfloat16, device=DEV)
+        c.fused_geometry(attn.cos_sin_cache)
+        if parts == 1:
+            qr = c.append_select_fused(0, q, k, v, pos, attn.cos_sin_cache)
+            c.sparse_attention_fused(0, qr, c.sparse_end + c._gen_offset(0), attn.cos_sin_cache, out=out)
+        else:
+            c.decode_step_microbatched(0, q, k, v, pos, attn.cos_sin_cache, out, parts, max_ctas=5)
+        torch.cuda.synchronize()
+        res.append((bits(out), c.slots[0].cpu().numpy().copy()))
+        del layer
+    assert np.array_equal(res[0][1], res[1][1])
+    assert np.array_equal(res[0][0], res[1][0])
