@@ -461,7 +461,7 @@ def run_b200(args, world, rank, local):
                      "frac": link_achieved / link_peak if link_peak else None,
                      # sysmem bytes read per launch in the ncu capture of this workload
                      # (profiles/sparse_attend_kernel_config1.md): equal to the missed bytes
-                     "traffic": (4.098e6 if cfg.name == "config1" and not args.split else None),
+                     "traffic": (4.080e6 if cfg.name == "config1" and not args.split and B == 1 else None),
                      "traffic_kind": "sysmem (host link) bytes read per launch, ncu",
                      "peak_kind": "measured in-run: pinned H2D copy-engine bandwidth"},
         "step_roofline": {"t_roof_us": t_roof * 1e6, "t_step_us": ms_step * 1e3,
