@@ -67,10 +67,24 @@ class ShadowAttention:
         out = kv.attention(layer_idx, query_states, key_states.shape[2])
         return out.view(out.shape[0], 1, out.shape[1], out.shape[2])
 
-    def decode_fused(self, query_states, key_states, value_states, position_ids, layer_idx):
+    def decode_fused(self, query_states, key_states, value_states, position_ids, layer_idx, microbatch=None):
         """Same step on the fused kernels (slot-stable reuse cache): scoring +
-        selection, then one launch for value fetch, key reconstruction and attention."""
+        selection, then one launch for value fetch, key reconstruction and attention.
+
+        ``microbatch``: batch slices whose selection overlaps the previous slice's
+        fetch (``decode_step_microbatched``); ``None`` picks min(8, B // 2) slices
+        from 8 sequences up and one slice below."""
         kv = self.kv_cache
+        B = kv.batch_size
+        parts = microbatch if microbatch is not None else (min(8, B // 2) if B >= 8 else 1)
+        while parts > 1 and B % parts:
+            parts -= 1
+        if parts > 1:
+            out = torch.empty(B, kv.num_attention_heads, kv.head_dim, dtype=kv.dtype, device=kv.device)
+            kv.decode_step_microbatched(layer_idx, query_states.contiguous(), key_states.contiguous(),
+                                        value_states.contiguous(), position_ids.contiguous(), self.cos_sin_cache,
+                                        out, parts)
+            return out.view(B, 1, out.shape[1], out.shape[2])
         query_states = kv.append_select_fused(layer_idx, query_states.contiguous(), key_states.contiguous(),
                                               value_states.contiguous(), position_ids.contiguous(),
                                               self.cos_sin_cache)

@@ -344,3 +344,21 @@ def test_microbatched_step_matches_whole_batch():
         del layer
     assert np.array_equal(res[0][1], res[1][1])
     assert np.array_equal(res[0][0], res[1][0])
+
+
+def test_decode_fused_picks_microbatching_at_large_batch():
+    """ShadowAttention.decode_fused at 8 sequences runs the step in 4 slices and
+    returns the same bits as the single-slice step."""
+    res = []
+    for mb in (1, None):
+        layer = _tiny_batch_layer(29, batch=8)
+        torch.manual_seed(8)
+        q, k, v = layer.next_inputs()
+        pos = torch.full((8, 1), layer.cache.sparse_end + 100, dtype=torch.int64, device=DEV)
+        out = layer.attn.decode_fused(q, k, v, pos, 0, microbatch=mb)
+        torch.cuda.synchronize()
+        res.append((bits(out), layer.cache.slots[0].cpu().numpy().copy(), getattr(layer.cache, "_mb_state", None)))
+        del layer
+    assert res[0][2] is None and res[1][2] is not None and res[1][2][0] == (4, 2)
+    assert np.array_equal(res[0][1], res[1][1])
+    assert np.array_equal(res[0][0], res[1][0])
