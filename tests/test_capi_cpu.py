@@ -104,3 +104,15 @@ def test_prefill_geometry_checks_are_pure_host():
                 dict(q_heads=7)):            # q heads not a multiple of kv heads
         g = dict(ok, **bad)
         assert _lib.lib.skv_prefill_workspace(ctypes.byref(_lib.PrefillGeom(**g))) == 0, bad
+
+
+def test_peer_output_description_is_built_on_the_host():
+    from shadowkv_b200.peer import PeerOutput
+    p = PeerOutput(batch=2, q_heads_total=32, q_head0=16, merges_per_step=16, rank=1, blocks=[0x1000, 0x2000],
+                   own_block=0)  # own_block 0: nothing to free
+    assert (p.pg.world, p.pg.rank, p.pg.q_head0, p.pg.q_heads_total, p.pg.merges_per_step) == (2, 1, 16, 32, 16)
+    assert list(p.pg.block[:2]) == [0x1000, 0x2000] and not any(p.pg.block[2:])
+    with pytest.raises(RuntimeError):
+        PeerOutput(1, 8, 0, 2, 0, [0x1000] * 9, 0)  # more ranks than the library supports
+    with pytest.raises(RuntimeError):
+        PeerOutput(1, 8, 0, 2, 0, [], 0)
