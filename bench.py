@@ -188,6 +188,9 @@ def run_b200(args, world, rank, local):
     heads_sharded = args.shard == "heads" and world > 1
     if heads_sharded and NL > 1:
         raise SystemExit("--layers > 1 runs with --shard batch")
+    if args.microbatch is None:
+        from shadowkv_b200.kvcache import auto_microbatch
+        args.microbatch = 1 if heads_sharded or args.split else auto_microbatch(cfg.batch)
     full_cfg = cfg
     if heads_sharded:
         # rank r owns kv heads [r*Hkv/N, (r+1)*Hkv/N) and their GQA groups; inside the step
@@ -584,8 +587,9 @@ def main():
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
                     help="--shard heads: how every rank gets all heads' attention rows")
     ap.add_argument("--batch", type=int, default=0, help="sequences per GPU (default: the config's, 1)")
-    ap.add_argument("--microbatch", type=int, default=1,
-                    help="batch slices whose selection overlaps the previous slice's value fetch")
+    ap.add_argument("--microbatch", type=int, default=None,
+                    help="batch slices whose selection overlaps the previous slice's value fetch "
+                         "(default: as ShadowAttention.decode_fused picks, 1 below 8 sequences per GPU)")
     ap.add_argument("--fetch-ctas", type=int, default=64,
                     help="--microbatch: CTAs of each slice's fetch + attention (the rest run the next selection)")
     ap.add_argument("--layers", type=int, default=1,

@@ -16,7 +16,7 @@ from __future__ import annotations
 
 import torch
 
-from .kvcache import ShadowKVCache_CPU
+from .kvcache import ShadowKVCache_CPU, auto_microbatch
 from .tensor_op import apply_rotary_pos_emb_cuda
 
 
@@ -76,7 +76,7 @@ class ShadowAttention:
         from 8 sequences up and one slice below."""
         kv = self.kv_cache
         B = kv.batch_size
-        parts = microbatch if microbatch is not None else (min(8, B // 2) if B >= 8 else 1)
+        parts = microbatch if microbatch is not None else auto_microbatch(B)
         while parts > 1 and B % parts:
             parts -= 1
         if parts > 1:

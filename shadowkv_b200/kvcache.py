@@ -33,6 +33,15 @@ from . import shadowkv
 from .tensor_op import batch_gather_gemm_rotary_pos_emb_cuda
 
 
+def auto_microbatch(batch: int) -> int:
+    """Slices of ``decode_step_microbatched`` for a batch: one below 8 sequences (the selection
+    is short next to the fetch), else min(8, batch // 2) lowered to a divisor of the batch."""
+    parts = min(8, batch // 2) if batch >= 8 else 1
+    while parts > 1 and batch % parts:
+        parts -= 1
+    return parts
+
+
 class ShadowKVCache_CPU:
     """ShadowKV cache with host-offloaded values (reference models/kvcache/shadow.py:301)."""
 

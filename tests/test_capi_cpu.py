@@ -116,3 +116,11 @@ def test_peer_output_description_is_built_on_the_host():
         PeerOutput(1, 8, 0, 2, 0, [0x1000] * 9, 0)  # more ranks than the library supports
     with pytest.raises(RuntimeError):
         PeerOutput(1, 8, 0, 2, 0, [], 0)
+
+
+def test_auto_microbatch_divides_the_batch():
+    from shadowkv_b200.kvcache import auto_microbatch
+    assert [auto_microbatch(b) for b in (1, 2, 7)] == [1, 1, 1]  # short selections: one slice
+    assert [auto_microbatch(b) for b in (8, 12, 16, 32, 48)] == [4, 6, 8, 8, 8]
+    for b in range(1, 130):
+        assert b % auto_microbatch(b) == 0 and 1 <= auto_microbatch(b) <= 8
