@@ -152,7 +152,7 @@ def link_bandwidth_gbs(nbytes=256 << 20, reps=5) -> float:
 
 
 def algorithmic_bytes(cache, misses: int, seq_len: int):
-    """HBM and host-link bytes of one step (per-unit figures of the roofline model)."""
+    """HBM and host-link bytes of one layer of a step (per-unit figures of the roofline model)."""
     B, H, D = cache.batch_size, cache.num_key_value_heads, cache.head_dim
     L = cache.k_landmark.shape[-2]
     r = cache.rank
@@ -377,11 +377,11 @@ def run_b200(args, world, rank, local):
     value = tokens / (ms_step_max / 1e3)
     misses = statistics.mean(misses_all)
     hit_rate = 1.0 - misses / (B * Hkv * cache.select_sets)
-    hbm_b, host_b = algorithmic_bytes(cache, misses, statistics.mean(seqlens))
-    hbm_b, host_b = hbm_b * NL, host_b * NL  # the misses of the last layer stand for every layer
+    hbm_1, host_1 = algorithmic_bytes(cache, misses, statistics.mean(seqlens))  # one layer, one launch
+    hbm_b, host_b = hbm_1 * NL, host_1 * NL  # the misses of layer 0 stand for every layer of the step
     t_roof = max(hbm_b / (hbm_peak * 1e9), host_b / (link_peak * 1e9))
-    fetch_avg = statistics.mean(fetch_ms)
-    link_achieved = host_b / (fetch_avg * 1e-3) / 1e9 if fetch_avg > 0 else 0.0
+    fetch_avg = statistics.mean(fetch_ms)  # one launch of the fetching kernel on layer 0
+    link_achieved = host_1 / (fetch_avg * 1e-3) / 1e9 if fetch_avg > 0 else 0.0
 
     # ---- e2e: inputs copied from pinned host memory, the output brought back, every step
     # per step: the inputs packed in one pinned host buffer (q, k, v, position)
