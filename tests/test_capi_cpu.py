@@ -124,3 +124,26 @@ def test_auto_microbatch_divides_the_batch():
     assert [auto_microbatch(b) for b in (8, 12, 16, 32, 48)] == [4, 6, 8, 8, 8]
     for b in range(1, 130):
         assert b % auto_microbatch(b) == 0 and 1 <= auto_microbatch(b) <= 8
+
+
+def test_every_entry_point_rejects_null_arguments_before_launching():
+    """All-null / all-zero arguments give a non-zero status and a message, never a crash."""
+    from shadowkv_b200 import _lib
+    lib = _lib.lib
+    special = {"skv_last_error", "skv_version",
+               "skv_device_errors",          # null outputs are allowed (the counts are only reset)
+               "skv_peer_free"}              # freeing null is a no-op, as free()
+    checked = 0
+    for name, args in _lib.SIGNATURES.items():
+        if name in special or name in _lib._RET or not args:
+            continue
+        vals = [0 if a in (ctypes.c_int, ctypes.c_size_t) else 0.0 if a is ctypes.c_float else None for a in args]
+        rc = getattr(lib, name)(*vals)
+        if name == "skv_decode_select_kernels":
+            assert rc == 0  # a kernel count: 0 = not a valid geometry
+        else:
+            assert rc == 1, (name, rc, lib.skv_last_error())
+            assert lib.skv_last_error(), name
+        checked += 1
+    assert checked >= 30
+    assert lib.skv_peer_free(None) == 0
