@@ -147,3 +147,27 @@ def test_every_entry_point_rejects_null_arguments_before_launching():
         checked += 1
     assert checked >= 30
     assert lib.skv_peer_free(None) == 0
+
+
+def test_last_error_is_per_host_thread():
+    """Calls from several host threads: each thread reads its own last error."""
+    import threading
+    from shadowkv_b200._lib import lib
+    gate = threading.Barrier(2)
+    seen = {}
+
+    def caller(tag):
+        if tag == "null":
+            rc = lib.skv_reorder_keys_and_compute_offsets(None, None, None, None, 1, 8, 256, None)
+        else:
+            rc = lib.skv_reorder_keys_and_compute_offsets(8, 8, 8, 8, 1, 8, 2048, None)
+        gate.wait()  # both errors are set before either thread reads
+        seen[tag] = (rc, lib.skv_last_error())
+
+    ts = [threading.Thread(target=caller, args=(t,)) for t in ("null", "map")]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    assert seen["null"][0] == 1 and b"null" in seen["null"][1]
+    assert seen["map"][0] == 2 and b"map_size" in seen["map"][1]
