@@ -171,3 +171,60 @@ def test_last_error_is_per_host_thread():
         t.join()
     assert seen["null"][0] == 1 and b"null" in seen["null"][1]
     assert seen["map"][0] == 2 and b"map_size" in seen["map"][1]
+
+
+C_HOST = r"""
+#include <stdio.h>
+#include <string.h>
+#include "shadowkv_b200.h"
+int main(void) {
+    skv_decode_geom g;
+    skv_prefill_geom p;
+    memset(&g, 0, sizeof g);
+    g.batch = 1; g.kv_heads = 8; g.q_heads = 32; g.head_dim = 128; g.rank = 160; g.chunk_size = 8;
+    g.select_sets = 256; g.num_landmarks = 15308; g.num_chunks = 15360; g.ctx_len = 122880;
+    g.buf_len = 2720; g.sparse_start = 416; g.rope_mode = 0; g.cos_sin_stride = 128;
+    g.cos_sin_rows = 124928; g.scale = 0.08838834764831845f;
+    memset(&p, 0, sizeof p);
+    p.batch = 1; p.kv_heads = 8; p.q_heads = 32; p.tokens = 122880; p.chunks = 15356;
+    p.outlier_chunk = 48; p.select_sets = 256; p.buf_len = 2720; p.host_chunks = 15360;
+    int st = skv_reorder_keys_and_compute_offsets(NULL, NULL, NULL, NULL, 1, 8, 256, NULL);
+    printf("%d %zu %zu %zu %zu %d %s\n", skv_version(), skv_decode_select_workspace(&g),
+           skv_decode_sparse_attention_workspace(&g, 2465), skv_prefill_workspace(&p),
+           skv_peer_block_bytes(32, 32), st, skv_last_error());
+    return 0;
+}
+"""
+
+
+def test_c_host_program_uses_the_header_and_library(tmp_path):
+    """The boundary from plain C: the header compiles as C99 (-pedantic, no warnings), the
+    program links against the library, and its host-side answers equal the ctypes binding's."""
+    import shutil
+    import subprocess
+    from shadowkv_b200 import _lib
+    from shadowkv_b200.decode import Geometry
+    if shutil.which("gcc") is None:
+        pytest.skip("no C compiler")
+    src = tmp_path / "host.c"
+    src.write_text(C_HOST)
+    exe = tmp_path / "host"
+    libdir = os.path.dirname(_lib.LIB_PATH)
+    build = subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror",
+                            "-I", os.path.join(ROOT, "include"), str(src), "-L", libdir, "-lshadowkv_b200",
+                            f"-Wl,-rpath,{libdir}", "-o", str(exe)], capture_output=True, text=True)
+    assert build.returncode == 0, build.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert run.returncode == 0, run.stderr
+    f = run.stdout.split(maxsplit=6)
+    g = Geometry(batch=1, kv_heads=8, q_heads=32, rank=160, select_sets=256, num_landmarks=15308,
+                 num_chunks=15360, ctx_len=122880, buf_len=2720, sparse_start=416, cos_sin_rows=124928).c()
+    pg = _lib.PrefillGeom(batch=1, kv_heads=8, q_heads=32, tokens=122880, chunks=15356, outlier_chunk=48,
+                          select_sets=256, buf_len=2720, host_chunks=15360)
+    lib = _lib.lib
+    assert int(f[0]) == lib.skv_version()
+    assert int(f[1]) == lib.skv_decode_select_workspace(ctypes.byref(g)) > 0
+    assert int(f[2]) == lib.skv_decode_sparse_attention_workspace(ctypes.byref(g), 2465) > 0
+    assert int(f[3]) == lib.skv_prefill_workspace(ctypes.byref(pg)) > 0
+    assert int(f[4]) == lib.skv_peer_block_bytes(32, 32) > 0
+    assert int(f[5]) == 1 and "null" in f[6]
