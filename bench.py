@@ -488,6 +488,61 @@ def run_b200(args, world, rank, local):
     return res
 
 
+def run_kat(args):
+    """The reference's own benchmark of the reuse-cache copy, on the drop-in bindings.
+
+    kernels/test_cached_gather_copy.cu:50-61,224-300,356-362,479-525: 192 (sequence,
+    head) blocks of 256 chunk slots over a 128K-token page-locked value store per
+    block, 154 of the 256 chunks kept from the previous selection; the reorder runs
+    before each copy, CUDA events bracket the copy alone (3 warm-up + 10 timed
+    iterations), and the reported bandwidth counts all 256 chunks of every block
+    (GiB/s), as the reference prints it.  The link figure counts the missed
+    chunks only."""
+    import numpy as np
+    from shadowkv_b200 import shadowkv as skv
+    nb, m, hits, cpu_chunks = 24 * 8, 256, 154, 128 * 1024 // 8
+    rng = np.random.default_rng(12345)
+    keys = np.empty((nb, m), np.int64)
+    query = np.empty((nb, m), np.int64)
+    for b in range(nb):
+        k = np.sort(rng.choice(cpu_chunks, m, replace=False))
+        fresh = rng.choice(np.setdiff1d(np.arange(cpu_chunks), k), m - hits, replace=False)
+        keys[b], query[b] = k, np.concatenate([k[rng.choice(m, hits, replace=False)], fresh])
+    values = torch.empty(nb * cpu_chunks * 1024, dtype=torch.bfloat16, pin_memory=True)  # 6.4 GB
+    stride = m * 8 * 128
+    buf = torch.zeros(nb * stride, dtype=torch.bfloat16, device="cuda")
+    temp = torch.zeros(1, dtype=torch.bfloat16, device="cuda")  # unused by this library
+    keys_d = torch.from_numpy(keys).cuda()
+    query_d = torch.from_numpy(query).cuda()
+    cached = torch.empty_like(keys_d)
+    offsets = torch.empty(nb * m, dtype=torch.int32, device="cuda")
+    cnts = torch.empty(nb, dtype=torch.int32, device="cuda")
+    signals = torch.zeros(nb, dtype=torch.int32, device="cuda")
+    copy_ms, reorder_ms = [], []
+    warmup, iters = max(3, args.warmup), 10
+    for i in range(warmup + iters):
+        cached.copy_(keys_d)
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        evs[0].record()
+        skv.reorder_keys_and_compute_offsets(cached, query_d, offsets, cnts, 24, 8, m)
+        evs[1].record()
+        skv.gather_copy_with_offsets(values, buf, temp, offsets, cnts, signals, 24, 8, cpu_chunks * 1024,
+                                     m * 1024, 0, stride, m)
+        evs[2].record()
+        evs[2].synchronize()
+        if i >= warmup:
+            reorder_ms.append(evs[0].elapsed_time(evs[1]))
+            copy_ms.append(evs[1].elapsed_time(evs[2]))
+    assert int(cnts.sum().item()) == nb * hits
+    t = statistics.mean(copy_ms) * 1e-3
+    return {"metric": "reuse-cache copy bandwidth (reference test_cached_gather_copy.cu)",
+            "value": m * 2048 * nb / t / 2 ** 30, "unit": "GiB/s (all 256 chunks per block, as the reference counts)",
+            "link_gbs": (m - hits) * 2048 * nb / t / 1e9, "copy_us": t * 1e6,
+            "reorder_us": statistics.mean(reorder_ms) * 1e3, "iterations": iters, "warmup": warmup,
+            "config": {"blocks": nb, "map_size": m, "hits": hits, "host_chunks_per_block": cpu_chunks},
+            "higher_is_better": True, "n_gpus": 1}
+
+
 def run_prefill(args):
     """Prefill state build of one layer (config1 shapes, B=1): torch restatement vs skv_prefill_build.
 
@@ -582,6 +637,8 @@ def main():
     ap.add_argument("--config", default="config1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying a CUDA graph")
+    ap.add_argument("--kat", action="store_true",
+                    help="the reference's reuse-cache copy benchmark (test_cached_gather_copy.cu) on the drop-in bindings")
     ap.add_argument("--prefill", action="store_true",
                     help="time the prefill state build of one layer (torch path vs skv_prefill_build)")
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
@@ -613,6 +670,9 @@ def main():
         return
     if args.prefill:
         print(json.dumps(run_prefill(args)), flush=True)
+        return
+    if args.kat:
+        print(json.dumps(run_kat(args)), flush=True)
         return
     world, rank, local = dist_setup()
     res = run_b200(args, world, rank, local)
