@@ -72,7 +72,8 @@ class ShadowKVCache_CPU:
         self.svd_method = svd
         self.gen_len = gen_len
         self.select_sets = self.sparse_budget // self.chunk_size
-        assert self.select_sets * self.chunk_size == self.sparse_budget
+        if self.select_sets * self.chunk_size != self.sparse_budget:
+            raise RuntimeError(f"sparse_budget {self.sparse_budget} is not a multiple of chunk_size {chunk_size}")
 
         H, D, B, L = self.num_key_value_heads, self.head_dim, batch_size, self.num_layers
         self.host_chunks = max_length // chunk_size
