@@ -19,6 +19,8 @@
 // Rank 0 then computes the slot-stable diff from the two bitmaps.
 #include "select.cuh"
 
+#include <atomic>
+
 namespace skv {
 
 __device__ __forceinline__ uint32_t dsmem_addr(const void *local, unsigned rank)
@@ -718,13 +720,14 @@ int launch_keys(const KeysArgs &k, int BH, cudaStream_t stream)
 // (a non-portable cluster size), decided once per device.
 bool select_cluster16_ok(size_t smem)
 {
-    static int cached[64];
+    static std::atomic<int> cached[64];  // 0: not probed yet, 1: yes, -1: no (host threads may race here)
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
         cudaGetLastError();
         return false;
     }
-    if (cached[dev]) return cached[dev] > 0;
+    const int known = cached[dev].load(std::memory_order_relaxed);
+    if (known) return known > 0;
     int ok = -1;
     const void *fn = (const void *)select_cluster_kernel<16>;
     if (cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess &&
@@ -744,7 +747,7 @@ bool select_cluster16_ok(size_t smem)
         if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) == cudaSuccess && n >= 1) ok = 1;
     }
     cudaGetLastError();
-    cached[dev] = ok;
+    cached[dev].store(ok, std::memory_order_relaxed);
     return ok > 0;
 }
 
