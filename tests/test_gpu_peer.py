@@ -75,3 +75,26 @@ def test_peer_gather_rejects_bad_descriptions():
     finally:
         for x in p:
             x.close()
+
+
+def test_finish_wait_runs_out_and_reports_a_status():
+    """Nothing raises the arrival counter: the finish kernel's bounded wait runs out, a wait
+    error is counted for the host to read, and the context stays usable."""
+    import time
+    from shadowkv_b200._lib import device_errors
+    from shadowkv_b200.peer import PeerOutput
+    device_errors()  # clear
+    (p,) = PeerOutput.in_process(1, 8, [0], merges_per_step=2)
+    try:
+        out = torch.empty(1, 8, 128, dtype=torch.bfloat16, device=DEV)
+        t0 = time.time()
+        p.finish(out)  # no attention launch: the counter stays at zero
+        torch.cuda.synchronize()
+        waited = time.time() - t0
+        assert device_errors() == (1, 4)  # one DEV_ERR_WAIT
+        assert waited < 60
+    finally:
+        p.close()
+    x = torch.arange(1024, device=DEV, dtype=torch.float32)
+    assert float(x.sum().item()) == 1023 * 1024 / 2
+    assert device_errors() == (0, 0)
