@@ -246,6 +246,14 @@ def run_b200(args, world, rank, local):
     # (a real data dependency between the layers, as in the model)
     s_mid = [torch.empty(B, Hq, 128, dtype=torch.bfloat16, device="cuda") for _ in range(2)]
     cache.fused_geometry(attn.cos_sin_cache)
+    # the one-call step (skv_decode_step), pipelined over kv-head groups at batch 1
+    use_step = not (args.split or args.two_calls or heads_sharded or args.microbatch > 1)
+    from shadowkv_b200.kvcache import auto_head_groups
+    head_groups = (args.head_groups or auto_head_groups(B, Hkv)) if use_step else 1
+
+    def step_misses():
+        ws = cache._step_ws if use_step else cache._fused_ws
+        return int(ws.miss_count.sum().item())
 
     def load_inputs(i):
         q, k, v = inputs[i % len(inputs)]
@@ -264,6 +272,11 @@ def run_b200(args, world, rank, local):
                 seq_len = cache.sparse_end + cache.gen_offset + 1
                 cache.decode_step_microbatched(li, q_in, s_k, s_v, s_pos, attn.cos_sin_cache, out,
                                                args.microbatch, q_out=s_qr, max_ctas=args.fetch_ctas)
+                continue
+            if use_step:
+                cache.decode_step_fused(li, q_in, s_k, s_v, s_pos, attn.cos_sin_cache, out=out,
+                                        head_groups=head_groups, q_out=s_qr)
+                seq_len = cache.sparse_end + cache._gen_offset(li)
                 continue
             qr = cache.append_select_fused(li, q_in, s_k, s_v, s_pos, attn.cos_sin_cache, q_out=s_qr)
             seq_len = cache.sparse_end + cache._gen_offset(li)
@@ -324,7 +337,7 @@ def run_b200(args, world, rank, local):
             e.record(main)
             e.synchronize()
             per_step.append(s.elapsed_time(e))
-            misses_all.append(int(cache._fused_ws.miss_count.sum().item()))
+            misses_all.append(step_misses())
             seqlens.append(seq_len)
         barrier(world)
         t_wall = time.perf_counter() - t_wall
@@ -456,7 +469,9 @@ def run_b200(args, world, rank, local):
                                     f"kv-head-sharded x{world} (NCCL all-gather of the attention output)")
                                    if heads_sharded else f"batch-sharded x{world}"),
                    "l2": "flushed between timed steps (256 MB write)", "hit_rate": hit_rate,
-                   "microbatch": args.microbatch, "fetch_ctas": args.fetch_ctas if args.microbatch > 1 else None},
+                   "microbatch": args.microbatch, "fetch_ctas": args.fetch_ctas if args.microbatch > 1 else None,
+                   "step": (f"skv_decode_step, {head_groups} kv-head group(s)" if use_step else
+                            "append_select + fetch/reconstruct/attend launches")},
         "roofline": {"kernel": ("fetch_misses_kernel (zero-copy V gather)" if args.split else
                                 "sparse_attend_kernel (zero-copy V gather + key reconstruction + attention)"),
                      "bound": "host_link",
@@ -475,7 +490,8 @@ def run_b200(args, world, rank, local):
         "kernel_us": kernel_us,
         "graph": used_graph,
         "gpu_launches": (select_kernels(cache) + (3 if args.split else 1)) * NL * args.steps
-                        * (args.microbatch if args.microbatch > 1 and not args.split and not heads_sharded else 1),
+                        * (args.microbatch if args.microbatch > 1 and not args.split and not heads_sharded else 1)
+                        * head_groups,
         "clocks": clk.summary(),
         "wall_s": t_wall,
     }
@@ -655,6 +671,10 @@ def main():
     ap.add_argument("--shard", default="batch", choices=["batch", "heads"],
                     help="multi-GPU partition: one sequence per rank (weak scaling) or the kv heads of one "
                          "sequence split over the ranks with an NCCL all-gather of the outputs (strong scaling)")
+    ap.add_argument("--head-groups", type=int, default=None,
+                    help="kv-head groups of the pipelined one-call step at batch 1 (default: auto, 4 for 8 kv heads)")
+    ap.add_argument("--two-calls", action="store_true",
+                    help="run the step as append_select + sparse_attention (all heads in one chain)")
     ap.add_argument("--split", action="store_true",
                     help="fetch / reconstruction / attention as three launches instead of the fused kernel")
     args = ap.parse_args()

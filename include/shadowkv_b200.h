@@ -356,6 +356,39 @@ SKV_API int skv_decode_sparse_attention(const skv_decode_geom *g, const void *q,
                                         int seq_len, void *out, void *workspace,
                                         size_t workspace_bytes, void *stream);
 
+/* Bytes of scratch skv_decode_step needs for any seq_len up to buf_len (0 if
+ * the geometry or head_groups is rejected).  Zero-fill it before its first
+ * use; calls leave it ready for the next call; launches that can run at the
+ * same time must not share it. */
+SKV_API size_t skv_decode_step_workspace(const skv_decode_geom *g, int head_groups);
+
+/* One decode step of one layer: skv_decode_append_select (new token's RoPE +
+ * append at buffer row `row`, scoring, top-k, reuse diff) followed by
+ * skv_decode_sparse_attention (value fetch, key reconstruction, attention),
+ * with the same results.  The selection's miss lists live in the workspace;
+ * miss_count, if not null, receives the number of missed chunks of every
+ * (sequence, kv head) [batch * kv_heads] int32 (the reference's cnts are the
+ * hits: select_sets - miss_count).
+ * head_groups > 1 (batch 1, dividing kv_heads, at most 8) pipelines the step
+ * over groups of kv heads: each group's chain runs on a library stream, the
+ * groups' scoring passes one after the other, so the first group's value
+ * fetch starts after a fraction of the landmark scan and the other groups'
+ * scoring and selection overlap it.  The fork and join are event waits on
+ * `stream`, so stream capture records the whole step.  The library streams
+ * and events of a device are created by its first call with head_groups > 1:
+ * make that call outside stream capture.
+ * Replaces, per step, shadowkv.batch_gemm_softmax + torch.topk +
+ * reorder_keys_and_compute_offsets + gather_copy_with_offsets +
+ * gather_copy_d2d_with_offsets + batch_gather_gemm + the push-cache RoPE and
+ * flash_attn_with_kvcache (models/kvcache/shadow.py:547-633,
+ * models/attention/shadow.py:22-48). */
+SKV_API int skv_decode_step(const skv_decode_geom *g, const void *q, const void *k_new, const void *v_new,
+                            const int64_t *positions, const void *cos_sin, void *q_out, void *k_buf,
+                            void *v_buf, int row, const void *landmarks, const int64_t *landmark_idx,
+                            int32_t *slots, const void *U, const void *SVt, const void *v_host,
+                            int seq_len, void *out, int32_t *miss_count, int head_groups,
+                            void *workspace, size_t workspace_bytes, void *stream);
+
 /* ---- prefill state builder (ShadowKVCache_CPU.prefill_kv_cache,
  * models/kvcache/shadow.py:463-544) for one layer of `batch` sequences. */
 typedef struct {

@@ -7,7 +7,8 @@ tensor_op  the reference's decode-path helpers of models/tensor_op.py
 kvcache    ``ShadowKVCache_CPU`` (reference path and fused slot-stable path)
 attention  ``ShadowAttention.decode`` / ``decode_fused``
 decode     torch wrappers of the fused ``skv_decode_*`` C ABI
-sharding   batch / KV-head sharding across GPUs (NCCL all-gather of head shards)
+sharding   batch / KV-head partition across GPUs (head ranges; NCCL all-gather helper)
+peer       kv-head outputs exchanged by the attention kernel over NVLink peer memory
 workload   seeded synthetic workloads with the benchmark shapes
 build      nvcc build of ``libshadowkv_b200.so``
 

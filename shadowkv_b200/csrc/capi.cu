@@ -2,6 +2,7 @@
 #include "common.cuh"
 
 #include <string.h>
+#include <atomic>
 #include <mutex>
 
 namespace skv {
@@ -111,8 +112,29 @@ int out_to_device_ptr(void *p, void **dev, const char *name)
     return SKV_ERR_INVALID_ARGUMENT;
 }
 
+int device_sm_count()
+{
+    static std::atomic<int> cached[64];  // 0: not queried yet (host threads may race here)
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        return 148;
+    }
+    int n = cached[dev].load(std::memory_order_relaxed);
+    if (n > 0) return n;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        return 148;
+    }
+    cached[dev].store(n, std::memory_order_relaxed);
+    return n;
+}
+
 __device__ unsigned int g_dev_err_count = 0;
 __device__ unsigned int g_dev_err_first = 0;
+#ifdef SKV_TRACE
+__device__ unsigned long long g_trace[2 * SKV_TRACE_EVENTS];
+#endif
 
 }  // namespace skv
 
@@ -133,5 +155,30 @@ int skv_device_errors(uint32_t *count, uint32_t *first_code)
     if (first_code) *first_code = f;
     return SKV_OK;
 }
+
+#ifdef SKV_TRACE
+__global__ void trace_mark_kernel(int e) { skv::trace_stamp(e); }
+// Trace builds only: one thread stamps event e on the stream.
+SKV_API int skv_trace_mark(int e, void *stream)
+{
+    trace_mark_kernel<<<1, 1, 0, (cudaStream_t)stream>>>(e);
+    return skv::check_launch("trace_mark_kernel");
+}
+// Trace builds only (not part of the public header): copy the 2 * n trace
+// slots into out (earliest / latest stamp of each event, ns of the global
+// timer) and reset them.
+SKV_API int skv_trace_read(unsigned long long *out, int n)
+{
+    unsigned long long h[2 * skv::SKV_TRACE_EVENTS];
+    SKV_CUDA(cudaMemcpyFromSymbol(h, skv::g_trace, sizeof(h)));
+    if (out) memcpy(out, h, sizeof(unsigned long long) * 2 * (n < skv::SKV_TRACE_EVENTS ? n : skv::SKV_TRACE_EVENTS));
+    for (int e = 0; e < skv::SKV_TRACE_EVENTS; ++e) {
+        h[2 * e] = ~0ull;
+        h[2 * e + 1] = 0ull;
+    }
+    SKV_CUDA(cudaMemcpyToSymbol(skv::g_trace, h, sizeof(h)));
+    return SKV_OK;
+}
+#endif
 
 }  // extern "C"

@@ -61,6 +61,10 @@ int out_to_device_ptr(void *p, void **dev, const char *name);
 
 inline bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// Streaming multiprocessors of the current device (queried once per device;
+// 148 on a B200).  Grids are sized from it, not from a constant.
+int device_sm_count();
+
 // ---------------------------------------------------------------------------
 // Device-side error counter: a kernel that finds an index out of range skips
 // the access and records it here (read back by skv_device_errors()).
@@ -75,6 +79,40 @@ __device__ __forceinline__ void report_dev_error(uint32_t code)
     unsigned int prev = atomicAdd(&g_dev_err_count, 1u);
     if (prev == 0) atomicExch(&g_dev_err_first, code);
 }
+
+// ---------------------------------------------------------------------------
+// Phase tracing (builds with -DSKV_TRACE only): thread 0 of a CTA stamps the
+// global timer into event e; slot 2e keeps the earliest stamp of any CTA,
+// slot 2e+1 the latest.  skv_trace_read() (exported by trace builds only)
+// copies the slots out and resets them.  Without SKV_TRACE the stamps
+// compile to nothing.
+// ---------------------------------------------------------------------------
+constexpr int SKV_TRACE_EVENTS = 32;
+#ifdef SKV_TRACE
+extern __device__ unsigned long long g_trace[2 * SKV_TRACE_EVENTS];
+__device__ __forceinline__ void trace_stamp(int e)
+{
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    atomicMin(&g_trace[2 * e], t);
+    atomicMax(&g_trace[2 * e + 1], t);
+}
+#define SKV_TRACE_CTA(e)                                    \
+    do {                                                    \
+        if (threadIdx.x == 0) ::skv::trace_stamp(e);        \
+    } while (0)
+#else
+#define SKV_TRACE_CTA(e) ((void)0)
+#endif
+// trace events of the fused decode step
+enum TraceEvent : int {
+    TR_SCORE_START = 0, TR_SCORE_TILE0 = 1, TR_SCORE_END = 2,
+    TR_SEL_START = 3, TR_SEL_WAITED = 4, TR_SEL_KEYS = 5, TR_SEL_CAND = 6, TR_SEL_END = 7,
+    TR_SA_START = 8, TR_SA_WAITED = 9, TR_SA_ISSUED = 10, TR_SA_KEYS = 11, TR_SA_VALUES = 12,
+    TR_SA_TICKET = 13, TR_SA_MERGED = 14, TR_MARK_BEFORE = 15, TR_MARK_AFTER = 16,
+    TR_SEL_C = 17, TR_SEL_TILE = 18, TR_SEL_HIST = 19, TR_SEL_SYNC1 = 20, TR_SEL_SCAN = 21, TR_SEL_MARKED = 22,
+    TR_SEL_RANKED = 23, TR_SEL_DIFF = 24, TR_SA_LISTS = 25,
+};
 
 // ---------------------------------------------------------------------------
 // Device helpers

@@ -77,16 +77,19 @@ __device__ __forceinline__ void merge_stats(float &m, float &s, float m2, float 
 // Fused path, kernel 1: logits[bh][c][g] = scale * q_g . LM_c and per-split
 // online (max, sum-exp) per query head.
 //
-// grid = (nsplit, B*Hkv); 8 consumer warps + 1 producer warp.  The producer
-// streams the CTA's landmark rows through a 3-stage ring of 128-row (32 KB)
-// shared-memory tiles with bulk (TMA) copies completed on mbarriers; each
-// consumer warp multiplies 16 rows of a tile per stage on the tensor cores.
+// grid = (nsplit, B*Hkv); 8 consumer warps + 1 producer warp, two CTAs per
+// SM.  The producer streams the CTA's landmark rows through a 3-stage ring of
+// 128-row (32 KB) shared-memory tiles with bulk (TMA) copies completed on
+// mbarriers; each consumer warp multiplies 16 rows of a tile per stage on the
+// tensor cores.  The three stages are requested before anything else the CTA
+// does, so the landmark stream is in flight during the launch's prologue.
+// The host sizes the grid from the device's SM count (the rows of a head split
+// evenly over its CTAs), leaving a few SMs to the selection kernel that follows.
 // With APPEND the kernel also performs the new-token step: it rotates the
 // query rows of its GQA group itself, and the split-0 CTA of each head writes
 // the rotated query, the rotated key and the value of the new token.
 // ---------------------------------------------------------------------------
-constexpr int ST_STAGES = 3;   // 3 x 32 KB tiles: two CTAs per SM
-constexpr int ST_PRE = 1;     // stages issued before the query prologue
+constexpr int ST_STAGES = 3;  // 3 x 32 KB tiles: two CTAs per SM
 constexpr int ST_ROWS = 128;
 constexpr int ST_CONSUMERS = 8;
 constexpr int ST_THREADS = (ST_CONSUMERS + 1) * 32;
@@ -108,7 +111,7 @@ struct ScoreArgs {
 };
 
 template <int NT, bool APPEND>
-__global__ void __launch_bounds__(ST_THREADS) score_tma_kernel(ScoreArgs a)
+__global__ void __launch_bounds__(ST_THREADS, 2) score_tma_kernel(ScoreArgs a)
 {
     extern __shared__ unsigned char smem_dyn[];
     unsigned char *smem = reinterpret_cast<unsigned char *>(((uintptr_t)smem_dyn + 1023) & ~(uintptr_t)1023);
@@ -129,6 +132,7 @@ __global__ void __launch_bounds__(ST_THREADS) score_tma_kernel(ScoreArgs a)
     const __nv_bfloat16 *lmh = a.lm + (int64_t)bh * L * 128;
 
     pdl_launch_dependents();  // the selection kernel may be scheduled early (it waits for this grid)
+    SKV_TRACE_CTA(TR_SCORE_START);
     const bool producer = warp == ST_CONSUMERS && lane == 0;
     if (producer) {
         for (int s = 0; s < ST_STAGES; ++s) {
@@ -137,10 +141,9 @@ __global__ void __launch_bounds__(ST_THREADS) score_tma_kernel(ScoreArgs a)
         }
         s_abort = 0;
         mbar_fence_init();
-        // the first tile goes out before the query prologue below; the other
-        // stages follow once the prologue's own loads are back, so they do
-        // not queue behind a burst of tile traffic
-        for (int i = 0; i < min(nst, ST_PRE); ++i) {
+        // every stage of the ring is requested before the query prologue
+        // below: the landmark stream is the bound of the kernel
+        for (int i = 0; i < min(nst, ST_STAGES); ++i) {
             const int r0 = r_begin + i * ST_ROWS;
             const int nr = min(ST_ROWS, r_end - r0);
             mbar_arrive_expect_tx(&full[i], (unsigned)nr * 256u);
@@ -200,7 +203,7 @@ __global__ void __launch_bounds__(ST_THREADS) score_tma_kernel(ScoreArgs a)
     if (warp == ST_CONSUMERS) {
         // ---- producer: one elected lane streams the row tiles
         if (lane == 0) {
-            for (int i = ST_PRE; i < nst; ++i) {
+            for (int i = ST_STAGES; i < nst; ++i) {
                 const int s = i % ST_STAGES;
                 if (i >= ST_STAGES && !mbar_wait(&empty[s], ((i / ST_STAGES) - 1) & 1)) {
                     report_dev_error(DEV_ERR_WAIT);
@@ -230,6 +233,7 @@ __global__ void __launch_bounds__(ST_THREADS) score_tma_kernel(ScoreArgs a)
                 atomicExch(&s_abort, 1);
                 break;
             }
+            if (i == 0) SKV_TRACE_CTA(TR_SCORE_TILE0);
             const __nv_bfloat16 *tile = sT + (size_t)s * ST_ROWS * 128;
             const int lr = warp * 16 + g;  // local rows lr and lr+8
             uint4 ra[4], rb[4];
@@ -295,6 +299,7 @@ __global__ void __launch_bounds__(ST_THREADS) score_tma_kernel(ScoreArgs a)
         for (int w = 0; w < ST_CONSUMERS; ++w) merge_stats(mm, ss, s_part[w][tid].x, s_part[w][tid].y);
         a.part[((int64_t)bh * G + tid) * nsplit + split] = make_float2(mm, ss);  // [BH][G][nsplit]
     }
+    SKV_TRACE_CTA(TR_SCORE_END);
 }
 
 // ---------------------------------------------------------------------------
@@ -427,17 +432,28 @@ static SelectPlan plan_select(const skv_decode_geom *g)
     SelectPlan p = {};
     const int G = g->q_heads / g->kv_heads;
     const int BH = g->batch * g->kv_heads;
-    const int stages = ceil_div(g->num_landmarks, ST_ROWS);  // 128-row tiles per head
-    int per = ceil_div(stages * BH, 2 * 148);                  // about two CTAs per SM
-    if (per < 1) per = 1;
-    p.rows_per_split = per * ST_ROWS;
-    p.nsplit = ceil_div(g->num_landmarks, p.rows_per_split);
+    const int sms_all = device_sm_count();
+    const int tiles = ceil_div(g->num_landmarks, ST_ROWS);  // 128-row tiles per head
+    // SMs left to the selection kernel that follows (programmatic dependent
+    // launch): its CTAs become resident there while the scan runs and do the
+    // work that does not need the scores (landmark ids, bitmaps, slots) early.
+    // Two selection CTAs fit an SM; the scan keeps at least 3/4 of the SMs.
+    const int sel_ctas = BH * (g->num_landmarks > 8 * 4096 ? 16 : 8);
+    const int reserve = min(ceil_div(sel_ctas, 2), sms_all / 4);
+    const int sms = sms_all - reserve;
+    // Scoring grid: two CTAs per SM on the SMs not reserved, the rows of a head
+    // split evenly over nsplit of them (every SM reads about the same bytes).
+    {
+        const int ns = max(1, min(tiles, 2 * sms / BH));
+        p.rows_per_split = ceil_div(g->num_landmarks, ns);
+        p.nsplit = ceil_div(g->num_landmarks, p.rows_per_split);
+    }
     // very long contexts (more than 4096 landmarks per CTA at 8): the keys are
     // computed by keys_kernel on the whole GPU (the selection's clusters would
     // spend long reading the logits) and the selection uses 16-CTA clusters
     const int L = g->num_landmarks;
     p.keys_pre = L > 8 * 4096;
-    const int64_t kr = ((int64_t)L * BH + 2 * 148 - 1) / (2 * 148);  // about two CTAs per SM
+    const int64_t kr = ((int64_t)L * BH + 2 * sms_all - 1) / (2 * sms_all);  // about two CTAs per SM
     p.keys_rows = kr < 512 ? 512 : (int)kr;
     p.cl = 8;
     if (p.keys_pre) {
@@ -493,16 +509,11 @@ static int run_select(const skv_decode_geom *g, const ScoreArgs &sa_in, const in
     sa.scale = g->scale;
     const void *fn = G <= 8 ? (append ? (const void *)score_tma_kernel<1, true> : (const void *)score_tma_kernel<1, false>)
                             : (append ? (const void *)score_tma_kernel<2, true> : (const void *)score_tma_kernel<2, false>);
-    int st = ensure_smem_attr(fn, ST_SMEM, "score_tma_kernel");
+    const int smem = ST_SMEM;
+    int st = ensure_smem_attr(fn, smem, "score_tma_kernel");
     if (st) return st;
-    dim3 grid(p.nsplit, BH);
-    if (G <= 8) {
-        if (append) score_tma_kernel<1, true><<<grid, ST_THREADS, ST_SMEM, s>>>(sa);
-        else score_tma_kernel<1, false><<<grid, ST_THREADS, ST_SMEM, s>>>(sa);
-    } else {
-        if (append) score_tma_kernel<2, true><<<grid, ST_THREADS, ST_SMEM, s>>>(sa);
-        else score_tma_kernel<2, false><<<grid, ST_THREADS, ST_SMEM, s>>>(sa);
-    }
+    void *kargs[] = {&sa};
+    SKV_CUDA(cudaLaunchKernel(fn, dim3(p.nsplit, BH), dim3(ST_THREADS), kargs, (size_t)smem, s));
     st = check_launch("score_tma_kernel");
     if (st) return st;
     SelectArgs a = {};
@@ -570,6 +581,21 @@ int skv_decode_append_select(const skv_decode_geom *g, const void *q, const void
                              int32_t *slots, int32_t *miss_slot, int32_t *miss_chunk, int32_t *miss_count,
                              void *workspace, size_t workspace_bytes, void *stream)
 {
+    return skv::append_select_launch(g, q, k_new, v_new, positions, cos_sin, q_out, k_buf, v_buf, row, landmarks,
+                                     landmark_idx, slots, miss_slot, miss_chunk, miss_count, workspace,
+                                     workspace_bytes, (cudaStream_t)stream);
+}
+
+}  // extern "C"
+
+namespace skv {
+
+int append_select_launch(const skv_decode_geom *g, const void *q, const void *k_new, const void *v_new,
+                         const int64_t *positions, const void *cos_sin, void *q_out, void *k_buf, void *v_buf,
+                         int row, const void *landmarks, const int64_t *landmark_idx, int32_t *slots,
+                         int32_t *miss_slot, int32_t *miss_chunk, int32_t *miss_count, void *workspace,
+                         size_t workspace_bytes, cudaStream_t stream)
+{
     int st = check_geom(g);
     if (st) return st;
     SKV_CHECK_ARG(q && k_new && v_new && positions && cos_sin && q_out && k_buf && v_buf && landmarks &&
@@ -597,8 +623,12 @@ int skv_decode_append_select(const skv_decode_geom *g, const void *q, const void
     sa.cs_stride = g->cos_sin_stride;
     sa.cs_rows = g->cos_sin_rows;
     return run_select(g, sa, landmark_idx, slots, miss_slot, miss_chunk, miss_count, workspace, workspace_bytes,
-                      true, (cudaStream_t)stream);
+                      true, stream);
 }
+
+}  // namespace skv
+
+extern "C" {
 
 int skv_batch_gemm_softmax(const void *A, const void *B, void *D, float *Norm, float *Sum,
                            void *Softmax, int batch_count, int m, int n, int k, float alpha,

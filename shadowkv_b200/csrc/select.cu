@@ -328,6 +328,7 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
     // The fused attention that follows (one CTA per SM) may become resident on
     // the SMs this grid leaves free; it waits for this grid before reading.
     pdl_launch_dependents();
+    SKV_TRACE_CTA(TR_SEL_START);
 
     // 0) loads that do not depend on the scores: the cached slots (rank 0,
     //    thread t owns slots 2t, 2t+1) and the chunk ids of this slice
@@ -356,6 +357,7 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
     if (tid < CL) s_ccnt[tid] = 0;
 
     pdl_wait();  // the scoring kernel's logits and partials are complete from here on
+    SKV_TRACE_CTA(TR_SEL_WAITED);
 
     // the logits of this CTA's landmarks come in through bulk (TMA) copies,
     // SEL_RING tiles in flight, issued before the split partials are merged;
@@ -384,6 +386,7 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
         if (lane == 0) s_C[warp_id()] = C;
     }
     __syncthreads();
+    SKV_TRACE_CTA(TR_SEL_C);
     bool hit[2] = {false, false};
     if (rank == 0) {
 #pragma unroll
@@ -425,6 +428,7 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
                 if (tid == 0) report_dev_error(DEV_ERR_WAIT);
                 mbar_wait(&s_full[i % SEL_RING], (i / SEL_RING) & 1);  // the tile must land before it is reused
             }
+            if (i == 0) SKV_TRACE_CTA(TR_SEL_TILE);
             const float4 *tile = reinterpret_cast<const float4 *>(ring + (size_t)(i % SEL_RING) * (SEL_RSTAGE / 4));
             const int k0 = i * kps, cnt = min(kps, n - k0);
             switch (G) {
@@ -443,13 +447,16 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
         }
     }
     __syncthreads();
+    SKV_TRACE_CTA(TR_SEL_HIST);
     for (int t = tid; t < SEL_BINS; t += SEL_T) {
         unsigned h = 0;
 #pragma unroll
         for (int w = 0; w < SEL_T / 32; ++w) h += s_hw[w][t];
         s_h1[t] = h;
     }
+    SKV_TRACE_CTA(TR_SEL_KEYS);
     cluster_sync();  // every CTA's first-pass histogram is complete; rank 0's bitmaps are zero
+    SKV_TRACE_CTA(TR_SEL_SYNC1);
 
     // 3) every CTA sums the CL histograms and finds the bin holding the K-th
     //    largest key.  Warp r copies CTA r's histogram into row r of this
@@ -503,6 +510,7 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
         }
     }
     __syncthreads();
+    SKV_TRACE_CTA(TR_SEL_SCAN);
     const int bstar = s_bin, bin_above = s_bin_above, bin_cnt = s_bin_cnt;
     const uint32_t bmA0 = dsmem_addr(bmA, 0);
     auto chunk_of = [&](int c) -> int {
@@ -545,8 +553,10 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
                 }
             }
         }
+        SKV_TRACE_CTA(TR_SEL_MARKED);
         cluster_sync();  // rank 0 holds the candidates and the bits of the keys above them
         if (rank != 0) return;
+        SKV_TRACE_CTA(TR_SEL_CAND);
         // the regions, compacted
         if (tid == 0) {
             int acc = 0;
@@ -593,6 +603,7 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
         if (rank != 0) return;
     }
     __syncthreads();
+    SKV_TRACE_CTA(TR_SEL_RANKED);
 
     // 6) classify the cached slots against the new set; count the missed ids
     //    (in A, not in B) of this thread's bitmap words; one scan gives both
@@ -621,6 +632,7 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
         }
     }
     __syncthreads();
+    SKV_TRACE_CTA(TR_SEL_DIFF);
 
     // 7) refill the free slots (ascending) with the misses (ascending)
     const int nassign = min(nfree, nmiss);
@@ -640,6 +652,7 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
         a.miss_count[bh] = nassign;
         if (nfree != nmiss) report_dev_error(DEV_ERR_SLOT);
     }
+    SKV_TRACE_CTA(TR_SEL_END);
 }
 
 size_t select_smem_bytes(int L, int num_chunks, int G, bool keys_global, int cl, bool keys_pre)
@@ -717,9 +730,12 @@ int launch_keys(const KeysArgs &k, int BH, cudaStream_t stream)
 }
 
 // Whether this device can schedule 16-CTA clusters of the selection kernel
-// (a non-portable cluster size), decided once per device.
+// (a non-portable cluster size) with `smem` bytes of dynamic shared memory per
+// CTA.  Decided once per device, probed at SEL_SMEM_CAP -- the largest size
+// plan_select asks for -- so a yes holds for every smaller plan.
 bool select_cluster16_ok(size_t smem)
 {
+    if (smem > SEL_SMEM_CAP) return false;
     static std::atomic<int> cached[64];  // 0: not probed yet, 1: yes, -1: no (host threads may race here)
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
@@ -731,11 +747,11 @@ bool select_cluster16_ok(size_t smem)
     int ok = -1;
     const void *fn = (const void *)select_cluster_kernel<16>;
     if (cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess &&
-        ensure_smem_attr(fn, (int)smem, "select_cluster_kernel<16>") == SKV_OK) {
+        ensure_smem_attr(fn, (int)SEL_SMEM_CAP, "select_cluster_kernel<16>") == SKV_OK) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(16, 1, 1);
         cfg.blockDim = dim3(SEL_T, 1, 1);
-        cfg.dynamicSmemBytes = smem;
+        cfg.dynamicSmemBytes = SEL_SMEM_CAP;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
         attr[0].val.clusterDim.x = 16;

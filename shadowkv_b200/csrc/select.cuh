@@ -81,4 +81,11 @@ bool select_cluster16_ok(size_t smem);
 
 int launch_select(const SelectArgs &a, int BH, size_t smem, int cl, cudaStream_t stream);
 
+// skv_decode_append_select on a cudaStream_t (for the library's own callers)
+int append_select_launch(const skv_decode_geom *g, const void *q, const void *k_new, const void *v_new,
+                         const int64_t *positions, const void *cos_sin, void *q_out, void *k_buf, void *v_buf,
+                         int row, const void *landmarks, const int64_t *landmark_idx, int32_t *slots,
+                         int32_t *miss_slot, int32_t *miss_chunk, int32_t *miss_count, void *workspace,
+                         size_t workspace_bytes, cudaStream_t stream);
+
 }  // namespace skv

@@ -102,7 +102,9 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
         mbar_init(&s_bar, 1);
         mbar_fence_init();
     }
+    SKV_TRACE_CTA(TR_SA_START);
     pdl_wait();  // the selection (and the scoring before it) are complete from here on
+    SKV_TRACE_CTA(TR_SA_WAITED);
 
     // Work items: (kv head, 128-row block), the blocks that hold selected slots
     // first -- with more items than CTAs the ones left for later are the light
@@ -186,6 +188,7 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
         }
     }
     __syncthreads();
+    SKV_TRACE_CTA(TR_SA_LISTS);
     const bool any_miss = s_any_miss != 0;
 
     // 3) zero-copy loads of the missed value chunks (2 KiB each), issued
@@ -200,6 +203,7 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
         if (s_kind[gi] == 1)
             vreg[u] = ld_stream_v4(a.v_host + ((int64_t)bh * a.num_chunks + s_chunk[gi]) * 128 + (p & 127));
     }
+    if (any_miss) SKV_TRACE_CTA(TR_SA_ISSUED);
 
     // 4) device-memory rows as bulk (TMA) copies: SV^T of the head, U and
     //    cos/sin rows of the missed groups, K and V rows of the buffer groups.
@@ -355,6 +359,7 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
         }
     }
     __syncthreads();
+    if (any_miss) SKV_TRACE_CTA(TR_SA_KEYS);
 
     // 6) S = K q^T: warp w scores keys 16w .. 16w+15
     {
@@ -433,6 +438,7 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
         }
     }
     __syncthreads();
+    if (any_miss) SKV_TRACE_CTA(TR_SA_VALUES);
 
     // 8) O = P V: warp w computes dims 16w .. 16w+15 for the 16 head rows
     float o[2][4];
@@ -467,6 +473,7 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
     __threadfence();
     __syncthreads();
     if (tid == 0) s_last = atomicAdd(&a.ticket[bh], 1u) == (unsigned)(a.nblk - 1) ? 1u : 0u;
+    SKV_TRACE_CTA(TR_SA_TICKET);
     __syncthreads();
     if (s_last) {
     __threadfence();
@@ -545,6 +552,7 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
             for (int r = 0; r < a.world; ++r) atomicAdd_system(a.counter[r], 1u);
     }
     if (tid == 0) a.ticket[bh] = 0;  // ready for the next launch
+    SKV_TRACE_CTA(TR_SA_MERGED);
     }  // the head's last block
     }  // work items
 }

@@ -1,0 +1,198 @@
+// One whole decode step of one layer, pipelined over groups of kv heads.
+//
+// Replaces, for a step, the reference's sequence (models/attention/shadow.py:
+// 22-48 with models/kvcache/shadow.py:547-633): new-token RoPE + append,
+// landmark scoring and top-k, value gather with the reuse cache, key
+// reconstruction and attention -- the work of skv_decode_append_select
+// followed by skv_decode_sparse_attention.
+//
+// The step is bound by the host link (the missed value chunks), and no byte
+// of it can be requested before the selection of its head is done.  With all
+// kv heads in one launch chain the link waits for every head's scoring and
+// selection.  Here the heads are split into `head_groups` groups, each with
+// its own launch chain on a library stream, forked from and joined back to the
+// caller's stream:
+//
+//   caller stream:  fork ---------------------------------------------- join
+//   group 0:        score0 > select0 > fetch/reconstruct/attend0 --------+
+//   group 1:        score1 ...> select1 > fetch/reconstruct/attend1 -----+
+//   group 2:        score2 ......> select2 > ...                         +
+//
+// The GPU hands out the CTAs of the groups' scoring kernels in launch order,
+// so group 0's landmark scan gets the SMs first and its selection and value
+// fetch start after a fraction of the whole scan; the later groups' scans and
+// selections overlap the host-link transfer of the earlier ones.  (Making
+// each scan wait for the previous one was measured slower: the groups'
+// attention CTAs, one per SM while they wait on the link, then starve the
+// later scans.)  The results are the same bits as one
+// skv_decode_append_select + skv_decode_sparse_attention over all heads
+// (the heads are independent).
+//
+// Library streams and events are created per device on the first call that
+// needs them (make that call before any stream capture); the fork and join are
+// event waits, so a capture of the caller's stream captures the whole DAG.
+// Calls from several host threads are serialised on a per-device lock while
+// they enqueue work.
+#include <mutex>
+
+#include "select.cuh"
+
+namespace skv {
+
+constexpr int STEP_MAX_GROUPS = 8;
+constexpr int STEP_MAX_DEVICES = 64;
+
+struct StepStreams {
+    bool ready = false;
+    cudaStream_t s[STEP_MAX_GROUPS] = {};
+    cudaEvent_t fork = nullptr, done[STEP_MAX_GROUPS] = {};
+    std::mutex mu;
+};
+static StepStreams g_step[STEP_MAX_DEVICES];
+
+static int step_streams(int dev, StepStreams **out)
+{
+    SKV_CHECK_SUPPORTED(dev >= 0 && dev < STEP_MAX_DEVICES, "device index %d above %d", dev, STEP_MAX_DEVICES - 1);
+    StepStreams &st = g_step[dev];
+    // called with st.mu held
+    if (!st.ready) {
+        int lo = 0, hi = 0;
+        SKV_CUDA(cudaDeviceGetStreamPriorityRange(&lo, &hi));
+        for (int i = 0; i < STEP_MAX_GROUPS; ++i) {
+            SKV_CUDA(cudaStreamCreateWithPriority(&st.s[i], cudaStreamNonBlocking, hi));
+            SKV_CUDA(cudaEventCreateWithFlags(&st.done[i], cudaEventDisableTiming));
+        }
+        SKV_CUDA(cudaEventCreateWithFlags(&st.fork, cudaEventDisableTiming));
+        st.ready = true;
+    }
+    *out = &st;
+    return SKV_OK;
+}
+
+static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// Per-group workspace: miss slots, miss chunk ids, miss counts, selection
+// scratch, attention partials (each 256-byte aligned).
+struct StepLayout {
+    size_t miss_slot, miss_chunk, miss_count, sel, sel_bytes, att, att_bytes, group_bytes;
+};
+
+// The layout depends on the geometry only (the attention part is sized for
+// buf_len rows, the longest step): the tickets of every group stay at fixed
+// offsets from one call to the next.
+static bool step_layout(const skv_decode_geom *gp, StepLayout *L)
+{
+    const size_t bh = (size_t)gp->batch * gp->kv_heads, K = (size_t)gp->select_sets;
+    L->sel_bytes = skv_decode_select_workspace(gp);
+    L->att_bytes = skv_decode_sparse_attention_workspace(gp, gp->buf_len);
+    if (L->sel_bytes == 0 || L->att_bytes == 0) return false;
+    L->att = 0;  // attention partials first: their tickets must be zero on the first call
+    L->miss_slot = align256(L->att_bytes);
+    L->miss_chunk = L->miss_slot + align256(bh * K * 4);
+    L->miss_count = L->miss_chunk + align256(bh * K * 4);
+    L->sel = L->miss_count + align256(bh * 4);
+    L->group_bytes = L->sel + align256(L->sel_bytes);
+    return true;
+}
+
+static skv_decode_geom group_geom(const skv_decode_geom *g, int groups)
+{
+    skv_decode_geom gp = *g;
+    gp.kv_heads = g->kv_heads / groups;
+    gp.q_heads = g->q_heads / groups;
+    return gp;
+}
+
+}  // namespace skv
+
+using namespace skv;
+
+extern "C" {
+
+size_t skv_decode_step_workspace(const skv_decode_geom *g, int head_groups)
+{
+    if (!g || head_groups < 1 || head_groups > STEP_MAX_GROUPS || g->kv_heads <= 0 ||
+        g->kv_heads % head_groups != 0 || (head_groups > 1 && g->batch != 1))
+        return 0;
+    const skv_decode_geom gp = group_geom(g, head_groups);
+    StepLayout L;
+    if (!step_layout(&gp, &L)) return 0;
+    return L.group_bytes * head_groups;
+}
+
+int skv_decode_step(const skv_decode_geom *g, const void *q, const void *k_new, const void *v_new,
+                    const int64_t *positions, const void *cos_sin, void *q_out, void *k_buf, void *v_buf,
+                    int row, const void *landmarks, const int64_t *landmark_idx, int32_t *slots, const void *U,
+                    const void *SVt, const void *v_host, int seq_len, void *out, int32_t *miss_count,
+                    int head_groups, void *workspace, size_t workspace_bytes, void *stream)
+{
+    SKV_CHECK_ARG(g != nullptr, "null geometry");
+    SKV_CHECK_ARG(q && k_new && v_new && positions && cos_sin && q_out && k_buf && v_buf && landmarks &&
+                      landmark_idx && slots && U && SVt && v_host && out && workspace,
+                  "null pointer argument");
+    SKV_CHECK_ARG(head_groups >= 1 && head_groups <= STEP_MAX_GROUPS && g->kv_heads > 0 &&
+                      g->kv_heads % head_groups == 0,
+                  "head_groups must divide kv_heads and be in 1..%d", STEP_MAX_GROUPS);
+    SKV_CHECK_SUPPORTED(head_groups == 1 || g->batch == 1,
+                        "head groups need batch 1 (a head group of a batch is not one contiguous block)");
+    SKV_CHECK_ARG(aligned(workspace, 256), "workspace must be 256-byte aligned");
+    const skv_decode_geom gp = group_geom(g, head_groups);
+    StepLayout L;
+    SKV_CHECK_ARG(step_layout(&gp, &L), "geometry rejected (see skv_decode_select_workspace)");
+    SKV_CHECK_ARG(workspace_bytes >= L.group_bytes * head_groups, "workspace of %zu bytes needed, %zu given",
+                  L.group_bytes * head_groups, workspace_bytes);
+    const int G = g->q_heads / g->kv_heads, hg = gp.kv_heads;
+    unsigned char *ws = static_cast<unsigned char *>(workspace);
+    const cudaStream_t caller = (cudaStream_t)stream;
+
+    auto group = [&](int i, cudaStream_t s) -> int {
+        const int64_t h0 = (int64_t)i * hg;  // first kv head of the group (batch 1 when groups > 1)
+        unsigned char *w = ws + L.group_bytes * i;
+        int32_t *ms = reinterpret_cast<int32_t *>(w + L.miss_slot);
+        int32_t *mc = reinterpret_cast<int32_t *>(w + L.miss_chunk);
+        int32_t *mn = miss_count ? miss_count + h0 : reinterpret_cast<int32_t *>(w + L.miss_count);
+        const __nv_bfloat16 *qb = (const __nv_bfloat16 *)q + h0 * G * 128;
+        __nv_bfloat16 *qo = (__nv_bfloat16 *)q_out + h0 * G * 128;
+        __nv_bfloat16 *kb = (__nv_bfloat16 *)k_buf + h0 * g->buf_len * 128;
+        __nv_bfloat16 *vb = (__nv_bfloat16 *)v_buf + h0 * g->buf_len * 128;
+        int st = append_select_launch(&gp, qb, (const __nv_bfloat16 *)k_new + h0 * 128,
+                                      (const __nv_bfloat16 *)v_new + h0 * 128, positions, cos_sin, qo, kb, vb, row,
+                                      (const __nv_bfloat16 *)landmarks + h0 * g->num_landmarks * 128,
+                                      landmark_idx + h0 * g->num_landmarks, slots + h0 * g->select_sets, ms, mc, mn,
+                                      w + L.sel, L.sel_bytes, s);
+        if (st) return st;
+        return skv_decode_sparse_attention(&gp, qo, U, (const __nv_bfloat16 *)SVt + h0 * 128 * g->rank, cos_sin,
+                                           (const __nv_bfloat16 *)v_host + h0 * (int64_t)g->num_chunks * 1024, kb, vb,
+                                           ms, mc, mn, seq_len, (__nv_bfloat16 *)out + h0 * G * 128, w + L.att,
+                                           L.att_bytes, s);
+    };
+
+    if (head_groups == 1) return group(0, caller);
+
+    int dev = 0;
+    SKV_CUDA(cudaGetDevice(&dev));
+    SKV_CHECK_SUPPORTED(dev >= 0 && dev < STEP_MAX_DEVICES, "device index %d above %d", dev, STEP_MAX_DEVICES - 1);
+    std::lock_guard<std::mutex> lock(g_step[dev].mu);
+    StepStreams *ss = nullptr;
+    int st = step_streams(dev, &ss);
+    if (st) return st;
+    SKV_CUDA(cudaEventRecord(ss->fork, caller));
+    for (int i = 0; i < head_groups; ++i) {
+        // group i's scoring after group i-1's (its whole bandwidth), after the fork
+        SKV_CUDA(cudaStreamWaitEvent(ss->s[i], ss->fork, 0));
+        st = group(i, ss->s[i]);
+        if (st) {
+            // join what was enqueued so far, so the caller's stream is not left forked
+            for (int j = 0; j <= i; ++j) {
+                cudaEventRecord(ss->done[j], ss->s[j]);
+                cudaStreamWaitEvent(caller, ss->done[j], 0);
+            }
+            return st;
+        }
+        SKV_CUDA(cudaEventRecord(ss->done[i], ss->s[i]));
+    }
+    for (int i = 0; i < head_groups; ++i) SKV_CUDA(cudaStreamWaitEvent(caller, ss->done[i], 0));
+    return SKV_OK;
+}
+
+}  // extern "C"

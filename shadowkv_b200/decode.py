@@ -97,6 +97,41 @@ class DecodeWorkspace:
         self.miss_count = torch.zeros(bh, dtype=torch.int32, device=device)
 
 
+class StepWorkspace:
+    """Scratch of ``step`` (zero-filled once; the step leaves it ready for the next call)."""
+
+    def __init__(self, geom: Geometry, head_groups: int, device):
+        self.geom, self.head_groups = geom, head_groups
+        self.nbytes = int(lib.skv_decode_step_workspace(ctypes.byref(geom.c()), int(head_groups)))
+        if self.nbytes == 0:
+            check(1, f"skv_decode_step_workspace (geometry or head_groups={head_groups} rejected)")
+        self.buf = torch.zeros(self.nbytes, dtype=torch.uint8, device=device)
+        self.miss_count = torch.zeros(geom.batch * geom.kv_heads, dtype=torch.int32, device=device)
+
+
+def step(geom: Geometry, ws: StepWorkspace, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+         positions: torch.Tensor, cos_sin: torch.Tensor, q_out: torch.Tensor, k_buf: torch.Tensor,
+         v_buf: torch.Tensor, row: int, landmarks: torch.Tensor, landmark_idx: torch.Tensor, slots: torch.Tensor,
+         U: torch.Tensor, SVt: torch.Tensor, v_host: torch.Tensor, seq_len: int, out: torch.Tensor,
+         stream=None) -> torch.Tensor:
+    """One whole decode step of a layer (``append_select`` + ``sparse_attention`` over buffer rows
+    [0, seq_len)), pipelined over ``ws.head_groups`` groups of kv heads; ``ws.miss_count`` receives
+    the misses per (b, kv head)."""
+    if v_host.is_cuda or not v_host.is_pinned() or v_host.dtype != torch.bfloat16 or not v_host.is_contiguous():
+        raise RuntimeError("v_host must be a contiguous pinned CPU bf16 tensor")
+    g = geom.c()
+    check(lib.skv_decode_step(
+        ctypes.byref(g), _req(q, "q", torch.bfloat16), _req(k_new, "k_new", torch.bfloat16),
+        _req(v_new, "v_new", torch.bfloat16), _req(positions, "positions", torch.int64),
+        _req(cos_sin, "cos_sin", torch.bfloat16), _req(q_out, "q_out", torch.bfloat16),
+        _req(k_buf, "k_buf", torch.bfloat16), _req(v_buf, "v_buf", torch.bfloat16), int(row),
+        _req(landmarks, "landmarks", torch.bfloat16), _req(landmark_idx, "landmark_idx", torch.int64),
+        _req(slots, "slots", torch.int32), _req(U, "U", torch.bfloat16), _req(SVt, "SVt", torch.bfloat16),
+        v_host.data_ptr(), int(seq_len), _req_out(out), ws.miss_count.data_ptr(), int(ws.head_groups),
+        ws.buf.data_ptr(), ws.nbytes, _stream(stream)), "skv_decode_step")
+    return out
+
+
 def append(geom: Geometry, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, positions: torch.Tensor,
            cos_sin: torch.Tensor, q_out: torch.Tensor, k_buf: torch.Tensor, v_buf: torch.Tensor, row: int,
            stream=None) -> torch.Tensor:

@@ -42,6 +42,17 @@ def auto_microbatch(batch: int) -> int:
     return parts
 
 
+def auto_head_groups(batch: int, kv_heads: int) -> int:
+    """Kv-head groups of the pipelined step (``decode_step_fused``): 4 (or the largest divisor of
+    ``kv_heads`` up to 4) for one sequence, 1 for a batch (sliced by sequence instead)."""
+    if batch != 1:
+        return 1
+    for p in (4, 2):
+        if kv_heads % p == 0 and kv_heads >= p:
+            return p
+    return 1
+
+
 class ShadowKVCache_CPU:
     """ShadowKV cache with host-offloaded values (reference models/kvcache/shadow.py:301)."""
 
@@ -463,6 +474,40 @@ class ShadowKVCache_CPU:
                                       cos_sin_cache, self.v_cache_cpu[layer_idx], self.k_cache_buffer[layer_idx],
                                       self.v_cache_buffer[layer_idx], seq_len, out)
 
+    def decode_step_fused(self, layer_idx, query_states, key_states, value_states, positions, cos_sin_cache,
+                          out=None, head_groups: int | None = None, q_out=None):
+        """One whole decode step of a layer in one library call (``skv_decode_step``): RoPE of the
+        new token's q/k and append at ``sparse_end + gen_offset``, scoring, top-k, slot-stable reuse
+        diff, fetch of the missed values, reconstruction of the missed keys, attention over
+        ``[0, sparse_end + gen_offset + 1)``.  Same results as ``append_select_fused`` +
+        ``sparse_attention_fused``.  ``head_groups`` > 1 (batch 1) pipelines the step over groups
+        of kv heads so the first group's value fetch starts after a fraction of the landmark scan
+        (default ``auto_head_groups``).  Returns ``out`` [B, Hq, D]."""
+        B, Hq, Hk, D = self.batch_size, self.num_attention_heads, self.num_key_value_heads, self.head_dim
+        if head_groups is None:
+            head_groups = auto_head_groups(B, Hk)
+        g = self.fused_geometry(cos_sin_cache)
+        row = self.sparse_end + self.gen_offset
+        if row >= self.buf_len:
+            raise RuntimeError("generated-token region of the K/V buffer is full")
+        sws = getattr(self, "_step_ws", None)
+        if sws is None or sws.head_groups != head_groups:
+            sws = self._step_ws = fused.StepWorkspace(g, head_groups, self.device)
+        if q_out is None:
+            q_out = torch.empty(B, Hq, 1, D, dtype=self.dtype, device=self.device)
+        if out is None:
+            out = torch.empty(B, Hq, D, dtype=self.dtype, device=self.device)
+        fused.step(g, sws, query_states.reshape(B, Hq, D), key_states.reshape(B, Hk, D),
+                   value_states.reshape(B, Hk, D), positions.reshape(B), cos_sin_cache, q_out,
+                   self.k_cache_buffer[layer_idx], self.v_cache_buffer[layer_idx], row, self.k_landmark[layer_idx],
+                   self.k_landmark_idx[layer_idx], self.slots[layer_idx], self.U[layer_idx], self.SV[layer_idx],
+                   self.v_cache_cpu[layer_idx], row + 1, out)
+        self.incoming_q_len = 1
+        if layer_idx == self.num_layers - 1:
+            self.kv_offset += 1
+            self.gen_offset += 1
+        return out
+
     def decode_step_microbatched(self, layer_idx, query_states, key_states, value_states, positions, cos_sin_cache,
                                  out, parts: int, q_out=None, max_ctas: int = 64):
         """The fused step (``append_select_fused`` + ``sparse_attention_fused``) in ``parts`` slices of
@@ -549,11 +594,13 @@ class ShadowKVCache_CPU:
             out = torch.empty_like(q)
         return fused.attention(g, ws, q, self.k_cache_buffer[layer_idx], self.v_cache_buffer[layer_idx], seq_len, out)
 
-    def hit_rate(self) -> float:
-        """Fraction of selected chunks served from the reuse cache in the last fused selection."""
-        if self._fused_ws is None:
+    def hit_rate(self, step: bool = False) -> float:
+        """Fraction of selected chunks served from the reuse cache in the last fused selection
+        (``step``: in the last ``decode_step_fused``)."""
+        ws = getattr(self, "_step_ws", None) if step else self._fused_ws
+        if ws is None:
             return float("nan")
-        miss = self._fused_ws.miss_count.sum().item()
+        miss = ws.miss_count.sum().item()
         return 1.0 - miss / (self.batch_size * self.num_key_value_heads * self.select_sets)
 
     def sync_slots_from_position_ids(self, layer_idx=None):

@@ -4,7 +4,7 @@ The twelve functions below have the names, positional arguments and return
 value (``None``; outputs written in place) of the reference's pybind module
 (kernels/main.cu:24-37, signatures kernels/functions.h:23-121).  A host
 process that did ``from kernels import shadowkv`` can use
-``from shadowkv_b200 import shadowkv`` instead (see INTEGRATION.md).
+``from shadowkv_b200 import shadowkv`` instead.
 
 Differences a caller can observe, all deliberate:
 

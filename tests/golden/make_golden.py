@@ -209,8 +209,11 @@ def make_rope_fixture(rope_single, glm_rope, out_path, seed=1):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("SHADOWKV_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("SHADOWKV_REFERENCE"),
+                    help="root of the reference checkout (or set SHADOWKV_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference or set SHADOWKV_REFERENCE")
     shadow, rope_single, glm_rope = _load_reference(args.reference)
     make_torch_class_fixture(shadow, rope_single, os.path.join(HERE, "torch_class_decode.npz"))
     make_rope_fixture(rope_single, glm_rope, os.path.join(HERE, "rope_bf16.npz"))
