@@ -184,6 +184,100 @@ def make_torch_class_fixture(shadow, rope_single, out_path, T=1024, Hq=8, Hkv=2,
     print("wrote", out_path, os.path.getsize(out_path), "bytes")
 
 
+def config0_values(T=8192, Hkv=2, seed=1):
+    """The value cache of the config-0 fixture, regenerated by the tests instead of stored:
+    V ~ N(0, 1) from numpy's PCG64 with this seed, rounded to bf16 (as float32)."""
+    v = np.random.default_rng(seed).standard_normal((1, Hkv, T, 128), dtype=np.float32)
+    return _bf16(torch.from_numpy(v)).numpy()
+
+
+def make_config0_fixture(shadow, rope_single, out_path, T=8192, Hq=8, Hkv=2, r_true=32, rank=64, budget=512,
+                         outliers=8, steps=3, seed=0):
+    """BASELINE configs[0] through the reference's ``ShadowKVCache`` on CPU in float32.
+
+    Pre-RoPE K = U0 W0 + 0.05 N(0,1) with U0 [T, 32] ~ N(0,1) and W0 [32, 256] ~ N(0, 1/sqrt(32))
+    (variance), V ~ N(0,1), q ~ N(0,1); rank-64 SVD, RoPE theta 500000, chunk 8, budget 512
+    (64 chunks), 8 outlier chunks, 32-token local window.  Inputs are bf16-representable.
+    V and the RoPE table are not stored (``config0_values`` and ``cos_sin_cache`` regenerate them;
+    their SHA-256 digests are stored to check that);
+    the reconstructed keys are stored for step 0 (the oracle is pinned on them), the chunk ids
+    and gathered values' checksum for every step."""
+    import hashlib
+    D = 128
+    rng = np.random.default_rng(seed)
+    U0 = torch.from_numpy(rng.standard_normal((T, r_true), dtype=np.float32))
+    W0 = torch.from_numpy(rng.standard_normal((r_true, Hkv * D), dtype=np.float32)) / math.sqrt(math.sqrt(r_true))
+    noise = torch.from_numpy(rng.standard_normal((T, Hkv * D), dtype=np.float32))
+    k_pre = _bf16(U0 @ W0 + 0.05 * noise).unsqueeze(0)  # [1, T, Hkv*D]
+    v_np = config0_values(T, Hkv)
+    v = torch.from_numpy(v_np)
+    cs = _bf16(cos_sin_cache(T + 1024))
+    cos = torch.cat((cs[:, :64], cs[:, :64]), dim=-1)
+    sin = torch.cat((cs[:, 64:], cs[:, 64:]), dim=-1)
+
+    def rope_func(x, position_ids):
+        return rope_single(x, cos, sin, position_ids)
+
+    cfg = types.SimpleNamespace(num_attention_heads=Hq, num_key_value_heads=Hkv,
+                                hidden_size=Hq * D, num_hidden_layers=1)
+    cache = shadow.ShadowKVCache(cfg, batch_size=1, max_length=T, device="cpu", dtype=torch.float32,
+                                 sparse_budget=budget, chunk_size=8, rank=rank)
+    cache.outlier_chunk = outliers
+    cache.get_svd(k_pre, layer_idx=0)
+    cache.U.copy_(_bf16(cache.U))
+    cache.SV.copy_(_bf16(cache.SV))
+    k_heads = k_pre.view(1, T, Hkv, D).transpose(1, 2)
+    pos = torch.arange(T)
+    k_roped = k_heads * cos[pos] + torch.cat((-k_heads[..., 64:], k_heads[..., :64]), dim=-1) * sin[pos]
+    q_last = torch.from_numpy(rng.standard_normal((1, Hq, 1, D), dtype=np.float32))
+    cache.prefill_kv_cache(v, 0, k_roped, _bf16(q_last))
+    cache.k_landmark.copy_(_bf16(cache.k_landmark))
+    rec = {
+        "T": T, "Hq": Hq, "Hkv": Hkv, "rank": rank, "budget": budget, "outliers": outliers,
+        "sparse_start": cache.sparse_start, "sparse_end": cache.sparse_end,
+        "prefill_local": cache.prefill_local, "chunks": cache.chunks,
+        "v_sha256": np.frombuffer(hashlib.sha256(v_np.tobytes()).digest(), dtype=np.uint8),
+        # the RoPE table is regenerated by the tests (cos_sin_cache(T + 1024)[:T + 64] in bf16)
+        "cos_sin_sha256": np.frombuffer(hashlib.sha256(
+            cs[: T + 64].to(torch.bfloat16).view(torch.int16).numpy().tobytes()).digest(), dtype=np.uint8),
+        "U": cache.U[0].to(torch.bfloat16).view(torch.int16).numpy(),
+        "SV": cache.SV[0].to(torch.bfloat16).view(torch.int16).numpy(),
+        "k_landmark": cache.k_landmark[0].to(torch.bfloat16).view(torch.int16).numpy(),
+        "k_landmark_idx": cache.k_landmark_idx[0].numpy(),
+        "k_prefix": cache.k_cache_buffer[0][:, :, : cache.sparse_start].numpy(),
+        "v_prefix": cache.v_cache_buffer[0][:, :, : cache.sparse_start].to(torch.bfloat16).view(torch.int16).numpy(),
+    }
+    qs, new_ks, new_vs, sel, seqlens, vsums = [], [], [], [], [], []
+    ss, se = cache.sparse_start, cache.sparse_end
+    for step in range(steps):
+        q = _bf16(torch.from_numpy(rng.standard_normal((1, Hq, 1, D), dtype=np.float32)))
+        k_new = _bf16(torch.from_numpy(rng.standard_normal((1, Hkv, 1, D), dtype=np.float32)))
+        v_new = _bf16(torch.from_numpy(rng.standard_normal((1, Hkv, 1, D), dtype=np.float32)))
+        cache.update_kv_cache(k_new, v_new, 0)
+        pid = cache.get_retrieval_position_ids(layer_idx=0, query_states=q)
+        vv = cache.get_value_cache(0, pid)
+        kk = cache.get_key_cache(layer_idx=0, position_ids=pid, rope_func=rope_func, cos_sin_cache=cs)
+        qs.append(q.numpy())
+        new_ks.append(k_new.numpy())
+        new_vs.append(v_new.numpy())
+        sel.append(cache.selected_chunk_idx[0].clone().numpy())
+        seqlens.append(kk.shape[2])
+        vb = vv[:, :, ss:se].contiguous().numpy()
+        vsums.append(np.frombuffer(hashlib.sha256(vb.tobytes()).digest(), dtype=np.uint8))
+        if step == 0:
+            rec["k_sparse0"] = kk[:, :, ss:se].clone().numpy()
+        if step == steps - 1:
+            rec["k_gen"] = kk[:, :, se:].clone().numpy()
+    rec["q"] = np.stack(qs)
+    rec["k_new"] = np.stack(new_ks)
+    rec["v_new"] = np.stack(new_vs)
+    rec["selected_chunk_idx"] = np.stack(sel)
+    rec["seq_len"] = np.array(seqlens)
+    rec["v_sparse_sha256"] = np.stack(vsums)  # float32 rows [sparse_start, sparse_end) per step
+    np.savez_compressed(out_path, **rec)
+    print("wrote", out_path, os.path.getsize(out_path), "bytes")
+
+
 def make_rope_fixture(rope_single, glm_rope, out_path, seed=1):
     g = torch.Generator().manual_seed(seed)
     B, H, S, D = 1, 4, 32, 128  # the reference helper broadcasts only with B=1
@@ -216,6 +310,7 @@ def main():
         ap.error("give --reference or set SHADOWKV_REFERENCE")
     shadow, rope_single, glm_rope = _load_reference(args.reference)
     make_torch_class_fixture(shadow, rope_single, os.path.join(HERE, "torch_class_decode.npz"))
+    make_config0_fixture(shadow, rope_single, os.path.join(HERE, "torch_class_config0.npz"))
     make_rope_fixture(rope_single, glm_rope, os.path.join(HERE, "rope_bf16.npz"))
 
 

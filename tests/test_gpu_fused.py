@@ -111,6 +111,75 @@ def test_fused_step_matches_reference_torch_class(fix):
         np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=2e-2, rtol=1e-2)
 
 
+def test_config0_matches_reference_torch_class(golden_dir):
+    """BASELINE configs[0] (T=8192, 8/2 heads, rank 64, budget 512, 8 outliers, fp32 in the
+    reference) through the reference's ShadowKVCache (tests/golden/make_golden.py), three steps
+    of the shipped kernels: scoring + selection, then value fetch + key reconstruction +
+    attention in one launch.
+
+    Chunk ids and gathered V: bit-exact.  Reconstructed keys and attention: atol 2e-2 / rtol 1e-2.
+    """
+    import hashlib
+    from shadowkv_b200 import decode as fz
+    from tests.test_oracle_golden import config0_inputs
+    d = np.load(os.path.join(golden_dir, "torch_class_config0.npz"))
+    v_np, cs_bits = config0_inputs(d)
+    Hq, Hkv, T, rank = int(d["Hq"]), int(d["Hkv"]), int(d["T"]), int(d["rank"])
+    K = int(d["budget"]) // 8
+    ss, se = int(d["sparse_start"]), int(d["sparse_end"])
+    L = d["k_landmark"].shape[2]
+    buf_len = se + 8
+    g = make_geom(batch=1, kv_heads=Hkv, q_heads=Hq, rank=rank, select_sets=K, num_landmarks=L,
+                  num_chunks=T // 8, ctx_len=T, buf_len=buf_len, sparse_start=ss, cos_sin_rows=cs_bits.shape[0])
+    ws = fz.DecodeWorkspace(g, DEV)
+    lm = torch.from_numpy(d["k_landmark"]).view(torch.bfloat16).to(DEV).contiguous()
+    lidx = torch.from_numpy(d["k_landmark_idx"]).to(DEV)
+    U = torch.from_numpy(d["U"]).view(torch.bfloat16).to(DEV)
+    SVt = torch.from_numpy(d["SV"]).view(torch.bfloat16).to(DEV).transpose(-1, -2).contiguous()
+    cos_sin = torch.from_numpy(cs_bits).view(torch.bfloat16).to(DEV)
+    v_host = torch.from_numpy(v_np).to(torch.bfloat16).reshape(1, Hkv, T // 8, 1024).contiguous().pin_memory()
+    kbuf = torch.zeros(1, Hkv, buf_len, 128, dtype=torch.bfloat16, device=DEV)
+    vbuf = torch.zeros_like(kbuf)
+    kbuf[:, :, :ss] = torch.from_numpy(d["k_prefix"]).to(DEV).to(torch.bfloat16)
+    vbuf[:, :, :ss] = torch.from_numpy(d["v_prefix"]).view(torch.bfloat16).to(DEV)
+    slots = torch.full((1, Hkv, K), -1, dtype=torch.int32, device=DEV)
+    out = torch.empty(1, Hq, 128, dtype=torch.bfloat16, device=DEV)
+    U_f, SV_f, cs_f = bf(d["U"]), bf(d["SV"]), bf(cs_bits)
+    for step in range(d["q"].shape[0]):
+        kbuf[:, :, se + step] = torch.from_numpy(d["k_new"][step][:, :, 0]).to(DEV).to(torch.bfloat16)
+        vbuf[:, :, se + step] = torch.from_numpy(d["v_new"][step][:, :, 0]).to(DEV).to(torch.bfloat16)
+        q = torch.from_numpy(d["q"][step][:, :, 0, :]).to(DEV).to(torch.bfloat16).contiguous()
+        seq_len = int(d["seq_len"][step])
+        fz.select(g, ws, q, lm, lidx, slots)
+        fz.sparse_attention(g, ws, q, U, SVt, cos_sin, v_host, kbuf, vbuf, seq_len, out)
+        torch.cuda.synchronize()
+        assert no_device_errors()
+        sel = d["selected_chunk_idx"][step]  # reference topk order
+        new_slots = slots.cpu().numpy()
+        assert np.array_equal(np.sort(new_slots, -1), np.sort(sel, -1)), f"chunk ids, step {step}"
+        vb = vbuf.float().cpu().numpy()
+        kb = kbuf.float().cpu().numpy()
+        # our slot-stable rows in the reference's slot order: then the reference's checksum applies
+        where = {(h, int(c)): sl for h in range(Hkv) for sl, c in enumerate(new_slots[0, h])}
+        v_ref_order = np.zeros((1, Hkv, 8 * K, 128), np.float32)
+        k_ref_order = np.zeros_like(v_ref_order)
+        for h in range(Hkv):
+            for j in range(K):
+                sl = where[(h, int(sel[0, h, j]))]
+                v_ref_order[0, h, 8 * j: 8 * j + 8] = vb[0, h, ss + 8 * sl: ss + 8 * sl + 8]
+                k_ref_order[0, h, 8 * j: 8 * j + 8] = kb[0, h, ss + 8 * sl: ss + 8 * sl + 8]
+        assert hashlib.sha256(np.ascontiguousarray(v_ref_order).tobytes()).digest() == \
+            d["v_sparse_sha256"][step].tobytes(), f"gathered values, step {step}"
+        k_expect = d["k_sparse0"] if step == 0 else o.reconstruct_keys_fp32(U_f, SV_f, sel, cs_f)
+        np.testing.assert_allclose(k_ref_order, k_expect, atol=2e-2, rtol=1e-2)
+        kfull = np.concatenate([d["k_prefix"], k_expect, d["k_gen"][:, :, : step + 1]], axis=2)
+        vfull = np.concatenate([bf(d["v_prefix"]), v_ref_order,
+                                d["v_new"][: step + 1, :, :, 0].transpose(1, 2, 0, 3)], axis=2)
+        assert kfull.shape[2] == seq_len
+        ref = o.decode_attention(d["q"][step][:, :, 0, :], kfull, vfull, seq_len)
+        np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=2e-2, rtol=1e-2)
+
+
 # ------------------------------------------------------------------ kernels one by one
 
 @pytest.mark.parametrize("G,L,K,H", [(4, 15308, 256, 3), (16, 6000, 256, 2), (1, 700, 64, 2), (4, 2000, 1000, 1),

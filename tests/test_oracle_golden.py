@@ -167,3 +167,54 @@ def test_batch_gemm_softmax_oracle_rows_sum_to_one():
     np.testing.assert_allclose(P.sum(-1), 1.0, atol=2e-2)
     ref = o.landmark_scores(A.reshape(2, 1, 4, 128), B.reshape(2, 1, 700, 128))
     np.testing.assert_allclose(P.max(1), ref[:, 0], atol=1e-2)
+
+
+# ------------------------------------------------------------------ BASELINE configs[0]
+
+def config0_inputs(d):
+    """V and the RoPE table of the config-0 fixture, regenerated and checked against its digests."""
+    import hashlib
+    import torch
+    from tests.golden.make_golden import config0_values, cos_sin_cache
+    T, Hkv = int(d["T"]), int(d["Hkv"])
+    v = config0_values(T, Hkv)
+    assert hashlib.sha256(v.tobytes()).digest() == d["v_sha256"].tobytes(), "regenerated V differs"
+    cs = cos_sin_cache(T + 1024).to(torch.bfloat16)[: T + 64]
+    cs_bits = cs.view(torch.int16).numpy()
+    assert hashlib.sha256(cs_bits.tobytes()).digest() == d["cos_sin_sha256"].tobytes(), "regenerated RoPE table differs"
+    return v, cs_bits
+
+
+@pytest.fixture(scope="module")
+def config0_fix(golden_dir):
+    return np.load(os.path.join(golden_dir, "torch_class_config0.npz"))
+
+
+def test_config0_selection_matches_reference_torch_class(config0_fix):
+    """BASELINE configs[0] (T=8192, budget 512, fp32) through models/kvcache/shadow.py:208-229:
+    the oracle's chunk ids are the reference's, bit for bit, at every step."""
+    d = config0_fix
+    Hq, Hkv = int(d["Hq"]), int(d["Hkv"])
+    lm, lidx = bf(d["k_landmark"]), d["k_landmark_idx"]
+    K = int(d["budget"]) // 8
+    assert K == 64 and lm.shape[2] == 1012
+    for step in range(d["q"].shape[0]):
+        q = d["q"][step][:, :, 0, :].reshape(1, Hkv, Hq // Hkv, 128)
+        ids, _ = o.select_chunks(q, lm, lidx, K)
+        assert np.array_equal(ids, np.sort(d["selected_chunk_idx"][step], axis=-1))
+
+
+def test_config0_values_and_keys_match_reference_torch_class(config0_fix):
+    """shadow.py:231-256 at config 0: gathered V bit-exact (checksum of the reference's rows),
+    reconstructed keys of step 0 within 1e-4 (fp32)."""
+    import hashlib
+    d = config0_fix
+    v, cs_bits = config0_inputs(d)
+    for step in range(d["q"].shape[0]):
+        sel = d["selected_chunk_idx"][step]
+        tok = (sel[..., None] * 8 + np.arange(8)).reshape(1, sel.shape[1], -1)
+        vg = np.ascontiguousarray(np.take_along_axis(v, tok[..., None], axis=2))
+        assert hashlib.sha256(vg.tobytes()).digest() == d["v_sparse_sha256"][step].tobytes()
+    U, SV = bf(d["U"]), bf(d["SV"])
+    kr = o.reconstruct_keys_fp32(U, SV, d["selected_chunk_idx"][0], bf(cs_bits))
+    np.testing.assert_allclose(kr, d["k_sparse0"], atol=1e-4, rtol=1e-4)
