@@ -446,6 +446,14 @@ def run_b200(args, world, rank, local):
         e.synchronize()
         e2e_ms.append(s.elapsed_time(e))
     e2e_step = max_over_ranks(sum(e2e_ms) / len(e2e_ms), world)
+    # every rank's own figures (the slowest rank sets the step; the links are per GPU)
+    mine = [rank, ms_step * 1e3, link_peak, link_achieved, hit_rate]
+    per_rank = [mine]
+    if world > 1:
+        t = torch.tensor(mine, dtype=torch.float64, device="cuda")
+        allt = [torch.empty_like(t) for _ in range(world)]
+        torch.distributed.all_gather(allt, t)
+        per_rank = [x.tolist() for x in allt]
     h2d = nbytes
     d2h = h_out.numel() * h_out.element_size()
     used_graph = graph is not None
@@ -499,6 +507,9 @@ def run_b200(args, world, rank, local):
         "e2e": {"value": tokens / (e2e_step / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "kernel_us": kernel_us,
+        "per_rank": [{"rank": int(r), "step_us": round(st, 2), "link_peak_gbs": round(lp, 2),
+                      "link_achieved_gbs": round(la, 2), "hit_rate": round(hr, 4)}
+                     for r, st, lp, la, hr in per_rank],
         "graph": used_graph,
         "gpu_launches": (select_kernels(cache) + (3 if args.split else 1)) * NL * args.steps
                         * (args.microbatch if args.microbatch > 1 and not args.split and not heads_sharded else 1)

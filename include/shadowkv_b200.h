@@ -449,17 +449,23 @@ SKV_API int skv_decode_sparse_attention_ctas(const skv_decode_geom *g, const voi
  * rank's landing buffer over NVLink and bumps every rank's arrival counter,
  * and skv_peer_gather_finish waits for the counter and copies the full
  * output out of the landing buffer.  Each rank owns one peer block
- * (skv_peer_block_bytes): [arrival counter | epoch | landing buffer
+ * (skv_peer_block_bytes): [arrival counter | status | epoch | landing buffer
  * [2][batch][q_heads_total][128] bf16]; the landing half used by a step is
  * epoch & 1, so a rank one step ahead never writes the half a slower rank
- * still reads.  Blocks are shared through CUDA IPC handles (64 bytes). */
+ * still reads.  Blocks are shared through CUDA IPC handles (64 bytes).
+ * A finish whose wait runs out sets the block's status (sticky) and neither
+ * copies nor advances the epoch; every later finish on that block does
+ * nothing.  Read it with skv_peer_status; after a non-zero status every rank
+ * must re-create its peer blocks (the step counts of the ranks disagree). */
 #define SKV_MAX_PEERS 8
 typedef struct {
     int world;            /* ranks sharing the output, 1..SKV_MAX_PEERS */
     int rank;             /* this rank */
     int q_head0;          /* first query head of this rank in the full output */
     int q_heads_total;    /* query heads of the full output */
-    int merges_per_step;  /* (sequence, kv head) units of one step summed over all ranks */
+    int merges_per_step;  /* (sequence, kv head) units of one step summed over all ranks:
+                             batch * q_heads_total / (q heads per kv head) */
+    int batch;            /* sequences of a step: the landing buffers hold this many */
     void *block[SKV_MAX_PEERS];  /* every rank's peer block, as addressed from this GPU */
 } skv_peer_gather;
 
@@ -474,7 +480,9 @@ SKV_API int skv_peer_import(const void *handle64, void **block);
 SKV_API int skv_peer_close(void *block);
 
 /* skv_decode_sparse_attention with the output written to every rank's
- * landing buffer (rows q_head0 .. q_head0 + q_heads of the full output). */
+ * landing buffer (rows q_head0 .. q_head0 + q_heads of the full output).
+ * g->batch must equal pg->batch and pg->merges_per_step must equal
+ * g->batch * pg->q_heads_total / (g->q_heads / g->kv_heads). */
 SKV_API int skv_decode_sparse_attention_gather(const skv_decode_geom *g, const void *q, const void *U,
                                                const void *SVt, const void *cos_sin, const void *v_host,
                                                void *k_buf, void *v_buf, const int32_t *miss_slot,
@@ -482,12 +490,18 @@ SKV_API int skv_decode_sparse_attention_gather(const skv_decode_geom *g, const v
                                                int seq_len, const skv_peer_gather *pg, void *workspace,
                                                size_t workspace_bytes, void *stream);
 
-/* Waits (bounded; a timeout is counted in skv_device_errors) until every
- * rank's rows of this step have arrived, copies the full output
- * [batch][q_heads_total][128] into `out` (device memory) and advances the
- * epoch.  One call per step, after skv_decode_sparse_attention_gather, on
- * the same stream. */
+/* Waits (bounded, about one second) until every rank's rows of this step
+ * have arrived, copies the full output [batch][q_heads_total][128] into `out`
+ * (device memory) and advances the epoch.  A wait that runs out sets the
+ * block's status to 4 (also counted in skv_device_errors) and copies nothing.
+ * batch must equal pg->batch.  One call per step, after
+ * skv_decode_sparse_attention_gather, on the same stream. */
 SKV_API int skv_peer_gather_finish(const skv_peer_gather *pg, int batch, void *out, void *stream);
+
+/* The status word of this rank's peer block (0: fine; 4: a finish timed out).
+ * Synchronous: waits for the work of the current device (a device-to-host
+ * copy of 4 bytes); call it between steps. */
+SKV_API int skv_peer_status(const skv_peer_gather *pg, uint32_t *status);
 
 #ifdef __cplusplus
 }

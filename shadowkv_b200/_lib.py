@@ -48,7 +48,7 @@ class PeerGather(ctypes.Structure):
 
     _fields_ = [
         ("world", c_int), ("rank", c_int), ("q_head0", c_int), ("q_heads_total", c_int),
-        ("merges_per_step", c_int), ("block", c_void_p * SKV_MAX_PEERS),
+        ("merges_per_step", c_int), ("batch", c_int), ("block", c_void_p * SKV_MAX_PEERS),
     ]
 
 
@@ -96,6 +96,7 @@ SIGNATURES = {
     "skv_peer_import": [P, ctypes.POINTER(c_void_p)],
     "skv_peer_close": [P],
     "skv_peer_gather_finish": [ctypes.POINTER(PeerGather), c_int, P, P],
+    "skv_peer_status": [ctypes.POINTER(PeerGather), P],
 }
 _RET = {"skv_last_error": c_char_p, "skv_decode_select_workspace": c_size_t,
         "skv_decode_attention_workspace": c_size_t, "skv_decode_sparse_attention_workspace": c_size_t,

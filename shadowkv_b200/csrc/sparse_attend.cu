@@ -557,11 +557,12 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
     }  // work items
 }
 
-// Peer block layout: arrival counter, this rank's epoch, landing buffer.
-constexpr size_t PEER_COUNTER_OFF = 0, PEER_EPOCH_OFF = 128, PEER_LANDING_OFF = 256;
+// Peer block layout: arrival counter, status, this rank's epoch, landing buffer.
+constexpr size_t PEER_COUNTER_OFF = 0, PEER_STATUS_OFF = 64, PEER_EPOCH_OFF = 128, PEER_LANDING_OFF = 256;
 
 struct PeerFinishArgs {
     const unsigned *counter;  // arrivals of (sequence, kv head) rows from every rank
+    unsigned *status;         // sticky: DEV_ERR_WAIT once a wait ran out
     unsigned *epoch;          // steps completed by this rank
     const uint4 *landing;     // [2][n16] 16-byte words
     uint4 *out;               // [n16]
@@ -570,29 +571,39 @@ struct PeerFinishArgs {
 };
 
 // One CTA: a bounded wait until every rank's rows of this step have arrived
-// (counter >= (epoch + 1) * merges; a timeout is counted as a device error
-// and the copy goes ahead), the copy of the landing half epoch & 1, and the
-// epoch advance.
+// (counter >= (epoch + 1) * merges), the copy of the landing half epoch & 1,
+// and the epoch advance.  A wait that runs out sets the sticky status (and
+// counts a device error) instead: no copy, no epoch advance -- a late arrival
+// must not count toward the next step -- and every later finish on the block
+// returns at once.
 __global__ void __launch_bounds__(256) peer_gather_finish_kernel(PeerFinishArgs f)
 {
-    __shared__ unsigned s_e;
+    __shared__ unsigned s_e, s_ok;
     if (threadIdx.x == 0) {
         const unsigned e = *f.epoch;
         const unsigned target = (e + 1u) * f.merges;
-        bool ok = false;
-        for (unsigned it = 0; it < (1u << 22); ++it) {
-            unsigned v;
-            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f.counter) : "memory");
-            if ((int)(v - target) >= 0) {
-                ok = true;
-                break;
+        bool ok = *f.status == 0u;  // a block that timed out before stays stopped
+        if (ok) {
+            ok = false;
+            for (unsigned it = 0; it < (1u << 22); ++it) {
+                unsigned v;
+                asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f.counter) : "memory");
+                if ((int)(v - target) >= 0) {
+                    ok = true;
+                    break;
+                }
+                __nanosleep(64);
             }
-            __nanosleep(64);
+            if (!ok) {
+                *f.status = DEV_ERR_WAIT;
+                report_dev_error(DEV_ERR_WAIT);
+            }
         }
-        if (!ok) report_dev_error(DEV_ERR_WAIT);
         s_e = e;
+        s_ok = ok ? 1u : 0u;
     }
     __syncthreads();
+    if (!s_ok) return;
     const uint4 *src = f.landing + (int64_t)(s_e & 1u) * f.n16;
     for (int64_t i = threadIdx.x; i < f.n16; i += blockDim.x) f.out[i] = __ldcg(src + i);
     __syncthreads();
@@ -666,7 +677,12 @@ static int launch_sparse_attention(const skv_decode_geom *g, const void *q, cons
         SKV_CHECK_ARG(pg->q_head0 >= 0 && pg->q_head0 + g->q_heads <= pg->q_heads_total,
                       "peer gather: query heads [%d, %d) outside the %d of the full output", pg->q_head0,
                       pg->q_head0 + g->q_heads, pg->q_heads_total);
-        SKV_CHECK_ARG(pg->merges_per_step >= g->batch * g->kv_heads, "peer gather: merges_per_step too small");
+        SKV_CHECK_ARG(pg->batch == g->batch, "peer gather: the blocks hold batch %d, the step has %d", pg->batch,
+                      g->batch);
+        SKV_CHECK_ARG(pg->q_heads_total % G == 0 &&
+                          (int64_t)pg->merges_per_step == (int64_t)g->batch * (pg->q_heads_total / G),
+                      "peer gather: merges_per_step must be batch * q_heads_total / %d = %lld", G,
+                      (long long)g->batch * (pg->q_heads_total / (G > 0 ? G : 1)));
         for (int r = 0; r < pg->world; ++r)
             SKV_CHECK_ARG(pg->block[r] && aligned(pg->block[r], 256), "peer gather: block %d null or unaligned", r);
     }
@@ -860,13 +876,16 @@ int skv_peer_gather_finish(const skv_peer_gather *pg, int batch, void *out, void
 {
     SKV_CHECK_ARG(pg && out && batch > 0, "null pointer argument or batch <= 0");
     SKV_CHECK_ARG(pg->world >= 1 && pg->world <= SKV_MAX_PEERS && pg->rank >= 0 && pg->rank < pg->world &&
-                      pg->q_heads_total > 0 && pg->merges_per_step > 0,
+                      pg->q_heads_total > 0 && pg->merges_per_step > 0 &&
+                      (int64_t)pg->merges_per_step <= (int64_t)pg->batch * pg->q_heads_total,
                   "bad peer gather description");
+    SKV_CHECK_ARG(batch == pg->batch, "peer gather: the blocks hold batch %d, finish asked for %d", pg->batch, batch);
     SKV_CHECK_ARG(pg->block[pg->rank] && aligned(pg->block[pg->rank], 256) && aligned(out, 16),
                   "peer block or output unaligned");
     unsigned char *blk = static_cast<unsigned char *>(pg->block[pg->rank]);
     PeerFinishArgs f;
     f.counter = reinterpret_cast<const unsigned *>(blk + PEER_COUNTER_OFF);
+    f.status = reinterpret_cast<unsigned *>(blk + PEER_STATUS_OFF);
     f.epoch = reinterpret_cast<unsigned *>(blk + PEER_EPOCH_OFF);
     f.landing = reinterpret_cast<const uint4 *>(blk + PEER_LANDING_OFF);
     f.out = static_cast<uint4 *>(out);
@@ -874,6 +893,15 @@ int skv_peer_gather_finish(const skv_peer_gather *pg, int batch, void *out, void
     f.merges = (unsigned)pg->merges_per_step;
     peer_gather_finish_kernel<<<1, 256, 0, (cudaStream_t)stream>>>(f);
     return check_launch("peer_gather_finish_kernel");
+}
+
+int skv_peer_status(const skv_peer_gather *pg, uint32_t *status)
+{
+    SKV_CHECK_ARG(pg && status && pg->rank >= 0 && pg->rank < SKV_MAX_PEERS && pg->block[pg->rank],
+                  "null pointer argument or bad rank");
+    const unsigned char *blk = static_cast<const unsigned char *>(pg->block[pg->rank]);
+    SKV_CUDA(cudaMemcpy(status, blk + PEER_STATUS_OFF, sizeof(uint32_t), cudaMemcpyDeviceToHost));
+    return SKV_OK;
 }
 
 }  // extern "C"

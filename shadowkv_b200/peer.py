@@ -15,6 +15,11 @@ handles exchanged with ``torch.distributed.all_gather_object``.  The
 landing buffer is double-buffered by step parity, so a rank one step ahead
 never overwrites rows a slower rank is still copying.  Every rank must call
 ``attention`` and ``finish`` once per step, in that order, on one stream.
+
+A ``finish`` whose bounded wait runs out (a rank died or stopped stepping)
+sets its block's sticky status and copies nothing; every later ``finish`` on
+the block does nothing.  ``check`` (between steps) raises ``ShadowKVError``
+once that happened; the ranks must then re-create their peer blocks.
 """
 from __future__ import annotations
 
@@ -23,7 +28,7 @@ import ctypes
 import torch
 
 from . import decode
-from ._lib import SKV_MAX_PEERS, PeerGather, check, lib
+from ._lib import SKV_MAX_PEERS, PeerGather, ShadowKVError, check, lib
 
 
 class PeerOutput:
@@ -35,6 +40,7 @@ class PeerOutput:
         self.pg = PeerGather()
         self.pg.world, self.pg.rank = len(blocks), rank
         self.pg.q_head0, self.pg.q_heads_total, self.pg.merges_per_step = q_head0, q_heads_total, merges_per_step
+        self.pg.batch = batch
         for r, b in enumerate(blocks):
             self.pg.block[r] = b
         self._own = own_block
@@ -99,6 +105,19 @@ class PeerOutput:
         check(lib.skv_peer_gather_finish(ctypes.byref(self.pg), self.batch, out.data_ptr(), decode._stream(stream)),
               "skv_peer_gather_finish")
         return out
+
+    def status(self) -> int:
+        """This rank's block status (0: fine; 4: a finish timed out).  Synchronises the device."""
+        st = ctypes.c_uint32(0)
+        check(lib.skv_peer_status(ctypes.byref(self.pg), ctypes.byref(st)), "skv_peer_status")
+        return int(st.value)
+
+    def check(self) -> None:
+        """Raise if a finish of this rank timed out (the peer blocks must then be re-created)."""
+        st = self.status()
+        if st:
+            raise ShadowKVError(f"peer gather of rank {self.pg.rank}: a finish timed out waiting for the other "
+                                f"ranks' rows (status {st}); re-create the peer blocks on every rank")
 
     def close(self, free_own: bool = True):
         """Unmap the peers' blocks and free this rank's (after every rank is done with it)."""

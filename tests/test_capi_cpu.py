@@ -81,12 +81,12 @@ def test_ctypes_signatures_match_header_parameter_counts():
 
 def test_peer_gather_struct_and_block_size_match_the_header():
     from shadowkv_b200 import _lib
-    # int world, rank, q_head0, q_heads_total, merges_per_step; void *block[8]
+    # int world, rank, q_head0, q_heads_total, merges_per_step, batch; void *block[8]
     assert ctypes.sizeof(_lib.PeerGather) == 24 + 8 * _lib.SKV_MAX_PEERS
-    assert _lib.PeerGather.block.offset == 24
+    assert _lib.PeerGather.block.offset == 24 and _lib.PeerGather.batch.offset == 20
     src = open(os.path.join(ROOT, "include", "shadowkv_b200.h")).read()
     assert re.search(r"#define SKV_MAX_PEERS\s+%d\b" % _lib.SKV_MAX_PEERS, src)
-    # counter | epoch | landing [2][batch][q_heads_total][128] bf16
+    # counter | status | epoch | landing [2][batch][q_heads_total][128] bf16
     assert _lib.lib.skv_peer_block_bytes(1, 32) == 256 + 2 * 32 * 128 * 2
     assert _lib.lib.skv_peer_block_bytes(0, 32) == 0 and _lib.lib.skv_peer_block_bytes(2, 0) == 0
 
@@ -110,7 +110,8 @@ def test_peer_output_description_is_built_on_the_host():
     from shadowkv_b200.peer import PeerOutput
     p = PeerOutput(batch=2, q_heads_total=32, q_head0=16, merges_per_step=16, rank=1, blocks=[0x1000, 0x2000],
                    own_block=0)  # own_block 0: nothing to free
-    assert (p.pg.world, p.pg.rank, p.pg.q_head0, p.pg.q_heads_total, p.pg.merges_per_step) == (2, 1, 16, 32, 16)
+    assert (p.pg.world, p.pg.rank, p.pg.q_head0, p.pg.q_heads_total, p.pg.merges_per_step, p.pg.batch) == \
+        (2, 1, 16, 32, 16, 2)
     assert list(p.pg.block[:2]) == [0x1000, 0x2000] and not any(p.pg.block[2:])
     with pytest.raises(RuntimeError):
         PeerOutput(1, 8, 0, 2, 0, [0x1000] * 9, 0)  # more ranks than the library supports
@@ -228,3 +229,16 @@ def test_c_host_program_uses_the_header_and_library(tmp_path):
     assert int(f[3]) == lib.skv_prefill_workspace(ctypes.byref(pg)) > 0
     assert int(f[4]) == lib.skv_peer_block_bytes(32, 32) > 0
     assert int(f[5]) == 1 and "null" in f[6]
+
+
+def test_peer_finish_refuses_a_batch_the_blocks_do_not_hold():
+    """Checked on the host before any launch: a finish for another batch than the blocks were
+    sized for, or a merge count above batch * q_heads_total, is an invalid argument."""
+    from shadowkv_b200 import _lib
+    from shadowkv_b200.peer import PeerOutput
+    p = PeerOutput(batch=2, q_heads_total=32, q_head0=0, merges_per_step=16, rank=0, blocks=[0x1000], own_block=0)
+    st = _lib.lib.skv_peer_gather_finish(ctypes.byref(p.pg), 3, ctypes.c_void_p(0x2000), None)
+    assert st == 1 and b"batch" in _lib.lib.skv_last_error()
+    p.pg.merges_per_step = 2 * 32 + 1
+    st = _lib.lib.skv_peer_gather_finish(ctypes.byref(p.pg), 2, ctypes.c_void_p(0x2000), None)
+    assert st == 1

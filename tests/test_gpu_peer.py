@@ -79,20 +79,33 @@ def test_peer_gather_rejects_bad_descriptions():
 
 def test_finish_wait_runs_out_and_reports_a_status():
     """Nothing raises the arrival counter: the finish kernel's bounded wait runs out, a wait
-    error is counted for the host to read, and the context stays usable."""
+    error is counted for the host to read, and the context stays usable.  The block's status
+    is sticky: that finish copied nothing, the next finish returns at once without waiting or
+    copying, and ``check`` raises until the blocks are re-created."""
     import time
-    from shadowkv_b200._lib import device_errors
+    from shadowkv_b200._lib import ShadowKVError, device_errors
     from shadowkv_b200.peer import PeerOutput
     device_errors()  # clear
     (p,) = PeerOutput.in_process(1, 8, [0], merges_per_step=2)
     try:
-        out = torch.empty(1, 8, 128, dtype=torch.bfloat16, device=DEV)
+        assert p.status() == 0
+        p.check()
+        out = torch.full((1, 8, 128), 7.0, dtype=torch.bfloat16, device=DEV)
         t0 = time.time()
         p.finish(out)  # no attention launch: the counter stays at zero
         torch.cuda.synchronize()
         waited = time.time() - t0
         assert device_errors() == (1, 4)  # one DEV_ERR_WAIT
         assert waited < 60
+        assert p.status() == 4
+        assert bool((out.float() == 7.0).all()), "a timed-out finish copies nothing"
+        with pytest.raises(ShadowKVError):
+            p.check()
+        t0 = time.time()
+        p.finish(out)  # stopped block: returns at once
+        torch.cuda.synchronize()
+        assert time.time() - t0 < 0.5 * max(waited, 0.2)
+        assert device_errors() == (0, 0) and bool((out.float() == 7.0).all())
     finally:
         p.close()
     x = torch.arange(1024, device=DEV, dtype=torch.float32)
