@@ -377,6 +377,12 @@ SKV_API size_t skv_decode_step_workspace(const skv_decode_geom *g, int head_grou
  * `stream`, so stream capture records the whole step.  The library streams
  * and events of a device are created by its first call with head_groups > 1:
  * make that call outside stream capture.
+ * row_dev (optional, device int32): the append row read on the device at run
+ * time -- the attention then covers rows [0, *row_dev + 1) -- so a captured
+ * step can be replayed at later positions (advance *row_dev between
+ * replays); `row` and `seq_len` are then the largest row and row count the
+ * position may reach (they size the launches).  A position outside them is
+ * counted in skv_device_errors (code 3) and the launch's own values are used.
  * Replaces, per step, shadowkv.batch_gemm_softmax + torch.topk +
  * reorder_keys_and_compute_offsets + gather_copy_with_offsets +
  * gather_copy_d2d_with_offsets + batch_gather_gemm + the push-cache RoPE and
@@ -384,7 +390,8 @@ SKV_API size_t skv_decode_step_workspace(const skv_decode_geom *g, int head_grou
  * models/attention/shadow.py:22-48). */
 SKV_API int skv_decode_step(const skv_decode_geom *g, const void *q, const void *k_new, const void *v_new,
                             const int64_t *positions, const void *cos_sin, void *q_out, void *k_buf,
-                            void *v_buf, int row, const void *landmarks, const int64_t *landmark_idx,
+                            void *v_buf, int row, const int32_t *row_dev, const void *landmarks,
+                            const int64_t *landmark_idx,
                             int32_t *slots, const void *U, const void *SVt, const void *v_host,
                             int seq_len, void *out, int32_t *miss_count, int head_groups,
                             void *workspace, size_t workspace_bytes, void *stream);

@@ -6,7 +6,8 @@ shadowkv   drop-in for the reference's ``kernels.shadowkv`` extension (12 bindin
 tensor_op  the reference's decode-path helpers of models/tensor_op.py
 kvcache    ``ShadowKVCache_CPU`` (reference path and fused slot-stable path)
 attention  ``ShadowAttention.decode`` / ``decode_fused``
-decode     torch wrappers of the fused ``skv_decode_*`` C ABI
+decode     torch wrappers of the fused ``skv_decode_*`` C ABI (``step``: the one-call step)
+graph      ``DecodeGraph``: the decode step of every layer captured as one CUDA graph
 sharding   batch / KV-head partition across GPUs (head ranges; NCCL all-gather helper)
 peer       kv-head outputs exchanged by the attention kernel over NVLink peer memory
 workload   seeded synthetic workloads with the benchmark shapes

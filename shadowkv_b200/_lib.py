@@ -85,7 +85,7 @@ SIGNATURES = {
     "skv_decode_sparse_attention_gather": [ctypes.POINTER(DecodeGeom)] + [P] * 10
                                           + [c_int, ctypes.POINTER(PeerGather), P, c_size_t, P],
     "skv_decode_step_workspace": [ctypes.POINTER(DecodeGeom), c_int],
-    "skv_decode_step": [ctypes.POINTER(DecodeGeom)] + [P] * 8 + [c_int] + [P] * 6 + [c_int, P, P, c_int, P, c_size_t, P],
+    "skv_decode_step": [ctypes.POINTER(DecodeGeom)] + [P] * 8 + [c_int] + [P] * 7 + [c_int, P, P, c_int, P, c_size_t, P],
     "skv_prefill_workspace": [ctypes.POINTER(PrefillGeom)],
     "skv_prefill_store_values": [ctypes.POINTER(PrefillGeom), P, P, P],
     "skv_prefill_build": [ctypes.POINTER(PrefillGeom)] + [P] * 10 + [c_size_t, P],

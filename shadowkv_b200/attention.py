@@ -92,6 +92,12 @@ class ShadowAttention:
         out = kv.sparse_attention_fused(layer_idx, query_states, seq_len, self.cos_sin_cache)
         return out.view(out.shape[0], 1, out.shape[1], out.shape[2])
 
+    def decode_graph(self, head_groups: int | None = None, chain: bool = False):
+        """A ``graph.DecodeGraph`` over this attention's cache: the decode step of every layer
+        captured once as a CUDA graph and replayed for the following tokens."""
+        from .graph import DecodeGraph
+        return DecodeGraph(self, head_groups=head_groups, chain=chain)
+
     def decode_fused_split(self, query_states, key_states, value_states, position_ids, layer_idx):
         """decode_fused with fetch, reconstruction and attention as three launches
         (fetch on the copy stream, overlapping the reconstruction)."""

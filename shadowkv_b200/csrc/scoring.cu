@@ -108,6 +108,7 @@ struct ScoreArgs {
     const int64_t *positions;
     __nv_bfloat16 *q_out, *k_buf, *v_buf;
     int buf_len, row, rope_mode, cs_stride, cs_rows;
+    const int32_t *row_dev;  // if set: the append row, read on the device (graph replays of later steps)
 };
 
 template <int NT, bool APPEND>
@@ -181,9 +182,12 @@ __global__ void __launch_bounds__(ST_THREADS, 2) score_tma_kernel(ScoreArgs a)
             if (r < G && pos_ok) rope_pair_bf16(s_raw + r * 128, sQ + r * 128, cs, t, a.rope_mode);
             else if (r >= G) { sQ[r * 128 + t] = f2bf(0.f); sQ[r * 128 + t + 64] = f2bf(0.f); }
         }
-        if (split == 0 && pos_ok) {
+        const int row = a.row_dev ? *a.row_dev : a.row;
+        const bool row_ok = row >= 0 && row < a.buf_len;
+        if (!row_ok && tid == 0 && split == 0) report_dev_error(DEV_ERR_ROW);
+        if (split == 0 && pos_ok && row_ok) {
             // new token: rotated key and value of head h at buffer row `row`
-            const int64_t brow = ((int64_t)bh * a.buf_len + a.row) * 128;
+            const int64_t brow = ((int64_t)bh * a.buf_len + row) * 128;
             if (tid < 64) rope_pair_bf16(s_raw + 16 * 128, a.k_buf + brow, cs, tid, a.rope_mode);
             else if (tid < 80) st_v4(a.v_buf + brow + (tid - 64) * 8, vnew);
         }
@@ -583,7 +587,7 @@ int skv_decode_append_select(const skv_decode_geom *g, const void *q, const void
 {
     return skv::append_select_launch(g, q, k_new, v_new, positions, cos_sin, q_out, k_buf, v_buf, row, landmarks,
                                      landmark_idx, slots, miss_slot, miss_chunk, miss_count, workspace,
-                                     workspace_bytes, (cudaStream_t)stream);
+                                     workspace_bytes, (cudaStream_t)stream, nullptr);
 }
 
 }  // extern "C"
@@ -594,7 +598,7 @@ int append_select_launch(const skv_decode_geom *g, const void *q, const void *k_
                          const int64_t *positions, const void *cos_sin, void *q_out, void *k_buf, void *v_buf,
                          int row, const void *landmarks, const int64_t *landmark_idx, int32_t *slots,
                          int32_t *miss_slot, int32_t *miss_chunk, int32_t *miss_count, void *workspace,
-                         size_t workspace_bytes, cudaStream_t stream)
+                         size_t workspace_bytes, cudaStream_t stream, const int32_t *row_dev)
 {
     int st = check_geom(g);
     if (st) return st;
@@ -619,6 +623,7 @@ int append_select_launch(const skv_decode_geom *g, const void *q, const void *k_
     sa.v_buf = (__nv_bfloat16 *)v_buf;
     sa.buf_len = g->buf_len;
     sa.row = row;
+    sa.row_dev = row_dev;
     sa.rope_mode = g->rope_mode;
     sa.cs_stride = g->cos_sin_stride;
     sa.cs_rows = g->cos_sin_rows;

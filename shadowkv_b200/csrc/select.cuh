@@ -81,11 +81,21 @@ bool select_cluster16_ok(size_t smem);
 
 int launch_select(const SelectArgs &a, int BH, size_t smem, int cl, cudaStream_t stream);
 
-// skv_decode_append_select on a cudaStream_t (for the library's own callers)
+// skv_decode_append_select on a cudaStream_t (for the library's own callers);
+// row_dev (optional): the append row read on the device instead of `row`
 int append_select_launch(const skv_decode_geom *g, const void *q, const void *k_new, const void *v_new,
                          const int64_t *positions, const void *cos_sin, void *q_out, void *k_buf, void *v_buf,
                          int row, const void *landmarks, const int64_t *landmark_idx, int32_t *slots,
                          int32_t *miss_slot, int32_t *miss_chunk, int32_t *miss_count, void *workspace,
-                         size_t workspace_bytes, cudaStream_t stream);
+                         size_t workspace_bytes, cudaStream_t stream, const int32_t *row_dev);
+
+// skv_decode_sparse_attention with a device-side position: row_dev (optional)
+// holds the row the step appended at; the attention covers [0, *row_dev + 1),
+// at most seq_len rows (which sizes the grid and the workspace)
+int sparse_attention_launch(const skv_decode_geom *g, const void *q, const void *U, const void *SVt,
+                            const void *cos_sin, const void *v_host, void *k_buf, void *v_buf,
+                            const int32_t *miss_slot, const int32_t *miss_chunk, const int32_t *miss_count,
+                            int seq_len, void *out, void *workspace, size_t workspace_bytes, cudaStream_t stream,
+                            const int32_t *row_dev);
 
 }  // namespace skv

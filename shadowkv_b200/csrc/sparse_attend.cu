@@ -32,7 +32,7 @@
 // the merge overlaps the value transfer.
 #include <string.h>
 
-#include "common.cuh"
+#include "select.cuh"
 
 namespace skv {
 
@@ -64,6 +64,9 @@ struct SparseAttendArgs {
     __nv_bfloat16 *landing[SKV_MAX_PEERS];
     unsigned *counter[SKV_MAX_PEERS];
     const unsigned *epoch;
+    // if set: the row this step appended at, read on the device; the attention
+    // then covers [0, *row_dev + 1) (at most seq_len rows, which sized the grid)
+    const int32_t *row_dev;
 };
 
 __device__ __forceinline__ void sa_ldsm(uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3, const void *p)
@@ -112,7 +115,7 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
     // link.  One item per CTA for a full grid; a grid of fewer CTAs (leaving
     // SMs to other work while the link is busy) walks the items in strides.
     unsigned iter = 0;
-    for (int item = blockIdx.x; item < a.total; item += gridDim.x, ++iter) {
+    for (int item = blockIdx.x; item < a.total; item += gridDim.x) {
     __syncthreads();  // the previous item's shared memory is no longer read
     int blk, bh;
     {
@@ -131,11 +134,20 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
             blk = j < blo ? j : j + nheavy;
         }
     }
+    // rows of this step: seq_len from the launch, or the device-side position
+    int seq_len = a.seq_len;
+    if (a.row_dev) {
+        const int r1 = *a.row_dev + 1;
+        if (r1 >= a.sparse_start + 8 * a.K && r1 <= a.seq_len) seq_len = r1;
+        else if (threadIdx.x == 0 && blk == 0) report_dev_error(DEV_ERR_ROW);
+    }
+    const int nblk = ceil_div(seq_len, SA_ROWS);  // blocks of this step (a.nblk: of the grid and the partials' stride)
+    if (blk >= nblk) continue;                    // past this step's rows: no work, no ticket
     const int b = bh / a.Hkv;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = a.G;
     const int row0 = blk * SA_ROWS;
-    const int nrows = min(SA_ROWS, a.seq_len - row0);
+    const int nrows = min(SA_ROWS, seq_len - row0);
     const int sparse_end = a.sparse_start + 8 * a.K;
     const bool has_slots = row0 < sparse_end && row0 + SA_ROWS > a.sparse_start;
     const int ppr = a.rank / 8;  // 16-byte pieces per U / SV^T row
@@ -472,7 +484,7 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
     }
     __threadfence();
     __syncthreads();
-    if (tid == 0) s_last = atomicAdd(&a.ticket[bh], 1u) == (unsigned)(a.nblk - 1) ? 1u : 0u;
+    if (tid == 0) s_last = atomicAdd(&a.ticket[bh], 1u) == (unsigned)(nblk - 1) ? 1u : 0u;
     SKV_TRACE_CTA(TR_SA_TICKET);
     __syncthreads();
     if (s_last) {
@@ -484,30 +496,30 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
     // w_j = exp(m_j - M) / L meanwhile (the tiles' shared memory is free).
     {
         constexpr int SA_MERGE_REGS = 16;
-        const int nml = a.nblk * G;
+        const int nml = nblk * G;  // the step's partials: the head's first nblk
         float2 *s_ml = reinterpret_cast<float2 *>(smem_raw);  // [nblk][G]
         float *s_w = reinterpret_cast<float *>(s_ml + nml);  // [nblk][G]
-        const float2 *ml = a.part_ml + (int64_t)bh * nml;
+        const float2 *ml = a.part_ml + (int64_t)bh * a.nblk * G;
         const float *po_head = a.part_o + (int64_t)bh * a.nblk * G * 128;
         float4 pre[SA_MERGE_REGS];
         if (tid < G * 32) {
             const float *po = po_head + (tid >> 5) * 128 + (tid & 31) * 4;
 #pragma unroll
             for (int j = 0; j < SA_MERGE_REGS; ++j)
-                if (j < a.nblk) pre[j] = __ldcg(reinterpret_cast<const float4 *>(po + (int64_t)j * G * 128));
+                if (j < nblk) pre[j] = __ldcg(reinterpret_cast<const float4 *>(po + (int64_t)j * G * 128));
         }
         for (int t = tid; t < nml; t += SA_THREADS) s_ml[t] = __ldcg(&ml[t]);
         __syncthreads();
         for (int gg = warp; gg < G; gg += SA_THREADS / 32) {
             float M = -INFINITY, L = 0.f;
-            for (int j = lane; j < a.nblk; j += 32) M = fmaxf(M, s_ml[j * G + gg].x);
+            for (int j = lane; j < nblk; j += 32) M = fmaxf(M, s_ml[j * G + gg].x);
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-            for (int j = lane; j < a.nblk; j += 32) L += s_ml[j * G + gg].y * __expf(s_ml[j * G + gg].x - M);
+            for (int j = lane; j < nblk; j += 32) L += s_ml[j * G + gg].y * __expf(s_ml[j * G + gg].x - M);
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
             const float inv = 1.f / L;
-            for (int j = lane; j < a.nblk; j += 32) s_w[j * G + gg] = __expf(s_ml[j * G + gg].x - M) * inv;
+            for (int j = lane; j < nblk; j += 32) s_w[j * G + gg] = __expf(s_ml[j * G + gg].x - M) * inv;
         }
         __syncthreads();
         for (int p = tid; p < G * 32; p += SA_THREADS) {
@@ -518,14 +530,14 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
             if (p == tid) {  // the first row: partials already in registers
 #pragma unroll
                 for (int j = 0; j < SA_MERGE_REGS; ++j)
-                    if (j < a.nblk) {
+                    if (j < nblk) {
                         const float w = s_w[j * G + gg];
                         acc.x += pre[j].x * w, acc.y += pre[j].y * w, acc.z += pre[j].z * w, acc.w += pre[j].w * w;
                     }
-                j0 = min(a.nblk, SA_MERGE_REGS);
+                j0 = min(nblk, SA_MERGE_REGS);
             }
 #pragma unroll 8
-            for (int j = j0; j < a.nblk; ++j) {
+            for (int j = j0; j < nblk; ++j) {
                 const float4 v = __ldcg(reinterpret_cast<const float4 *>(po + (int64_t)j * G * 128));
                 const float w = s_w[j * G + gg];
                 acc.x += v.x * w, acc.y += v.y * w, acc.z += v.z * w, acc.w += v.w * w;
@@ -554,6 +566,7 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
     if (tid == 0) a.ticket[bh] = 0;  // ready for the next launch
     SKV_TRACE_CTA(TR_SA_MERGED);
     }  // the head's last block
+    ++iter;  // items that did work: the phase of the copy barrier
     }  // work items
 }
 
@@ -638,7 +651,7 @@ static int launch_sparse_attention(const skv_decode_geom *g, const void *q, cons
                                    const int32_t *miss_slot, const int32_t *miss_chunk,
                                    const int32_t *miss_count, int seq_len, void *out,
                                    const skv_peer_gather *pg, void *workspace, size_t workspace_bytes,
-                                   void *stream, int max_ctas = 0)
+                                   void *stream, int max_ctas = 0, const int32_t *row_dev = nullptr)
 {
     SKV_CHECK_ARG(g && q && U && SVt && cos_sin && k_buf && v_buf && miss_slot && miss_chunk && miss_count &&
                       (out || pg) && workspace,
@@ -729,6 +742,7 @@ static int launch_sparse_attention(const skv_decode_geom *g, const void *q, cons
     a.buf_len = g->buf_len;
     a.sparse_start = g->sparse_start;
     a.seq_len = seq_len;
+    a.row_dev = row_dev;
     a.nblk = nblk;
     a.total = nblk * BH;
     a.rope_mode = g->rope_mode;
@@ -760,6 +774,17 @@ static int launch_sparse_attention(const skv_decode_geom *g, const void *q, cons
         return SKV_ERR_CUDA;
     }
     return SKV_OK;
+}
+
+int skv::sparse_attention_launch(const skv_decode_geom *g, const void *q, const void *U, const void *SVt,
+                                 const void *cos_sin, const void *v_host, void *k_buf, void *v_buf,
+                                 const int32_t *miss_slot, const int32_t *miss_chunk, const int32_t *miss_count,
+                                 int seq_len, void *out, void *workspace, size_t workspace_bytes, cudaStream_t stream,
+                                 const int32_t *row_dev)
+{
+    SKV_CHECK_ARG(out != nullptr, "null pointer argument");
+    return launch_sparse_attention(g, q, U, SVt, cos_sin, v_host, k_buf, v_buf, miss_slot, miss_chunk, miss_count,
+                                   seq_len, out, nullptr, workspace, workspace_bytes, stream, 0, row_dev);
 }
 
 extern "C" {

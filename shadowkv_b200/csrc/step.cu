@@ -122,7 +122,8 @@ size_t skv_decode_step_workspace(const skv_decode_geom *g, int head_groups)
 
 int skv_decode_step(const skv_decode_geom *g, const void *q, const void *k_new, const void *v_new,
                     const int64_t *positions, const void *cos_sin, void *q_out, void *k_buf, void *v_buf,
-                    int row, const void *landmarks, const int64_t *landmark_idx, int32_t *slots, const void *U,
+                    int row, const int32_t *row_dev, const void *landmarks, const int64_t *landmark_idx,
+                    int32_t *slots, const void *U,
                     const void *SVt, const void *v_host, int seq_len, void *out, int32_t *miss_count,
                     int head_groups, void *workspace, size_t workspace_bytes, void *stream)
 {
@@ -159,12 +160,12 @@ int skv_decode_step(const skv_decode_geom *g, const void *q, const void *k_new, 
                                       (const __nv_bfloat16 *)v_new + h0 * 128, positions, cos_sin, qo, kb, vb, row,
                                       (const __nv_bfloat16 *)landmarks + h0 * g->num_landmarks * 128,
                                       landmark_idx + h0 * g->num_landmarks, slots + h0 * g->select_sets, ms, mc, mn,
-                                      w + L.sel, L.sel_bytes, s);
+                                      w + L.sel, L.sel_bytes, s, row_dev);
         if (st) return st;
-        return skv_decode_sparse_attention(&gp, qo, U, (const __nv_bfloat16 *)SVt + h0 * 128 * g->rank, cos_sin,
-                                           (const __nv_bfloat16 *)v_host + h0 * (int64_t)g->num_chunks * 1024, kb, vb,
-                                           ms, mc, mn, seq_len, (__nv_bfloat16 *)out + h0 * G * 128, w + L.att,
-                                           L.att_bytes, s);
+        return sparse_attention_launch(&gp, qo, U, (const __nv_bfloat16 *)SVt + h0 * 128 * g->rank, cos_sin,
+                                       (const __nv_bfloat16 *)v_host + h0 * (int64_t)g->num_chunks * 1024, kb, vb,
+                                       ms, mc, mn, seq_len, (__nv_bfloat16 *)out + h0 * G * 128, w + L.att,
+                                       L.att_bytes, s, row_dev);
     };
 
     if (head_groups == 1) return group(0, caller);

@@ -113,10 +113,11 @@ def step(geom: Geometry, ws: StepWorkspace, q: torch.Tensor, k_new: torch.Tensor
          positions: torch.Tensor, cos_sin: torch.Tensor, q_out: torch.Tensor, k_buf: torch.Tensor,
          v_buf: torch.Tensor, row: int, landmarks: torch.Tensor, landmark_idx: torch.Tensor, slots: torch.Tensor,
          U: torch.Tensor, SVt: torch.Tensor, v_host: torch.Tensor, seq_len: int, out: torch.Tensor,
-         stream=None) -> torch.Tensor:
+         stream=None, row_dev: torch.Tensor | None = None) -> torch.Tensor:
     """One whole decode step of a layer (``append_select`` + ``sparse_attention`` over buffer rows
     [0, seq_len)), pipelined over ``ws.head_groups`` groups of kv heads; ``ws.miss_count`` receives
-    the misses per (b, kv head)."""
+    the misses per (b, kv head).  ``row_dev`` (one int32 on the device): the append row read at run
+    time, the attention then covering [0, row_dev + 1); ``row`` / ``seq_len`` are then its bounds."""
     if v_host.is_cuda or not v_host.is_pinned() or v_host.dtype != torch.bfloat16 or not v_host.is_contiguous():
         raise RuntimeError("v_host must be a contiguous pinned CPU bf16 tensor")
     g = geom.c()
@@ -125,6 +126,7 @@ def step(geom: Geometry, ws: StepWorkspace, q: torch.Tensor, k_new: torch.Tensor
         _req(v_new, "v_new", torch.bfloat16), _req(positions, "positions", torch.int64),
         _req(cos_sin, "cos_sin", torch.bfloat16), _req(q_out, "q_out", torch.bfloat16),
         _req(k_buf, "k_buf", torch.bfloat16), _req(v_buf, "v_buf", torch.bfloat16), int(row),
+        _req(row_dev, "row_dev", torch.int32, (1,)) if row_dev is not None else None,
         _req(landmarks, "landmarks", torch.bfloat16), _req(landmark_idx, "landmark_idx", torch.int64),
         _req(slots, "slots", torch.int32), _req(U, "U", torch.bfloat16), _req(SVt, "SVt", torch.bfloat16),
         v_host.data_ptr(), int(seq_len), _req_out(out), ws.miss_count.data_ptr(), int(ws.head_groups),

@@ -475,14 +475,17 @@ class ShadowKVCache_CPU:
                                       self.v_cache_buffer[layer_idx], seq_len, out)
 
     def decode_step_fused(self, layer_idx, query_states, key_states, value_states, positions, cos_sin_cache,
-                          out=None, head_groups: int | None = None, q_out=None):
+                          out=None, head_groups: int | None = None, q_out=None, row_dev=None):
         """One whole decode step of a layer in one library call (``skv_decode_step``): RoPE of the
         new token's q/k and append at ``sparse_end + gen_offset``, scoring, top-k, slot-stable reuse
         diff, fetch of the missed values, reconstruction of the missed keys, attention over
         ``[0, sparse_end + gen_offset + 1)``.  Same results as ``append_select_fused`` +
         ``sparse_attention_fused``.  ``head_groups`` > 1 (batch 1) pipelines the step over groups
         of kv heads so the first group's value fetch starts after a fraction of the landmark scan
-        (default ``auto_head_groups``).  Returns ``out`` [B, Hq, D]."""
+        (default ``auto_head_groups``).  ``row_dev`` (one int32 on the device, = sparse_end +
+        gen_offset): the append position read at run time (``graph.DecodeGraph`` replays a captured
+        step at later positions with it); the launches are then sized for the whole buffer.
+        Returns ``out`` [B, Hq, D]."""
         B, Hq, Hk, D = self.batch_size, self.num_attention_heads, self.num_key_value_heads, self.head_dim
         if head_groups is None:
             head_groups = auto_head_groups(B, Hk)
@@ -497,11 +500,13 @@ class ShadowKVCache_CPU:
             q_out = torch.empty(B, Hq, 1, D, dtype=self.dtype, device=self.device)
         if out is None:
             out = torch.empty(B, Hq, D, dtype=self.dtype, device=self.device)
+        if row_dev is not None:  # launches sized for the last row of the buffer
+            row = self.buf_len - 1
         fused.step(g, sws, query_states.reshape(B, Hq, D), key_states.reshape(B, Hk, D),
                    value_states.reshape(B, Hk, D), positions.reshape(B), cos_sin_cache, q_out,
                    self.k_cache_buffer[layer_idx], self.v_cache_buffer[layer_idx], row, self.k_landmark[layer_idx],
                    self.k_landmark_idx[layer_idx], self.slots[layer_idx], self.U[layer_idx], self.SV[layer_idx],
-                   self.v_cache_cpu[layer_idx], row + 1, out)
+                   self.v_cache_cpu[layer_idx], row + 1, out, row_dev=row_dev)
         self.incoming_q_len = 1
         if layer_idx == self.num_layers - 1:
             self.kv_offset += 1
