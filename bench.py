@@ -620,11 +620,43 @@ def run_prefill(args):
                     times["build"].append(b0.elapsed_time(b1))
     tn, tt, tb = (statistics.median(times[k]) for k in ("native", "torch", "build"))
     host_bytes = (T // 8) * 8 * D * 2 * Hk
+    # the rank-r factorisation of the pre-RoPE keys (get_svd): the tensor-core Gram kernel alone,
+    # the whole Gram path (Gram + float64 eigensolve of the D x D matrix + U = K V / s), and the
+    # reference's method, torch.svd of K in fp32 (skipped past 131072 rows: minutes, not ms)
+    from shadowkv_b200 import decode
+    k_pre = torch.randn(1, T, Hk * D, generator=g, device="cuda").to(torch.bfloat16)
+    svd = {"gram_kernel": [], "gram_path": [], "torch_svd": []}
+    methods = ["gram", "exact"] if T <= 131072 else ["gram"]
+    for i in range(args.warmup + max(3, args.steps // 4)):
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        decode.gram(k_pre[0])
+        e.record()
+        e.synchronize()
+        if i >= args.warmup:
+            svd["gram_kernel"].append(s.elapsed_time(e))
+        for m in methods:
+            cache.svd_method = m
+            cache.prefilled_batch = 0
+            torch.cuda.synchronize()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            cache.get_svd(k_pre, 0)
+            e.record()
+            e.synchronize()
+            if i >= args.warmup:
+                svd["gram_path" if m == "gram" else "torch_svd"].append(s.elapsed_time(e))
+    svd_ms = {k: statistics.median(v) for k, v in svd.items() if v}
+    gram_flops = 2.0 * T * (Hk * D) ** 2 / 2  # upper triangle (and diagonal blocks) of K^T K
     return {"metric": f"prefill state build ms ({cfg.name} shapes, one layer)", "value": tn, "unit": "ms",
             "higher_is_better": False, "steps": args.steps, "warmup": args.warmup,
             "torch_path_ms": tt, "speedup_vs_torch_path": tt / tn,
             "device_state_kernels_ms": tb, "host_store_bytes": host_bytes,
             "host_store_gbs": host_bytes / (tn * 1e-3) / 1e9,
+            "factorisation_ms": svd_ms,
+            "gram_kernel_tflops": gram_flops / (svd_ms["gram_kernel"] * 1e-3) / 1e12,
+            "gram_kernel_gbs": (T * Hk * D * 2 * ((Hk * D // 128) + 1) / 2) / (svd_ms["gram_kernel"] * 1e-3) / 1e9,
             "config": {"workload": f"{cfg.name}: B=1, {Hq}q/{Hk}kv heads, T {T}, {cfg.outliers} outliers, "
                                    f"budget {cfg.budget}; includes the device-to-host copy of the values"},
             "data": "synthetic (seeded normal keys/values)"}

@@ -447,6 +447,22 @@ SKV_API int skv_decode_sparse_attention_ctas(const skv_decode_geom *g, const voi
                                              int seq_len, void *out, int max_ctas, void *workspace,
                                              size_t workspace_bytes, void *stream);
 
+/* ---- rank-r factorisation of the prompt's keys (ShadowKVCache_CPU.get_svd,
+ * models/kvcache/shadow.py:411-444: torch.svd of K [T, H*128], leading
+ * `rank` triplets).  The library forms the Gram matrix K^T K on the tensor
+ * cores; its leading eigenvectors are K's right singular vectors (the
+ * eigensolve of the D x D matrix and U = K V / s are left to the caller). */
+
+/* Bytes of scratch skv_gram needs for `tokens` rows of `dim` columns (0 if
+ * dim is not a multiple of 128 in 128..8192). */
+SKV_API size_t skv_gram_workspace(int tokens, int dim);
+
+/* gram [dim][dim] float64 = K^T K for K [tokens][ld] bf16 (the first `dim`
+ * columns of each row; ld >= dim, a multiple of 8).  bf16 products with fp32
+ * accumulation over slices of the rows, the slices summed in float64. */
+SKV_API int skv_gram(const void *k, int tokens, int dim, int ld, double *gram, void *workspace,
+                     size_t workspace_bytes, void *stream);
+
 /* ---- attention output gathered over peer memory (kv heads split over ranks)
  *
  * With the kv heads of a sequence split over `world` GPUs (one process per

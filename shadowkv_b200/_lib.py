@@ -86,6 +86,8 @@ SIGNATURES = {
                                           + [c_int, ctypes.POINTER(PeerGather), P, c_size_t, P],
     "skv_decode_step_workspace": [ctypes.POINTER(DecodeGeom), c_int],
     "skv_decode_step": [ctypes.POINTER(DecodeGeom)] + [P] * 8 + [c_int] + [P] * 7 + [c_int, P, P, c_int, P, c_size_t, P],
+    "skv_gram_workspace": [c_int, c_int],
+    "skv_gram": [P, c_int, c_int, c_int, P, P, c_size_t, P],
     "skv_prefill_workspace": [ctypes.POINTER(PrefillGeom)],
     "skv_prefill_store_values": [ctypes.POINTER(PrefillGeom), P, P, P],
     "skv_prefill_build": [ctypes.POINTER(PrefillGeom)] + [P] * 10 + [c_size_t, P],
@@ -100,7 +102,7 @@ SIGNATURES = {
 }
 _RET = {"skv_last_error": c_char_p, "skv_decode_select_workspace": c_size_t,
         "skv_decode_attention_workspace": c_size_t, "skv_decode_sparse_attention_workspace": c_size_t,
-        "skv_decode_step_workspace": c_size_t,
+        "skv_decode_step_workspace": c_size_t, "skv_gram_workspace": c_size_t,
         "skv_peer_block_bytes": c_size_t, "skv_prefill_workspace": c_size_t}
 
 

@@ -1,0 +1,283 @@
+// Gram matrix K^T K of the prompt's pre-RoPE keys on the 5th-generation tensor
+// cores -- the contraction of the rank-r factorisation of the prefill.
+//
+// Reference: ShadowKVCache_CPU.get_svd (models/kvcache/shadow.py:411-444) runs
+// torch.svd on K [T, H*128] (fp32) and keeps the leading `rank` singular
+// triplets.  The library computes the same leading subspace from the Gram
+// matrix: K^T K = V S^2 V^T, its `rank` leading eigenvectors are the right
+// singular vectors, and U = K V / s.  The T x D x D contraction (D = H*128,
+// T up to 1M) is the heavy part; the D x D eigensolve stays a library call.
+//
+// One CTA per (128 x 128 output tile of the upper triangle, slice of the T
+// rows):
+//   * 256 threads stream 64-row slices of the tile's two 128-column blocks of
+//     K through a 4-stage ring with 16-byte cp.async, straight into the
+//     no-swizzle MN-major core-matrix layout (a 16-byte piece of a K row holds
+//     8 consecutive columns = one core-matrix row; 8 rows of the slice make a
+//     core matrix; column blocks SBO = 128 B apart, 8-row groups LBO = 2 KB
+//     apart), so K needs no transposition;
+//   * one thread issues 4 tcgen05.mma (kind::f16, bf16 -> fp32, M = N = 128,
+//     K = 16, both operands MN-major) per slice, committed to the slice's
+//     mbarrier, which frees the stage for the next load (bounded waits);
+//   * the fp32 accumulator (128 tensor-memory columns) is read back with
+//     tcgen05.ld and stored as the slice's partial tile.
+// gram_reduce_kernel then sums the partials of every tile in float64 and
+// writes both triangles of the D x D result.
+#include "common.cuh"
+
+namespace skv {
+
+constexpr int GR_THREADS = 256;
+constexpr int GR_ROWS = 64;                      // K rows (the contraction dim) per stage
+constexpr int GR_STAGES = 4;
+constexpr int GR_OPER_BYTES = GR_ROWS * 128 * 2;  // one 128-column operand slice: 16 KB
+constexpr int GR_STAGE_BYTES = 2 * GR_OPER_BYTES;
+// stages, then slack: a descriptor read of the layout with its two offsets
+// exchanged still lands inside the allocation
+constexpr int GR_SMEM = GR_STAGES * GR_STAGE_BYTES + 32 * 1024 + 1024;
+constexpr uint32_t GR_SBO = 128;   // between 8-column blocks (MN direction)
+constexpr uint32_t GR_LBO = 2048;  // between 8-row groups (K direction): 16 column blocks x 128 B
+constexpr uint32_t GR_TMEM_COLS = 128;
+// kind::f16: D fp32, A and B bf16, A and B MN-major (bits 15, 16), N/8 at 17, M/16 at 24
+constexpr uint32_t GR_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) | (1u << 16) | ((128u >> 3) << 17) |
+                              ((128u >> 4) << 24);
+
+__device__ __forceinline__ uint64_t gr_sdesc(uint32_t saddr)
+{
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((GR_LBO >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((GR_SBO >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+
+__device__ __forceinline__ void gr_cp16(void *smem, const void *gmem)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem));
+}
+
+struct GramArgs {
+    const __nv_bfloat16 *k;  // [T][ld]
+    float *part;             // [splits][pairs][128][128]
+    int T, D, ld, nb, pairs, splits, rows_per_split;
+};
+
+__device__ __forceinline__ void gr_pair(int p, int nb, int *bi, int *bj)
+{
+    // p enumerates the upper-triangle block pairs (bi <= bj) row by row
+    int i = 0;
+    while (p >= nb - i) {
+        p -= nb - i;
+        ++i;
+    }
+    *bi = i;
+    *bj = i + p;
+}
+
+__global__ void __launch_bounds__(GR_THREADS, 1) gram_tc_kernel(GramArgs a)
+{
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    unsigned char *smem = reinterpret_cast<unsigned char *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    __shared__ uint32_t s_tmem;
+    __shared__ __align__(8) uint64_t s_mma[GR_STAGES];  // MMAs of the slice in the stage are done
+    __shared__ __align__(8) uint64_t s_fin;
+
+    const int pair = blockIdx.x, split = blockIdx.y;
+    int bi, bj;
+    gr_pair(pair, a.nb, &bi, &bj);
+    const bool diag = bi == bj;
+    const int t0 = split * a.rows_per_split, t1 = min(a.T, t0 + a.rows_per_split);
+    const int nk = t1 > t0 ? (t1 - t0 + GR_ROWS - 1) / GR_ROWS : 0;
+    const int tid = threadIdx.x, warp = tid >> 5;
+
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(smem_u32(&s_tmem)), "r"(GR_TMEM_COLS) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (tid == 0) {
+        for (int s = 0; s < GR_STAGES; ++s) mbar_init(&s_mma[s], 1);
+        mbar_init(&s_fin, 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = s_tmem;
+
+    // slice it of the CTA's rows into stage it % GR_STAGES: operand A = columns
+    // 128 bi .. +127, B = columns 128 bj .. (not loaded on the diagonal)
+    auto load = [&](int it) {
+        unsigned char *st = smem + (size_t)(it % GR_STAGES) * GR_STAGE_BYTES;
+        const int r0 = t0 + it * GR_ROWS;
+        const int nops = diag ? 1 : 2;
+        for (int p = tid; p < nops * GR_ROWS * 16; p += GR_THREADS) {
+            const int op = p / (GR_ROWS * 16), q = p % (GR_ROWS * 16);
+            const int r = q >> 4, c = q & 15;  // row of the slice, 8-column block
+            unsigned char *dst = st + (size_t)op * GR_OPER_BYTES + (size_t)(r >> 3) * GR_LBO + (size_t)c * GR_SBO +
+                                 (size_t)(r & 7) * 16;
+            const int t = r0 + r;
+            if (t < t1) gr_cp16(dst, a.k + (int64_t)t * a.ld + (op == 0 ? bi : bj) * 128 + c * 8);
+            else st_v4(dst, make_uint4(0, 0, 0, 0));
+        }
+    };
+
+    // GR_STAGES - 1 copy groups in flight before the loop, empty ones too: the
+    // wait_group count below assumes it however few slices the CTA has
+    for (int it = 0; it < GR_STAGES - 1; ++it) {
+        if (it < nk) load(it);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+    bool ok = true;
+    for (int it = 0; it < nk; ++it) {
+        // this thread's copies of slice `it` are done, then everyone's are visible to the tensor core
+        asm volatile("cp.async.wait_group %0;" ::"n"(GR_STAGES - 2) : "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncthreads();
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (tid == 0) {
+            const uint32_t sa = smem_u32(smem + (size_t)(it % GR_STAGES) * GR_STAGE_BYTES);
+            const uint32_t sb = diag ? sa : sa + GR_OPER_BYTES;
+#pragma unroll
+            for (int ks = 0; ks < GR_ROWS / 16; ++ks) {
+                const uint64_t ad = gr_sdesc(sa + (uint32_t)ks * 2u * GR_LBO);
+                const uint64_t bd = gr_sdesc(sb + (uint32_t)ks * 2u * GR_LBO);
+                const uint32_t acc = (it > 0 || ks > 0) ? 1u : 0u;
+                asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                             "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
+                             ::"r"(tmem), "l"(ad), "l"(bd), "r"(GR_IDESC), "r"(acc), "r"(0u) : "memory");
+            }
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                         ::"r"(smem_u32(&s_mma[it % GR_STAGES])) : "memory");
+        }
+        // the next load reuses the stage of slice it - 1: wait for that slice's MMAs
+        const int nxt = it + GR_STAGES - 1;
+        if (nxt < nk) {
+            if (it >= 1 && !mbar_wait(&s_mma[(it - 1) % GR_STAGES], ((it - 1) / GR_STAGES) & 1)) {
+                ok = false;
+                if ((tid & 31) == 0) report_dev_error(DEV_ERR_WAIT);
+                mbar_wait(&s_mma[(it - 1) % GR_STAGES], ((it - 1) / GR_STAGES) & 1);
+            }
+            load(nxt);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    // every MMA issued so far is complete once the last commit arrives
+    if (tid == 0) {
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                     ::"r"(smem_u32(&s_fin)) : "memory");
+    }
+    __syncwarp();
+    if (!mbar_wait(&s_fin, 0)) {
+        if ((tid & 31) == 0) report_dev_error(DEV_ERR_WAIT);
+        mbar_wait(&s_fin, 0);  // the MMAs must be done before the tensor memory is read or released
+    }
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    (void)ok;
+
+    // epilogue: warp w reads tensor-memory lanes 32 (w % 4) .. +31 (one output
+    // row per thread), warps 0-3 columns 0..63, warps 4-7 columns 64..127
+    {
+        const int q = warp & 3, half = warp >> 2;
+        const int r = q * 32 + (tid & 31);
+        float *dst = a.part + (((int64_t)split * a.pairs + pair) * 128 + r) * 128 + half * 64;
+        const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(half * 64);
+#pragma unroll
+        for (int c = 0; c < 64; c += 16) {
+            uint32_t v[16];
+            asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+                         "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                         : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+                           "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+                           "=r"(v[14]), "=r"(v[15])
+                         : "r"(trow + (uint32_t)c));
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+            for (int i = 0; i < 16; i += 4)
+                *reinterpret_cast<uint4 *>(dst + c + i) = make_uint4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(GR_TMEM_COLS) : "memory");
+    }
+}
+
+// gram[D][D] (float64) = the sum over the splits of each tile's partials;
+// grid (pairs, 128): block (p, r) writes row r of tile p and, off the
+// diagonal, the mirrored column.
+__global__ void __launch_bounds__(128) gram_reduce_kernel(const float *part, double *gram, int D, int nb, int pairs,
+                                                         int splits)
+{
+    const int pair = blockIdx.x, r = blockIdx.y, c = threadIdx.x;
+    int bi, bj;
+    gr_pair(pair, nb, &bi, &bj);
+    double s = 0.0;
+    for (int k = 0; k < splits; ++k) s += (double)part[(((int64_t)k * pairs + pair) * 128 + r) * 128 + c];
+    const int i = bi * 128 + r, j = bj * 128 + c;
+    gram[(int64_t)i * D + j] = s;
+    if (bi != bj) gram[(int64_t)j * D + i] = s;
+}
+
+struct GramPlan {
+    int nb, pairs, splits, rows_per_split;
+    size_t part_bytes;
+};
+
+static GramPlan plan_gram(int T, int D)
+{
+    GramPlan p;
+    p.nb = D / 128;
+    p.pairs = p.nb * (p.nb + 1) / 2;
+    const int sms = device_sm_count();
+    int s = max(1, sms / p.pairs);  // one CTA per SM
+    s = min(s, ceil_div(T, GR_ROWS));
+    p.rows_per_split = ceil_div(ceil_div(T, s), GR_ROWS) * GR_ROWS;
+    p.splits = ceil_div(T, p.rows_per_split);
+    p.part_bytes = (size_t)p.splits * p.pairs * 128 * 128 * 4;
+    return p;
+}
+
+}  // namespace skv
+
+using namespace skv;
+
+extern "C" {
+
+size_t skv_gram_workspace(int tokens, int dim)
+{
+    if (tokens <= 0 || dim <= 0 || dim % 128 != 0 || dim > 8192) return 0;
+    return plan_gram(tokens, dim).part_bytes;
+}
+
+int skv_gram(const void *k, int tokens, int dim, int ld, double *gram, void *workspace, size_t workspace_bytes,
+             void *stream)
+{
+    SKV_CHECK_ARG(k && gram && workspace, "null pointer argument");
+    SKV_CHECK_SUPPORTED(tokens > 0 && dim > 0 && dim % 128 == 0 && dim <= 8192,
+                        "dim must be a multiple of 128 in 128..8192 (tokens > 0)");
+    SKV_CHECK_ARG(ld >= dim && ld % 8 == 0, "ld must be >= dim and a multiple of 8 (16-byte rows)");
+    SKV_CHECK_ARG(aligned(k, 16) && aligned(workspace, 16) && aligned(gram, 8), "k, workspace (16 B) or gram unaligned");
+    const GramPlan p = plan_gram(tokens, dim);
+    SKV_CHECK_ARG(workspace_bytes >= p.part_bytes, "workspace of %zu bytes needed, %zu given", p.part_bytes,
+                  workspace_bytes);
+    int st = ensure_smem_attr((const void *)gram_tc_kernel, GR_SMEM, "gram_tc_kernel");
+    if (st) return st;
+    GramArgs a;
+    a.k = (const __nv_bfloat16 *)k;
+    a.part = (float *)workspace;
+    a.T = tokens;
+    a.D = dim;
+    a.ld = ld;
+    a.nb = p.nb;
+    a.pairs = p.pairs;
+    a.splits = p.splits;
+    a.rows_per_split = p.rows_per_split;
+    cudaStream_t s = (cudaStream_t)stream;
+    gram_tc_kernel<<<dim3(p.pairs, p.splits), GR_THREADS, GR_SMEM, s>>>(a);
+    st = check_launch("gram_tc_kernel");
+    if (st) return st;
+    gram_reduce_kernel<<<dim3(p.pairs, 128), 128, 0, s>>>(a.part, gram, dim, p.nb, p.pairs, p.splits);
+    return check_launch("gram_reduce_kernel");
+}
+
+}  // extern "C"

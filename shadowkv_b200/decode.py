@@ -228,3 +228,20 @@ def sparse_attention(geom: Geometry, ws: DecodeWorkspace, q: torch.Tensor, U: to
     else:
         check(lib.skv_decode_sparse_attention(*args, *tail), "skv_decode_sparse_attention")
     return out
+
+
+def gram(k: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """K^T K [D, D] float64 of K [T, D] bf16 (rows may be strided, columns contiguous) on the
+    tensor cores (``skv_gram``): bf16 products, fp32 accumulation per slice of rows, float64 sum."""
+    if not k.is_cuda or k.dtype != torch.bfloat16 or k.dim() != 2 or k.stride(1) != 1:
+        raise RuntimeError("k must be a CUDA bf16 [T, D] tensor with contiguous rows")
+    T, D = k.shape
+    nbytes = int(lib.skv_gram_workspace(T, D))
+    if nbytes == 0:
+        check(1, f"skv_gram_workspace (T={T}, D={D}: D must be a multiple of 128)")
+    if out is None:
+        out = torch.empty(D, D, dtype=torch.float64, device=k.device)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=k.device)
+    check(lib.skv_gram(k.data_ptr(), T, D, int(k.stride(0)), _req(out, "out", torch.float64, (D, D)),
+                       ws.data_ptr(), nbytes, _stream(stream)), "skv_gram")
+    return out

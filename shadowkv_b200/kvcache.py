@@ -136,17 +136,20 @@ class ShadowKVCache_CPU:
             self.U = torch.zeros(self.num_layers, self.batch_size, T, self.rank, dtype=self.dtype, device=self.device)
             self.SV = torch.zeros(self.num_layers, self.batch_size, self.num_key_value_heads, self.head_dim, self.rank,
                                   dtype=self.dtype, device=self.device)
-        kf = k.to(self.device).float()
         if self.svd_method == "gram":
-            # same leading subspace via the eigen-decomposition of K^T K (float64)
-            kd = kf.double()
-            evals, evecs = torch.linalg.eigh(kd.transpose(1, 2) @ kd)
+            # the same leading subspace from the Gram matrix: K^T K on the tensor cores
+            # (skv_gram, float64 result), its leading eigenvectors V (float64 eigensolve),
+            # then U = K V / s
+            kb = k.to(self.device).to(torch.bfloat16)
+            G = torch.stack([fused.gram(kb[i]) for i in range(bsz)])
+            evals, evecs = torch.linalg.eigh(G)
             order = torch.argsort(evals, dim=-1, descending=True)[:, : self.rank]
             v = torch.gather(evecs, 2, order.unsqueeze(1).expand(-1, evecs.shape[1], -1))  # [b, HD, r]
             s = torch.sqrt(torch.clamp(torch.gather(evals, 1, order), min=0))
-            u = (kd @ v) / torch.clamp(s, min=1e-30).unsqueeze(1)
-            u, s, vt = u.float(), s.float(), v.transpose(1, 2).float()
+            u = (kb.float() @ v.float()) / torch.clamp(s, min=1e-30).float().unsqueeze(1)
+            s, vt = s.float(), v.transpose(1, 2).float()
         else:
+            kf = k.to(self.device).float()
             u, s, v = torch.svd(kf)
             u, s, vt = u[:, :, : self.rank], s[:, : self.rank], v.transpose(1, 2)[:, : self.rank]
         pb = self.prefilled_batch
