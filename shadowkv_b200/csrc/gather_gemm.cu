@@ -68,7 +68,9 @@ int skv_decode_reconstruct_keys(const skv_decode_geom *gm, const void *U, const 
     SKV_CHECK_ARG(gm->cos_sin_stride >= (gm->rope_mode == 0 ? 128 : 64), "cos_sin_stride too small");
     SKV_CHECK_ARG(gm->sparse_start >= 0 && gm->sparse_start + 8 * (int64_t)gm->select_sets <= gm->buf_len,
                   "selected rows exceed buf_len");
-    SKV_CHECK_ARG(aligned(U, 16) && aligned(SVt, 16) && aligned(k_buf, 16), "operands must be 16-byte aligned");
+    SKV_CHECK_ARG(aligned(U, 16) && aligned(SVt, 16) && aligned(k_buf, 16) && aligned(cos_sin, 16) &&
+                      gm->cos_sin_stride % 8 == 0,
+                  "operands and cos/sin rows must be 16-byte aligned");
     GatherGemmArgs g = {};
     g.U = (const __nv_bfloat16 *)U;
     g.SVt = (const __nv_bfloat16 *)SVt;
