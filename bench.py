@@ -250,6 +250,8 @@ def run_b200(args, world, rank, local):
     cache.fused_geometry(attn.cos_sin_cache)
     # the one-call step (skv_decode_step), pipelined over kv-head groups at batch 1
     use_step = not (args.split or args.two_calls or heads_sharded or args.microbatch > 1)
+    from shadowkv_b200 import decode as fz
+    fz.early_fetch(args.early_fetch)
     from shadowkv_b200.kvcache import auto_head_groups
     head_groups = (args.head_groups or auto_head_groups(B, Hkv)) if use_step else 1
 
@@ -486,7 +488,8 @@ def run_b200(args, world, rank, local):
                                    if heads_sharded else f"batch-sharded x{world}"),
                    "l2": "flushed between timed steps (256 MB write)", "hit_rate": hit_rate,
                    "microbatch": args.microbatch, "fetch_ctas": args.fetch_ctas if args.microbatch > 1 else None,
-                   "step": (f"skv_decode_step, {head_groups} kv-head group(s)" if use_step else
+                   "step": (f"skv_decode_step, {head_groups} kv-head group(s), early fetch "
+                            f"{'on' if args.early_fetch else 'off'}" if use_step else
                             "append_select + fetch/reconstruct/attend launches")},
         "roofline": {"kernel": ("fetch_misses_kernel (zero-copy V gather)" if args.split else
                                 "sparse_attend_kernel (zero-copy V gather + key reconstruction + attention)"),
@@ -727,6 +730,9 @@ def main():
                          "sequence split over the ranks with an NCCL all-gather of the outputs (strong scaling)")
     ap.add_argument("--head-groups", type=int, default=None,
                     help="kv-head groups of the pipelined one-call step at batch 1 (default: auto, 4 for 8 kv heads)")
+    ap.add_argument("--early-fetch", action="store_true",
+                    help="the one-call step with the early value fetch (the selection kernel fetches the misses "
+                         "and computes the attention)")
     ap.add_argument("--two-calls", action="store_true",
                     help="run the step as append_select + sparse_attention (all heads in one chain)")
     ap.add_argument("--split", action="store_true",

@@ -383,6 +383,13 @@ SKV_API size_t skv_decode_step_workspace(const skv_decode_geom *g, int head_grou
  * replays); `row` and `seq_len` are then the largest row and row count the
  * position may reach (they size the launches).  A position outside them is
  * counted in skv_device_errors (code 3) and the launch's own values are used.
+ * Early fetch (off by default, skv_decode_step_early_fetch): where the selection's shared memory allows it
+ * (8-CTA selection clusters: at most 32768 landmarks per head), the
+ * selection kernel itself requests the value chunks of the misses that are
+ * certain once its score histogram has located the k-th score, before the
+ * selection is complete, reconstructs the missed keys and stores keys and
+ * values into their slots; the attention kernel then reads every selected row
+ * from the buffers.  State and output are the same bits as without it.
  * Replaces, per step, shadowkv.batch_gemm_softmax + torch.topk +
  * reorder_keys_and_compute_offsets + gather_copy_with_offsets +
  * gather_copy_d2d_with_offsets + batch_gather_gemm + the push-cache RoPE and
@@ -395,6 +402,13 @@ SKV_API int skv_decode_step(const skv_decode_geom *g, const void *q, const void 
                             int32_t *slots, const void *U, const void *SVt, const void *v_host,
                             int seq_len, void *out, int32_t *miss_count, int head_groups,
                             void *workspace, size_t workspace_bytes, void *stream);
+
+/* Turn the early fetch of skv_decode_step on (enable != 0) or off (the
+ * default) for the whole process; returns the previous setting.  Calls enqueued
+ * afterwards use the new setting (a captured graph keeps the path it was
+ * captured with).  For comparisons and diagnosis: both paths give the same
+ * results. */
+SKV_API int skv_decode_step_early_fetch(int enable);
 
 /* ---- prefill state builder (ShadowKVCache_CPU.prefill_kv_cache,
  * models/kvcache/shadow.py:463-544) for one layer of `batch` sequences. */

@@ -85,6 +85,7 @@ SIGNATURES = {
     "skv_decode_sparse_attention_gather": [ctypes.POINTER(DecodeGeom)] + [P] * 10
                                           + [c_int, ctypes.POINTER(PeerGather), P, c_size_t, P],
     "skv_decode_step_workspace": [ctypes.POINTER(DecodeGeom), c_int],
+    "skv_decode_step_early_fetch": [c_int],
     "skv_decode_step": [ctypes.POINTER(DecodeGeom)] + [P] * 8 + [c_int] + [P] * 7 + [c_int, P, P, c_int, P, c_size_t, P],
     "skv_gram_workspace": [c_int, c_int],
     "skv_gram": [P, c_int, c_int, c_int, P, P, c_size_t, P],

@@ -134,6 +134,8 @@ __device__ unsigned int g_dev_err_count = 0;
 __device__ unsigned int g_dev_err_first = 0;
 #ifdef SKV_TRACE
 __device__ unsigned long long g_trace[2 * SKV_TRACE_EVENTS];
+__device__ unsigned long long g_trace_rec[SKV_TRACE_RECS * SKV_TRACE_FIELDS];
+__device__ unsigned int g_trace_nrec = 0;
 #endif
 
 }  // namespace skv
@@ -178,6 +180,19 @@ SKV_API int skv_trace_read(unsigned long long *out, int n)
     }
     SKV_CUDA(cudaMemcpyToSymbol(skv::g_trace, h, sizeof(h)));
     return SKV_OK;
+}
+// Trace builds only: copy up to max per-CTA records (SKV_TRACE_FIELDS words
+// each) into out, reset them; returns the number of records opened.
+SKV_API int skv_trace_records(unsigned long long *out, int max)
+{
+    unsigned int n = 0, zero = 0;
+    SKV_CUDA(cudaMemcpyFromSymbol(&n, skv::g_trace_nrec, sizeof(n)));
+    const int m = (int)(n < (unsigned)max ? n : (unsigned)max);
+    const int k = m < skv::SKV_TRACE_RECS ? m : skv::SKV_TRACE_RECS;
+    if (out && k > 0)
+        SKV_CUDA(cudaMemcpyFromSymbol(out, skv::g_trace_rec, sizeof(unsigned long long) * skv::SKV_TRACE_FIELDS * k));
+    SKV_CUDA(cudaMemcpyToSymbol(skv::g_trace_nrec, &zero, sizeof(zero)));
+    return (int)n;
 }
 #endif
 

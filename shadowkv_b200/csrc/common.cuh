@@ -101,8 +101,45 @@ __device__ __forceinline__ void trace_stamp(int e)
     do {                                                    \
         if (threadIdx.x == 0) ::skv::trace_stamp(e);        \
     } while (0)
+// Per-CTA records (trace builds only): a record of SKV_TRACE_FIELDS words per
+// opened slot; skv_trace_records() copies them out and resets the count.
+constexpr int SKV_TRACE_RECS = 4096, SKV_TRACE_FIELDS = 8;
+extern __device__ unsigned long long g_trace_rec[SKV_TRACE_RECS * SKV_TRACE_FIELDS];
+extern __device__ unsigned int g_trace_nrec;
+__device__ __forceinline__ unsigned long long trace_now()
+{
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ unsigned trace_smid()
+{
+    unsigned s;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(s));
+    return s;
+}
+__device__ __forceinline__ int trace_rec_open()
+{
+    const unsigned i = atomicAdd(&g_trace_nrec, 1u);
+    return i < (unsigned)SKV_TRACE_RECS ? (int)i : -1;
+}
+#define SKV_TRACE_REC_DECL int skv_trace_slot = -1
+#define SKV_TRACE_REC_OPEN()                                                  \
+    do {                                                                      \
+        if (threadIdx.x == 0) skv_trace_slot = ::skv::trace_rec_open();       \
+    } while (0)
+#define SKV_TRACE_REC(f, v)                                                   \
+    do {                                                                      \
+        if (threadIdx.x == 0 && skv_trace_slot >= 0)                          \
+            ::skv::g_trace_rec[skv_trace_slot * ::skv::SKV_TRACE_FIELDS + (f)] = (v); \
+    } while (0)
+#define SKV_TRACE_REC_NOW(f) SKV_TRACE_REC(f, ::skv::trace_now())
 #else
 #define SKV_TRACE_CTA(e) ((void)0)
+#define SKV_TRACE_REC_DECL ((void)0)
+#define SKV_TRACE_REC_OPEN() ((void)0)
+#define SKV_TRACE_REC(f, v) ((void)0)
+#define SKV_TRACE_REC_NOW(f) ((void)0)
 #endif
 // trace events of the fused decode step
 enum TraceEvent : int {
@@ -112,6 +149,7 @@ enum TraceEvent : int {
     TR_SA_TICKET = 13, TR_SA_MERGED = 14, TR_MARK_BEFORE = 15, TR_MARK_AFTER = 16,
     TR_SEL_C = 17, TR_SEL_TILE = 18, TR_SEL_HIST = 19, TR_SEL_SYNC1 = 20, TR_SEL_SCAN = 21, TR_SEL_MARKED = 22,
     TR_SEL_RANKED = 23, TR_SEL_DIFF = 24, TR_SA_LISTS = 25,
+    TR_FX_TAIL = 26, TR_FX_KEYS = 27, TR_FX_VALUES = 28, TR_FX_END = 29,
 };
 
 // ---------------------------------------------------------------------------
@@ -238,12 +276,23 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar)
 {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+// Raise the transaction count of the current phase without arriving (the
+// copies that complete it may be issued by several threads; one arrival,
+// after all of them, closes the phase).
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, unsigned bytes)
+{
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
 // Programmatic dependent launch (sm_90+).  A kernel launched with the
 // programmatic-serialization attribute may start while the previous kernel of
 // its stream still runs; pdl_wait() blocks until that kernel has completed and
 // its memory is visible (a no-op for an ordinary launch).
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Orders this thread's earlier generic accesses to shared memory before the
+// bulk (async-proxy) copies it issues next into the same bytes.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // Bounded wait for the phase with the given parity; false if it did not complete.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity, unsigned max_iter = 1u << 22)

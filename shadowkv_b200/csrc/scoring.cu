@@ -494,8 +494,10 @@ static int check_geom(const skv_decode_geom *g)
 
 static int run_select(const skv_decode_geom *g, const ScoreArgs &sa_in, const int64_t *landmark_idx,
                       int32_t *slots, int32_t *miss_slot, int32_t *miss_chunk, int32_t *miss_count,
-                      void *workspace, size_t workspace_bytes, bool append, cudaStream_t s)
+                      void *workspace, size_t workspace_bytes, bool append, cudaStream_t s,
+                      const SelectArgs *fetch = nullptr, bool *fetched = nullptr)
 {
+    if (fetched) *fetched = false;
     const SelectPlan p = plan_select(g);
     SKV_CHECK_ARG(workspace != nullptr && workspace_bytes >= p.total,
                   "workspace of %zu bytes needed, %zu given", p.total, workspace_bytes);
@@ -540,6 +542,43 @@ static int run_select(const skv_decode_geom *g, const ScoreArgs &sa_in, const in
         st = launch_keys(k, BH, s);
         if (st) return st;
         a.keys_in = k.keys;
+    }
+    if (fetch && p.cl == SEL_CL && !p.keys_pre && !p.keys_global) {
+        const FetchLayout f = fetch_layout(g->num_landmarks, g->num_chunks, G, g->select_sets, g->rank, g->buf_len);
+        if (f.bytes) {
+            a.v_host = fetch->v_host;
+            a.U = fetch->U;
+            a.SVt = fetch->SVt;
+            a.cos_sin = fetch->cos_sin;
+            a.k_buf = fetch->k_buf;
+            a.v_buf = fetch->v_buf;
+            a.Hkv = g->kv_heads;
+            a.rank = g->rank;
+            a.ctx = g->ctx_len;
+            a.buf_len = g->buf_len;
+            a.sparse_start = g->sparse_start;
+            a.rope_mode = g->rope_mode;
+            a.cs_stride = g->cos_sin_stride;
+            a.cs_rows = g->cos_sin_rows;
+            a.cap = f.cap;
+            a.stage_off = f.stage_off;
+            a.list_off = f.list_off;
+            a.msg_off = f.msg_off;
+            a.bmc_off = f.bmc_off;
+            a.recon_off = f.recon_off;
+            a.q_rot = fetch->q_rot;
+            a.out = fetch->out;
+            a.part_o = fetch->part_o;
+            a.part_ml = fetch->part_ml;
+            a.row_dev = fetch->row_dev;
+            a.seq_len = fetch->seq_len;
+            a.pstride = fetch->pstride;
+            a.att_workers = f.att_workers;
+            a.scale = g->scale;
+            st = launch_select_fetch(a, BH, f.bytes, s);
+            if (st == SKV_OK && fetched) *fetched = true;
+            return st;
+        }
     }
     return launch_select(a, BH, p.sel_smem, p.cl, s);
 }
@@ -598,7 +637,8 @@ int append_select_launch(const skv_decode_geom *g, const void *q, const void *k_
                          const int64_t *positions, const void *cos_sin, void *q_out, void *k_buf, void *v_buf,
                          int row, const void *landmarks, const int64_t *landmark_idx, int32_t *slots,
                          int32_t *miss_slot, int32_t *miss_chunk, int32_t *miss_count, void *workspace,
-                         size_t workspace_bytes, cudaStream_t stream, const int32_t *row_dev)
+                         size_t workspace_bytes, cudaStream_t stream, const int32_t *row_dev,
+                         const SelectArgs *fetch, bool *fetched)
 {
     int st = check_geom(g);
     if (st) return st;
@@ -628,7 +668,7 @@ int append_select_launch(const skv_decode_geom *g, const void *q, const void *k_
     sa.cs_stride = g->cos_sin_stride;
     sa.cs_rows = g->cos_sin_rows;
     return run_select(g, sa, landmark_idx, slots, miss_slot, miss_chunk, miss_count, workspace, workspace_bytes,
-                      true, stream);
+                      true, stream, fetch, fetched);
 }
 
 }  // namespace skv

@@ -17,6 +17,7 @@
 // win.  Should more than SEL_REGION keys share the bin, the cluster falls back
 // to an exact 4-pass radix select (8 bits per pass) with the same tie rule.
 // Rank 0 then computes the slot-stable diff from the two bitmaps.
+#include "attn_block.cuh"
 #include "select.cuh"
 
 #include <atomic>
@@ -43,6 +44,38 @@ __device__ __forceinline__ void cluster_sync()
 {
     asm volatile("barrier.cluster.arrive.release.aligned;\n"
                  "barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+
+// Split cluster barrier: arrive (releasing this thread's earlier memory
+// accesses to the cluster) and, later, wait (acquiring the others').  A
+// thread that requests bulk copies from host memory arrives before it issues
+// them: a release issued while such copies are in flight waits for them.
+__device__ __forceinline__ void cluster_arrive_release()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire()
+{
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// 16 bytes into CTA-of-the-cluster shared memory (remote_addr), completing as
+// transaction bytes on that CTA's mbarrier (remote_bar): data and signal in
+// one, no fence.
+__device__ __forceinline__ void st_async_v4(uint32_t remote_addr, uint4 v, uint32_t remote_bar)
+{
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];"
+                 ::"r"(remote_addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(remote_bar) : "memory");
+}
+// 16-byte asynchronous copy global -> shared through the load path (these do
+// not queue behind bulk copies from host memory, which wait on the host link).
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gmem_src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all()
+{
+    asm volatile("cp.async.commit_group;\n"
+                 "cp.async.wait_group 0;\n" ::: "memory");
 }
 
 __device__ __forceinline__ void merge_ms(float &m, float &s, float m2, float s2)
@@ -281,7 +314,298 @@ __device__ __noinline__ void select_radix_fallback(const uint32_t *keys, int n, 
     }
 }
 
-template <int CL>
+// FETCH tail of the selection kernel.  Rank 0's message (every miss of the
+// head, ascending chunk id, with its slot and whether it was decided only by
+// the exact ranking) arrives on this CTA's mbarrier; this CTA's chunks are the
+// certain misses it found at the scan (their values already requested) and
+// the ranking-decided misses r with r % cl == rank.  `cap` chunks at a time:
+// request the values not requested yet, reconstruct the chunks' keys
+// (FETCH_ROWS rows per pass, the same arithmetic as the fused attention; the
+// U, cos/sin and SV^T rows come in through the load path, which bulk copies
+// waiting on the host link do not hold up) into their slots of k_buf, wait
+// for the values and store them into the slots of v_buf.  Invalid chunk ids
+// or slots are counted as device errors and skipped.
+__device__ __forceinline__ void fetch_tail(const SelectArgs &a, int bh, unsigned rank, unsigned cl,
+                                           unsigned char *smem_raw, uint64_t *vbar, uint64_t *mbar, unsigned nC_raw,
+                                           unsigned *s_nB)
+{
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int K = a.K;
+    const int KP = a.rank + 8, KT = fetch_kt(a.rank);
+    const int b = bh / a.Hkv;
+    unsigned char *stage = smem_raw + a.stage_off;
+    const int *lC = reinterpret_cast<const int *>(smem_raw + a.list_off);
+    int *lB = reinterpret_cast<int *>(smem_raw + a.list_off) + K;
+    const int2 *msg = reinterpret_cast<const int2 *>(smem_raw + a.msg_off);  // [0]: count; [1 + r]: miss r
+    __nv_bfloat16 *sU = reinterpret_cast<__nv_bfloat16 *>(smem_raw + a.recon_off);  // [FETCH_ROWS][KT] U rows, then keys
+    __nv_bfloat16 *sB = sU + FETCH_ROWS * KT;                                          // [128][KP] SV^T of the head
+    __nv_bfloat16 *sCS = sB + 128 * KP;                                                // [FETCH_ROWS][FETCH_PITCH]
+    const uint4 *vh = a.v_host + (int64_t)bh * a.num_chunks * 128;
+    const int ppr = a.rank / 8, csp = a.rope_mode == 0 ? 16 : 8;  // 16-byte pieces per U / cos-sin row
+
+    if (!mbar_wait(mbar, 0)) {
+        if (tid == 0) report_dev_error(DEV_ERR_WAIT);
+        mbar_wait(mbar, 0);  // the message must be complete before it is read
+    }
+    SKV_TRACE_CTA(TR_FX_TAIL);
+    const int count = min(max(msg[0].x, 0), K);
+    // the ranking-decided misses of this CTA
+    if (warp == 0) {
+        int nb = 0;
+        for (int r0 = 0; r0 < count; r0 += 32) {
+            const int r = r0 + lane;
+            const bool mine = r < count && (msg[1 + r].y < 0) && (unsigned)r % cl == rank;
+            const unsigned ball = __ballot_sync(0xffffffffu, mine);
+            if (mine) lB[nb + __popc(ball & ((1u << lane) - 1u))] = msg[1 + r].x;
+            nb += __popc(ball);
+        }
+        if (lane == 0) *s_nB = (unsigned)nb;
+    }
+    __syncthreads();
+    const int nC = (int)min(nC_raw, (unsigned)K), nB = (int)min(*s_nB, (unsigned)K);
+    const int nW = nC + nB, cap = a.cap;
+    auto entry = [&](int i) -> int { return i < nC ? lC[i] : lB[i - nC]; };
+    auto valid = [&](int cid) -> bool { return cid >= 0 && cid < a.num_chunks && (int64_t)cid * 8 + 8 <= a.ctx; };
+    auto slot_of = [&](int cid) -> int {  // binary search of the message (ascending chunk ids)
+        int lo = 0, hi = count;
+        while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (msg[1 + mid].x < cid) lo = mid + 1;
+            else hi = mid;
+        }
+        if (lo < count && msg[1 + lo].x == cid) {
+            const int sl = msg[1 + lo].y & 0x7fffffff;
+            return sl < K ? sl : -1;
+        }
+        return -1;
+    };
+    SKV_TRACE_REC_DECL;
+    SKV_TRACE_REC_OPEN();
+    SKV_TRACE_REC(0, (unsigned long long)rank | ((unsigned long long)bh << 8) | ((unsigned long long)nC << 24) |
+                         ((unsigned long long)nB << 40));
+    SKV_TRACE_REC(1, (unsigned long long)(uintptr_t)a.k_buf);
+    SKV_TRACE_REC_NOW(2);
+    SKV_TRACE_REC(7, 0xF0F0ull);  // marks a record of this tail
+    bool svt = false;
+    for (int r0 = 0, round = 0; r0 < nW; r0 += cap, ++round) {
+        const int rn = min(cap, nW - r0);
+        // the round's value chunks that were not requested at the scan (later
+        // rounds reuse the staging area: every copy of the last round is in)
+        if (round > 0) fence_proxy_async_smem();
+        for (int j = tid; j < rn; j += SEL_T) {
+            const int i = r0 + j;
+            if (i < nC && i < cap) continue;
+            const int cid = entry(i);
+            if (cid < 0 || cid >= a.num_chunks) continue;
+            mbar_expect_tx(&vbar[1], 2048u);
+            bulk_g2s(stage + (size_t)j * 2048, vh + (int64_t)cid * 128, 2048u, &vbar[1]);
+        }
+        __syncthreads();
+        if (tid == 0) mbar_arrive(&vbar[1]);  // close this round's phase
+        // keys of the round's chunks, FETCH_ROWS / 8 chunks per pass
+        for (int p0 = 0; p0 < rn; p0 += FETCH_ROWS / 8) {
+            const int pn = min(FETCH_ROWS / 8, rn - p0);
+            // U and cos/sin rows of the pass's chunks (and SV^T once), through the load path
+            const int nu = pn * 8 * ppr, ncs = pn * 8 * csp, nsv = svt ? 0 : 128 * ppr;
+            for (int p = tid; p < nu + ncs + nsv; p += SEL_T) {
+                if (p < nu) {
+                    const int r = p / ppr, c = p % ppr;
+                    const int cid = entry(r0 + p0 + (r >> 3));
+                    if (valid(cid))
+                        cp_async16(sU + r * KT + c * 8, a.U + ((int64_t)b * a.ctx + (int64_t)cid * 8 + (r & 7)) * a.rank + c * 8);
+                } else if (p < nu + ncs) {
+                    const int q = p - nu, r = q / csp, c = q % csp;
+                    const int cid = entry(r0 + p0 + (r >> 3));
+                    const int64_t pos = (int64_t)cid * 8 + (r & 7);
+                    if (valid(cid) && pos < a.cs_rows) cp_async16(sCS + r * FETCH_PITCH + c * 8, a.cos_sin + pos * a.cs_stride + c * 8);
+                } else {
+                    const int q = p - nu - ncs, r = q / ppr, c = q % ppr;
+                    cp_async16(sB + r * KP + c * 8, a.SVt + ((int64_t)bh * 128 + r) * a.rank + c * 8);
+                }
+            }
+            cp_async_wait_all();
+            __syncthreads();
+            svt = true;
+            // warp w < 8: rows 16 (w & 3) .. +15, output half w >> 2
+            const int rg = warp & 3, half = (warp >> 2) & 1, g = lane >> 2, t4 = lane & 3;
+            const bool mine = warp < 8 && 2 * rg < pn;
+            uint32_t kres[16];
+            if (mine) {
+                float acc[8][4];
+                recon_half(acc, sU + (rg * 16 + (lane & 15)) * KT + (lane >> 4) * 8, sB, KP, a.rank, half, lane);
+#pragma unroll
+                for (int hr = 0; hr < 2; ++hr) {
+                    const int r = rg * 16 + g + 8 * hr, q = r >> 3;
+                    float v[8][2];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        v[i][0] = acc[i][2 * hr];
+                        v[i][1] = acc[i][2 * hr + 1];
+                    }
+                    const int cid = q < pn ? entry(r0 + p0 + q) : -1;
+                    if (valid(cid)) {
+                        if ((int64_t)cid * 8 + (r & 7) < a.cs_rows)
+                            recon_rope(v, sCS + r * FETCH_PITCH, a.rope_mode, half, t4);
+                        else if (t4 == 0)
+                            report_dev_error(DEV_ERR_ROW);
+                    }
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) kres[hr * 8 + i] = pack_bf2(v[i][0], v[i][1]);
+                }
+            }
+            __syncthreads();  // every warp is done reading the U rows
+            if (mine) {
+#pragma unroll
+                for (int hr = 0; hr < 2; ++hr) {
+                    const int r = rg * 16 + g + 8 * hr;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        *reinterpret_cast<uint32_t *>(sU + r * KT + recon_col(half, i, t4)) = kres[hr * 8 + i];
+                }
+            }
+            __syncthreads();
+            // the keys into their slots of k_buf
+            for (int p = tid; p < pn * 8 * 16; p += SEL_T) {
+                const int r = p >> 4, c = (p & 15) * 8;
+                const int cid = entry(r0 + p0 + (r >> 3));
+                if (!valid(cid)) continue;
+                const int sl = slot_of(cid);
+                if (sl < 0) {
+                    if ((p & 127) == 0) report_dev_error(DEV_ERR_SLOT);
+                    continue;
+                }
+                st_v4(a.k_buf + ((int64_t)bh * a.buf_len + a.sparse_start + 8 * sl + (r & 7)) * 128 + c,
+                      ld_v4(sU + r * KT + c));
+            }
+            __syncthreads();  // the tile is free for the next pass
+        }
+        if (round == 0) {
+            SKV_TRACE_CTA(TR_FX_KEYS);
+            SKV_TRACE_REC_NOW(3);
+        }
+        // the round's values into their slots of v_buf
+        bool ok = mbar_wait(&vbar[1], (unsigned)round & 1u);
+        if (round == 0) ok = mbar_wait(&vbar[0], 0) && ok;
+        if (!ok) {
+            if (tid == 0) report_dev_error(DEV_ERR_WAIT);
+            // the copies must land before the staging area is read or reused
+            mbar_wait(&vbar[1], (unsigned)round & 1u);
+            if (round == 0) mbar_wait(&vbar[0], 0);
+        }
+        if (round == 0) {
+            SKV_TRACE_CTA(TR_FX_VALUES);
+            SKV_TRACE_REC_NOW(4);
+        }
+        for (int p = tid; p < rn * 128; p += SEL_T) {
+            const int j = p >> 7, piece = p & 127;
+            const int cid = entry(r0 + j);
+            if (!valid(cid)) continue;
+            const int sl = slot_of(cid);
+            if (sl < 0) continue;
+            st_v4(a.v_buf + ((int64_t)bh * a.buf_len + a.sparse_start + 8 * sl) * 128 + piece * 8,
+                  ld_v4(stage + (size_t)j * 2048 + piece * 16));
+        }
+        __syncthreads();  // the staging area is free for the next round
+    }
+    if (nW == 0) {
+        // nothing of ours in flight except the (empty) phase of the scan
+        if (!mbar_wait(&vbar[0], 0) && tid == 0) report_dev_error(DEV_ERR_WAIT);
+    }
+    SKV_TRACE_CTA(TR_FX_END);
+    SKV_TRACE_REC_NOW(5);
+}
+
+// Shared memory of one attention worker (8 warps): K and V tiles, query rows,
+// weights and scores of a 128-row block.
+constexpr size_t FETCH_AB_BYTES = (size_t)2 * AB_ROWS * AB_PITCH * 2 + (size_t)2 * 16 * AB_PITCH * 2 + AB_ROWS * 16 * 4;
+
+// The step's attention, by the cluster of a head, once every CTA's keys and
+// values are in the buffers: CTA `rank` computes the partials of blocks
+// rank, rank + cl, ... (att_workers blocks at a time, 8 warps each) -- the same
+// 128-row blocks and arithmetic as the fused attention kernel -- then rank 0
+// merges the head's partials into the output.  Rows come in through the load
+// path; rows past the step's end are zero.
+__device__ __forceinline__ void fetch_attend(const SelectArgs &a, int bh, unsigned rank, unsigned cl,
+                                             unsigned char *smem_raw, float (*s_am)[16], float (*s_al)[16])
+{
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int G = a.G, W = a.att_workers;
+    int seq_len = a.seq_len;
+    if (a.row_dev) {
+        const int r1 = *a.row_dev + 1;
+        if (r1 >= a.sparse_start + 8 * a.K && r1 <= a.seq_len) seq_len = r1;
+        else if (tid == 0 && rank == 0) report_dev_error(DEV_ERR_ROW);
+    }
+    const int nblk = ceil_div(seq_len, AB_ROWS);
+    const int worker = warp >> 3, wwarp = warp & 7, wtid = tid & 255;
+    const bool working = worker < W;
+    unsigned char *base = smem_raw + a.stage_off + (size_t)worker * FETCH_AB_BYTES;
+    __nv_bfloat16 *sK = reinterpret_cast<__nv_bfloat16 *>(base);
+    __nv_bfloat16 *sV = sK + AB_ROWS * AB_PITCH;
+    __nv_bfloat16 *sQ = sV + AB_ROWS * AB_PITCH;
+    __nv_bfloat16 *sP = sQ + 16 * AB_PITCH;
+    float *sS = reinterpret_cast<float *>(sP + 16 * AB_PITCH);
+    if (working) {
+        const __nv_bfloat16 *qrows = a.q_rot + (int64_t)bh * G * 128;
+        for (int p = wtid; p < 16 * 16; p += 256) {
+            const int r = p >> 4, c = (p & 15) * 8;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (r < G) v = ld_nc_v4(qrows + (int64_t)r * 128 + c);
+            st_v4(sQ + r * AB_PITCH + c, v);
+        }
+    }
+    const __nv_bfloat16 *kb = a.k_buf + (int64_t)bh * a.buf_len * 128, *vb = a.v_buf + (int64_t)bh * a.buf_len * 128;
+    for (int k0 = 0; (int)rank + (int)cl * k0 < nblk; k0 += W) {
+        const int j = (int)rank + (int)cl * (k0 + worker);
+        const bool active = working && j < nblk;
+        const int row0 = j * AB_ROWS, nrows = active ? min(AB_ROWS, seq_len - row0) : 0;
+        if (active) {
+            for (int p = wtid; p < AB_ROWS * 32; p += 256) {
+                const int r = (p >> 4) & (AB_ROWS - 1), c = (p & 15) * 8;
+                const bool isv = p >= AB_ROWS * 16;
+                __nv_bfloat16 *dst = (isv ? sV : sK) + r * AB_PITCH + c;
+                if (r < nrows) cp_async16(dst, (isv ? vb : kb) + (int64_t)(row0 + r) * 128 + c);
+                else st_v4(dst, make_uint4(0, 0, 0, 0));
+            }
+        }
+        cp_async_wait_all();
+        __syncthreads();
+        if (active) {
+            if (G <= 8) ab_scores<1>(sK, AB_PITCH, sQ, sS, nrows, a.scale, wwarp, lane);
+            else ab_scores<2>(sK, AB_PITCH, sQ, sS, nrows, a.scale, wwarp, lane);
+        }
+        __syncthreads();
+        if (active) ab_softmax(sS, sP, s_am[worker], s_al[worker], G, wwarp, lane);
+        __syncthreads();
+        if (active) {
+            float o[2][4];
+            ab_pv(sP, sV, o, wwarp, lane);
+            ab_partial(o, a.part_o + ((int64_t)bh * a.pstride + j) * G * 128, a.part_ml + ((int64_t)bh * a.pstride + j) * G,
+                       s_am[worker], s_al[worker], G, wwarp, lane, wtid);
+        }
+        __syncthreads();  // the tiles are free for the next blocks
+    }
+    cluster_sync();  // every block partial of the head is written
+    if (rank == 0) {
+        __nv_bfloat16 *out = a.out + (int64_t)bh * G * 128;
+        ab_merge(a.part_o + (int64_t)bh * a.pstride * G * 128, a.part_ml + (int64_t)bh * a.pstride * G, nblk, G,
+                 smem_raw + a.stage_off, tid, SEL_T,
+                 [&](int gg, int d, uint2 pk) { *reinterpret_cast<uint2 *>(out + (int64_t)gg * 128 + d) = pk; });
+    }
+}
+
+// FETCH (the decode step): the kernel also fetches the values of the missed
+// chunks and writes their keys and values into their slots.  Every CTA loads
+// the cached slots; right after the boundary bin is known, the chunks above it
+// that are not cached -- certain misses -- are requested from the host value
+// store with bulk copies into this CTA's shared memory (bulk copies do not
+// hold up the SM's other memory requests while they wait on the host link;
+// loads through the load/store unit would), rank 0 hands the misses decided
+// later (boundary bin, or the exact fallback) to the CTAs round-robin, and
+// after the slot diff every CTA reconstructs the keys of its chunks, waits
+// for their values and stores both into the chunks' slots.  The host transfer
+// thus starts several microseconds before the selection is complete.
+template <int CL, bool FETCH>
 __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
 {
     constexpr int REGION = SEL_CAND / CL;  // candidates a CTA may push on the fast path
@@ -303,6 +627,12 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
     __shared__ int s_lchunk[SEL_REGION];
     __shared__ int s_bin, s_bin_above, s_bin_cnt;
     __shared__ unsigned s_eq_rank[CL];
+    // FETCH: value copies issued at the scan ([0]) and later ([1], one phase per
+    // round); reconstruction operands; chunks of this CTA (certain misses found
+    // here, misses handed over by rank 0); rank 0: misses handed to each CTA
+    __shared__ __align__(8) uint64_t s_vbar[2], s_mbar;  // s_mbar: rank 0's message of the misses
+    __shared__ unsigned s_nC, s_nB;
+    __shared__ float s_am[2][16], s_al[2][16];          // FETCH: block (max, sum) of each attention worker
 
     const unsigned rank = blockIdx.x;
     const int bh = blockIdx.y, tid = threadIdx.x, lane = tid & 31;
@@ -327,13 +657,37 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
 
     // The fused attention that follows (one CTA per SM) may become resident on
     // the SMs this grid leaves free; it waits for this grid before reading.
-    pdl_launch_dependents();
+    // (FETCH: this grid runs until the values are in; the attention launches
+    // as the grid ends rather than hold SMs that long.)
+    if constexpr (!FETCH) pdl_launch_dependents();
     SKV_TRACE_CTA(TR_SEL_START);
+    SKV_TRACE_REC_DECL;
+#ifdef SKV_TRACE
+    __shared__ int s_trec2;  // a second record of this CTA, written by any thread
+#define SKV_TRACE_R2(f) do { if (s_trec2 >= 0) ::skv::g_trace_rec[s_trec2 * ::skv::SKV_TRACE_FIELDS + (f)] = ::skv::trace_now(); } while (0)
+#else
+#define SKV_TRACE_R2(f) ((void)0)
+#endif
+    if constexpr (FETCH) {
+        SKV_TRACE_REC_OPEN();
+        SKV_TRACE_REC(0, (unsigned long long)rank | ((unsigned long long)bh << 8));
+        SKV_TRACE_REC(1, 0x5E1ull);  // marks a record of the selection phases
+        SKV_TRACE_REC_NOW(2);
+#ifdef SKV_TRACE
+        if (tid == 0) {
+            s_trec2 = ::skv::trace_rec_open();
+            if (s_trec2 >= 0) {
+                ::skv::g_trace_rec[s_trec2 * 8 + 0] = (unsigned long long)rank | ((unsigned long long)bh << 8);
+                ::skv::g_trace_rec[s_trec2 * 8 + 1] = 0x5E2ull;
+            }
+        }
+#endif
+    }
 
     // 0) loads that do not depend on the scores: the cached slots (rank 0,
     //    thread t owns slots 2t, 2t+1) and the chunk ids of this slice
     int old[2] = {-1, -1};
-    if (rank == 0) {
+    if (rank == 0 || FETCH) {
         for (int w = tid; w < 2 * nbw; w += SEL_T) bmA[w] = 0;  // bmA and bmB are contiguous
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
@@ -355,6 +709,23 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
     for (int i = tid; i < (SEL_T / 32) * SEL_BINS; i += SEL_T) (&s_hw[0][0])[i] = 0;
     if (tid == 0) s_nloc = 0;
     if (tid < CL) s_ccnt[tid] = 0;
+    if constexpr (FETCH) {
+        if (tid == 0) {
+            s_nC = 0;
+            s_nB = 0;
+            mbar_init(&s_vbar[0], 1);
+            mbar_init(&s_vbar[1], 1);
+            mbar_init(&s_mbar, 1);
+            mbar_fence_init();
+            // rank 0's message comes as transaction bytes on s_mbar: expected before
+            // the first cluster barrier, which precedes its sending
+            mbar_arrive_expect_tx(&s_mbar, fetch_msg_bytes(K));
+        }
+        if (rank == 0) {
+            uint32_t *bmC = reinterpret_cast<uint32_t *>(smem_raw + a.bmc_off);
+            for (int w = tid; w < nbw; w += SEL_T) bmC[w] = 0;
+        }
+    }
 
     pdl_wait();  // the scoring kernel's logits and partials are complete from here on
     SKV_TRACE_CTA(TR_SEL_WAITED);
@@ -388,7 +759,7 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
     __syncthreads();
     SKV_TRACE_CTA(TR_SEL_C);
     bool hit[2] = {false, false};
-    if (rank == 0) {
+    if (rank == 0 || FETCH) {
 #pragma unroll
         for (int u = 0; u < 2; ++u)
             if (old[u] >= 0 && old[u] < a.num_chunks) atomicOr(&bmB[old[u] >> 5], 1u << (old[u] & 31));
@@ -511,6 +882,7 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
     }
     __syncthreads();
     SKV_TRACE_CTA(TR_SEL_SCAN);
+    SKV_TRACE_REC_NOW(3);
     const int bstar = s_bin, bin_above = s_bin_above, bin_cnt = s_bin_cnt;
     const uint32_t bmA0 = dsmem_addr(bmA, 0);
     auto chunk_of = [&](int c) -> int {
@@ -531,11 +903,28 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
         const uint32_t reg0 = (uint32_t)rank * REGION;
         const uint32_t ckey0 = dsmem_addr(s_ckey, 0), clm0 = dsmem_addr(s_clm, 0), cch0 = dsmem_addr(s_cchunk, 0);
         const uint32_t ccnt0 = dsmem_addr(&s_ccnt[rank], 0);
+        int *lC = nullptr;
+        unsigned char *stage = nullptr;
+        if constexpr (FETCH) {
+            lC = reinterpret_cast<int *>(smem_raw + a.list_off);
+            stage = smem_raw + a.stage_off;  // the histograms and the logits ring are no longer read
+            fence_proxy_async_smem();
+        }
         for (int base = (tid & ~31); base < n; base += SEL_T) {
             const int c = base + lane;
             const uint32_t k = c < n ? keys[c] : 0u;
             const int bin = sel_key_bin(k);
-            if (c < n && bin > bstar) mark(chunk_of(c));
+            if (c < n && bin > bstar) {
+                const int cid = chunk_of(c);
+                mark(cid);
+                if constexpr (FETCH) {
+                    // a certain miss: listed here, its value requested after the barrier below
+                    if (cid >= 0 && !((bmB[cid >> 5] >> (cid & 31)) & 1u)) {
+                        const unsigned pos = atomicAdd(&s_nC, 1u);
+                        if (pos < (unsigned)K) lC[pos] = cid;
+                    }
+                }
+            }
             const bool cand = c < n && bin == bstar;
             const unsigned ballot = __ballot_sync(0xffffffffu, cand);
             if (ballot) {
@@ -554,8 +943,34 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
             }
         }
         SKV_TRACE_CTA(TR_SEL_MARKED);
-        cluster_sync();  // rank 0 holds the candidates and the bits of the keys above them
-        if (rank != 0) return;
+        if constexpr (FETCH) {
+            // rank 0 holds the candidates and the bits of the keys above them once
+            // every thread has arrived; the last warp requests the certain misses'
+            // values between its arrival and its wait (a release issued while they
+            // are in flight would wait for the host link)
+            __syncthreads();  // the list of certain misses is complete
+            cluster_arrive_release();
+            if (warp_id() == SEL_T / 32 - 1) {
+                if (lane == 0) SKV_TRACE_R2(2);
+                const int ne = min(min((int)s_nC, K), a.cap);
+                for (int j = lane; j < ne; j += 32) {
+                    mbar_expect_tx(&s_vbar[0], 2048u);
+                    bulk_g2s(stage + (size_t)j * 2048, a.v_host + ((int64_t)bh * a.num_chunks + lC[j]) * 128, 2048u,
+                             &s_vbar[0]);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_vbar[0]);  // every copy of the scan is issued: close the phase
+                if (lane == 0) SKV_TRACE_R2(3);
+            }
+            SKV_TRACE_REC_NOW(4);
+            cluster_wait_acquire();
+            SKV_TRACE_REC_NOW(5);
+        } else {
+            cluster_sync();  // rank 0 holds the candidates and the bits of the keys above them
+            if (rank != 0) return;
+        }
+    }
+    if (rank == 0 && bin_cnt <= REGION) {
         SKV_TRACE_CTA(TR_SEL_CAND);
         // the regions, compacted
         if (tid == 0) {
@@ -575,6 +990,7 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
             }
         }
         __syncthreads();
+        if (tid == 0) SKV_TRACE_R2(4);
         // 5) exact order among the candidates (key descending, landmark index
         //    ascending); the first K - bin_above of them are selected.  Two
         //    threads per candidate (nc <= REGION <= SEL_T / 2) count the
@@ -590,20 +1006,34 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
             before += __shfl_xor_sync(0xffffffffu, before, 1);
             if (i < nc && (tid & 1) == 0 && (int)before < need) {
                 const int cid = s_lchunk[i];
-                if (cid >= 0) atomicOr(&bmA[cid >> 5], 1u << (cid & 31));
-                else report_dev_error(DEV_ERR_HOST_CHUNK);
+                if (cid >= 0) {
+                    atomicOr(&bmA[cid >> 5], 1u << (cid & 31));
+                    // FETCH: a miss decided by the ranking (no CTA requested it at the scan)
+                    if (FETCH && !((bmB[cid >> 5] >> (cid & 31)) & 1u))
+                        atomicOr(reinterpret_cast<uint32_t *>(smem_raw + a.bmc_off) + (cid >> 5), 1u << (cid & 31));
+                } else {
+                    report_dev_error(DEV_ERR_HOST_CHUNK);
+                }
             }
         }
-    } else {
+    }
+    if (bin_cnt > REGION) {
         // 4') more than REGION keys share the boundary bin (e.g. many equal
         //     scores): exact cluster-wide radix select, out of line
         select_radix_fallback<CL>(keys, n, K, c0, rank, lidx_s, lidx, a.num_chunks, bmA0, s_hist, s_tot, s_warp,
                                   s_eq_rank);
         cluster_sync();  // rank 0's bitmap holds the complete selection
-        if (rank != 0) return;
+        if constexpr (FETCH) {
+            if (tid == 0) mbar_arrive(&s_vbar[0]);  // nothing was requested early: the phase closes empty
+        } else {
+            if (rank != 0) return;
+        }
     }
+    if (rank == 0) {
+    if (tid == 0) SKV_TRACE_R2(5);
     __syncthreads();
     SKV_TRACE_CTA(TR_SEL_RANKED);
+    SKV_TRACE_REC_NOW(6);
 
     // 6) classify the cached slots against the new set; count the missed ids
     //    (in A, not in B) of this thread's bitmap words; one scan gives both
@@ -646,13 +1076,49 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
             slots[sl] = id;
             a.miss_slot[(int64_t)bh * K + r] = sl;
             a.miss_chunk[(int64_t)bh * K + r] = id;
+            if constexpr (FETCH) reinterpret_cast<int *>(smem_raw + a.list_off)[K + r] = sl;  // slot of miss r
         }
     }
     if (tid == 0) {
         a.miss_count[bh] = nassign;
         if (nfree != nmiss) report_dev_error(DEV_ERR_SLOT);
     }
+    if constexpr (FETCH) {
+        if (tid == 0) SKV_TRACE_R2(6);
+        // the message to every CTA: [count, 0], then (chunk id, slot) of miss r in
+        // ascending id order, the slot negated-bit marked (bit 31) when the miss was
+        // decided by the ranking or the exact fallback (no CTA requested it early)
+        __syncthreads();
+        const uint32_t *bmC = reinterpret_cast<const uint32_t *>(smem_raw + a.bmc_off);
+        const int *slot_r = reinterpret_cast<const int *>(smem_raw + a.list_off) + K;
+        const bool all_late = bin_cnt > REGION;
+        auto pair = [&](int p) -> int2 {
+            if (p == 0) return make_int2(nassign, 0);
+            const int r = p - 1;
+            if (r >= nassign) return make_int2(-1, -1);
+            const int id = s_misssorted[r];
+            const bool late = all_late || ((bmC[id >> 5] >> (id & 31)) & 1u);
+            return make_int2(id, late ? (int)(0x80000000u | (unsigned)slot_r[r]) : slot_r[r]);
+        };
+        const int nw = (int)(fetch_msg_bytes(K) / 16);  // 16-byte words per message
+        for (int w = tid; w < nw * CL; w += SEL_T) {
+            const unsigned t = (unsigned)(w / nw);
+            const int wi = w % nw;
+            const int2 x = pair(2 * wi), y = pair(2 * wi + 1);
+            st_async_v4(dsmem_addr(smem_raw + a.msg_off + (size_t)wi * 16, t),
+                        make_uint4((unsigned)x.x, (unsigned)x.y, (unsigned)y.x, (unsigned)y.y), dsmem_addr(&s_mbar, t));
+        }
+    }
     SKV_TRACE_CTA(TR_SEL_END);
+    SKV_TRACE_REC_NOW(7);
+    }  // rank 0
+    if constexpr (FETCH) {
+        fetch_tail(a, bh, rank, CL, smem_raw, &s_vbar[0], &s_mbar, s_nC, &s_nB);
+        // every CTA's keys and values are in the buffers once all have arrived
+        // (no host copies are in flight any more: the barrier is cheap)
+        cluster_sync();
+        fetch_attend(a, bh, rank, CL, smem_raw, s_am, s_al);
+    }
 }
 
 size_t select_smem_bytes(int L, int num_chunks, int G, bool keys_global, int cl, bool keys_pre)
@@ -745,7 +1211,7 @@ bool select_cluster16_ok(size_t smem)
     const int known = cached[dev].load(std::memory_order_relaxed);
     if (known) return known > 0;
     int ok = -1;
-    const void *fn = (const void *)select_cluster_kernel<16>;
+    const void *fn = (const void *)select_cluster_kernel<16, false>;
     if (cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess &&
         ensure_smem_attr(fn, (int)SEL_SMEM_CAP, "select_cluster_kernel<16>") == SKV_OK) {
         cudaLaunchConfig_t cfg = {};
@@ -767,9 +1233,70 @@ bool select_cluster16_ok(size_t smem)
     return ok > 0;
 }
 
+FetchLayout fetch_layout(int L, int num_chunks, int G, int K, int rank, int buf_len)
+{
+    FetchLayout f = {};
+    auto a128 = [](size_t x) { return (x + 127) & ~(size_t)127; };
+    const size_t base = a128(select_base_bytes(L, num_chunks, false, SEL_CL));
+    const size_t hist_ring = (size_t)(SEL_T / 32) * SEL_BINS * 4 + select_ring_bytes(L, G, SEL_CL);
+    const size_t list = a128((size_t)2 * K * 4), msg = a128(fetch_msg_bytes(K));
+    const size_t bmc = a128((size_t)((num_chunks + 31) / 32) * 4);
+    const size_t recon = a128((size_t)FETCH_ROWS * fetch_kt(rank) * 2 + (size_t)128 * (rank + 8) * 2 +
+                              (size_t)FETCH_ROWS * FETCH_PITCH * 2);
+    const size_t fixed = base + list + msg + bmc + recon;
+    if (fixed + 16 * 2048 > FETCH_SMEM_CAP) return f;  // fewer than 16 chunks staged at once: not used
+    int cap = (int)((FETCH_SMEM_CAP - fixed) / 2048);
+    if (cap > 64) cap = 64;
+    const size_t stage = a128((size_t)cap * 2048) > a128(hist_ring) ? a128((size_t)cap * 2048) : a128(hist_ring);
+    if (fixed + stage > FETCH_SMEM_CAP) return f;
+    size_t bytes = fixed + stage;
+    // the attention tiles and the merge scratch reuse everything from the staging area on
+    const size_t merge = (size_t)((buf_len + AB_ROWS - 1) / AB_ROWS) * G * 12;
+    const size_t need1 = FETCH_AB_BYTES > merge ? FETCH_AB_BYTES : merge;
+    if (bytes - base < need1) bytes = base + need1;
+    if (bytes > FETCH_SMEM_CAP) return f;
+    f.att_workers = bytes - base >= 2 * FETCH_AB_BYTES ? 2 : 1;
+    f.cap = cap;
+    f.stage_off = (unsigned)base;
+    f.list_off = (unsigned)(base + stage);
+    f.msg_off = (unsigned)(f.list_off + list);
+    f.bmc_off = (unsigned)(f.msg_off + msg);
+    f.recon_off = (unsigned)(f.bmc_off + bmc);
+    f.bytes = (unsigned)bytes;
+    return f;
+}
+
+int launch_select_fetch(const SelectArgs &a, int BH, size_t smem, cudaStream_t stream)
+{
+    const void *fn = (const void *)select_cluster_kernel<SEL_CL, true>;
+    int st = ensure_smem_attr(fn, (int)smem, "select_cluster_kernel<fetch>");
+    if (st) return st;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(SEL_CL, BH, 1);
+    cfg.blockDim = dim3(SEL_T, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = SEL_CL;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, select_cluster_kernel<SEL_CL, true>, a);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        set_error("launch of select_cluster_kernel<fetch> failed: %s", cudaGetErrorString(e));
+        return SKV_ERR_CUDA;
+    }
+    return SKV_OK;
+}
+
 int launch_select(const SelectArgs &a, int BH, size_t smem, int cl, cudaStream_t stream)
 {
-    const void *fn = cl == 16 ? (const void *)select_cluster_kernel<16> : (const void *)select_cluster_kernel<8>;
+    const void *fn = cl == 16 ? (const void *)select_cluster_kernel<16, false> : (const void *)select_cluster_kernel<8, false>;
     int st = ensure_smem_attr(fn, (int)smem, "select_cluster_kernel");
     if (st) return st;
     if (cl == 16 && cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
@@ -792,8 +1319,8 @@ int launch_select(const SelectArgs &a, int BH, size_t smem, int cl, cudaStream_t
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    cudaError_t e = cl == 16 ? cudaLaunchKernelEx(&cfg, select_cluster_kernel<16>, a)
-                             : cudaLaunchKernelEx(&cfg, select_cluster_kernel<8>, a);
+    cudaError_t e = cl == 16 ? cudaLaunchKernelEx(&cfg, select_cluster_kernel<16, false>, a)
+                             : cudaLaunchKernelEx(&cfg, select_cluster_kernel<8, false>, a);
     if (e != cudaSuccess) {
         cudaGetLastError();
         set_error("launch of select_cluster_kernel failed: %s", cudaGetErrorString(e));

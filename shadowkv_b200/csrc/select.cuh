@@ -34,7 +34,40 @@ struct SelectArgs {
     // [BH][L] keys already computed by keys_kernel (long contexts), or null:
     // the selection then computes them from the logits itself
     const uint32_t *keys_in;
+    // Early fetch (the FETCH variant only): value chunks, keys and slots of
+    // the misses, written by the selection kernel itself.
+    const uint4 *v_host;              // device view of the page-locked values [BH][num_chunks][128 x 16 B]
+    const __nv_bfloat16 *U;           // [B][ctx][rank]
+    const __nv_bfloat16 *SVt;         // [BH][128][rank]
+    const __nv_bfloat16 *cos_sin;     // [cs_rows][cs_stride]
+    __nv_bfloat16 *k_buf, *v_buf;     // [BH][buf_len][128]
+    int Hkv, rank, ctx, buf_len, sparse_start, rope_mode, cs_stride, cs_rows;
+    int cap;                          // value chunks staged in shared memory at once
+    unsigned stage_off, list_off, msg_off, bmc_off, recon_off;  // byte offsets in dynamic shared memory
+    // ... and the step's attention over the buffers, by the cluster of each head
+    const __nv_bfloat16 *q_rot;       // [BH][G][128] rotated queries (written by the scoring kernel)
+    __nv_bfloat16 *out;               // [BH][G][128]
+    float *part_o;                    // [BH][pstride][G][128] block partials
+    float2 *part_ml;                  // [BH][pstride][G] (max, sum) of the block partials
+    const int32_t *row_dev;           // optional: the append row, read on the device
+    int seq_len, pstride, att_workers;
+    float scale;
 };
+
+// Early-fetch variant of the selection (decode step): shared-memory layout of
+// one CTA for rank `rank` and `cap` staged chunks; 0 when it does not fit.
+constexpr int FETCH_ROWS = 64;            // rows of one key-reconstruction pass
+constexpr int FETCH_PITCH = 136;          // bf16 row pitch of the cos/sin rows
+constexpr size_t FETCH_SMEM_CAP = 190 * 1024;  // dynamic shared memory of a FETCH CTA (static ~37 KB)
+struct FetchLayout {
+    unsigned stage_off, list_off, msg_off, bmc_off, recon_off, bytes;
+    int cap, att_workers;  // attention: 128-row blocks processed at once (tiles from stage_off on)
+};
+// Rank 0's message to every CTA of the cluster: a (count, 0) pair and K
+// (chunk id, slot) pairs, padded to 16 bytes.
+__host__ __device__ inline unsigned fetch_msg_bytes(int K) { return (unsigned)(((K + 2) & ~1) * 8); }
+__host__ __device__ inline int fetch_kt(int rank) { return rank + 8 > FETCH_PITCH ? rank + 8 : FETCH_PITCH; }
+FetchLayout fetch_layout(int L, int num_chunks, int G, int K, int rank, int buf_len);
 
 // keys_kernel: the selection keys of every landmark from the scoring
 // kernel's logits and split partials, spread over the whole GPU (long
@@ -80,6 +113,10 @@ size_t select_smem_bytes(int L, int num_chunks, int G, bool keys_global, int cl,
 bool select_cluster16_ok(size_t smem);
 
 int launch_select(const SelectArgs &a, int BH, size_t smem, int cl, cudaStream_t stream);
+int launch_select_fetch(const SelectArgs &a, int BH, size_t smem, cudaStream_t stream);
+
+// Whether skv_decode_step uses the early-fetch selection (process-wide; off by default).
+bool step_early_fetch();
 
 // skv_decode_append_select on a cudaStream_t (for the library's own callers);
 // row_dev (optional): the append row read on the device instead of `row`
@@ -87,7 +124,13 @@ int append_select_launch(const skv_decode_geom *g, const void *q, const void *k_
                          const int64_t *positions, const void *cos_sin, void *q_out, void *k_buf, void *v_buf,
                          int row, const void *landmarks, const int64_t *landmark_idx, int32_t *slots,
                          int32_t *miss_slot, int32_t *miss_chunk, int32_t *miss_count, void *workspace,
-                         size_t workspace_bytes, cudaStream_t stream, const int32_t *row_dev);
+                         size_t workspace_bytes, cudaStream_t stream, const int32_t *row_dev,
+                         const SelectArgs *fetch = nullptr, bool *fetched = nullptr);
+// fetch (optional): the early-fetch fields of SelectArgs (v_host .. v_buf and
+// q_rot .. seq_len, pstride; already validated); when the geometry allows it
+// the selection runs as the FETCH variant, which leaves the missed rows' keys
+// and values in k_buf / v_buf and writes the step's attention output, and
+// *fetched is set.
 
 // skv_decode_sparse_attention with a device-side position: row_dev (optional)
 // holds the row the step appended at; the attention covers [0, *row_dev + 1),

@@ -32,6 +32,7 @@
 // the merge overlaps the value transfer.
 #include <string.h>
 
+#include "attn_block.cuh"
 #include "select.cuh"
 
 namespace skv {
@@ -68,17 +69,6 @@ struct SparseAttendArgs {
     // then covers [0, *row_dev + 1) (at most seq_len rows, which sized the grid)
     const int32_t *row_dev;
 };
-
-__device__ __forceinline__ void sa_ldsm(uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3, const void *p)
-{
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(smem_u32(p)));
-}
-__device__ __forceinline__ void sa_ldsm_t(uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3, const void *p)
-{
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(smem_u32(p)));
-}
 
 // NT: n-tiles of query heads in S = K q^T (1: G <= 8, 2: G <= 16)
 template <int NT>
@@ -143,6 +133,11 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
     }
     const int nblk = ceil_div(seq_len, SA_ROWS);  // blocks of this step (a.nblk: of the grid and the partials' stride)
     if (blk >= nblk) continue;                    // past this step's rows: no work, no ticket
+    SKV_TRACE_REC_DECL;
+    SKV_TRACE_REC_OPEN();
+    SKV_TRACE_REC(0, (unsigned long long)::skv::trace_smid() | ((unsigned long long)bh << 8) | ((unsigned long long)blk << 20));
+    SKV_TRACE_REC(1, (unsigned long long)(uintptr_t)a.k_buf);
+    SKV_TRACE_REC_NOW(2);
     const int b = bh / a.Hkv;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = a.G;
@@ -216,6 +211,7 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
             vreg[u] = ld_stream_v4(a.v_host + ((int64_t)bh * a.num_chunks + s_chunk[gi]) * 128 + (p & 127));
     }
     if (any_miss) SKV_TRACE_CTA(TR_SA_ISSUED);
+    SKV_TRACE_REC_NOW(3);
 
     // 4) device-memory rows as bulk (TMA) copies: SV^T of the head, U and
     //    cos/sin rows of the missed groups, K and V rows of the buffer groups.
@@ -285,30 +281,11 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
     if (any_miss && (s_kind[2 * warp] == 1 || s_kind[2 * warp + 1] == 1)) {
         const int g = lane >> 2, t4 = lane & 3;
         const __nv_bfloat16 *aRow = sK + (warp * 16 + (lane & 15)) * KT + (lane >> 4) * 8;
-        const int bColOff = ((lane >> 3) & 1) * 8;
         uint32_t kres[2][16];  // packed bf16 keys: [half][row g / g+8][8 n-tiles]
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
-            // n-tiles {4h .. 4h+3} and {8+4h .. 8+4h+3}: the rotate-half pairs
-            // (t, t+64) of a row stay in one thread
             float acc[8][4];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-            for (int k0 = 0; k0 < a.rank; k0 += 16) {
-                uint32_t a0, a1, a2, a3;
-                sa_ldsm(a0, a1, a2, a3, aRow + k0);
-#pragma unroll
-                for (int pr = 0; pr < 4; ++pr) {
-                    // one x4 ldmatrix: SV^T rows of n-tile (4h + pr) for lanes 0-15 and of
-                    // n-tile (8 + 4h + pr) for lanes 16-31, k halves by lane bit 3
-                    const int ntA = 4 * half + pr, ntB = 8 + 4 * half + pr;
-                    const int rsel = (lane & 7) + ((lane >> 4) ? ntB * 8 : ntA * 8);
-                    uint32_t b0, b1, b2, b3;
-                    sa_ldsm(b0, b1, b2, b3, sB + rsel * KP + k0 + bColOff);
-                    mma_bf16_16816(acc[pr], a0, a1, a2, a3, b0, b1);
-                    mma_bf16_16816(acc[4 + pr], a0, a1, a2, a3, b2, b3);
-                }
-            }
+            recon_half(acc, aRow, sB, KP, a.rank, half, lane);
             // epilogue of this half: acc[pr] is n-tile 4h + pr, acc[4 + pr] is 8 + 4h + pr
 #pragma unroll
             for (int hr = 0; hr < 2; ++hr) {
@@ -325,30 +302,7 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
                     if (pos >= a.cs_rows) {
                         if (t4 == 0) report_dev_error(DEV_ERR_ROW);
                     } else {
-                        const __nv_bfloat16 *cs = sCS + r * SA_PITCH;
-                        if (a.rope_mode == 0) {
-#pragma unroll
-                            for (int pr = 0; pr < 4; ++pr) {
-#pragma unroll
-                                for (int u = 0; u < 2; ++u) {
-                                    const int t = (4 * half + pr) * 8 + t4 * 2 + u;  // < 64
-                                    const float cc = bf2f(cs[t]), ss = bf2f(cs[t + 64]);
-                                    const float x1 = v[pr][u], x2 = v[4 + pr][u];
-                                    v[pr][u] = x1 * cc - x2 * ss;
-                                    v[4 + pr][u] = x2 * cc + x1 * ss;
-                                }
-                            }
-                        } else {
-                            // GLM: pairs (2i, 2i+1) of the first 64 dims, both in one thread
-#pragma unroll
-                            for (int pr = 0; pr < 4; ++pr) {
-                                const int tp = ((4 * half + pr) * 8 + t4 * 2) >> 1;  // pair index < 32
-                                const float cc = bf2f(cs[tp]), ss = bf2f(cs[tp + 32]);
-                                const float xe = v[pr][0], xo = v[pr][1];
-                                v[pr][0] = xe * cc - xo * ss;
-                                v[pr][1] = xo * cc + xe * ss;
-                            }
-                        }
+                        recon_rope(v, sCS + r * SA_PITCH, a.rope_mode, half, t4);
                     }
                 }
 #pragma unroll
@@ -363,69 +317,19 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
                 const int r = warp * 16 + g + 8 * hr;
                 if (s_kind[r >> 3] != 1) continue;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int nt = i < 4 ? 4 * half + i : 8 + 4 * half + (i - 4);
-                    *reinterpret_cast<uint32_t *>(sK + r * KT + nt * 8 + t4 * 2) = kres[half][hr * 8 + i];
-                }
+                for (int i = 0; i < 8; ++i)
+                    *reinterpret_cast<uint32_t *>(sK + r * KT + recon_col(half, i, t4)) = kres[half][hr * 8 + i];
             }
         }
     }
     __syncthreads();
     if (any_miss) SKV_TRACE_CTA(TR_SA_KEYS);
+    SKV_TRACE_REC_NOW(4);
 
-    // 6) S = K q^T: warp w scores keys 16w .. 16w+15
-    {
-        float sc[NT][4];
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
-        const __nv_bfloat16 *aRow = sK + (warp * 16 + (lane & 15)) * KT + (lane >> 4) * 8;
-        const int bRow = (lane & 7) + ((lane >> 4) << 3);
-        const int bCol = ((lane >> 3) & 1) * 8;
-#pragma unroll
-        for (int kk = 0; kk < 128; kk += 16) {
-            uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
-            sa_ldsm(a0, a1, a2, a3, aRow + kk);
-            sa_ldsm(b0, b1, b2, b3, sQ + bRow * SA_PITCH + kk + bCol);
-            mma_bf16_16816(sc[0], a0, a1, a2, a3, b0, b1);
-            if (NT == 2) mma_bf16_16816(sc[NT - 1], a0, a1, a2, a3, b2, b3);
-        }
-        const int g = lane >> 2, t4 = lane & 3;
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            const int r0 = warp * 16 + g, r1 = r0 + 8;
-            const int n0 = nt * 8 + 2 * t4;
-            sS[r0 * 16 + n0] = r0 < nrows ? sc[nt][0] * a.scale : -INFINITY;
-            sS[r0 * 16 + n0 + 1] = r0 < nrows ? sc[nt][1] * a.scale : -INFINITY;
-            sS[r1 * 16 + n0] = r1 < nrows ? sc[nt][2] * a.scale : -INFINITY;
-            sS[r1 * 16 + n0 + 1] = r1 < nrows ? sc[nt][3] * a.scale : -INFINITY;
-        }
-    }
+    // 6) S = K q^T: warp w scores keys 16w .. 16w+15, then the softmax of the tile
+    ab_scores<NT>(sK, KT, sQ, sS, nrows, a.scale, warp, lane);
     __syncthreads();
-    // softmax of the tile: warp w handles heads w and w+8 (128 keys, 4 per lane)
-    for (int gg = warp; gg < 16; gg += 8) {
-        if (gg < G) {
-            float x[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) x[u] = sS[(lane + 32 * u) * 16 + gg];
-            const float m = warp_max(fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3])));  // finite: nrows >= 1
-            float psum = 0.f;
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const float p = x[u] == -INFINITY ? 0.f : __expf(x[u] - m);
-                const __nv_bfloat16 pb = f2bf(p);
-                sP[gg * SA_PITCH + lane + 32 * u] = pb;
-                psum += bf2f(pb);  // the sum uses the same rounded weights as P V
-            }
-            psum = warp_sum(psum);
-            if (lane == 0) {
-                s_m[gg] = m;
-                s_l[gg] = psum;
-            }
-        } else {
-#pragma unroll
-            for (int u = 0; u < 4; ++u) sP[gg * SA_PITCH + lane + 32 * u] = f2bf(0.f);
-        }
-    }
+    ab_softmax(sS, sP, s_m, s_l, G, warp, lane);
 
     // 7) the fetched values: into the V tile and back to the slot in v_buf.
     //    Global stores come only now: issued earlier, they would queue behind
@@ -451,111 +355,35 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
     }
     __syncthreads();
     if (any_miss) SKV_TRACE_CTA(TR_SA_VALUES);
+    SKV_TRACE_REC_NOW(5);
 
     // 8) O = P V: warp w computes dims 16w .. 16w+15 for the 16 head rows
     float o[2][4];
-#pragma unroll
-    for (int i = 0; i < 2; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-    {
-        const __nv_bfloat16 *aRow = sP + (lane & 15) * SA_PITCH + (lane >> 4) * 8;
-        const int vRow = (lane & 7) + ((lane >> 3) & 1) * 8;
-        const int vCol = warp * 16 + (lane >> 4) * 8;
-#pragma unroll
-        for (int kk = 0; kk < SA_ROWS; kk += 16) {
-            uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
-            sa_ldsm(a0, a1, a2, a3, aRow + kk);
-            sa_ldsm_t(b0, b1, b2, b3, sV + (kk + vRow) * SA_PITCH + vCol);
-            mma_bf16_16816(o[0], a0, a1, a2, a3, b0, b1);
-            mma_bf16_16816(o[1], a0, a1, a2, a3, b2, b3);
-        }
-    }
+    ab_pv(sP, sV, o, warp, lane);
 
     // 9) partial of this CTA, then the last CTA of the head merges
-    {
-        const int g = lane >> 2, t4 = lane & 3;
-        float *po = a.part_o + ((int64_t)bh * a.nblk + blk) * G * 128;
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const int d = warp * 16 + i * 8 + 2 * t4;
-            if (g < G) *reinterpret_cast<float2 *>(po + g * 128 + d) = make_float2(o[i][0], o[i][1]);
-            if (g + 8 < G) *reinterpret_cast<float2 *>(po + (g + 8) * 128 + d) = make_float2(o[i][2], o[i][3]);
-        }
-        if (tid < G) a.part_ml[((int64_t)bh * a.nblk + blk) * G + tid] = make_float2(s_m[tid], s_l[tid]);
-    }
+    ab_partial(o, a.part_o + ((int64_t)bh * a.nblk + blk) * G * 128, a.part_ml + ((int64_t)bh * a.nblk + blk) * G, s_m,
+               s_l, G, warp, lane, tid);
     __threadfence();
     __syncthreads();
     if (tid == 0) s_last = atomicAdd(&a.ticket[bh], 1u) == (unsigned)(nblk - 1) ? 1u : 0u;
     SKV_TRACE_CTA(TR_SA_TICKET);
+    SKV_TRACE_REC_NOW(6);
     __syncthreads();
     if (s_last) {
     __threadfence();
-    // merge of the head's nblk partial outputs: each thread sums 4 columns of
-    // one query row over the partials.  Its first row's partials (up to
-    // SA_MERGE_REGS of them) and all (m, l) pairs are loaded in one round;
-    // warp w turns the pairs of heads w, w + 8 into weights
-    // w_j = exp(m_j - M) / L meanwhile (the tiles' shared memory is free).
-    {
-        constexpr int SA_MERGE_REGS = 16;
-        const int nml = nblk * G;  // the step's partials: the head's first nblk
-        float2 *s_ml = reinterpret_cast<float2 *>(smem_raw);  // [nblk][G]
-        float *s_w = reinterpret_cast<float *>(s_ml + nml);  // [nblk][G]
-        const float2 *ml = a.part_ml + (int64_t)bh * a.nblk * G;
-        const float *po_head = a.part_o + (int64_t)bh * a.nblk * G * 128;
-        float4 pre[SA_MERGE_REGS];
-        if (tid < G * 32) {
-            const float *po = po_head + (tid >> 5) * 128 + (tid & 31) * 4;
-#pragma unroll
-            for (int j = 0; j < SA_MERGE_REGS; ++j)
-                if (j < nblk) pre[j] = __ldcg(reinterpret_cast<const float4 *>(po + (int64_t)j * G * 128));
-        }
-        for (int t = tid; t < nml; t += SA_THREADS) s_ml[t] = __ldcg(&ml[t]);
-        __syncthreads();
-        for (int gg = warp; gg < G; gg += SA_THREADS / 32) {
-            float M = -INFINITY, L = 0.f;
-            for (int j = lane; j < nblk; j += 32) M = fmaxf(M, s_ml[j * G + gg].x);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-            for (int j = lane; j < nblk; j += 32) L += s_ml[j * G + gg].y * __expf(s_ml[j * G + gg].x - M);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-            const float inv = 1.f / L;
-            for (int j = lane; j < nblk; j += 32) s_w[j * G + gg] = __expf(s_ml[j * G + gg].x - M) * inv;
-        }
-        __syncthreads();
-        for (int p = tid; p < G * 32; p += SA_THREADS) {
-            const int gg = p >> 5, d = (p & 31) * 4;
-            const float *po = po_head + gg * 128 + d;
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            int j0 = 0;
-            if (p == tid) {  // the first row: partials already in registers
-#pragma unroll
-                for (int j = 0; j < SA_MERGE_REGS; ++j)
-                    if (j < nblk) {
-                        const float w = s_w[j * G + gg];
-                        acc.x += pre[j].x * w, acc.y += pre[j].y * w, acc.z += pre[j].z * w, acc.w += pre[j].w * w;
-                    }
-                j0 = min(nblk, SA_MERGE_REGS);
-            }
-#pragma unroll 8
-            for (int j = j0; j < nblk; ++j) {
-                const float4 v = __ldcg(reinterpret_cast<const float4 *>(po + (int64_t)j * G * 128));
-                const float w = s_w[j * G + gg];
-                acc.x += v.x * w, acc.y += v.y * w, acc.z += v.z * w, acc.w += v.w * w;
-            }
-            __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
-            uint2 pk;
-            pk.x = *reinterpret_cast<uint32_t *>(&lo);
-            pk.y = *reinterpret_cast<uint32_t *>(&hi);
-            if (a.world == 0) {
-                *reinterpret_cast<uint2 *>(a.out + ((int64_t)bh * G + gg) * 128 + d) = pk;
-            } else {
-                const int b = bh / a.Hkv, h = bh % a.Hkv;
-                const int64_t o = (((int64_t)(*a.epoch & 1u) * (a.total / a.nblk / a.Hkv) + b) * a.q_heads_total +
-                                   a.q_head0 + h * G + gg) * 128 + d;
-                for (int r = 0; r < a.world; ++r) *reinterpret_cast<uint2 *>(a.landing[r] + o) = pk;
-            }
-        }
-    }
+    // merge of the head's nblk partial outputs (the tiles' shared memory is free)
+    ab_merge(a.part_o + (int64_t)bh * a.nblk * G * 128, a.part_ml + (int64_t)bh * a.nblk * G, nblk, G, smem_raw, tid,
+             SA_THREADS, [&](int gg, int d, uint2 pk) {
+                 if (a.world == 0) {
+                     *reinterpret_cast<uint2 *>(a.out + ((int64_t)bh * G + gg) * 128 + d) = pk;
+                 } else {
+                     const int b = bh / a.Hkv, h = bh % a.Hkv;
+                     const int64_t o = (((int64_t)(*a.epoch & 1u) * (a.total / a.nblk / a.Hkv) + b) * a.q_heads_total +
+                                        a.q_head0 + h * G + gg) * 128 + d;
+                     for (int r = 0; r < a.world; ++r) *reinterpret_cast<uint2 *>(a.landing[r] + o) = pk;
+                 }
+             });
     if (a.world > 0) {
         // the rows are in every rank's memory before any counter moves
         __threadfence_system();
@@ -565,6 +393,7 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
     }
     if (tid == 0) a.ticket[bh] = 0;  // ready for the next launch
     SKV_TRACE_CTA(TR_SA_MERGED);
+    SKV_TRACE_REC_NOW(7);
     }  // the head's last block
     ++iter;  // items that did work: the phase of the copy barrier
     }  // work items

@@ -28,11 +28,23 @@
 // skv_decode_append_select + skv_decode_sparse_attention over all heads
 // (the heads are independent).
 //
+// Early fetch (off by default: at the config1 decode step it measures slower
+// than the attention kernel's own fetch; skv_decode_step_early_fetch(1) turns
+// it on where the selection's shared memory allows it):
+// the selection kernel of each group requests the value chunks of the
+// certain misses from the host as soon as its histogram has located the
+// boundary score, reconstructs the missed keys, writes keys and values into
+// their slots and, once every value of the head is in, computes the head's
+// attention itself (the same 128-row blocks and merge as the attention
+// kernel): the step is then two kernels per group.  The state and output are
+// the same bits either way.
+//
 // Library streams and events are created per device on the first call that
 // needs them (make that call before any stream capture); the fork and join are
 // event waits, so a capture of the caller's stream captures the whole DAG.
 // Calls from several host threads are serialised on a per-device lock while
 // they enqueue work.
+#include <atomic>
 #include <mutex>
 
 #include "select.cuh"
@@ -49,6 +61,9 @@ struct StepStreams {
     std::mutex mu;
 };
 static StepStreams g_step[STEP_MAX_DEVICES];
+static std::atomic<int> g_early_fetch{0};
+
+bool step_early_fetch() { return g_early_fetch.load(std::memory_order_relaxed) != 0; }
 
 static int step_streams(int dev, StepStreams **out)
 {
@@ -71,8 +86,8 @@ static int step_streams(int dev, StepStreams **out)
 
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
-// Per-group workspace: miss slots, miss chunk ids, miss counts, selection
-// scratch, attention partials (each 256-byte aligned).
+// Per-group workspace: attention partials, miss slots, miss chunk ids, miss
+// counts, selection scratch (each 256-byte aligned).
 struct StepLayout {
     size_t miss_slot, miss_chunk, miss_count, sel, sel_bytes, att, att_bytes, group_bytes;
 };
@@ -108,6 +123,11 @@ static skv_decode_geom group_geom(const skv_decode_geom *g, int groups)
 using namespace skv;
 
 extern "C" {
+
+int skv_decode_step_early_fetch(int enable)
+{
+    return g_early_fetch.exchange(enable ? 1 : 0);
+}
 
 size_t skv_decode_step_workspace(const skv_decode_geom *g, int head_groups)
 {
@@ -146,6 +166,29 @@ int skv_decode_step(const skv_decode_geom *g, const void *q, const void *k_new, 
     unsigned char *ws = static_cast<unsigned char *>(workspace);
     const cudaStream_t caller = (cudaStream_t)stream;
 
+    // operands of the early fetch, checked before anything is launched
+    const bool early = step_early_fetch();
+    const void *hdev = nullptr;
+    void *dout = nullptr;
+    if (early) {
+        SKV_CHECK_ARG(seq_len >= g->sparse_start + 8 * g->select_sets && seq_len <= g->buf_len,
+                      "seq_len %d must cover the selected rows and fit in buf_len", seq_len);
+        int so = out_to_device_ptr(out, &dout, "out");
+        if (so != SKV_OK) return so;
+        SKV_CHECK_ARG(aligned(dout, 8), "out must be 8-byte aligned");
+        SKV_CHECK_SUPPORTED(g->rank % 16 == 0 && g->rank >= 16 && g->rank <= 256,
+                            "rank must be a multiple of 16 in 16..256");
+        SKV_CHECK_ARG(g->sparse_start >= 0 && g->sparse_start % 8 == 0 &&
+                          g->sparse_start + 8 * (int64_t)g->select_sets <= g->buf_len,
+                      "selected rows exceed buf_len (or sparse_start not a multiple of 8)");
+        SKV_CHECK_ARG(aligned(U, 16) && aligned(SVt, 16) && aligned(k_buf, 16) && aligned(v_buf, 16) &&
+                          aligned(cos_sin, 16) && g->cos_sin_stride % 8 == 0,
+                      "U, SVt, k_buf, v_buf and cos_sin rows must be 16-byte aligned");
+        int st = host_to_device_ptr(v_host, &hdev, "v_host");
+        if (st != SKV_OK) return st;
+        SKV_CHECK_ARG(aligned(hdev, 16), "v_host must be 16-byte aligned");
+    }
+
     auto group = [&](int i, cudaStream_t s) -> int {
         const int64_t h0 = (int64_t)i * hg;  // first kv head of the group (batch 1 when groups > 1)
         unsigned char *w = ws + L.group_bytes * i;
@@ -156,13 +199,38 @@ int skv_decode_step(const skv_decode_geom *g, const void *q, const void *k_new, 
         __nv_bfloat16 *qo = (__nv_bfloat16 *)q_out + h0 * G * 128;
         __nv_bfloat16 *kb = (__nv_bfloat16 *)k_buf + h0 * g->buf_len * 128;
         __nv_bfloat16 *vb = (__nv_bfloat16 *)v_buf + h0 * g->buf_len * 128;
+        const __nv_bfloat16 *svt = (const __nv_bfloat16 *)SVt + h0 * 128 * g->rank;
+        SelectArgs fx = {};
+        if (early) {
+            fx.v_host = (const uint4 *)hdev + h0 * (int64_t)g->num_chunks * 128;
+            fx.U = (const __nv_bfloat16 *)U;
+            fx.SVt = svt;
+            fx.cos_sin = (const __nv_bfloat16 *)cos_sin;
+            fx.k_buf = kb;
+            fx.v_buf = vb;
+            // the attention: block partials in the group's attention workspace
+            // (one ticket word per head first, as the attention kernel lays it out)
+            const int64_t bhg = (int64_t)gp.batch * gp.kv_heads;
+            const int pstride = ceil_div(g->buf_len, 128);
+            unsigned char *att = w + L.att;
+            fx.part_ml = reinterpret_cast<float2 *>(att + align256((size_t)bhg * 4));
+            fx.part_o = reinterpret_cast<float *>(att + align256((size_t)bhg * 4) +
+                                                  align256((size_t)bhg * pstride * G * 8));
+            fx.q_rot = qo;
+            fx.out = (__nv_bfloat16 *)dout + h0 * G * 128;
+            fx.row_dev = row_dev;
+            fx.seq_len = seq_len;
+            fx.pstride = pstride;
+        }
+        bool fetched = false;
         int st = append_select_launch(&gp, qb, (const __nv_bfloat16 *)k_new + h0 * 128,
                                       (const __nv_bfloat16 *)v_new + h0 * 128, positions, cos_sin, qo, kb, vb, row,
                                       (const __nv_bfloat16 *)landmarks + h0 * g->num_landmarks * 128,
                                       landmark_idx + h0 * g->num_landmarks, slots + h0 * g->select_sets, ms, mc, mn,
-                                      w + L.sel, L.sel_bytes, s, row_dev);
+                                      w + L.sel, L.sel_bytes, s, row_dev, early ? &fx : nullptr, &fetched);
         if (st) return st;
-        return sparse_attention_launch(&gp, qo, U, (const __nv_bfloat16 *)SVt + h0 * 128 * g->rank, cos_sin,
+        if (fetched) return SKV_OK;  // the selection kernel computed the attention too
+        return sparse_attention_launch(&gp, qo, U, svt, cos_sin,
                                        (const __nv_bfloat16 *)v_host + h0 * (int64_t)g->num_chunks * 1024, kb, vb,
                                        ms, mc, mn, seq_len, (__nv_bfloat16 *)out + h0 * G * 128, w + L.att,
                                        L.att_bytes, s, row_dev);

@@ -134,6 +134,14 @@ def step(geom: Geometry, ws: StepWorkspace, q: torch.Tensor, k_new: torch.Tensor
     return out
 
 
+def early_fetch(enable: bool) -> bool:
+    """Turn ``step``'s early value fetch on or off for the process (off by default): the selection
+    kernel requests the certain misses' values before the selection is complete, writes keys and
+    values into their slots and computes the attention itself.  Returns the previous setting.
+    Both give the same bits."""
+    return bool(lib.skv_decode_step_early_fetch(1 if enable else 0))
+
+
 def append(geom: Geometry, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, positions: torch.Tensor,
            cos_sin: torch.Tensor, q_out: torch.Tensor, k_buf: torch.Tensor, v_buf: torch.Tensor, row: int,
            stream=None) -> torch.Tensor:

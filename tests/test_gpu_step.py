@@ -3,7 +3,10 @@
 It must leave exactly the state and output of ``append_select`` + ``sparse_attention`` (the
 two-call fused path that the other tests check against the oracle): same slots, same K/V
 buffer bits, same rotated query, same attention output, same miss counts -- for every head
-grouping, over several steps (so later steps hit the reuse cache the earlier ones filled).
+grouping, with the early value fetch (the selection kernel writing the missed rows) on and
+off, over several steps (so later steps hit the reuse cache the earlier ones filled); also
+when the selection concentrates in one selection CTA's landmarks, whose certain misses then
+exceed its staging area and are fetched in several rounds, and for a batch of sequences.
 """
 import dataclasses
 
@@ -44,16 +47,10 @@ def _run(layer, inputs, mode, head_groups=None):
     return outs, (cache.k_cache_buffer[0].clone(), cache.v_cache_buffer[0].clone(), cache.slots[0].clone())
 
 
-@pytest.mark.parametrize("name,kw,groups", [
-    ("tiny", {}, [1, 2]),
-    # Llama-3-8B head layout (32 q / 8 kv heads) at a shorter context
-    ("config1", {"ctx": 16384}, [1, 2, 4, 8]),
-])
-def test_step_matches_two_call_path(name, kw, groups):
+def _compare_paths(layer, inputs, groups):
+    from shadowkv_b200 import decode as fz
     from shadowkv_b200._lib import device_errors
-    layer = _layer(name, **kw)
     cache = layer.cache
-    inputs = [layer.next_inputs() for _ in range(3)]
     start = (cache.k_cache_buffer[0].clone(), cache.v_cache_buffer[0].clone(), cache.slots[0].clone())
 
     def restore():
@@ -63,20 +60,55 @@ def test_step_matches_two_call_path(name, kw, groups):
 
     ref_outs, ref_state = _run(layer, inputs, "two_calls")
     assert device_errors()[0] == 0
-    for p in groups:
-        restore()
-        outs, state = _run(layer, inputs, "step", head_groups=p)
-        assert device_errors()[0] == 0
-        for s, ((qr, o, m), (qr2, o2, m2)) in enumerate(zip(ref_outs, outs)):
-            assert torch.equal(qr.view(torch.int16), qr2.view(torch.int16)), f"rotated query, step {s}, groups {p}"
-            assert torch.equal(o.view(torch.int16), o2.view(torch.int16)), f"output, step {s}, groups {p}"
-            assert torch.equal(m, m2), f"miss counts, step {s}, groups {p}"
-        assert torch.equal(state[2], ref_state[2]), f"slots, groups {p}"
-        assert torch.equal(state[0].view(torch.int16), ref_state[0].view(torch.int16)), f"K buffer, groups {p}"
-        assert torch.equal(state[1].view(torch.int16), ref_state[1].view(torch.int16)), f"V buffer, groups {p}"
+    before = fz.early_fetch(False)
+    try:
+        for early in (True, False):
+            fz.early_fetch(early)
+            for p in groups:
+                restore()
+                outs, state = _run(layer, inputs, "step", head_groups=p)
+                assert device_errors()[0] == 0
+                tag = f"groups {p}, early fetch {early}"
+                for s, ((qr, o, m), (qr2, o2, m2)) in enumerate(zip(ref_outs, outs)):
+                    assert torch.equal(qr.view(torch.int16), qr2.view(torch.int16)), f"rotated query, step {s}, {tag}"
+                    assert torch.equal(o.view(torch.int16), o2.view(torch.int16)), f"output, step {s}, {tag}"
+                    assert torch.equal(m, m2), f"miss counts, step {s}, {tag}"
+                assert torch.equal(state[2], ref_state[2]), f"slots, {tag}"
+                assert torch.equal(state[0].view(torch.int16), ref_state[0].view(torch.int16)), f"K buffer, {tag}"
+                assert torch.equal(state[1].view(torch.int16), ref_state[1].view(torch.int16)), f"V buffer, {tag}"
+    finally:
+        fz.early_fetch(before)
+    return ref_outs
+
+
+@pytest.mark.parametrize("name,kw,groups", [
+    ("tiny", {}, [1, 2]),
+    # Llama-3-8B head layout (32 q / 8 kv heads) at a shorter context
+    ("config1", {"ctx": 16384}, [1, 2, 4, 8]),
+    # GLM partial rotary, 32 q / 2 kv heads
+    ("config3", {"ctx": 16384}, [1, 2]),
+    # a batch of sequences (head groups need batch 1)
+    ("config1", {"ctx": 8192, "batch": 3}, [1]),
+])
+def test_step_matches_two_call_path(name, kw, groups):
+    layer = _layer(name, **kw)
+    inputs = [layer.next_inputs() for _ in range(3)]
+    ref_outs = _compare_paths(layer, inputs, groups)
     # the later steps hit the reuse cache (the same query stream is not required for that:
     # consecutive random queries share part of their selection)
     assert int(ref_outs[0][2].sum()) > 0
+
+
+def test_step_with_selection_in_one_cta_slice():
+    """Landmarks of the first eighth of each head scaled up: the top-k falls mostly into the
+    first selection CTA's slice, whose certain misses exceed its staging area (several rounds)."""
+    layer = _layer("config1", ctx=32768)
+    cache = layer.cache
+    lm = cache.k_landmark[0]                       # [B, Hkv, L, 128]
+    L = lm.shape[-2]
+    lm[..., : (L + 7) // 8, :] *= 3
+    inputs = [layer.next_inputs() for _ in range(2)]
+    _compare_paths(layer, inputs, [1, 4])
 
 
 def test_step_rejects_bad_groups():
