@@ -566,14 +566,11 @@ static int run_select(const skv_decode_geom *g, const ScoreArgs &sa_in, const in
             a.msg_off = f.msg_off;
             a.bmc_off = f.bmc_off;
             a.recon_off = f.recon_off;
+            a.att_off = f.att_off;
             a.q_rot = fetch->q_rot;
             a.out = fetch->out;
-            a.part_o = fetch->part_o;
-            a.part_ml = fetch->part_ml;
             a.row_dev = fetch->row_dev;
             a.seq_len = fetch->seq_len;
-            a.pstride = fetch->pstride;
-            a.att_workers = f.att_workers;
             a.scale = g->scale;
             st = launch_select_fetch(a, BH, f.bytes, s);
             if (st == SKV_OK && fetched) *fetched = true;

@@ -314,41 +314,217 @@ __device__ __noinline__ void select_radix_fallback(const uint32_t *keys, int n, 
     }
 }
 
+// ---- the FETCH tail: value fetch, key reconstruction and attention ----------
+
+// Value chunks a CTA requests right after the scan: its certain misses, up to
+// the staging area, at most 16 for rank 0.  Rank 0 still has to send its
+// message with asynchronous shared-memory stores, which can queue behind the
+// bulk copies of its SM when many are in flight; the rest of its chunks are
+// requested after the message is out.
+__host__ __device__ __forceinline__ int fx_early_count(int nC, int K, int cap, unsigned rank)
+{
+    const int n = nC < K ? nC : K;
+    const int m = n < cap ? n : cap;
+    return rank == 0 && m > 16 ? 16 : m;
+}
+
+// Scores S = K q^T * scale of a 32-row tile (warps 0 and 1, 16 rows each)
+// against the G query rows of sQ (row G of sQ is zero); rows >= nrows get
+// -inf.  sK rows have pitch KT; sS is [32][16].
+template <int NT>
+__device__ __forceinline__ void fx_scores(const __nv_bfloat16 *sK, int KT, const __nv_bfloat16 *sQ, int G, float *sS,
+                                          int nrows, float scale, int warp, int lane)
+{
+    float sc[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+    const __nv_bfloat16 *aRow = sK + (warp * 16 + (lane & 15)) * KT + (lane >> 4) * 8;
+    const int bRow = (lane & 7) + ((lane >> 4) << 3);
+    const __nv_bfloat16 *qRow = sQ + (bRow < G ? bRow : G) * AB_PITCH + ((lane >> 3) & 1) * 8;
+#pragma unroll
+    for (int kk = 0; kk < 128; kk += 16) {
+        uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+        sa_ldsm(a0, a1, a2, a3, aRow + kk);
+        sa_ldsm(b0, b1, b2, b3, qRow + kk);
+        mma_bf16_16816(sc[0], a0, a1, a2, a3, b0, b1);
+        if (NT == 2) mma_bf16_16816(sc[NT - 1], a0, a1, a2, a3, b2, b3);
+    }
+    const int g = lane >> 2, t4 = lane & 3;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        const int r0 = warp * 16 + g, r1 = r0 + 8;
+        const int n0 = nt * 8 + 2 * t4;
+        sS[r0 * 16 + n0] = r0 < nrows ? sc[nt][0] * scale : -INFINITY;
+        sS[r0 * 16 + n0 + 1] = r0 < nrows ? sc[nt][1] * scale : -INFINITY;
+        sS[r1 * 16 + n0] = r1 < nrows ? sc[nt][2] * scale : -INFINITY;
+        sS[r1 * 16 + n0 + 1] = r1 < nrows ? sc[nt][3] * scale : -INFINITY;
+    }
+}
+
+// Softmax of a 32-row tile (warp gg for query row gg < G): weights P =
+// bf16(exp(s - m)) into P [G][FX_PPITCH], (m, sum of the rounded weights)
+// into ml[gg].  A tile has at least one row, so m is finite.
+__device__ __forceinline__ void fx_softmax(const float *sS, __nv_bfloat16 *P, float2 *ml, int G, int warp, int lane)
+{
+    for (int gg = warp; gg < G; gg += SEL_T / 32) {
+        const float x = sS[lane * 16 + gg];
+        const float m = warp_max(x);  // -inf only when every row of the tile is invalid
+        const float p = x == -INFINITY ? 0.f : __expf(x - m);
+        const __nv_bfloat16 pb = f2bf(p);
+        P[gg * FX_PPITCH + lane] = pb;
+        const float l = warp_sum(bf2f(pb));
+        if (lane == 0) ml[gg] = make_float2(m, l);
+    }
+}
+
+// O_t = P V of a 32-row tile (warps 0-7, dims 16w .. 16w+15; V rows of pitch
+// AB_PITCH) merged into the running (M, L, O) of the CTA:
+// M' = max(M, m_t), O = O e^{M - M'} + O_t e^{m_t - M'}, L likewise.
+__device__ __forceinline__ void fx_pv_merge(const __nv_bfloat16 *P, const __nv_bfloat16 *zp, const __nv_bfloat16 *sV,
+                                            const float2 *ml, float *sO, float *sM, float *sL, int G, int warp,
+                                            int lane, int tid)
+{
+    if (warp < 8) {
+        float o[2][4];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+        const int row = lane & 15;
+        const __nv_bfloat16 *aRow = (row < G ? P + row * FX_PPITCH : zp) + (lane >> 4) * 8;
+        const int vRow = (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int vCol = warp * 16 + (lane >> 4) * 8;
+#pragma unroll
+        for (int kk = 0; kk < FETCH_ROWS; kk += 16) {
+            uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+            sa_ldsm(a0, a1, a2, a3, aRow + kk);
+            sa_ldsm_t(b0, b1, b2, b3, sV + (kk + vRow) * AB_PITCH + vCol);
+            mma_bf16_16816(o[0], a0, a1, a2, a3, b0, b1);
+            mma_bf16_16816(o[1], a0, a1, a2, a3, b2, b3);
+        }
+        const int g = lane >> 2, t4 = lane & 3;
+#pragma unroll
+        for (int hr = 0; hr < 2; ++hr) {
+            const int r = g + 8 * hr;
+            if (r >= G) continue;
+            const float Mo = sM[r], mt = ml[r].x, Mn = fmaxf(Mo, mt);
+            const float ao = Mo == -INFINITY ? 0.f : __expf(Mo - Mn), at = mt == -INFINITY ? 0.f : __expf(mt - Mn);
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                float2 *po = reinterpret_cast<float2 *>(sO + r * 128 + warp * 16 + i * 8 + 2 * t4);
+                float2 v = *po;
+                v.x = v.x * ao + o[i][2 * hr] * at;
+                v.y = v.y * ao + o[i][2 * hr + 1] * at;
+                *po = v;
+            }
+        }
+    }
+    __syncthreads();  // every O row is rescaled with the old M
+    if (tid < G) {
+        const float Mo = sM[tid], mt = ml[tid].x, Mn = fmaxf(Mo, mt);
+        const float ao = Mo == -INFINITY ? 0.f : __expf(Mo - Mn), at = mt == -INFINITY ? 0.f : __expf(mt - Mn);
+        sM[tid] = Mn;
+        sL[tid] = sL[tid] * ao + ml[tid].y * at;
+    }
+    __syncthreads();
+}
+
 // FETCH tail of the selection kernel.  Rank 0's message (every miss of the
-// head, ascending chunk id, with its slot and whether it was decided only by
-// the exact ranking) arrives on this CTA's mbarrier; this CTA's chunks are the
-// certain misses it found at the scan (their values already requested) and
-// the ranking-decided misses r with r % cl == rank.  `cap` chunks at a time:
-// request the values not requested yet, reconstruct the chunks' keys
-// (FETCH_ROWS rows per pass, the same arithmetic as the fused attention; the
-// U, cos/sin and SV^T rows come in through the load path, which bulk copies
-// waiting on the host link do not hold up) into their slots of k_buf, wait
-// for the values and store them into the slots of v_buf.  Invalid chunk ids
-// or slots are counted as device errors and skipped.
+// head, ascending chunk id, with its slot and whether the exact ranking
+// decided it) arrives on this CTA's mbarrier.  This CTA's misses are the
+// certain ones it found at the scan (values already requested) and the
+// ranking-decided misses r with r % cl == rank; its buffer rows (prefix,
+// cached slots that stay, generated rows) are every cl-th 32-row tile of them.
+// The CTA attends over exactly those rows, keeping a running (max, sum, O):
+//   - buffer-row tiles first (their keys and values are in the buffers);
+//   - then its misses, `cap` at a time: the values not requested yet are
+//     requested, the keys are reconstructed 32 rows at a time (U, cos/sin and
+//     SV^T rows through the load path, which bulk copies waiting on the host
+//     link do not hold up; the same arithmetic as the fused attention), stored
+//     into their slots of k_buf and scored at once (softmax per tile); when
+//     the round's values are in, each tile's P V is added and the values are
+//     stored into their slots of v_buf.
+// Finally the cluster merges the CTAs' (max, sum, O) through distributed
+// shared memory: CTA r writes output columns 16r .. 16r+15.  No bulk copy is
+// in flight by then, so the cluster barriers cost their usual round trip.
+// Invalid chunk ids or slots are counted as device errors and skipped.
 __device__ __forceinline__ void fetch_tail(const SelectArgs &a, int bh, unsigned rank, unsigned cl,
                                            unsigned char *smem_raw, uint64_t *vbar, uint64_t *mbar, unsigned nC_raw,
-                                           unsigned *s_nB)
+                                           unsigned *s_nB, int *s_ngrp)
 {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int K = a.K;
+    const int K = a.K, G = a.G;
     const int KP = a.rank + 8, KT = fetch_kt(a.rank);
     const int b = bh / a.Hkv;
     unsigned char *stage = smem_raw + a.stage_off;
     const int *lC = reinterpret_cast<const int *>(smem_raw + a.list_off);
     int *lB = reinterpret_cast<int *>(smem_raw + a.list_off) + K;
+    int *lS = lB + K;  // [2K] slot of work entry i
     const int2 *msg = reinterpret_cast<const int2 *>(smem_raw + a.msg_off);  // [0]: count; [1 + r]: miss r
-    __nv_bfloat16 *sU = reinterpret_cast<__nv_bfloat16 *>(smem_raw + a.recon_off);  // [FETCH_ROWS][KT] U rows, then keys
+    __nv_bfloat16 *sU = reinterpret_cast<__nv_bfloat16 *>(smem_raw + a.recon_off);  // [32][KT] U rows, then keys
     __nv_bfloat16 *sB = sU + FETCH_ROWS * KT;                                          // [128][KP] SV^T of the head
-    __nv_bfloat16 *sCS = sB + 128 * KP;                                                // [FETCH_ROWS][FETCH_PITCH]
+    __nv_bfloat16 *sCS = sB + 128 * KP;                                                // [32][136] cos/sin, or V
+    const FxAttLayout L = fx_att_layout(G, a.cap, a.buf_len, K);
+    unsigned char *att = smem_raw + a.att_off;
+    __nv_bfloat16 *sQ = reinterpret_cast<__nv_bfloat16 *>(att + L.q);
+    float *sO = reinterpret_cast<float *>(att + L.o), *sM = reinterpret_cast<float *>(att + L.m);
+    float *sL = reinterpret_cast<float *>(att + L.l), *sS = reinterpret_cast<float *>(att + L.s);
+    __nv_bfloat16 *zp = reinterpret_cast<__nv_bfloat16 *>(att + L.zp);
+    __nv_bfloat16 *pt = reinterpret_cast<__nv_bfloat16 *>(att + L.pt);
+    __nv_bfloat16 *pTiles = reinterpret_cast<__nv_bfloat16 *>(att + L.p);
+    float2 *tml = reinterpret_cast<float2 *>(att + L.tml);  // [ntiles + 1][16]; the last for buffer-row tiles
+    int *grp = reinterpret_cast<int *>(att + L.grp);
+    uint32_t *msb = reinterpret_cast<uint32_t *>(att + L.msb);
     const uint4 *vh = a.v_host + (int64_t)bh * a.num_chunks * 128;
     const int ppr = a.rank / 8, csp = a.rope_mode == 0 ? 16 : 8;  // 16-byte pieces per U / cos-sin row
+    const __nv_bfloat16 *kb = a.k_buf + (int64_t)bh * a.buf_len * 128, *vb = a.v_buf + (int64_t)bh * a.buf_len * 128;
 
     if (!mbar_wait(mbar, 0)) {
         if (tid == 0) report_dev_error(DEV_ERR_WAIT);
         mbar_wait(mbar, 0);  // the message must be complete before it is read
     }
     SKV_TRACE_CTA(TR_FX_TAIL);
+#ifdef SKV_TRACE
+    __shared__ int s_trec3;
+    if (tid == 0) {
+        s_trec3 = ::skv::trace_rec_open();
+        if (s_trec3 >= 0) {
+            ::skv::g_trace_rec[s_trec3 * 8 + 0] = (unsigned long long)rank | ((unsigned long long)bh << 8);
+            ::skv::g_trace_rec[s_trec3 * 8 + 1] = 0xF1F1ull;
+            ::skv::g_trace_rec[s_trec3 * 8 + 2] = ::skv::trace_now();
+        }
+    }
+#define SKV_TRACE_R3(f) do { if (tid == 0 && s_trec3 >= 0) ::skv::g_trace_rec[s_trec3 * 8 + (f)] = ::skv::trace_now(); } while (0)
+#else
+#define SKV_TRACE_R3(f) ((void)0)
+#endif
     const int count = min(max(msg[0].x, 0), K);
+    // rows of this step: seq_len of the launch, or the device-side position
+    int seq_len = a.seq_len;
+    if (a.row_dev) {
+        const int r1 = *a.row_dev + 1;
+        if (r1 >= a.sparse_start + 8 * K && r1 <= a.seq_len) seq_len = r1;
+        else if (tid == 0 && rank == 0) report_dev_error(DEV_ERR_ROW);
+    }
+    const int sparse_end = a.sparse_start + 8 * K;
+    // the slots refilled by misses; the query rows; the running state
+    for (int w = tid; w < (K + 31) / 32; w += SEL_T) msb[w] = 0;
+    for (int i = tid; i < FX_PPITCH; i += SEL_T) zp[i] = f2bf(0.f);
+    for (int p = tid; p < (G + 1) * 16; p += SEL_T) {
+        const int r = p >> 4, c = (p & 15) * 8;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (r < G) v = ld_nc_v4(a.q_rot + ((int64_t)bh * G + r) * 128 + c);
+        st_v4(sQ + r * AB_PITCH + c, v);
+    }
+    for (int i = tid; i < G * 128; i += SEL_T) sO[i] = 0.f;
+    if (tid < 16) {
+        sM[tid] = -INFINITY;
+        sL[tid] = 0.f;
+    }
+    __syncthreads();
+    SKV_TRACE_R3(3);
+    for (int r = tid; r < count; r += SEL_T) {
+        const int sl = msg[1 + r].y & 0x7fffffff;
+        if (sl < K) atomicOr(&msb[sl >> 5], 1u << (sl & 31));
+    }
     // the ranking-decided misses of this CTA
     if (warp == 0) {
         int nb = 0;
@@ -362,23 +538,47 @@ __device__ __forceinline__ void fetch_tail(const SelectArgs &a, int bh, unsigned
         if (lane == 0) *s_nB = (unsigned)nb;
     }
     __syncthreads();
-    const int nC = (int)min(nC_raw, (unsigned)K), nB = (int)min(*s_nB, (unsigned)K);
-    const int nW = nC + nB, cap = a.cap;
+    SKV_TRACE_R3(4);
+    // the 8-row groups of buffer rows, in row order: prefix, cached slots that
+    // stay, generated rows (row0 | count << 24)
+    if (warp == 0) {
+        const int npre = a.sparse_start / 8;
+        for (int q = lane; q < npre; q += 32) grp[q] = (q * 8) | (8 << 24);
+        int n = npre;
+        for (int s0 = 0; s0 < K; s0 += 32) {
+            const int sl = s0 + lane;
+            const bool hit = sl < K && !((msb[sl >> 5] >> (sl & 31)) & 1u);
+            const unsigned ball = __ballot_sync(0xffffffffu, hit);
+            if (hit) grp[n + __popc(ball & ((1u << lane) - 1u))] = (a.sparse_start + 8 * sl) | (8 << 24);
+            n += __popc(ball);
+        }
+        for (int r0 = sparse_end + 8 * lane; r0 < seq_len; r0 += 256) grp[n + (r0 - sparse_end) / 8] = r0 | (min(8, seq_len - r0) << 24);
+        n += (max(seq_len - sparse_end, 0) + 7) / 8;
+        if (lane == 0) *s_ngrp = n;
+    }
+    const int nC = (int)min(nC_raw, (unsigned)K);
+    __syncthreads();
+    SKV_TRACE_R3(5);
+    const int nB = (int)min(*s_nB, (unsigned)K), ngrp = *s_ngrp;
+    const int nW = nC + nB, cap = a.cap, nEarly = fx_early_count((int)nC_raw, K, cap, rank);
     auto entry = [&](int i) -> int { return i < nC ? lC[i] : lB[i - nC]; };
     auto valid = [&](int cid) -> bool { return cid >= 0 && cid < a.num_chunks && (int64_t)cid * 8 + 8 <= a.ctx; };
-    auto slot_of = [&](int cid) -> int {  // binary search of the message (ascending chunk ids)
+    // the slot of every work entry (binary search of the message, ascending chunk ids)
+    for (int i = tid; i < nW; i += SEL_T) {
+        const int cid = entry(i);
         int lo = 0, hi = count;
         while (lo < hi) {
             const int mid = (lo + hi) >> 1;
             if (msg[1 + mid].x < cid) lo = mid + 1;
             else hi = mid;
         }
-        if (lo < count && msg[1 + lo].x == cid) {
-            const int sl = msg[1 + lo].y & 0x7fffffff;
-            return sl < K ? sl : -1;
-        }
-        return -1;
-    };
+        int sl = -1;
+        if (lo < count && msg[1 + lo].x == cid) sl = msg[1 + lo].y & 0x7fffffff;
+        if (sl >= K || !valid(cid)) sl = -1;
+        if (sl < 0) report_dev_error(DEV_ERR_SLOT);
+        lS[i] = sl;
+    }
+    SKV_TRACE_R3(6);
     SKV_TRACE_REC_DECL;
     SKV_TRACE_REC_OPEN();
     SKV_TRACE_REC(0, (unsigned long long)rank | ((unsigned long long)bh << 8) | ((unsigned long long)nC << 24) |
@@ -386,26 +586,65 @@ __device__ __forceinline__ void fetch_tail(const SelectArgs &a, int bh, unsigned
     SKV_TRACE_REC(1, (unsigned long long)(uintptr_t)a.k_buf);
     SKV_TRACE_REC_NOW(2);
     SKV_TRACE_REC(7, 0xF0F0ull);  // marks a record of this tail
+    __syncthreads();
+
+    auto score_tile = [&](int nrows, __nv_bfloat16 *P, float2 *ml) {
+        if (warp < 2) {
+            if (G <= 8) fx_scores<1>(sU, KT, sQ, G, sS, nrows, a.scale, warp, lane);
+            else fx_scores<2>(sU, KT, sQ, G, sS, nrows, a.scale, warp, lane);
+        }
+        __syncthreads();
+        fx_softmax(sS, P, ml, G, warp, lane);
+        __syncthreads();
+    };
+
+    // buffer-row tiles: every cl-th group of four 8-row groups
+    float2 *bml = tml + L.ntiles * 16;
+    for (int t = (int)rank; 4 * t < ngrp; t += (int)cl) {
+        int nrows = 0;
+        for (int q = 0; q < 4 && 4 * t + q < ngrp; ++q) nrows += grp[4 * t + q] >> 24;
+        for (int p = tid; p < FETCH_ROWS * 32; p += SEL_T) {
+            const int r = (p >> 4) & (FETCH_ROWS - 1), c = (p & 15) * 8, q = r >> 3;
+            const bool isv = p >= FETCH_ROWS * 16;
+            __nv_bfloat16 *dst = isv ? sCS + r * AB_PITCH + c : sU + r * KT + c;
+            const int gq = 4 * t + q < ngrp ? grp[4 * t + q] : 0;
+            if (4 * t + q < ngrp && (r & 7) < (gq >> 24)) {
+                const int64_t row = (gq & 0xffffff) + (r & 7);
+                cp_async16(dst, (isv ? vb : kb) + row * 128 + c);
+            } else {
+                st_v4(dst, make_uint4(0, 0, 0, 0));
+            }
+        }
+        cp_async_wait_all();
+        __syncthreads();
+        score_tile(nrows, pt, bml);
+        fx_pv_merge(pt, zp, sCS, bml, sO, sM, sL, G, warp, lane, tid);
+    }
+
     bool svt = false;
     for (int r0 = 0, round = 0; r0 < nW; r0 += cap, ++round) {
         const int rn = min(cap, nW - r0);
         // the round's value chunks that were not requested at the scan (later
         // rounds reuse the staging area: every copy of the last round is in)
         if (round > 0) fence_proxy_async_smem();
-        for (int j = tid; j < rn; j += SEL_T) {
+        {
+            // copy j by warp j % 16, lane j / 16 (the issue is spread over every warp; rn <= 64)
+            const int j = (tid & 31) * (SEL_T / 32) + (tid >> 5);
             const int i = r0 + j;
-            if (i < nC && i < cap) continue;
-            const int cid = entry(i);
-            if (cid < 0 || cid >= a.num_chunks) continue;
-            mbar_expect_tx(&vbar[1], 2048u);
-            bulk_g2s(stage + (size_t)j * 2048, vh + (int64_t)cid * 128, 2048u, &vbar[1]);
+            const int cid = j < rn && i >= nEarly ? entry(i) : -1;  // below nEarly: requested at the scan
+            if (cid >= 0 && cid < a.num_chunks) {
+                uint64_t *tb = &vbar[j / (FETCH_ROWS / 8)];
+                mbar_expect_tx(tb, 2048u);
+                bulk_g2s(stage + (size_t)j * 2048, vh + (int64_t)cid * 128, 2048u, tb);
+            }
         }
         __syncthreads();
-        if (tid == 0) mbar_arrive(&vbar[1]);  // close this round's phase
-        // keys of the round's chunks, FETCH_ROWS / 8 chunks per pass
+        // one arrival per tile of the round closes its phase: it completes when its chunks are in
+        const int ntr = (rn + FETCH_ROWS / 8 - 1) / (FETCH_ROWS / 8);
+        if (tid < ntr) mbar_arrive(&vbar[tid]);
+        // keys of the round's chunks, 4 chunks per pass: reconstructed, stored, scored
         for (int p0 = 0; p0 < rn; p0 += FETCH_ROWS / 8) {
             const int pn = min(FETCH_ROWS / 8, rn - p0);
-            // U and cos/sin rows of the pass's chunks (and SV^T once), through the load path
             const int nu = pn * 8 * ppr, ncs = pn * 8 * csp, nsv = svt ? 0 : 128 * ppr;
             for (int p = tid; p < nu + ncs + nsv; p += SEL_T) {
                 if (p < nu) {
@@ -417,7 +656,8 @@ __device__ __forceinline__ void fetch_tail(const SelectArgs &a, int bh, unsigned
                     const int q = p - nu, r = q / csp, c = q % csp;
                     const int cid = entry(r0 + p0 + (r >> 3));
                     const int64_t pos = (int64_t)cid * 8 + (r & 7);
-                    if (valid(cid) && pos < a.cs_rows) cp_async16(sCS + r * FETCH_PITCH + c * 8, a.cos_sin + pos * a.cs_stride + c * 8);
+                    if (valid(cid) && pos < a.cs_rows)
+                        cp_async16(sCS + r * FETCH_PITCH + c * 8, a.cos_sin + pos * a.cs_stride + c * 8);
                 } else {
                     const int q = p - nu - ncs, r = q / ppr, c = q % ppr;
                     cp_async16(sB + r * KP + c * 8, a.SVt + ((int64_t)bh * 128 + r) * a.rank + c * 8);
@@ -426,9 +666,9 @@ __device__ __forceinline__ void fetch_tail(const SelectArgs &a, int bh, unsigned
             cp_async_wait_all();
             __syncthreads();
             svt = true;
-            // warp w < 8: rows 16 (w & 3) .. +15, output half w >> 2
-            const int rg = warp & 3, half = (warp >> 2) & 1, g = lane >> 2, t4 = lane & 3;
-            const bool mine = warp < 8 && 2 * rg < pn;
+            // warp w < 4: rows 16 (w & 1) .. +15, output half (w >> 1)
+            const int rg = warp & 1, half = (warp >> 1) & 1, g = lane >> 2, t4 = lane & 3;
+            const bool mine = warp < 4 && 2 * rg < pn;
             uint32_t kres[16];
             if (mine) {
                 float acc[8][4];
@@ -463,135 +703,97 @@ __device__ __forceinline__ void fetch_tail(const SelectArgs &a, int bh, unsigned
                         *reinterpret_cast<uint32_t *>(sU + r * KT + recon_col(half, i, t4)) = kres[hr * 8 + i];
                 }
             }
+            // rows of invalid entries are zero keys (their weights are zero below)
+            for (int p = tid; p < FETCH_ROWS * 16; p += SEL_T) {
+                const int r = p >> 4, c = (p & 15) * 8, q = r >> 3;
+                if (q >= pn || lS[r0 + p0 + q] < 0) st_v4(sU + r * KT + c, make_uint4(0, 0, 0, 0));
+            }
             __syncthreads();
             // the keys into their slots of k_buf
             for (int p = tid; p < pn * 8 * 16; p += SEL_T) {
                 const int r = p >> 4, c = (p & 15) * 8;
-                const int cid = entry(r0 + p0 + (r >> 3));
-                if (!valid(cid)) continue;
-                const int sl = slot_of(cid);
-                if (sl < 0) {
-                    if ((p & 127) == 0) report_dev_error(DEV_ERR_SLOT);
-                    continue;
-                }
+                const int sl = lS[r0 + p0 + (r >> 3)];
+                if (sl < 0) continue;
                 st_v4(a.k_buf + ((int64_t)bh * a.buf_len + a.sparse_start + 8 * sl + (r & 7)) * 128 + c,
                       ld_v4(sU + r * KT + c));
             }
+            // scores and weights of the pass's rows (an invalid entry's rows count as -inf)
+            const int tp = p0 / (FETCH_ROWS / 8);
+            __nv_bfloat16 *Pt = pTiles + (size_t)tp * G * FX_PPITCH;
+            int nrows = pn * 8;
+            if (warp < 2) {
+                if (G <= 8) fx_scores<1>(sU, KT, sQ, G, sS, nrows, a.scale, warp, lane);
+                else fx_scores<2>(sU, KT, sQ, G, sS, nrows, a.scale, warp, lane);
+            }
+            __syncthreads();
+            for (int p = tid; p < FETCH_ROWS * 16; p += SEL_T) {
+                const int r = p >> 4, q = r >> 3;
+                if (q < pn && lS[r0 + p0 + q] < 0) sS[p] = -INFINITY;
+            }
+            __syncthreads();
+            fx_softmax(sS, Pt, tml + tp * 16, G, warp, lane);
             __syncthreads();  // the tile is free for the next pass
         }
         if (round == 0) {
             SKV_TRACE_CTA(TR_FX_KEYS);
             SKV_TRACE_REC_NOW(3);
         }
-        // the round's values into their slots of v_buf
-        bool ok = mbar_wait(&vbar[1], (unsigned)round & 1u);
-        if (round == 0) ok = mbar_wait(&vbar[0], 0) && ok;
-        if (!ok) {
-            if (tid == 0) report_dev_error(DEV_ERR_WAIT);
-            // the copies must land before the staging area is read or reused
-            mbar_wait(&vbar[1], (unsigned)round & 1u);
-            if (round == 0) mbar_wait(&vbar[0], 0);
+        // per tile, in order, once its values are in: the values into the V
+        // tile and their slots of v_buf, then P V
+        for (int p0 = 0; p0 < rn; p0 += FETCH_ROWS / 8) {
+            const int pn = min(FETCH_ROWS / 8, rn - p0), tp = p0 / (FETCH_ROWS / 8);
+            if (!mbar_wait(&vbar[tp], (unsigned)round & 1u)) {
+                if (tid == 0) report_dev_error(DEV_ERR_WAIT);
+                mbar_wait(&vbar[tp], (unsigned)round & 1u);  // the copies must land before the area is read
+            }
+            if (round == 0 && p0 + FETCH_ROWS / 8 >= rn) {
+                SKV_TRACE_CTA(TR_FX_VALUES);
+                SKV_TRACE_REC_NOW(4);
+            }
+            for (int p = tid; p < FETCH_ROWS * 16; p += SEL_T) {
+                const int r = p >> 4, c = (p & 15) * 8, q = r >> 3;
+                uint4 v = make_uint4(0, 0, 0, 0);
+                if (q < pn) {
+                    const int sl = lS[r0 + p0 + q];
+                    if (sl >= 0) {
+                        v = ld_v4(stage + (size_t)(p0 + q) * 2048 + ((r & 7) * 16 + (p & 15)) * 16);
+                        st_v4(a.v_buf + ((int64_t)bh * a.buf_len + a.sparse_start + 8 * sl + (r & 7)) * 128 + c, v);
+                    }
+                }
+                st_v4(sCS + r * AB_PITCH + c, v);
+            }
+            __syncthreads();
+            fx_pv_merge(pTiles + (size_t)tp * G * FX_PPITCH, zp, sCS, tml + tp * 16, sO, sM, sL, G, warp, lane, tid);
         }
-        if (round == 0) {
-            SKV_TRACE_CTA(TR_FX_VALUES);
-            SKV_TRACE_REC_NOW(4);
-        }
-        for (int p = tid; p < rn * 128; p += SEL_T) {
-            const int j = p >> 7, piece = p & 127;
-            const int cid = entry(r0 + j);
-            if (!valid(cid)) continue;
-            const int sl = slot_of(cid);
-            if (sl < 0) continue;
-            st_v4(a.v_buf + ((int64_t)bh * a.buf_len + a.sparse_start + 8 * sl) * 128 + piece * 8,
-                  ld_v4(stage + (size_t)j * 2048 + piece * 16));
-        }
-        __syncthreads();  // the staging area is free for the next round
-    }
-    if (nW == 0) {
-        // nothing of ours in flight except the (empty) phase of the scan
-        if (!mbar_wait(&vbar[0], 0) && tid == 0) report_dev_error(DEV_ERR_WAIT);
     }
     SKV_TRACE_CTA(TR_FX_END);
     SKV_TRACE_REC_NOW(5);
-}
 
-// Shared memory of one attention worker (8 warps): K and V tiles, query rows,
-// weights and scores of a 128-row block.
-constexpr size_t FETCH_AB_BYTES = (size_t)2 * AB_ROWS * AB_PITCH * 2 + (size_t)2 * 16 * AB_PITCH * 2 + AB_ROWS * 16 * 4;
-
-// The step's attention, by the cluster of a head, once every CTA's keys and
-// values are in the buffers: CTA `rank` computes the partials of blocks
-// rank, rank + cl, ... (att_workers blocks at a time, 8 warps each) -- the same
-// 128-row blocks and arithmetic as the fused attention kernel -- then rank 0
-// merges the head's partials into the output.  Rows come in through the load
-// path; rows past the step's end are zero.
-__device__ __forceinline__ void fetch_attend(const SelectArgs &a, int bh, unsigned rank, unsigned cl,
-                                             unsigned char *smem_raw, float (*s_am)[16], float (*s_al)[16])
-{
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int G = a.G, W = a.att_workers;
-    int seq_len = a.seq_len;
-    if (a.row_dev) {
-        const int r1 = *a.row_dev + 1;
-        if (r1 >= a.sparse_start + 8 * a.K && r1 <= a.seq_len) seq_len = r1;
-        else if (tid == 0 && rank == 0) report_dev_error(DEV_ERR_ROW);
-    }
-    const int nblk = ceil_div(seq_len, AB_ROWS);
-    const int worker = warp >> 3, wwarp = warp & 7, wtid = tid & 255;
-    const bool working = worker < W;
-    unsigned char *base = smem_raw + a.stage_off + (size_t)worker * FETCH_AB_BYTES;
-    __nv_bfloat16 *sK = reinterpret_cast<__nv_bfloat16 *>(base);
-    __nv_bfloat16 *sV = sK + AB_ROWS * AB_PITCH;
-    __nv_bfloat16 *sQ = sV + AB_ROWS * AB_PITCH;
-    __nv_bfloat16 *sP = sQ + 16 * AB_PITCH;
-    float *sS = reinterpret_cast<float *>(sP + 16 * AB_PITCH);
-    if (working) {
-        const __nv_bfloat16 *qrows = a.q_rot + (int64_t)bh * G * 128;
-        for (int p = wtid; p < 16 * 16; p += 256) {
-            const int r = p >> 4, c = (p & 15) * 8;
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (r < G) v = ld_nc_v4(qrows + (int64_t)r * 128 + c);
-            st_v4(sQ + r * AB_PITCH + c, v);
-        }
-    }
-    const __nv_bfloat16 *kb = a.k_buf + (int64_t)bh * a.buf_len * 128, *vb = a.v_buf + (int64_t)bh * a.buf_len * 128;
-    for (int k0 = 0; (int)rank + (int)cl * k0 < nblk; k0 += W) {
-        const int j = (int)rank + (int)cl * (k0 + worker);
-        const bool active = working && j < nblk;
-        const int row0 = j * AB_ROWS, nrows = active ? min(AB_ROWS, seq_len - row0) : 0;
-        if (active) {
-            for (int p = wtid; p < AB_ROWS * 32; p += 256) {
-                const int r = (p >> 4) & (AB_ROWS - 1), c = (p & 15) * 8;
-                const bool isv = p >= AB_ROWS * 16;
-                __nv_bfloat16 *dst = (isv ? sV : sK) + r * AB_PITCH + c;
-                if (r < nrows) cp_async16(dst, (isv ? vb : kb) + (int64_t)(row0 + r) * 128 + c);
-                else st_v4(dst, make_uint4(0, 0, 0, 0));
+    // the head's output: the cl partials merged through distributed shared memory
+    cluster_sync();  // every CTA's (M, L, O) is final
+    {
+        const int dpc = 128 / (int)cl;  // output columns per CTA
+        if (tid < G * dpc) {
+            const int g = tid / dpc, d = (int)rank * dpc + tid % dpc;
+            float Mj[16], Lj[16], Oj[16];
+            float M = -INFINITY;
+            for (unsigned j = 0; j < cl; ++j) {
+                Mj[j] = __uint_as_float(ld_dsmem_u32(dsmem_addr(sM + g, j)));
+                Lj[j] = __uint_as_float(ld_dsmem_u32(dsmem_addr(sL + g, j)));
+                Oj[j] = __uint_as_float(ld_dsmem_u32(dsmem_addr(sO + g * 128 + d, j)));
+                M = fmaxf(M, Mj[j]);
             }
+            float Ls = 0.f, Os = 0.f;
+            for (unsigned j = 0; j < cl; ++j) {
+                if (Mj[j] == -INFINITY) continue;
+                const float w = __expf(Mj[j] - M);
+                Ls += Lj[j] * w;
+                Os += Oj[j] * w;
+            }
+            a.out[((int64_t)bh * G + g) * 128 + d] = f2bf(Ls > 0.f ? Os / Ls : 0.f);
         }
-        cp_async_wait_all();
-        __syncthreads();
-        if (active) {
-            if (G <= 8) ab_scores<1>(sK, AB_PITCH, sQ, sS, nrows, a.scale, wwarp, lane);
-            else ab_scores<2>(sK, AB_PITCH, sQ, sS, nrows, a.scale, wwarp, lane);
-        }
-        __syncthreads();
-        if (active) ab_softmax(sS, sP, s_am[worker], s_al[worker], G, wwarp, lane);
-        __syncthreads();
-        if (active) {
-            float o[2][4];
-            ab_pv(sP, sV, o, wwarp, lane);
-            ab_partial(o, a.part_o + ((int64_t)bh * a.pstride + j) * G * 128, a.part_ml + ((int64_t)bh * a.pstride + j) * G,
-                       s_am[worker], s_al[worker], G, wwarp, lane, wtid);
-        }
-        __syncthreads();  // the tiles are free for the next blocks
     }
-    cluster_sync();  // every block partial of the head is written
-    if (rank == 0) {
-        __nv_bfloat16 *out = a.out + (int64_t)bh * G * 128;
-        ab_merge(a.part_o + (int64_t)bh * a.pstride * G * 128, a.part_ml + (int64_t)bh * a.pstride * G, nblk, G,
-                 smem_raw + a.stage_off, tid, SEL_T,
-                 [&](int gg, int d, uint2 pk) { *reinterpret_cast<uint2 *>(out + (int64_t)gg * 128 + d) = pk; });
-    }
+    cluster_sync();  // no CTA leaves while another may still read its shared memory
 }
 
 // FETCH (the decode step): the kernel also fetches the values of the missed
@@ -630,9 +832,11 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
     // FETCH: value copies issued at the scan ([0]) and later ([1], one phase per
     // round); reconstruction operands; chunks of this CTA (certain misses found
     // here, misses handed over by rank 0); rank 0: misses handed to each CTA
-    __shared__ __align__(8) uint64_t s_vbar[2], s_mbar;  // s_mbar: rank 0's message of the misses
+    // FETCH: completion of the value chunks of each 4-chunk tile of the staging
+    // area (one phase per round); s_mbar: rank 0's message of the misses
+    __shared__ __align__(8) uint64_t s_vbar[FX_MAX_TILES], s_mbar;
     __shared__ unsigned s_nC, s_nB;
-    __shared__ float s_am[2][16], s_al[2][16];          // FETCH: block (max, sum) of each attention worker
+    __shared__ int s_ngrp;                              // FETCH: groups of buffer rows attended here
 
     const unsigned rank = blockIdx.x;
     const int bh = blockIdx.y, tid = threadIdx.x, lane = tid & 31;
@@ -713,8 +917,7 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
         if (tid == 0) {
             s_nC = 0;
             s_nB = 0;
-            mbar_init(&s_vbar[0], 1);
-            mbar_init(&s_vbar[1], 1);
+            for (int t = 0; t < FX_MAX_TILES; ++t) mbar_init(&s_vbar[t], 1);
             mbar_init(&s_mbar, 1);
             mbar_fence_init();
             // rank 0's message comes as transaction bytes on s_mbar: expected before
@@ -949,18 +1152,34 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
             // values between its arrival and its wait (a release issued while they
             // are in flight would wait for the host link)
             __syncthreads();  // the list of certain misses is complete
-            cluster_arrive_release();
-            if (warp_id() == SEL_T / 32 - 1) {
-                if (lane == 0) SKV_TRACE_R2(2);
-                const int ne = min(min((int)s_nC, K), a.cap);
-                for (int j = lane; j < ne; j += 32) {
-                    mbar_expect_tx(&s_vbar[0], 2048u);
-                    bulk_g2s(stage + (size_t)j * 2048, a.v_host + ((int64_t)bh * a.num_chunks + lC[j]) * 128, 2048u,
-                             &s_vbar[0]);
+            {
+                // ascending chunk ids (the order of the list decides the attention's
+                // summation order: the same every run)
+                const int nCk = min((int)s_nC, K);
+                int *tmp = lC + 2 * K;
+                for (int t = tid; t < nCk; t += SEL_T) {
+                    const int v = lC[t];
+                    int r = 0;
+                    for (int j = 0; j < nCk; ++j) r += lC[j] < v ? 1 : 0;
+                    tmp[r] = v;
                 }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&s_vbar[0]);  // every copy of the scan is issued: close the phase
-                if (lane == 0) SKV_TRACE_R2(3);
+                __syncthreads();
+                for (int t = tid; t < nCk; t += SEL_T) lC[t] = tmp[t];
+                __syncthreads();
+            }
+            cluster_arrive_release();
+            {
+                // copy j is issued by warp j % 16, lane j / 16: the issue, which costs
+                // each issuing thread a while per copy, is spread over every warp
+                if (tid == 0) SKV_TRACE_R2(2);
+                const int ne = fx_early_count((int)s_nC, K, a.cap, rank);
+                const int j = (tid & 31) * (SEL_T / 32) + (tid >> 5);
+                if (j < ne) {
+                    uint64_t *tb = &s_vbar[j / (FETCH_ROWS / 8)];
+                    mbar_expect_tx(tb, 2048u);
+                    bulk_g2s(stage + (size_t)j * 2048, a.v_host + ((int64_t)bh * a.num_chunks + lC[j]) * 128, 2048u, tb);
+                }
+                if (tid == 0) SKV_TRACE_R2(3);
             }
             SKV_TRACE_REC_NOW(4);
             cluster_wait_acquire();
@@ -1024,7 +1243,6 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
                                   s_eq_rank);
         cluster_sync();  // rank 0's bitmap holds the complete selection
         if constexpr (FETCH) {
-            if (tid == 0) mbar_arrive(&s_vbar[0]);  // nothing was requested early: the phase closes empty
         } else {
             if (rank != 0) return;
         }
@@ -1112,13 +1330,7 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
     SKV_TRACE_CTA(TR_SEL_END);
     SKV_TRACE_REC_NOW(7);
     }  // rank 0
-    if constexpr (FETCH) {
-        fetch_tail(a, bh, rank, CL, smem_raw, &s_vbar[0], &s_mbar, s_nC, &s_nB);
-        // every CTA's keys and values are in the buffers once all have arrived
-        // (no host copies are in flight any more: the barrier is cheap)
-        cluster_sync();
-        fetch_attend(a, bh, rank, CL, smem_raw, s_am, s_al);
-    }
+    if constexpr (FETCH) fetch_tail(a, bh, rank, CL, smem_raw, &s_vbar[0], &s_mbar, s_nC, &s_nB, &s_ngrp);
 }
 
 size_t select_smem_bytes(int L, int num_chunks, int G, bool keys_global, int cl, bool keys_pre)
@@ -1239,31 +1451,30 @@ FetchLayout fetch_layout(int L, int num_chunks, int G, int K, int rank, int buf_
     auto a128 = [](size_t x) { return (x + 127) & ~(size_t)127; };
     const size_t base = a128(select_base_bytes(L, num_chunks, false, SEL_CL));
     const size_t hist_ring = (size_t)(SEL_T / 32) * SEL_BINS * 4 + select_ring_bytes(L, G, SEL_CL);
-    const size_t list = a128((size_t)2 * K * 4), msg = a128(fetch_msg_bytes(K));
+    const size_t list = a128((size_t)4 * K * 4), msg = a128(fetch_msg_bytes(K));
     const size_t bmc = a128((size_t)((num_chunks + 31) / 32) * 4);
     const size_t recon = a128((size_t)FETCH_ROWS * fetch_kt(rank) * 2 + (size_t)128 * (rank + 8) * 2 +
                               (size_t)FETCH_ROWS * FETCH_PITCH * 2);
-    const size_t fixed = base + list + msg + bmc + recon;
-    if (fixed + 16 * 2048 > FETCH_SMEM_CAP) return f;  // fewer than 16 chunks staged at once: not used
-    int cap = (int)((FETCH_SMEM_CAP - fixed) / 2048);
-    if (cap > 64) cap = 64;
-    const size_t stage = a128((size_t)cap * 2048) > a128(hist_ring) ? a128((size_t)cap * 2048) : a128(hist_ring);
-    if (fixed + stage > FETCH_SMEM_CAP) return f;
-    size_t bytes = fixed + stage;
-    // the attention tiles and the merge scratch reuse everything from the staging area on
-    const size_t merge = (size_t)((buf_len + AB_ROWS - 1) / AB_ROWS) * G * 12;
-    const size_t need1 = FETCH_AB_BYTES > merge ? FETCH_AB_BYTES : merge;
-    if (bytes - base < need1) bytes = base + need1;
-    if (bytes > FETCH_SMEM_CAP) return f;
-    f.att_workers = bytes - base >= 2 * FETCH_AB_BYTES ? 2 : 1;
-    f.cap = cap;
-    f.stage_off = (unsigned)base;
-    f.list_off = (unsigned)(base + stage);
-    f.msg_off = (unsigned)(f.list_off + list);
-    f.bmc_off = (unsigned)(f.msg_off + msg);
-    f.recon_off = (unsigned)(f.bmc_off + bmc);
-    f.bytes = (unsigned)bytes;
-    return f;
+    // the largest staging area that fits; the attention region reuses the
+    // selection's keys, ids and bitmaps when it fits there (they are no longer
+    // read once rank 0's message is out), else it comes on top
+    for (int cap = 64; cap >= 16; --cap) {
+        const FxAttLayout at = fx_att_layout(G, cap, buf_len, K);
+        const size_t att = at.bytes <= base ? 0 : a128(at.bytes);
+        const size_t stage = a128((size_t)cap * 2048) > a128(hist_ring) ? a128((size_t)cap * 2048) : a128(hist_ring);
+        const size_t bytes = base + stage + list + msg + bmc + recon + att;
+        if (bytes > FETCH_SMEM_CAP) continue;
+        f.cap = cap;
+        f.stage_off = (unsigned)base;
+        f.list_off = (unsigned)(base + stage);
+        f.msg_off = (unsigned)(f.list_off + list);
+        f.bmc_off = (unsigned)(f.msg_off + msg);
+        f.recon_off = (unsigned)(f.bmc_off + bmc);
+        f.att_off = att ? (unsigned)(f.recon_off + recon) : 0u;
+        f.bytes = (unsigned)bytes;
+        return f;
+    }
+    return f;  // fewer than 16 chunks staged at once: not used
 }
 
 int launch_select_fetch(const SelectArgs &a, int BH, size_t smem, cudaStream_t stream)

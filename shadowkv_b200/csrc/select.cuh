@@ -43,26 +43,60 @@ struct SelectArgs {
     __nv_bfloat16 *k_buf, *v_buf;     // [BH][buf_len][128]
     int Hkv, rank, ctx, buf_len, sparse_start, rope_mode, cs_stride, cs_rows;
     int cap;                          // value chunks staged in shared memory at once
-    unsigned stage_off, list_off, msg_off, bmc_off, recon_off;  // byte offsets in dynamic shared memory
-    // ... and the step's attention over the buffers, by the cluster of each head
+    unsigned stage_off, list_off, msg_off, bmc_off, recon_off, att_off;  // byte offsets in dynamic shared memory
+    // ... and the step's attention, by the cluster of each head
     const __nv_bfloat16 *q_rot;       // [BH][G][128] rotated queries (written by the scoring kernel)
     __nv_bfloat16 *out;               // [BH][G][128]
-    float *part_o;                    // [BH][pstride][G][128] block partials
-    float2 *part_ml;                  // [BH][pstride][G] (max, sum) of the block partials
     const int32_t *row_dev;           // optional: the append row, read on the device
-    int seq_len, pstride, att_workers;
+    int seq_len;
     float scale;
 };
 
 // Early-fetch variant of the selection (decode step): shared-memory layout of
 // one CTA for rank `rank` and `cap` staged chunks; 0 when it does not fit.
-constexpr int FETCH_ROWS = 64;            // rows of one key-reconstruction pass
+constexpr int FETCH_ROWS = 32;            // rows of one key-reconstruction pass / attention tile
 constexpr int FETCH_PITCH = 136;          // bf16 row pitch of the cos/sin rows
 constexpr size_t FETCH_SMEM_CAP = 190 * 1024;  // dynamic shared memory of a FETCH CTA (static ~37 KB)
 struct FetchLayout {
-    unsigned stage_off, list_off, msg_off, bmc_off, recon_off, bytes;
-    int cap, att_workers;  // attention: 128-row blocks processed at once (tiles from stage_off on)
+    unsigned stage_off, list_off, msg_off, bmc_off, recon_off, att_off, bytes;
+    int cap;
 };
+constexpr int FX_PPITCH = 40;  // bf16 row pitch of a tile's attention weights (32 rows + 8)
+constexpr int FX_MAX_TILES = 16;  // 4-chunk tiles of the staging area (at most 64 chunks)
+// The attention region of a FETCH CTA (offsets from att_off): the G rotated
+// query rows and a zero row, the running output O [G][128] and its row (max,
+// sum), the scores of one 32-row tile, a zero weight row, the weights of a
+// buffer-row tile, the weights and (max, sum) of the round's miss tiles, the
+// 8-row groups of buffer rows attended by the CTA and the bitmap of the slots
+// refilled by misses.
+struct FxAttLayout {
+    unsigned q, o, m, l, s, zp, pt, p, tml, grp, msb, bytes;
+    int ntiles;
+};
+__host__ __device__ inline FxAttLayout fx_att_layout(int G, int cap, int buf_len, int K)
+{
+    FxAttLayout f = {};
+    unsigned off = 0;
+    auto take = [&off](unsigned bytes) {
+        const unsigned o = off;
+        off = (off + bytes + 15u) & ~15u;
+        return o;
+    };
+    f.ntiles = (cap + FETCH_ROWS / 8 - 1) / (FETCH_ROWS / 8);
+    f.q = take((unsigned)(G + 1) * 136u * 2u);
+    f.o = take((unsigned)G * 128u * 4u);
+    f.m = take(16u * 4u);
+    f.l = take(16u * 4u);
+    f.s = take((unsigned)FETCH_ROWS * 16u * 4u);
+    f.zp = take((unsigned)FX_PPITCH * 2u);
+    f.pt = take((unsigned)G * FX_PPITCH * 2u);
+    f.p = take((unsigned)f.ntiles * G * FX_PPITCH * 2u);
+    f.tml = take((unsigned)(f.ntiles + 1) * 16u * 8u);
+    f.grp = take((unsigned)((buf_len + 7) / 8 + 1) * 4u);
+    f.msb = take((unsigned)((K + 31) / 32) * 4u);
+    f.bytes = off;
+    return f;
+}
 // Rank 0's message to every CTA of the cluster: a (count, 0) pair and K
 // (chunk id, slot) pairs, padded to 16 bytes.
 __host__ __device__ inline unsigned fetch_msg_bytes(int K) { return (unsigned)(((K + 2) & ~1) * 8); }

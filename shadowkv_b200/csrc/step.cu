@@ -34,10 +34,11 @@
 // the selection kernel of each group requests the value chunks of the
 // certain misses from the host as soon as its histogram has located the
 // boundary score, reconstructs the missed keys, writes keys and values into
-// their slots and, once every value of the head is in, computes the head's
-// attention itself (the same 128-row blocks and merge as the attention
-// kernel): the step is then two kernels per group.  The state and output are
-// the same bits either way.
+// their slots and computes the head's attention itself, each CTA over the
+// rows it fetched plus a share of the rows already in the buffers, merged
+// through distributed shared memory: the step is then two kernels per group.
+// The state is the same bits either way; the output differs only by fp32
+// summation order (a different split of the rows into partials).
 //
 // Library streams and events are created per device on the first call that
 // needs them (make that call before any stream capture); the fork and join are
@@ -208,19 +209,10 @@ int skv_decode_step(const skv_decode_geom *g, const void *q, const void *k_new, 
             fx.cos_sin = (const __nv_bfloat16 *)cos_sin;
             fx.k_buf = kb;
             fx.v_buf = vb;
-            // the attention: block partials in the group's attention workspace
-            // (one ticket word per head first, as the attention kernel lays it out)
-            const int64_t bhg = (int64_t)gp.batch * gp.kv_heads;
-            const int pstride = ceil_div(g->buf_len, 128);
-            unsigned char *att = w + L.att;
-            fx.part_ml = reinterpret_cast<float2 *>(att + align256((size_t)bhg * 4));
-            fx.part_o = reinterpret_cast<float *>(att + align256((size_t)bhg * 4) +
-                                                  align256((size_t)bhg * pstride * G * 8));
             fx.q_rot = qo;
             fx.out = (__nv_bfloat16 *)dout + h0 * G * 128;
             fx.row_dev = row_dev;
             fx.seq_len = seq_len;
-            fx.pstride = pstride;
         }
         bool fetched = false;
         int st = append_select_launch(&gp, qb, (const __nv_bfloat16 *)k_new + h0 * 128,

@@ -4,7 +4,9 @@ Several layers at the Llama-3-8B head layout (32 q / 8 kv heads, rank 160, budge
 shorter context keeps the test quick), several tokens in a row: the graph is captured on the
 first step and replayed, the append position advancing on the device.  Every step's outputs and
 the state it leaves (K/V buffers, slot tables) must equal, bit for bit, the same steps run
-eagerly through ``decode_step_fused`` one layer at a time.
+eagerly through ``decode_step_fused`` one layer at a time -- also with the early value fetch
+(selection kernels that fetch the misses and compute the attention, reading the position from
+the device).
 """
 import dataclasses
 
@@ -19,8 +21,17 @@ def _bits(t):
     return t.contiguous().view(torch.int16)
 
 
-@pytest.mark.parametrize("chain", [False, True])
-def test_graph_replays_match_eager_steps(chain):
+@pytest.mark.parametrize("chain,early", [(False, False), (True, False), (True, True)])
+def test_graph_replays_match_eager_steps(chain, early):
+    from shadowkv_b200 import decode as fz
+    before = fz.early_fetch(early)
+    try:
+        _graph_vs_eager(chain)
+    finally:
+        fz.early_fetch(before)
+
+
+def _graph_vs_eager(chain):
     from shadowkv_b200 import workload
     from shadowkv_b200._lib import device_errors
     from shadowkv_b200.graph import DecodeGraph

@@ -1,12 +1,15 @@
 """The one-call decode step (``skv_decode_step``), plain and pipelined over kv-head groups.
 
-It must leave exactly the state and output of ``append_select`` + ``sparse_attention`` (the
-two-call fused path that the other tests check against the oracle): same slots, same K/V
-buffer bits, same rotated query, same attention output, same miss counts -- for every head
-grouping, with the early value fetch (the selection kernel writing the missed rows) on and
-off, over several steps (so later steps hit the reuse cache the earlier ones filled); also
-when the selection concentrates in one selection CTA's landmarks, whose certain misses then
-exceed its staging area and are fetched in several rounds, and for a batch of sequences.
+It must leave exactly the state of ``append_select`` + ``sparse_attention`` (the two-call
+fused path that the other tests check against the oracle): same slots, same K/V buffer bits,
+same rotated query, same miss counts -- for every head grouping, with the early value fetch
+(the selection kernel fetching the missed rows and computing the attention) on and off, over
+several steps (so later steps hit the reuse cache the earlier ones filled); also when the
+selection concentrates in one selection CTA's landmarks, whose certain misses then exceed its
+staging area and are fetched in several rounds, and for a batch of sequences.  The attention
+output is the same bits without the early fetch; with it the rows are split into partials
+differently (per selection CTA, 32-row tiles) and the output agrees up to fp32 summation
+order and the rounding of the softmax weights to bf16: within 2^-6 relative + 2e-3.
 """
 import dataclasses
 
@@ -71,7 +74,11 @@ def _compare_paths(layer, inputs, groups):
                 tag = f"groups {p}, early fetch {early}"
                 for s, ((qr, o, m), (qr2, o2, m2)) in enumerate(zip(ref_outs, outs)):
                     assert torch.equal(qr.view(torch.int16), qr2.view(torch.int16)), f"rotated query, step {s}, {tag}"
-                    assert torch.equal(o.view(torch.int16), o2.view(torch.int16)), f"output, step {s}, {tag}"
+                    if early:
+                        err = (o2.float() - o.float()).abs()
+                        assert (err <= o.float().abs() * 2.0 ** -6 + 2e-3).all(), f"output, step {s}, {tag}"
+                    else:
+                        assert torch.equal(o.view(torch.int16), o2.view(torch.int16)), f"output, step {s}, {tag}"
                     assert torch.equal(m, m2), f"miss counts, step {s}, {tag}"
                 assert torch.equal(state[2], ref_state[2]), f"slots, {tag}"
                 assert torch.equal(state[0].view(torch.int16), ref_state[0].view(torch.int16)), f"K buffer, {tag}"
