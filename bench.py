@@ -167,6 +167,62 @@ def algorithmic_bytes(cache, misses: int, seq_len: int):
     return hbm, host
 
 
+def graph_kernel_times(cache, step_body, flush, load_inputs, stream, groups, steps, seq_len):
+    """Kernel times of the graph-replayed one-call step (skv_decode_step).
+
+    The step is captured once more with ``skv_decode_step_timing`` on: the same launches
+    (programmatic dependent launch included), whose CTAs stamp the GPU's global timer at their
+    start (after the wait for the kernel before them) and end into a span pair per (kv-head
+    group, kernel), stamped by every replay.  Each replay follows an L2 flush; its step is timed
+    with CUDA events on the caller's stream, its spans read after it.  Returns ``(kernel_us,
+    (host bytes, attention-phase us) per step, per-launch figures of the attention kernel)``;
+    the attention phase runs from the first attention CTA past its wait (the first group's
+    selection complete) to the last attention CTA's end."""
+    from shadowkv_b200 import decode as fz
+    torch.cuda.synchronize()
+    prev = fz.step_timing(True)
+    try:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step_body()
+        torch.cuda.synchronize()
+    finally:
+        fz.step_timing(prev)
+    score, sel, att, phase, first_att, step, host, launch_bytes = [], [], [], [], [], [], [], []
+    for i in steps:
+        flush.zero_()
+        load_inputs(i)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        g.replay()
+        b.record(stream)
+        b.synchronize()
+        step.append(1e3 * a.elapsed_time(b))
+        t = fz.step_kernel_times(groups)
+        mc = cache._step_ws.miss_count.view(-1).tolist()  # per (sequence, kv head)
+        per = len(mc) // groups  # the heads of a group (batch 1 when groups > 1)
+        for gi, (s0, e0, s1, e1, s2, e2) in enumerate(t):
+            score.append(e0 - s0)
+            sel.append(e1 - s1)
+            if s2 is not None:
+                att.append(e2 - s2)
+                launch_bytes.append(algorithmic_bytes(cache, sum(mc[gi * per:(gi + 1) * per]), seq_len)[1])
+        if all(x[4] is not None for x in t):
+            phase.append(max(x[5] for x in t) - min(x[4] for x in t))
+            first_att.append(min(x[4] for x in t))
+        host.append(algorithmic_bytes(cache, sum(mc), seq_len)[1])
+    del g
+    mean = statistics.mean
+    kernel_us = {"scoring": mean(score), "selection": mean(sel), "step_with_stamps": mean(step), "groups": groups}
+    per_launch = None
+    if att and phase:
+        kernel_us.update({"sparse_attention": mean(att), "attention_phase": mean(phase),
+                          "attention_phase_start": mean(first_att)})
+        per_launch = {"host_bytes": mean(launch_bytes), "us": mean(att),
+                      "gbs": mean(launch_bytes) / (mean(att) * 1e-6) / 1e9}
+    return kernel_us, (mean(host), mean(phase) if phase else None), per_launch
+
+
 def select_kernels(cache):
     """Kernels of one fused append+select call (2, or 3 with the keys kernel of long contexts)."""
     import ctypes
@@ -266,11 +322,13 @@ def run_b200(args, world, rank, local):
         s_v.copy_(v)
         s_pos.fill_(pos0 + i)
 
-    def step_body(final_out=None):
-        """One decode step of NL layers on the static inputs (appends at row sparse_end)."""
+    def step_body(final_out=None, ins=None):
+        """One decode step of NL layers on the static inputs (appends at row sparse_end); ``ins``:
+        other (q, k, v, position) tensors of the step (page-locked host ones for the e2e run)."""
         cache.gen_offset = 0
+        x_q, x_k, x_v, x_pos = ins if ins is not None else (s_q, s_k, s_v, s_pos)
         for li in range(NL):
-            q_in = s_q if li == 0 else s_mid[(li - 1) % 2]
+            q_in = x_q if li == 0 else s_mid[(li - 1) % 2]
             out = (s_out if final_out is None else final_out) if li == NL - 1 else s_mid[li % 2]
             if args.microbatch > 1 and not args.split and not heads_sharded:
                 seq_len = cache.sparse_end + cache.gen_offset + 1
@@ -278,7 +336,7 @@ def run_b200(args, world, rank, local):
                                                args.microbatch, q_out=s_qr, max_ctas=args.fetch_ctas)
                 continue
             if use_step:
-                cache.decode_step_fused(li, q_in, s_k, s_v, s_pos, attn.cos_sin_cache, out=out,
+                cache.decode_step_fused(li, q_in, x_k, x_v, x_pos, attn.cos_sin_cache, out=out,
                                         head_groups=head_groups, q_out=s_qr)
                 seq_len = cache.sparse_end + cache._gen_offset(li)
                 continue
@@ -353,44 +411,55 @@ def run_b200(args, world, rank, local):
     link_samples = [link_peak, link_bandwidth_gbs()]
     link_peak = max(link_samples)
 
-    # ---- per-kernel times: the same steps launched eagerly, one kernel group at a time,
-    # each bracketed by CUDA events on the stream it runs on (L2 flushed before each step)
-    names = (["append_select", "fetch_values", "reconstruct_keys", "attention"] if args.split
-             else ["append_select", "sparse_attention"])
-    parts = {k: [] for k in names}
-    for i in range(args.warmup, min(n, args.warmup + 100)):
-        flush.zero_()
-        load_inputs(i)
-        cache.gen_offset = 0
-        torch.cuda.synchronize()
+    # ---- per-kernel times.  The one-call step: the same step captured once more with CUDA
+    # events around each kv-head group's kernels (skv_decode_step_timing: event nodes on the
+    # groups' own streams, recorded by every replay), replayed after an L2 flush.  Other
+    # launch modes: the kernels launched eagerly, one group at a time.
+    graph_timed = use_step and graph is not None and NL == 1
+    per_launch = None
+    if graph_timed:
+        kernel_us, link_bytes_us, per_launch = graph_kernel_times(
+            cache, step_body, flush, load_inputs, main, head_groups, range(args.warmup, min(n, args.warmup + 50)),
+            statistics.mean(seqlens))
+    else:
+        # each kernel group bracketed by CUDA events on the stream it runs on (L2 flushed
+        # before each step)
+        names = (["append_select", "fetch_values", "reconstruct_keys", "attention"] if args.split
+                 else ["append_select", "sparse_attention"])
+        parts = {k: [] for k in names}
+        for i in range(args.warmup, min(n, args.warmup + 100)):
+            flush.zero_()
+            load_inputs(i)
+            cache.gen_offset = 0
+            torch.cuda.synchronize()
 
-        def timed(name, fn, stream):
-            # a GPU-side sleep keeps the stream busy until the launch is enqueued, so the
-            # events bracket device execution only, not host launch latency
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            with torch.cuda.stream(stream):
-                torch.cuda._sleep(400_000)
-                a.record(stream)
-                r = fn()
-                b.record(stream)
-            b.synchronize()
-            parts[name].append(a.elapsed_time(b))
-            return r
+            def timed(name, fn, stream):
+                # a GPU-side sleep keeps the stream busy until the launch is enqueued, so the
+                # events bracket device execution only, not host launch latency
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                with torch.cuda.stream(stream):
+                    torch.cuda._sleep(400_000)
+                    a.record(stream)
+                    r = fn()
+                    b.record(stream)
+                b.synchronize()
+                parts[name].append(a.elapsed_time(b))
+                return r
 
-        qr = timed("append_select", lambda: cache.append_select_fused(0, s_q, s_k, s_v, s_pos, attn.cos_sin_cache,
-                                                                      q_out=s_qr), main)
-        sl = cache.sparse_end + cache._gen_offset(0)
-        if args.split:
-            timed("fetch_values", lambda: cache.fetch_values_fused(0, copy_stream), copy_stream)
-            timed("reconstruct_keys", lambda: cache.reconstruct_keys_fused(0, attn.cos_sin_cache), main)
-            timed("attention", lambda: cache.attention(0, qr, sl, out=s_out), main)
-        else:
-            timed("sparse_attention", lambda: cache.sparse_attention_fused(0, qr, sl, attn.cos_sin_cache, out=s_out),
-                  main)
-        misses_all.append(int(cache._fused_ws.miss_count.sum().item()))
-        cache.gen_offset = 0
-    fetch_ms = parts["fetch_values" if args.split else "sparse_attention"]
-    kernel_us = {k: 1e3 * statistics.mean(v) for k, v in parts.items() if v}
+            qr = timed("append_select", lambda: cache.append_select_fused(0, s_q, s_k, s_v, s_pos, attn.cos_sin_cache,
+                                                                          q_out=s_qr), main)
+            sl = cache.sparse_end + cache._gen_offset(0)
+            if args.split:
+                timed("fetch_values", lambda: cache.fetch_values_fused(0, copy_stream), copy_stream)
+                timed("reconstruct_keys", lambda: cache.reconstruct_keys_fused(0, attn.cos_sin_cache), main)
+                timed("attention", lambda: cache.attention(0, qr, sl, out=s_out), main)
+            else:
+                timed("sparse_attention", lambda: cache.sparse_attention_fused(0, qr, sl, attn.cos_sin_cache, out=s_out),
+                      main)
+            misses_all.append(int(cache._fused_ws.miss_count.sum().item()))
+            cache.gen_offset = 0
+        fetch_ms = parts["fetch_values" if args.split else "sparse_attention"]
+        kernel_us = {k: 1e3 * statistics.mean(v) for k, v in parts.items() if v}
 
     ms_step = sum(per_step) / len(per_step)
     ms_step_max = max_over_ranks(ms_step, world)
@@ -401,8 +470,14 @@ def run_b200(args, world, rank, local):
     hbm_1, host_1 = algorithmic_bytes(cache, misses, statistics.mean(seqlens))  # one layer, one launch
     hbm_b, host_b = hbm_1 * NL, host_1 * NL  # the misses of layer 0 stand for every layer of the step
     t_roof = max(hbm_b / (hbm_peak * 1e9), host_b / (link_peak * 1e9))
-    fetch_avg = statistics.mean(fetch_ms)  # one launch of the fetching kernel on layer 0
-    link_achieved = host_1 / (fetch_avg * 1e-3) / 1e9 if fetch_avg > 0 else 0.0
+    if graph_timed and link_bytes_us[1]:
+        # host bytes of the step over the attention phase of the graph-replayed step
+        link_achieved = link_bytes_us[0] / (link_bytes_us[1] * 1e-6) / 1e9
+    elif graph_timed:  # early fetch: the values come in during the selection kernels
+        link_achieved = link_bytes_us[0] / (kernel_us["step_with_stamps"] * 1e-6) / 1e9
+    else:
+        fetch_avg = statistics.mean(fetch_ms)  # one launch of the fetching kernel on layer 0
+        link_achieved = host_1 / (fetch_avg * 1e-3) / 1e9 if fetch_avg > 0 else 0.0
 
     # ---- e2e: inputs copied from pinned host memory, the output brought back, every step
     # per step: the inputs packed in one pinned host buffer (q, k, v, position)
@@ -416,12 +491,17 @@ def run_b200(args, world, rank, local):
     # the fused step writes its output straight into the page-locked host buffer
     # (the merge stores it over the link: no separate device-to-host copy)
     out_direct = not heads_sharded and not args.split
+    # the one-call step of one layer reads its inputs from page-locked host memory itself (a
+    # staging kernel at its start, inside the timed region): the e2e graph is captured on the
+    # inputs' views of one page-locked buffer, into which each step's inputs are put
+    host_in = out_direct and use_step and graph is not None and NL == 1
+    h_stage = torch.zeros(nbytes, dtype=torch.uint8).pin_memory() if host_in else None
     graph_e2e = None
     if out_direct and graph is not None:
         torch.cuda.synchronize()
         graph_e2e = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph_e2e):
-            step_body(h_out)
+            step_body(h_out, staged(h_stage) if host_in else None)
         torch.cuda.synchronize()
     nin = len(inputs)
     e2e_ms = []
@@ -429,10 +509,13 @@ def run_b200(args, world, rank, local):
         flush.zero_()
         hb = h_in[i % nin]
         staged(hb)[3].fill_(pos0 + i)
+        if host_in:
+            h_stage.copy_(hb)  # this step's inputs, where the step reads them
         torch.cuda.synchronize()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record(main)
-        d_in.copy_(hb, non_blocking=True)  # the step's packed inputs, pinned host -> device
+        if not host_in:
+            d_in.copy_(hb, non_blocking=True)  # the step's packed inputs, pinned host -> device
         if out_direct:
             if graph_e2e is not None:
                 graph_e2e.replay()
@@ -456,7 +539,8 @@ def run_b200(args, world, rank, local):
         allt = [torch.empty_like(t) for _ in range(world)]
         torch.distributed.all_gather(allt, t)
         per_rank = [x.tolist() for x in allt]
-    h2d = nbytes
+    # host -> device bytes of a step: the inputs the staging kernel reads, or the packed buffer
+    h2d = sum(math.prod(shp) * torch.empty((), dtype=dt).element_size() for shp, dt in shapes) if host_in else nbytes
     d2h = h_out.numel() * h_out.element_size()
     used_graph = graph is not None
     del graph, graph_e2e
@@ -499,17 +583,31 @@ def run_b200(args, world, rank, local):
                      # host-link bytes per launch: the missed chunks of this run (2048 B each);
                      # the ncu capture of this workload read exactly the missed bytes over the link
                      "traffic": host_1,
-                     "traffic_kind": "computed: missed chunks x 2048 B per launch (equal to the ncu "
-                                     "sysmem read bytes of the capture in profiles/)",
+                     "traffic_kind": ("computed: missed chunks x 2048 B per "
+                                      + ("step (every kv-head group's launch)" if graph_timed else "launch")
+                                      + " (equal to the ncu sysmem read bytes of the capture in profiles/)"),
                      "peak_kind": "measured in-run: pinned H2D copy-engine bandwidth (best of the "
                                   "measurements before and after the timed steps)",
-                     "peak_samples": link_samples},
+                     "peak_samples": link_samples,
+                     "achieved_kind": ("host bytes of the step / attention phase of the graph-replayed step "
+                                       "(first attention CTA past its wait to the last attention CTA's end: "
+                                       "global-timer stamps of skv_decode_step_timing)" if graph_timed else
+                                       "host bytes of one launch / its eager duration (CUDA events on its stream)"),
+                     "per_launch": per_launch},
         "step_roofline": {"t_roof_us": t_roof * 1e6, "t_step_us": ms_step * 1e3,
                           "frac": t_roof / (ms_step * 1e-3), "hbm_bytes": hbm_b, "host_bytes": host_b,
                           "hbm_peak_gbs": hbm_peak, "hbm_peak_kind": peak_kind, "link_peak_gbs": link_peak},
         "e2e": {"value": tokens / (e2e_step / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h},
+                "d2h_bytes_per_step": d2h,
+                "inputs": ("read from page-locked host memory by the step (staging kernel in the timed region)"
+                           if host_in else "copied from page-locked host memory by cudaMemcpyAsync in the timed region"),
+                "output": ("written to page-locked host memory by the step's attention merge" if out_direct else
+                           "copied to page-locked host memory in the timed region")},
         "kernel_us": kernel_us,
+        "kernel_us_kind": ("graph-replayed step, the kernels' own global-timer spans per kv-head group "
+                           "(skv_decode_step_timing: first CTA start after its wait to last CTA end), "
+                           "L2 flushed before each replay" if graph_timed else
+                           "eager launches, one kernel group at a time, L2 flushed before each step"),
         "per_rank": [{"rank": int(r), "step_us": round(st, 2), "link_peak_gbs": round(lp, 2),
                       "link_achieved_gbs": round(la, 2), "hit_rate": round(hr, 4)}
                      for r, st, lp, la, hr in per_rank],

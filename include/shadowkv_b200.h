@@ -377,6 +377,11 @@ SKV_API size_t skv_decode_step_workspace(const skv_decode_geom *g, int head_grou
  * `stream`, so stream capture records the whole step.  The library streams
  * and events of a device are created by its first call with head_groups > 1:
  * make that call outside stream capture.
+ * q, k_new, v_new and positions may lie in device memory or in page-locked
+ * host memory mapped for the device (8-byte aligned): inputs in host memory
+ * are read over the host link into the workspace by a small staging kernel
+ * at the head of each kv-head group's chain (the step then needs no separate
+ * host-to-device copy of its inputs).
  * row_dev (optional, device int32): the append row read on the device at run
  * time -- the attention then covers rows [0, *row_dev + 1) -- so a captured
  * step can be replayed at later positions (advance *row_dev between
@@ -389,7 +394,9 @@ SKV_API size_t skv_decode_step_workspace(const skv_decode_geom *g, int head_grou
  * certain once its score histogram has located the k-th score, before the
  * selection is complete, reconstructs the missed keys and stores keys and
  * values into their slots; the attention kernel then reads every selected row
- * from the buffers.  State and output are the same bits as without it.
+ * from the buffers.  The state (buffers, slots, miss lists) is the same bits
+ * as without it; the output differs only in fp32 summation order (the rows
+ * are split into partials differently).
  * Replaces, per step, shadowkv.batch_gemm_softmax + torch.topk +
  * reorder_keys_and_compute_offsets + gather_copy_with_offsets +
  * gather_copy_d2d_with_offsets + batch_gather_gemm + the push-cache RoPE and
@@ -406,9 +413,30 @@ SKV_API int skv_decode_step(const skv_decode_geom *g, const void *q, const void 
 /* Turn the early fetch of skv_decode_step on (enable != 0) or off (the
  * default) for the whole process; returns the previous setting.  Calls enqueued
  * afterwards use the new setting (a captured graph keeps the path it was
- * captured with).  For comparisons and diagnosis: both paths give the same
- * results. */
+ * captured with).  For comparisons and diagnosis: both paths leave the same
+ * state, and outputs equal up to fp32 summation order. */
 SKV_API int skv_decode_step_early_fetch(int enable);
+
+/* Kernel timing of skv_decode_step, off by default, for the whole process;
+ * returns the previous setting.  The kernels of a step enqueued with it on
+ * (scoring, selection and attention of each kv-head group) stamp the GPU's
+ * global timer: thread 0 of every CTA at its start, after its wait for the
+ * kernel before it, and at its end, into a (earliest start, latest end) pair
+ * per kernel kept on the device.  The launches are those of an untimed step;
+ * a graph captured from a timed step stamps on every replay.  Results are
+ * unchanged. */
+SKV_API int skv_decode_step_timing(int enable);
+
+/* The spans of the last timed step (or replay of a graph captured from one)
+ * on the current device: waits for the device, then for groups
+ * i < min(*groups, max_groups) and kernels k (0 scoring, 1 selection,
+ * 2 attention) us[6 i + 2 k] = start, us[6 i + 2 k + 1] = end, in microseconds
+ * after the earliest start of any kernel of the step; -1 for a kernel that
+ * did not run (the attention of an early-fetch step runs in its selection
+ * kernel).  Clears the spans for the next step.  *groups = the step's head
+ * groups.  Returns an error if no step was enqueued with timing on, or if
+ * none of its kernels has run since the last read. */
+SKV_API int skv_decode_step_kernel_times(double *us, int max_groups, int *groups);
 
 /* ---- prefill state builder (ShadowKVCache_CPU.prefill_kv_cache,
  * models/kvcache/shadow.py:463-544) for one layer of `batch` sequences. */

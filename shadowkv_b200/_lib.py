@@ -10,7 +10,8 @@ import ctypes
 import os
 
 _PKG = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_PKG, "libshadowkv_b200.so")
+# SKV_LIB: another build of the same library (the trace build of build.build_trace)
+LIB_PATH = os.environ.get("SKV_LIB") or os.path.join(_PKG, "libshadowkv_b200.so")
 
 SKV_OK = 0
 _STATUS = {1: "invalid argument", 2: "unsupported", 3: "CUDA error", 4: "host memory not pinned/mapped"}
@@ -86,6 +87,8 @@ SIGNATURES = {
                                           + [c_int, ctypes.POINTER(PeerGather), P, c_size_t, P],
     "skv_decode_step_workspace": [ctypes.POINTER(DecodeGeom), c_int],
     "skv_decode_step_early_fetch": [c_int],
+    "skv_decode_step_timing": [c_int],
+    "skv_decode_step_kernel_times": [P, c_int, P],
     "skv_decode_step": [ctypes.POINTER(DecodeGeom)] + [P] * 8 + [c_int] + [P] * 7 + [c_int, P, P, c_int, P, c_size_t, P],
     "skv_gram_workspace": [c_int, c_int],
     "skv_gram": [P, c_int, c_int, c_int, P, P, c_size_t, P],

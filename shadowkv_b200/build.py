@@ -41,8 +41,8 @@ def _newest_header() -> float:
     return max((os.path.getmtime(h) for h in hs), default=0.0)
 
 
-def _compile(nvcc: str, src: str, extra: list[str]) -> str:
-    obj = os.path.join(BUILD, os.path.basename(src)[:-3] + ".o")
+def _compile(nvcc: str, src: str, extra: list[str], objdir: str = BUILD) -> str:
+    obj = os.path.join(objdir, os.path.basename(src)[:-3] + ".o")
     cmd = [nvcc, *ARCH, *NVCC_FLAGS, *extra, "-I", os.path.join(ROOT, "include"), "-c", src, "-o", obj]
     stamp = obj + ".cmd"
     fresh = (os.path.exists(obj) and os.path.exists(stamp) and open(stamp).read() == " ".join(cmd)
@@ -57,22 +57,39 @@ def _compile(nvcc: str, src: str, extra: list[str]) -> str:
     return obj
 
 
-def build(verbose: bool = False, extra: list[str] | None = None) -> str:
-    """Compile the library if any source changed; return its path."""
+TRACE_LIB = os.path.join(PKG, "libshadowkv_b200_trace.so")
+
+
+def build(verbose: bool = False, extra: list[str] | None = None, lib: str | None = None) -> str:
+    """Compile the library if any source changed; return its path.
+
+    ``extra``: more nvcc flags; ``lib``: output path (default the product
+    library).  A library built to another path keeps its objects in a folder
+    of its own, so that it and the product library are not rebuilt in turn.
+    """
     extra = list(extra or [])
-    os.makedirs(BUILD, exist_ok=True)
+    out = lib or LIB
+    objdir = BUILD if out == LIB else os.path.join(BUILD, os.path.basename(out)[:-3])
+    os.makedirs(objdir, exist_ok=True)
     nvcc = nvcc_path()
     srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
     with cf.ThreadPoolExecutor(max_workers=min(8, len(srcs))) as ex:
-        objs = list(ex.map(lambda s: _compile(nvcc, s, extra), srcs))
-    if not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):
-        cmd = [nvcc, *ARCH, "-shared", "-rdc=true", "-cudart", "static", "-Xcompiler", "-fPIC", *objs, "-o", LIB]
+        objs = list(ex.map(lambda s: _compile(nvcc, s, extra, objdir), srcs))
+    if not os.path.exists(out) or os.path.getmtime(out) < max(os.path.getmtime(o) for o in objs):
+        cmd = [nvcc, *ARCH, "-shared", "-rdc=true", "-cudart", "static", "-Xcompiler", "-fPIC", *objs, "-o", out]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
     if verbose:
-        print("built", LIB)
-    return LIB
+        print("built", out)
+    return out
+
+
+def build_trace(verbose: bool = False) -> str:
+    """The trace build (``-DSKV_TRACE``: per-phase stamps and per-CTA records,
+    read with ``skv_trace_*``) as ``libshadowkv_b200_trace.so``; load it with
+    ``SKV_LIB`` set to its path."""
+    return build(verbose, ["-DSKV_TRACE"], TRACE_LIB)
 
 
 def ptxas_report() -> str:

@@ -112,6 +112,31 @@ int out_to_device_ptr(void *p, void **dev, const char *name)
     return SKV_ERR_INVALID_ARGUMENT;
 }
 
+int in_to_device_ptr(const void *p, const void **dev, bool *host, const char *name)
+{
+    if (p == nullptr) {
+        set_error("%s is null", name);
+        return SKV_ERR_INVALID_ARGUMENT;
+    }
+    cudaPointerAttributes attr;
+    if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+        cudaGetLastError();
+        attr.type = cudaMemoryTypeUnregistered;
+    }
+    if (attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged) {
+        *dev = p;
+        *host = false;
+        return SKV_OK;
+    }
+    if (attr.type == cudaMemoryTypeHost && attr.devicePointer != nullptr) {
+        *dev = attr.devicePointer;
+        *host = true;
+        return SKV_OK;
+    }
+    set_error("%s must be device memory or page-locked host memory mapped for the device", name);
+    return SKV_ERR_INVALID_ARGUMENT;
+}
+
 int device_sm_count()
 {
     static std::atomic<int> cached[64];  // 0: not queried yet (host threads may race here)

@@ -33,10 +33,13 @@ void clear_error();
         }                                            \
     } while (0)
 
+// A failed runtime call is also kept as the thread's last CUDA error; it is
+// taken off here, so that the next launch check does not report it again.
 #define SKV_CUDA(call)                                                              \
     do {                                                                            \
         cudaError_t e_ = (call);                                                    \
         if (e_ != cudaSuccess) {                                                    \
+            (void)cudaGetLastError();                                               \
             ::skv::set_error("%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), \
                              __FILE__, __LINE__);                                   \
             return SKV_ERR_CUDA;                                                    \
@@ -58,12 +61,21 @@ int host_to_device_ptr(const void *p, const void **dev, const char *name);
 // Device address of an output that is device memory or page-locked host
 // memory (the kernel then writes it over the host link).
 int out_to_device_ptr(void *p, void **dev, const char *name);
+// The same for an input; *host tells which of the two it is.
+int in_to_device_ptr(const void *p, const void **dev, bool *host, const char *name);
 
 inline bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 // Streaming multiprocessors of the current device (queried once per device;
 // 148 on a B200).  Grids are sized from it, not from a constant.
 int device_sm_count();
+
+// Span pairs (see span_begin) of the kernels this host thread launches next;
+// null: no stamps.  Set by skv_decode_step while it enqueues a timed group.
+struct LaunchSpans {
+    unsigned long long *score = nullptr, *select = nullptr, *attend = nullptr;
+};
+LaunchSpans launch_spans();
 
 // ---------------------------------------------------------------------------
 // Device-side error counter: a kernel that finds an index out of range skips
@@ -78,6 +90,28 @@ __device__ __forceinline__ void report_dev_error(uint32_t code)
 {
     unsigned int prev = atomicAdd(&g_dev_err_count, 1u);
     if (prev == 0) atomicExch(&g_dev_err_first, code);
+}
+
+// Global timer of the GPU (nanoseconds).
+__device__ __forceinline__ unsigned long long globaltimer_ns()
+{
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Kernel spans of a timed decode step (skv_decode_step_timing): thread 0 of
+// every CTA stamps its start (after its dependency wait) and its end into the
+// kernel's pair; span[0] keeps the complement of the earliest start (an
+// atomic max of ~t, so that a zeroed pair is empty), span[1] the latest end.
+// A null pair stamps nothing.
+__device__ __forceinline__ void span_begin(unsigned long long *span)
+{
+    if (span && threadIdx.x == 0) atomicMax(span, ~globaltimer_ns());
+}
+__device__ __forceinline__ void span_finish(unsigned long long *span)
+{
+    if (span && threadIdx.x == 0) atomicMax(span + 1, globaltimer_ns());
 }
 
 // ---------------------------------------------------------------------------
@@ -106,12 +140,7 @@ __device__ __forceinline__ void trace_stamp(int e)
 constexpr int SKV_TRACE_RECS = 4096, SKV_TRACE_FIELDS = 8;
 extern __device__ unsigned long long g_trace_rec[SKV_TRACE_RECS * SKV_TRACE_FIELDS];
 extern __device__ unsigned int g_trace_nrec;
-__device__ __forceinline__ unsigned long long trace_now()
-{
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
+__device__ __forceinline__ unsigned long long trace_now() { return globaltimer_ns(); }
 __device__ __forceinline__ unsigned trace_smid()
 {
     unsigned s;

@@ -109,6 +109,7 @@ struct ScoreArgs {
     __nv_bfloat16 *q_out, *k_buf, *v_buf;
     int buf_len, row, rope_mode, cs_stride, cs_rows;
     const int32_t *row_dev;  // if set: the append row, read on the device (graph replays of later steps)
+    unsigned long long *span;  // optional: kernel span pair of a timed step (span_begin)
 };
 
 template <int NT, bool APPEND>
@@ -133,6 +134,7 @@ __global__ void __launch_bounds__(ST_THREADS, 2) score_tma_kernel(ScoreArgs a)
     const __nv_bfloat16 *lmh = a.lm + (int64_t)bh * L * 128;
 
     pdl_launch_dependents();  // the selection kernel may be scheduled early (it waits for this grid)
+    span_begin(a.span);
     SKV_TRACE_CTA(TR_SCORE_START);
     const bool producer = warp == ST_CONSUMERS && lane == 0;
     if (producer) {
@@ -304,6 +306,7 @@ __global__ void __launch_bounds__(ST_THREADS, 2) score_tma_kernel(ScoreArgs a)
         a.part[((int64_t)bh * G + tid) * nsplit + split] = make_float2(mm, ss);  // [BH][G][nsplit]
     }
     SKV_TRACE_CTA(TR_SCORE_END);
+    span_finish(a.span);
 }
 
 // ---------------------------------------------------------------------------
@@ -513,6 +516,7 @@ static int run_select(const skv_decode_geom *g, const ScoreArgs &sa_in, const in
     sa.L = g->num_landmarks;
     sa.rows_per_split = p.rows_per_split;
     sa.scale = g->scale;
+    sa.span = launch_spans().score;
     const void *fn = G <= 8 ? (append ? (const void *)score_tma_kernel<1, true> : (const void *)score_tma_kernel<1, false>)
                             : (append ? (const void *)score_tma_kernel<2, true> : (const void *)score_tma_kernel<2, false>);
     const int smem = ST_SMEM;
@@ -533,6 +537,7 @@ static int run_select(const skv_decode_geom *g, const ScoreArgs &sa_in, const in
     a.miss_count = miss_count;
     a.G = G, a.L = g->num_landmarks, a.K = g->select_sets, a.nsplit = p.nsplit;
     a.num_chunks = g->num_chunks;
+    a.span = launch_spans().select;
     if (p.keys_pre) {
         KeysArgs k;
         k.logits = sa.logits;

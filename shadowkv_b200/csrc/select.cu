@@ -887,6 +887,11 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
         }
 #endif
     }
+#ifdef SKV_TRACE
+    else if (tid == 0) {
+        s_trec2 = -1;  // no second record: shared memory starts undefined
+    }
+#endif
 
     // 0) loads that do not depend on the scores: the cached slots (rank 0,
     //    thread t owns slots 2t, 2t+1) and the chunk ids of this slice
@@ -931,6 +936,7 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
     }
 
     pdl_wait();  // the scoring kernel's logits and partials are complete from here on
+    span_begin(a.span);
     SKV_TRACE_CTA(TR_SEL_WAITED);
 
     // the logits of this CTA's landmarks come in through bulk (TMA) copies,
@@ -1331,6 +1337,7 @@ __global__ void __launch_bounds__(SEL_T) select_cluster_kernel(SelectArgs a)
     SKV_TRACE_REC_NOW(7);
     }  // rank 0
     if constexpr (FETCH) fetch_tail(a, bh, rank, CL, smem_raw, &s_vbar[0], &s_mbar, s_nC, &s_nB, &s_ngrp);
+    span_finish(a.span);  // (ranks other than 0 of a plain selection returned earlier)
 }
 
 size_t select_smem_bytes(int L, int num_chunks, int G, bool keys_global, int cl, bool keys_pre)

@@ -50,6 +50,7 @@ struct SelectArgs {
     const int32_t *row_dev;           // optional: the append row, read on the device
     int seq_len;
     float scale;
+    unsigned long long *span;         // optional: kernel span pair of a timed step (span_begin)
 };
 
 // Early-fetch variant of the selection (decode step): shared-memory layout of

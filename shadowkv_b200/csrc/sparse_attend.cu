@@ -68,6 +68,7 @@ struct SparseAttendArgs {
     // if set: the row this step appended at, read on the device; the attention
     // then covers [0, *row_dev + 1) (at most seq_len rows, which sized the grid)
     const int32_t *row_dev;
+    unsigned long long *span;  // optional: kernel span pair of a timed step (span_begin)
 };
 
 // NT: n-tiles of query heads in S = K q^T (1: G <= 8, 2: G <= 16)
@@ -97,6 +98,7 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
     }
     SKV_TRACE_CTA(TR_SA_START);
     pdl_wait();  // the selection (and the scoring before it) are complete from here on
+    span_begin(a.span);
     SKV_TRACE_CTA(TR_SA_WAITED);
 
     // Work items: (kv head, 128-row block), the blocks that hold selected slots
@@ -397,6 +399,7 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
     }  // the head's last block
     ++iter;  // items that did work: the phase of the copy barrier
     }  // work items
+    span_finish(a.span);
 }
 
 // Peer block layout: arrival counter, status, this rank's epoch, landing buffer.
@@ -578,6 +581,7 @@ static int launch_sparse_attention(const skv_decode_geom *g, const void *q, cons
     a.cs_stride = g->cos_sin_stride;
     a.cs_rows = g->cos_sin_rows;
     a.scale = g->scale;
+    a.span = launch_spans().attend;
 
     const int smem = (int)sa_smem_bytes(g->rank);
     SKV_CHECK_SUPPORTED((size_t)nblk * G * 12 <= (size_t)smem, "seq_len %d too long for the merge of the partials", seq_len);

@@ -64,6 +64,15 @@ def _req_out(t: torch.Tensor):
     return t.data_ptr()
 
 
+def _req_in(t: torch.Tensor, name: str, dtype):
+    """An input of ``step``: a CUDA tensor, or a page-locked CPU tensor (read over the host link)."""
+    if t.is_cuda:
+        return _req(t, name, dtype)
+    if not t.is_pinned() or t.dtype != dtype or not t.is_contiguous():
+        raise RuntimeError(f"{name} must be a contiguous {dtype} CUDA tensor or a page-locked CPU tensor")
+    return t.data_ptr()
+
+
 def _req(t: torch.Tensor, name: str, dtype, shape=None):
     if not t.is_cuda or t.dtype != dtype or not t.is_contiguous():
         raise RuntimeError(f"{name} must be a contiguous CUDA {dtype} tensor "
@@ -116,14 +125,15 @@ def step(geom: Geometry, ws: StepWorkspace, q: torch.Tensor, k_new: torch.Tensor
          stream=None, row_dev: torch.Tensor | None = None) -> torch.Tensor:
     """One whole decode step of a layer (``append_select`` + ``sparse_attention`` over buffer rows
     [0, seq_len)), pipelined over ``ws.head_groups`` groups of kv heads; ``ws.miss_count`` receives
-    the misses per (b, kv head).  ``row_dev`` (one int32 on the device): the append row read at run
-    time, the attention then covering [0, row_dev + 1); ``row`` / ``seq_len`` are then its bounds."""
+    the misses per (b, kv head).  ``q``, ``k_new``, ``v_new`` and ``positions`` may be page-locked CPU
+    tensors: the step then reads them over the host link itself (no separate host-to-device copy).
+    ``row_dev`` (one int32 on the device): the append row read at run time, the attention then covering [0, row_dev + 1); ``row`` / ``seq_len`` are then its bounds."""
     if v_host.is_cuda or not v_host.is_pinned() or v_host.dtype != torch.bfloat16 or not v_host.is_contiguous():
         raise RuntimeError("v_host must be a contiguous pinned CPU bf16 tensor")
     g = geom.c()
     check(lib.skv_decode_step(
-        ctypes.byref(g), _req(q, "q", torch.bfloat16), _req(k_new, "k_new", torch.bfloat16),
-        _req(v_new, "v_new", torch.bfloat16), _req(positions, "positions", torch.int64),
+        ctypes.byref(g), _req_in(q, "q", torch.bfloat16), _req_in(k_new, "k_new", torch.bfloat16),
+        _req_in(v_new, "v_new", torch.bfloat16), _req_in(positions, "positions", torch.int64),
         _req(cos_sin, "cos_sin", torch.bfloat16), _req(q_out, "q_out", torch.bfloat16),
         _req(k_buf, "k_buf", torch.bfloat16), _req(v_buf, "v_buf", torch.bfloat16), int(row),
         _req(row_dev, "row_dev", torch.int32, (1,)) if row_dev is not None else None,
@@ -138,8 +148,28 @@ def early_fetch(enable: bool) -> bool:
     """Turn ``step``'s early value fetch on or off for the process (off by default): the selection
     kernel requests the certain misses' values before the selection is complete, writes keys and
     values into their slots and computes the attention itself.  Returns the previous setting.
-    Both give the same bits."""
+    Both leave the same state; the outputs differ only in fp32 summation order."""
     return bool(lib.skv_decode_step_early_fetch(1 if enable else 0))
+
+
+def step_timing(enable: bool) -> bool:
+    """Turn ``step``'s kernel timing on or off for the process (off by default): the kernels of a
+    step enqueued with it on -- eagerly, or under stream capture, then on every replay -- stamp
+    the GPU's global timer at each CTA's start and end (launches and results unchanged).
+    Returns the previous setting."""
+    return bool(lib.skv_decode_step_timing(1 if enable else 0))
+
+
+def step_kernel_times(max_groups: int = 8) -> list[tuple]:
+    """Per kv-head group of the last timed step (or replay of a graph captured from one):
+    ``(scoring start, scoring end, selection start, selection end, attention start, attention
+    end)`` in microseconds after the step's earliest kernel start; ``None`` for a kernel that did
+    not run.  Waits for the device and clears the spans."""
+    us = (ctypes.c_double * (6 * max_groups))()
+    n = ctypes.c_int(0)
+    check(lib.skv_decode_step_kernel_times(us, max_groups, ctypes.byref(n)), "skv_decode_step_kernel_times")
+    return [tuple(None if us[6 * i + k] < 0 else us[6 * i + k] for k in range(6))
+            for i in range(min(n.value, max_groups))]
 
 
 def append(geom: Geometry, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, positions: torch.Tensor,

@@ -134,7 +134,8 @@ def test_every_entry_point_rejects_null_arguments_before_launching():
     special = {"skv_last_error", "skv_version",
                "skv_device_errors",          # null outputs are allowed (the counts are only reset)
                "skv_peer_free",              # freeing null is a no-op, as free()
-               "skv_decode_step_early_fetch"}  # a process setting: returns the previous value
+               "skv_decode_step_early_fetch",  # process settings: return the previous value
+               "skv_decode_step_timing"}
     checked = 0
     for name, args in _lib.SIGNATURES.items():
         if name in special or name in _lib._RET or not args:
