@@ -121,60 +121,81 @@ __device__ __forceinline__ void ab_partial(const float o[2][4], float *po, float
 
 // Merge of a head's nblk partials (po_head [nblk][G][128], ml [nblk][G]) by
 // `nthreads` threads: each of the first G * 32 threads sums 4 columns of one
-// query row over the partials.  Its first row's partials (up to AB_MERGE_REGS
-// of them) and all (m, l) pairs are loaded in one round; warp w turns the
-// pairs of heads w, w + nwarps, ... into weights w_j = exp(m_j - M) / L
-// meanwhile.  scratch: 2 nblk G floats of shared memory.  emit(gg, d, pk)
-// stores the 4 bf16 outputs (packed) of row gg, columns d .. d+3.
-constexpr int AB_MERGE_REGS = 16;
+// query row over the partials, in partial order.  The (m, l) pairs are loaded
+// and warp w turns those of heads w, w + nwarps, ... into weights
+// w_j = exp(m_j - M) / L.  scratch: 2 nblk G floats of shared memory.
+// stage (optional, 16-byte aligned shared memory of nblk G 512 bytes, free of
+// other readers and writers): the partials are brought in by bulk copies on
+// `bar` (an mbarrier of count 1 whose phase of parity `parity` is the next to
+// complete), issued before the weights are computed, so that the sums wait
+// for one transfer instead of a chain of loads.  The merge runs once per head
+// and step, always from a cold instruction cache: its loops are kept rolled
+// (fewer instructions to fetch).  emit(gg, d, pk) stores the 4 bf16 outputs
+// (packed) of row gg, columns d .. d+3.
+constexpr unsigned AB_STAGE_CHUNK = 32768;  // bytes per staging bulk copy
 template <typename Emit>
 __device__ __forceinline__ void ab_merge(const float *po_head, const float2 *ml, int nblk, int G, void *scratch,
-                                         int tid, int nthreads, Emit emit)
+                                         float *stage, uint64_t *bar, unsigned parity, int tid, int nthreads,
+                                         Emit emit)
 {
     const int lane = tid & 31, warp = tid >> 5, nwarps = nthreads / 32;
     const int nml = nblk * G;
     float2 *s_ml = reinterpret_cast<float2 *>(scratch);  // [nblk][G]
     float *s_w = reinterpret_cast<float *>(s_ml + nml);  // [nblk][G]
-    float4 pre[AB_MERGE_REGS];
-    if (tid < G * 32) {
-        const float *po = po_head + (tid >> 5) * 128 + (tid & 31) * 4;
-#pragma unroll
-        for (int j = 0; j < AB_MERGE_REGS; ++j)
-            if (j < nblk) pre[j] = __ldcg(reinterpret_cast<const float4 *>(po + (int64_t)j * G * 128));
+    if (stage && tid == 0) {
+        const unsigned bytes = (unsigned)nml * 512u;
+        fence_proxy_async_all();  // the generic accesses to this shared memory and the acquired partials come first
+        mbar_arrive_expect_tx(bar, bytes);
+#pragma unroll 1
+        for (unsigned o = 0; o < bytes; o += AB_STAGE_CHUNK)
+            bulk_g2s(reinterpret_cast<unsigned char *>(stage) + o, reinterpret_cast<const unsigned char *>(po_head) + o,
+                     min(AB_STAGE_CHUNK, bytes - o), bar);
     }
+#pragma unroll 1
     for (int t = tid; t < nml; t += nthreads) s_ml[t] = __ldcg(&ml[t]);
     __syncthreads();
+#pragma unroll 1
     for (int gg = warp; gg < G; gg += nwarps) {
         float M = -INFINITY, L = 0.f;
+#pragma unroll 1
         for (int j = lane; j < nblk; j += 32) M = fmaxf(M, s_ml[j * G + gg].x);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        M = warp_max(M);
+#pragma unroll 1
         for (int j = lane; j < nblk; j += 32) L += s_ml[j * G + gg].y * __expf(s_ml[j * G + gg].x - M);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        L = warp_sum(L);
         const float inv = 1.f / L;
+#pragma unroll 1
         for (int j = lane; j < nblk; j += 32) s_w[j * G + gg] = __expf(s_ml[j * G + gg].x - M) * inv;
     }
+    if (stage && !mbar_wait(bar, parity)) {
+        // a transfer that did not land in time is reported; the bytes in flight
+        // must still land before the shared memory is read or reused
+        if (tid == 0) report_dev_error(DEV_ERR_WAIT);
+        mbar_wait(bar, parity);
+    }
     __syncthreads();
+#pragma unroll 1
     for (int p = tid; p < G * 32; p += nthreads) {
         const int gg = p >> 5, d = (p & 31) * 4;
-        const float *po = po_head + gg * 128 + d;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        int j0 = 0;
-        if (p == tid) {  // the first row: partials already in registers
-#pragma unroll
-            for (int j = 0; j < AB_MERGE_REGS; ++j)
-                if (j < nblk) {
-                    const float w = s_w[j * G + gg];
-                    acc.x += pre[j].x * w, acc.y += pre[j].y * w, acc.z += pre[j].z * w, acc.w += pre[j].w * w;
-                }
-            j0 = min(nblk, AB_MERGE_REGS);
-        }
-#pragma unroll 8
-        for (int j = j0; j < nblk; ++j) {
-            const float4 v = __ldcg(reinterpret_cast<const float4 *>(po + (int64_t)j * G * 128));
-            const float w = s_w[j * G + gg];
-            acc.x += v.x * w, acc.y += v.y * w, acc.z += v.z * w, acc.w += v.w * w;
+        if (stage) {
+            const float *po = stage + gg * 128 + d;
+#pragma unroll 1
+            for (int j = 0; j < nblk; ++j) {
+                const float4 v = *reinterpret_cast<const float4 *>(po + j * G * 128);
+                const float w = s_w[j * G + gg];
+                acc.x = fmaf(v.x, w, acc.x), acc.y = fmaf(v.y, w, acc.y);
+                acc.z = fmaf(v.z, w, acc.z), acc.w = fmaf(v.w, w, acc.w);
+            }
+        } else {
+            const float *po = po_head + gg * 128 + d;
+#pragma unroll 1
+            for (int j = 0; j < nblk; ++j) {
+                const float4 v = __ldcg(reinterpret_cast<const float4 *>(po + (int64_t)j * G * 128));
+                const float w = s_w[j * G + gg];
+                acc.x = fmaf(v.x, w, acc.x), acc.y = fmaf(v.y, w, acc.y);
+                acc.z = fmaf(v.z, w, acc.z), acc.w = fmaf(v.w, w, acc.w);
+            }
         }
         __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
         uint2 pk;

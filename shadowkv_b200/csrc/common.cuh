@@ -322,6 +322,9 @@ __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepc
 // Orders this thread's earlier generic accesses to shared memory before the
 // bulk (async-proxy) copies it issues next into the same bytes.
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// The same for every state space: also orders global data this thread has
+// acquired from other CTAs before the bulk copies it issues next from it.
+__device__ __forceinline__ void fence_proxy_async_all() { asm volatile("fence.proxy.async;" ::: "memory"); }
 
 // Bounded wait for the phase with the given parity; false if it did not complete.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity, unsigned max_iter = 1u << 22)

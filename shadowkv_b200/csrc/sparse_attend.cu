@@ -69,6 +69,7 @@ struct SparseAttendArgs {
     // then covers [0, *row_dev + 1) (at most seq_len rows, which sized the grid)
     const int32_t *row_dev;
     unsigned long long *span;  // optional: kernel span pair of a timed step (span_begin)
+    int smem_bytes;            // dynamic shared memory of a CTA (the merge stages partials in it)
 };
 
 // NT: n-tiles of query heads in S = K q^T (1: G <= 8, 2: G <= 16)
@@ -91,9 +92,11 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
     __shared__ float s_m[16], s_l[16];
     __shared__ unsigned s_last;
     __shared__ __align__(8) uint64_t s_bar;  // completion of the bulk copies of the device-memory rows
+    __shared__ __align__(8) uint64_t s_mbar;  // completion of the staging copies of a merge
 
     if (threadIdx.x == 0) {
         mbar_init(&s_bar, 1);
+        mbar_init(&s_mbar, 1);
         mbar_fence_init();
     }
     SKV_TRACE_CTA(TR_SA_START);
@@ -107,8 +110,12 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
     // link.  One item per CTA for a full grid; a grid of fewer CTAs (leaving
     // SMs to other work while the link is busy) walks the items in strides.
     unsigned iter = 0;
+    unsigned nmerge = 0;  // staged merges done by this CTA: the phase of s_mbar
     for (int item = blockIdx.x; item < a.total; item += gridDim.x) {
-    __syncthreads();  // the previous item's shared memory is no longer read
+    // the previous item's (generic) shared-memory accesses are ordered before
+    // this item's bulk copies into the same bytes, and are complete
+    fence_proxy_async_smem();
+    __syncthreads();
     int blk, bh;
     {
         const int blo = a.sparse_start / SA_ROWS;
@@ -375,8 +382,12 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
     if (s_last) {
     __threadfence();
     // merge of the head's nblk partial outputs (the tiles' shared memory is free)
-    ab_merge(a.part_o + (int64_t)bh * a.nblk * G * 128, a.part_ml + (int64_t)bh * a.nblk * G, nblk, G, smem_raw, tid,
-             SA_THREADS, [&](int gg, int d, uint2 pk) {
+    // the partials come into the (free) tile memory after the merge scratch when they fit
+    const size_t scratch = ((size_t)nblk * G * 12 + 15) & ~(size_t)15;
+    float *stage = scratch + (size_t)nblk * G * 512 <= (size_t)a.smem_bytes
+                       ? reinterpret_cast<float *>(smem_raw + scratch) : nullptr;
+    ab_merge(a.part_o + (int64_t)bh * a.nblk * G * 128, a.part_ml + (int64_t)bh * a.nblk * G, nblk, G, smem_raw,
+             stage, &s_mbar, nmerge & 1u, tid, SA_THREADS, [&](int gg, int d, uint2 pk) {
                  if (a.world == 0) {
                      *reinterpret_cast<uint2 *>(a.out + ((int64_t)bh * G + gg) * 128 + d) = pk;
                  } else {
@@ -386,6 +397,7 @@ __global__ void __launch_bounds__(SA_THREADS, 1) sparse_attend_kernel(SparseAtte
                      for (int r = 0; r < a.world; ++r) *reinterpret_cast<uint2 *>(a.landing[r] + o) = pk;
                  }
              });
+    if (stage) ++nmerge;
     if (a.world > 0) {
         // the rows are in every rank's memory before any counter moves
         __threadfence_system();
@@ -584,6 +596,7 @@ static int launch_sparse_attention(const skv_decode_geom *g, const void *q, cons
     a.span = launch_spans().attend;
 
     const int smem = (int)sa_smem_bytes(g->rank);
+    a.smem_bytes = smem;
     SKV_CHECK_SUPPORTED((size_t)nblk * G * 12 <= (size_t)smem, "seq_len %d too long for the merge of the partials", seq_len);
     const void *fn = G <= 8 ? (const void *)sparse_attend_kernel<1> : (const void *)sparse_attend_kernel<2>;
     st = ensure_smem_attr(fn, smem, "sparse_attend_kernel");
