@@ -121,7 +121,7 @@ def test_peer_output_description_is_built_on_the_host():
 
 def test_auto_head_groups_keeps_two_heads_per_group():
     from shadowkv_b200.kvcache import auto_head_groups
-    assert [auto_head_groups(1, h) for h in (1, 2, 3, 4, 6, 8, 16)] == [1, 1, 1, 2, 1, 4, 4]
+    assert [auto_head_groups(1, h) for h in (1, 2, 3, 4, 6, 8, 16)] == [1, 1, 1, 2, 2, 4, 4]
     assert auto_head_groups(2, 8) == 1  # a batch is sliced by sequence instead
 
 
