@@ -799,6 +799,33 @@ def export_state(layer):
     return st
 
 
+def other_partitions(args, world, rank, local):
+    """At N > 1, beside the batch-sharded line: the same step sharded by kv head (B=1, each rank
+    Hkv/N heads, attention rows exchanged over NVLink peer memory), and BASELINE config 4's shape
+    (B=32 per box, sharded by kv head).  Each is measured like the main line (warm-up, L2 flush,
+    device events, max over ranks) and summarised here."""
+    import copy
+    import gc
+    out = {}
+    for name, over in (("shard_heads", dict(shard="heads", batch=0)),
+                       ("config4_shape", dict(shard="heads", batch=32))):
+        a = copy.copy(args)
+        for k, v in over.items():
+            setattr(a, k, v)
+        a.no_cpu_baseline = True
+        a.microbatch = None
+        gc.collect()
+        torch.cuda.empty_cache()
+        r = run_b200(a, world, rank, local)
+        out[name] = {k: r[k] for k in ("value", "unit", "ms_per_step", "scaling", "e2e", "per_rank", "kernel_us",
+                                       "gpu_launches")}
+        out[name]["config"] = {k: r["config"][k] for k in ("workload", "global_batch", "parallelism")}
+        out[name]["link_gbs"] = r["roofline"]["achieved"]
+        out[name]["step_roofline_frac"] = r["step_roofline"]["frac"]
+        out[name]["clocks"] = r["clocks"]
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -833,6 +860,8 @@ def main():
                          "and computes the attention)")
     ap.add_argument("--two-calls", action="store_true",
                     help="run the step as append_select + sparse_attention (all heads in one chain)")
+    ap.add_argument("--no-extra-shards", action="store_true",
+                    help="at N > 1, skip the kv-head-sharded and config-4-shape measurements beside the main line")
     ap.add_argument("--split", action="store_true",
                     help="fetch / reconstruction / attention as three launches instead of the fused kernel")
     args = ap.parse_args()
@@ -854,6 +883,8 @@ def main():
         return
     world, rank, local = dist_setup()
     res = run_b200(args, world, rank, local)
+    if world > 1 and args.shard == "batch" and not args.no_extra_shards:
+        res["other_partitions"] = other_partitions(args, world, rank, local)
     if rank == 0 and res is not None:
         print(json.dumps(res), flush=True)
     if world > 1:
