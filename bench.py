@@ -260,7 +260,9 @@ def run_b200(args, world, rank, local):
         cfg = dataclasses.replace(cfg, kv_heads=kn, q_heads=qn)
     peer_out = None
     torch.manual_seed(0)
-    layer = workload.Layer(cfg, device=f"cuda:{local}", seed=1000 + rank)
+    # kv heads sharded: every rank factorises the keys of all heads (one key seed), as one model
+    layer = workload.Layer(cfg, device=f"cuda:{local}", seed=1000 + rank,
+                           kv_heads_of=(k0, kn, full_cfg.kv_heads) if heads_sharded else None, key_seed=1000)
     cache, attn = layer.cache, layer.attn
     B, Hq, Hkv = cfg.batch, cfg.q_heads, cfg.kv_heads
     n = args.steps + args.warmup

@@ -129,12 +129,22 @@ class ShadowKVCache_CPU:
         return self.kv_offset
 
     # --------------------------------------------------------------- prefill
-    def get_svd(self, new_k_cache: torch.Tensor, layer_idx: int):
-        """Rank-r factors of the pre-RoPE keys (shadow.py:411-444): U [B,T,r], SV^T [B,H,D,r]."""
+    def get_svd(self, new_k_cache: torch.Tensor, layer_idx: int, heads: tuple[int, int] | None = None):
+        """Rank-r factors of the pre-RoPE keys (shadow.py:411-444): U [B,T,r], SV^T [B,H,D,r].
+
+        ``heads=(h0, hn)``: ``new_k_cache`` holds the keys of every kv head of the model and this
+        cache keeps kv heads h0 .. h0+hn-1 (the heads of one rank when the heads are sharded over
+        GPUs): the factorisation runs over all heads, as the reference's (U shared by every head),
+        and this cache keeps U and its heads' rows of SV."""
         if new_k_cache.dim() == 4 and new_k_cache.shape[1] <= 32:
-            k = new_k_cache.transpose(1, 2).reshape(new_k_cache.shape[0], -1, self.num_key_value_heads * self.head_dim)
+            k = new_k_cache.transpose(1, 2).reshape(new_k_cache.shape[0], -1, new_k_cache.shape[1] * self.head_dim)
         else:
             k = new_k_cache
+        h_all = k.shape[-1] // self.head_dim
+        h0, hn = heads if heads is not None else (0, h_all)
+        if hn != self.num_key_value_heads or h0 < 0 or h0 + hn > h_all:
+            raise RuntimeError(f"keys of {h_all} kv heads, heads {h0}..{h0 + hn - 1} for a cache of "
+                               f"{self.num_key_value_heads}")
         bsz, T, _ = k.shape
         if layer_idx == 0 and self.prefilled_batch == 0:
             self.U = torch.zeros(self.num_layers, self.batch_size, T, self.rank, dtype=self.dtype, device=self.device)
@@ -159,7 +169,7 @@ class ShadowKVCache_CPU:
         pb = self.prefilled_batch
         self.U[layer_idx][pb:pb + bsz].copy_(u.to(self.dtype))
         sv = torch.matmul(torch.diag_embed(s), vt).to(self.dtype)  # [b, r, H*D]
-        sv = sv.view(bsz, self.rank, self.num_key_value_heads, self.head_dim).permute(0, 2, 3, 1)  # [b, H, D, r]
+        sv = sv.view(bsz, self.rank, h_all, self.head_dim)[:, :, h0:h0 + hn].permute(0, 2, 3, 1)  # [b, H, D, r]
         self.SV[layer_idx][pb:pb + bsz].copy_(sv)
 
     def register_k_landmark(self, k_landmark, k_landmark_idx, layer_idx):

@@ -90,8 +90,17 @@ def rope_glm_torch(x: torch.Tensor, cos_sin: torch.Tensor, positions: torch.Tens
 class Layer:
     """One prefilled decode layer plus a seeded stream of decode inputs."""
 
-    def __init__(self, cfg: WorkloadConfig, device="cuda", seed: int = 0):
+    def __init__(self, cfg: WorkloadConfig, device="cuda", seed: int = 0, kv_heads_of=None, key_seed=None):
+        """``kv_heads_of=(k0, kn, Hkv_total)``: this layer holds kv heads k0 .. k0+kn-1 of a model of
+        Hkv_total (``cfg`` has kn kv heads and their q heads): every rank generates the keys of all
+        heads from ``key_seed`` (the same on every rank) and factorises them together, as the
+        reference does, then keeps its heads; values and queries come from ``seed``."""
         self.cfg = cfg
+        self.kv_heads_of = kv_heads_of
+        self.key_gen = None
+        if kv_heads_of is not None:
+            self.key_gen = torch.Generator(device=torch.device(device)).manual_seed(
+                key_seed if key_seed is not None else seed)
         self.device = torch.device(device)
         D = 128
         g = torch.Generator(device=self.device).manual_seed(seed)
@@ -115,27 +124,32 @@ class Layer:
     def _prefill_layer(self, layer, g):
         cfg, D, dev = self.cfg, 128, self.device
         B, T, Hq, Hk = cfg.batch, cfg.ctx, cfg.q_heads, cfg.kv_heads
+        k0, Hk_all = (self.kv_heads_of[0], self.kv_heads_of[2]) if self.kv_heads_of else (0, Hk)
+        gk = self.key_gen if self.key_gen is not None else g
         for b in range(B):
-            U0 = torch.randn(T, cfg.r_true, generator=g, device=dev)
-            W0 = torch.randn(cfg.r_true, Hk * D, generator=g, device=dev) / math.sqrt(math.sqrt(cfg.r_true))
-            k_pre = (U0 @ W0).add_(torch.randn(T, Hk * D, generator=g, device=dev), alpha=0.05)
-            k_pre = k_pre.to(torch.bfloat16).view(1, T, Hk, D).transpose(1, 2).contiguous()  # [1, Hk, T, D]
+            U0 = torch.randn(T, cfg.r_true, generator=gk, device=dev)
+            W0 = torch.randn(cfg.r_true, Hk_all * D, generator=gk, device=dev) / math.sqrt(math.sqrt(cfg.r_true))
+            k_all = (U0 @ W0).add_(torch.randn(T, Hk_all * D, generator=gk, device=dev), alpha=0.05)
+            k_all = k_all.to(torch.bfloat16).view(1, T, Hk_all, D).transpose(1, 2).contiguous()  # [1, Hk_all, T, D]
             del U0
+            k_pre = k_all[:, k0:k0 + Hk].contiguous()
             v = torch.randn(1, Hk, T, D, generator=g, device=dev).to(torch.bfloat16)
             q_last = torch.randn(1, Hq, 1, D, generator=g, device=dev).to(torch.bfloat16)
             pos = torch.arange(T, device=dev)
+            # every kv head's keys are factorised together (U shared by all heads)
+            svd_keys, svd_heads = (k_all, (k0, Hk)) if self.kv_heads_of else (k_pre, None)
             if cfg.rope == "llama":
-                self.cache.get_svd(k_pre, layer)
+                self.cache.get_svd(svd_keys, layer, heads=svd_heads)
                 cs = self.cos_sin[:T].float()
                 cos = torch.cat((cs[:, :64], cs[:, :64]), -1)
                 sin = torch.cat((cs[:, 64:], cs[:, 64:]), -1)
                 kf = k_pre.float()
                 k_roped = (kf * cos + torch.cat((-kf[..., 64:], kf[..., :64]), -1) * sin).to(torch.bfloat16)
             else:
-                self.cache.get_svd(k_pre, layer)
+                self.cache.get_svd(svd_keys, layer, heads=svd_heads)
                 k_roped = rope_glm_torch(k_pre.float(), self.cos_sin.float(), pos).to(torch.bfloat16)
             self.cache.prefill_kv_cache(v, layer, k_roped, q_last)
-            del k_pre, k_roped, v
+            del k_pre, k_all, svd_keys, k_roped, v
         torch.cuda.synchronize(self.device)
 
     def next_inputs(self):

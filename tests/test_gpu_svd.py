@@ -69,3 +69,27 @@ def test_gram_factors_reconstruct_keys_like_the_svd():
         del c
         torch.cuda.empty_cache()
     assert errs["gram"] <= errs["exact"] * 1.01 + 1e-4, errs
+
+
+@pytest.mark.parametrize("h0,hn", [(0, 1), (3, 1), (4, 4)])
+def test_factors_of_a_head_range_are_the_full_factors_rows(h0, hn):
+    """kv heads sharded over GPUs: a cache of heads h0 .. h0+hn-1 factorises the keys of all
+    8 heads (as the reference does, U shared) and keeps U and its heads' rows of SV -- bit for bit
+    the full cache's U and SV[h0 : h0+hn].  Rank 160 exceeds one head's 128 columns."""
+    from shadowkv_b200.kvcache import ShadowKVCache_CPU
+    T, H, rank = 8192, 8, 160
+    k = _keys(T, H * 128, 96, seed=5).view(1, T, H, 128).transpose(1, 2).contiguous()  # [1, H, T, 128]
+
+    def cache(heads):
+        cfg = types.SimpleNamespace(num_attention_heads=4 * heads, num_key_value_heads=heads,
+                                    hidden_size=4 * heads * 128, num_hidden_layers=1)
+        return ShadowKVCache_CPU(cfg, batch_size=1, max_length=T, device=DEV, sparse_budget=512, rank=rank,
+                                 outlier_chunk=8, svd="gram")
+
+    full, part = cache(H), cache(hn)
+    full.get_svd(k, 0)
+    part.get_svd(k, 0, heads=(h0, hn))
+    assert torch.equal(part.U, full.U)
+    assert torch.equal(part.SV[0][0], full.SV[0][0][h0:h0 + hn])
+    with pytest.raises(RuntimeError):
+        cache(hn).get_svd(k, 0, heads=(H - hn + 1, hn))  # past the last head
