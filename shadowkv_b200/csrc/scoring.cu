@@ -136,6 +136,18 @@ __global__ void __launch_bounds__(ST_THREADS, 2) score_tma_kernel(ScoreArgs a)
     pdl_launch_dependents();  // the selection kernel may be scheduled early (it waits for this grid)
     span_begin(a.span);
     SKV_TRACE_CTA(TR_SCORE_START);
+    // trace builds: a record per CTA (thread 0, a consumer): 0 = bh | split << 16,
+    // 1 = 0x5C0, 2 = start, 3 = first tile in, 4 = ns spent waiting for tiles,
+    // 5 = loop end, 6 = tiles, 7 = end
+    SKV_TRACE_REC_DECL;
+    SKV_TRACE_REC_OPEN();
+    SKV_TRACE_REC(0, (unsigned long long)bh | ((unsigned long long)split << 16));
+    SKV_TRACE_REC(1, 0x5C0ull);
+    SKV_TRACE_REC_NOW(2);
+    SKV_TRACE_REC(6, (unsigned long long)nst);
+#ifdef SKV_TRACE
+    unsigned long long tr_wait = 0;
+#endif
     const bool producer = warp == ST_CONSUMERS && lane == 0;
     if (producer) {
         for (int s = 0; s < ST_STAGES; ++s) {
@@ -234,11 +246,18 @@ __global__ void __launch_bounds__(ST_THREADS, 2) score_tma_kernel(ScoreArgs a)
         float *lg = a.logits + (int64_t)bh * L * G;
         for (int i = 0; i < nst; ++i) {
             const int s = i % ST_STAGES;
+#ifdef SKV_TRACE
+            const unsigned long long tw0 = ::skv::trace_now();
+#endif
             if (!mbar_wait(&full[s], (i / ST_STAGES) & 1)) {
                 report_dev_error(DEV_ERR_WAIT);
                 atomicExch(&s_abort, 1);
                 break;
             }
+#ifdef SKV_TRACE
+            tr_wait += ::skv::trace_now() - tw0;
+            if (i == 0) SKV_TRACE_REC_NOW(3);
+#endif
             if (i == 0) SKV_TRACE_CTA(TR_SCORE_TILE0);
             const __nv_bfloat16 *tile = sT + (size_t)s * ST_ROWS * 128;
             const int lr = warp * 16 + g;  // local rows lr and lr+8
@@ -278,6 +297,8 @@ __global__ void __launch_bounds__(ST_THREADS, 2) score_tma_kernel(ScoreArgs a)
                 }
             }
         }
+        SKV_TRACE_REC(4, tr_wait);
+        SKV_TRACE_REC_NOW(5);
         // reduce over the 8 lanes sharing j
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
@@ -306,6 +327,7 @@ __global__ void __launch_bounds__(ST_THREADS, 2) score_tma_kernel(ScoreArgs a)
         a.part[((int64_t)bh * G + tid) * nsplit + split] = make_float2(mm, ss);  // [BH][G][nsplit]
     }
     SKV_TRACE_CTA(TR_SCORE_END);
+    SKV_TRACE_REC_NOW(7);
     span_finish(a.span);
 }
 
@@ -445,8 +467,11 @@ static SelectPlan plan_select(const skv_decode_geom *g)
     // launch): its CTAs become resident there while the scan runs and do the
     // work that does not need the scores (landmark ids, bitmaps, slots) early.
     // Two selection CTAs fit an SM; the scan keeps at least 3/4 of the SMs.
-    const int sel_ctas = BH * (g->num_landmarks > 8 * 4096 ? 16 : 8);
-    const int reserve = min(ceil_div(sel_ctas, 2), sms_all / 4);
+    // With the keys pass between them (very long contexts, below) the selection
+    // cannot start during the scan, and the scan takes every SM.
+    const bool keys_between = g->num_landmarks > 8 * 4096;
+    const int sel_ctas = BH * (keys_between ? 16 : 8);
+    const int reserve = keys_between ? 0 : min(ceil_div(sel_ctas, 2), sms_all / 4);
     const int sms = sms_all - reserve;
     // Scoring grid: two CTAs per SM on the SMs not reserved, the rows of a head
     // split evenly over nsplit of them (every SM reads about the same bytes).

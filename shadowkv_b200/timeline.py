@@ -20,7 +20,10 @@ Record layout of the attention kernel (``sparse_attend_kernel``): word 0 = SM
 id | kv head << 8 | block << 20, word 1 = the group's K buffer address, words
 2..7 = global-timer stamps (item start, loads issued, keys done, values in,
 ticket, merge end or 0).  Selection records carry 0x5E1 / 0x5E2 in word 1,
-early-fetch tail records 0xF0F0 in word 7; they are not attention items.
+early-fetch tail records 0xF0F0 in word 7; they are not attention items.  Scan
+records (``score_tma_kernel``, one per CTA) carry 0x5C0 in word 1: word 0 =
+kv head | split << 16, words 2.. = start, first tile in, ns waiting for tiles,
+tile loop done, tiles, end.
 """
 from __future__ import annotations
 
@@ -34,7 +37,8 @@ EVENTS = ["score_start", "score_tile0", "score_end", "sel_start", "sel_waited", 
           "mark_after", "sel_C", "sel_tile", "sel_hist", "sel_sync1", "sel_scan", "sel_marked", "sel_ranked",
           "sel_diff", "sa_lists", "fx_tail", "fx_keys", "fx_values", "fx_end"]
 MARK_BEFORE, MARK_AFTER = 15, 16
-NOT_ATTENTION_W1 = (0x5E1, 0x5E2, 0xF1F1)
+SCAN_W1 = 0x5C0
+NOT_ATTENTION_W1 = (0x5E1, 0x5E2, 0xF1F1, SCAN_W1)
 FX_TAIL_W7 = 0xF0F0
 
 
@@ -46,6 +50,28 @@ def _pct(a, fs=(0, .25, .5, .75, .9, 1)):
 def attention_items(recs, t0):
     """Attention work-item records of one replay (stamps after t0)."""
     return [r for r in recs if r[1] not in NOT_ATTENTION_W1 and r[7] != FX_TAIL_W7 and r[2] > t0]
+
+
+def scan_items(recs, t0):
+    """Landmark-scan CTA records (``score_tma_kernel``) of one replay."""
+    return [r for r in recs if r[1] == SCAN_W1 and r[2] > t0]
+
+
+def summarise_scan(items, t0):
+    """Lines of the landmark-scan summary: per CTA start, first tile in, end, and the share of
+    its tile loop spent waiting for tiles."""
+    T = lambda x: (x - t0) / 1e3
+    first = [(r[3] - r[2]) / 1e3 for r in items if r[3]]
+    loop = [(r[5] - r[2]) / 1e3 for r in items if r[5]]
+    wait = [r[4] / 1e3 for r in items]
+    share = [r[4] / max(1, r[5] - r[2]) for r in items if r[5]]
+    return [f"  scan CTAs: {len(items)}, tiles per CTA {min(r[6] for r in items)}-{max(r[6] for r in items)}",
+            f"  scan CTA start (us) p0/p50/p100: {_pct([T(r[2]) for r in items], (0, .5, 1))}",
+            f"  scan CTA end   (us) p0/p50/p100: {_pct([T(r[7]) for r in items if r[7]], (0, .5, 1))}",
+            f"  start -> first tile in (us) p0/p50/p100: {_pct(first, (0, .5, 1))}",
+            f"  start -> tile loop done (us) p0/p50/p100: {_pct(loop, (0, .5, 1))}",
+            f"  waiting for tiles (us) p50/p100: {_pct(wait, (.5, 1))}, share of the loop p50: "
+            f"{sorted(share)[len(share) // 2]:.2f}"]
 
 
 def summarise(items, t0):
@@ -135,6 +161,9 @@ def run(config: str, groups: int, steps: int, early: bool) -> None:
     for nm in EVENTS:
         if nm in ev:
             print(f"  {nm:12s} first {ev[nm][0]:7.1f} last {ev[nm][1]:7.1f}")
+    scans = scan_items(recs, t0)
+    if scans:
+        print("\n".join(summarise_scan(scans, t0)))
     items = attention_items(recs, t0)
     if items:
         print("\n".join(summarise(items, t0)))
