@@ -153,6 +153,61 @@ def link_bandwidth_gbs(sizes=(64 << 20, 256 << 20), reps=8) -> float:
     return best
 
 
+def sm_read_link(cache, flush, misses_per_head=(2048, 256), reps=5) -> dict:
+    """Host-link rate of reads issued by the SMs, measured in-run with the library's own
+    zero-copy fetch kernel (``skv_decode_gather_values`` -> ``fetch_misses_kernel``, 16 chunks
+    of 2 KiB per CTA) from layer 0's page-locked value store: random distinct chunks of every
+    kv head of sequence 0 into a scratch buffer, the L2 flushed before each launch, CUDA events
+    on the launching stream.  For each entry of ``misses_per_head``: the median duration of a
+    launch and its rate; the first entry (32 MB at config 1) gives the sustained rate, the second
+    (the step's 4 MB of misses) the rate of one step-sized burst, ramp-up and drain included."""
+    import ctypes
+    from shadowkv_b200._lib import DecodeGeom, check, lib
+    host = cache.v_cache_cpu[0][:1]  # [1][H][host_chunks][1024], contiguous, page-locked
+    H, nch = host.shape[1], host.shape[2]
+    valid = min(nch, cache.k_landmark.shape[-2])  # chunks that hold prompt values
+    gen = torch.Generator().manual_seed(7)
+    out = {}
+    for M in misses_per_head:
+        M = min(M, valid)
+        geom = DecodeGeom(1, H, H, 128, 8, 8, M, 0, nch, nch * 8, 8 * M, 0, 0, 128, 0, 1.0)
+        v_buf = torch.empty(H, 8 * M, 128, dtype=torch.bfloat16, device="cuda")
+        slot = torch.arange(M, dtype=torch.int32).repeat(H, 1).cuda()
+        count = torch.full((H,), M, dtype=torch.int32, device="cuda")
+        times = []
+        for r in range(reps + 1):
+            chunk = torch.stack([torch.randperm(valid, generator=gen)[:M] for _ in range(H)]).to(torch.int32).cuda()
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            st = torch.cuda.current_stream()
+            a.record(st)
+            check(lib.skv_decode_gather_values(ctypes.byref(geom), host.data_ptr(), v_buf.data_ptr(),
+                                               slot.data_ptr(), chunk.data_ptr(), count.data_ptr(),
+                                               st.cuda_stream), "skv_decode_gather_values")
+            b.record(st)
+            b.synchronize()
+            if r:  # the first launch warms the kernel up
+                times.append(a.elapsed_time(b) * 1e3)
+        us = statistics.median(times)
+        nbytes = H * M * 2048
+        out[M] = {"bytes": nbytes, "us": us, "gbs": nbytes / (us * 1e-6) / 1e9}
+        del v_buf
+    return out
+
+
+def sm_link_fields(sm_link: dict, host_b: float, hbm_b: float, hbm_peak: float, ms_step: float) -> dict:
+    """``step_roofline`` context from ``sm_read_link``: the sustained rate of SM-issued host
+    reads, the roofline time at that rate, and the duration of one step-sized burst."""
+    big, burst = (sm_link[k] for k in sorted(sm_link, reverse=True)[:2])
+    t_sm = max(hbm_b / (hbm_peak * 1e9), host_b / (big["gbs"] * 1e9))
+    return {"link_sm_read_gbs": big["gbs"],
+            "link_sm_read_kind": (f"measured in-run: fetch_misses_kernel (zero-copy, 16 chunks of 2 KiB per "
+                                  f"CTA) over {big['bytes'] / 1e6:.1f} MB of random chunks of the value store, "
+                                  f"L2 flushed, median of 5 launches"),
+            "link_sm_read_burst": {"bytes": burst["bytes"], "us": burst["us"], "gbs": burst["gbs"]},
+            "t_roof_sm_read_us": t_sm * 1e6, "frac_sm_read": t_sm / (ms_step * 1e-3)}
+
+
 def algorithmic_bytes(cache, misses: int, seq_len: int):
     """HBM and host-link bytes of one layer of a step (per-unit figures of the roofline model)."""
     B, H, D = cache.batch_size, cache.num_key_value_heads, cache.head_dim
@@ -412,6 +467,9 @@ def run_b200(args, world, rank, local):
     # link peak is the best of the measurements before and after the timed steps
     link_samples = [link_peak, link_bandwidth_gbs()]
     link_peak = max(link_samples)
+    # the same link read by the SMs (the step's own fetch path), sustained and as one
+    # step-sized burst: what the attention phase can reach, against the copy-engine peak
+    sm_link = sm_read_link(cache, flush) if NL == 1 else None
 
     # ---- per-kernel times.  The one-call step: the same step captured once more with CUDA
     # events around each kv-head group's kernels (skv_decode_step_timing: event nodes on the
@@ -598,7 +656,8 @@ def run_b200(args, world, rank, local):
                      "per_launch": per_launch},
         "step_roofline": {"t_roof_us": t_roof * 1e6, "t_step_us": ms_step * 1e3,
                           "frac": t_roof / (ms_step * 1e-3), "hbm_bytes": hbm_b, "host_bytes": host_b,
-                          "hbm_peak_gbs": hbm_peak, "hbm_peak_kind": peak_kind, "link_peak_gbs": link_peak},
+                          "hbm_peak_gbs": hbm_peak, "hbm_peak_kind": peak_kind, "link_peak_gbs": link_peak,
+                          **(sm_link_fields(sm_link, host_b, hbm_b, hbm_peak, ms_step) if sm_link else {})},
         "e2e": {"value": tokens / (e2e_step / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
                 "inputs": ("read from page-locked host memory by the step (staging kernel in the timed region)"
