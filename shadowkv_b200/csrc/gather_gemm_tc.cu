@@ -9,11 +9,18 @@
 //
 // One CTA computes 16 chunks (M = 128 rows) x 128 output dims over the full
 // rank K:
-//   * 256 threads gather the U rows of the chunks and SV^T of the head into
-//     shared memory with 16-byte cp.async, in the no-swizzle K-major layout of
-//     the tensor-core descriptors: 8-row x 16-byte core matrices of 128
-//     contiguous bytes, 8-row groups 128 bytes apart, 16-byte k-chunks
-//     (M/8)*128 bytes apart;
+//   * the operands come in through tensor-map (TMA) copies that write the
+//     no-swizzle K-major core-matrix layout of the tensor-core descriptors
+//     directly (8-row x 16-byte core matrices of 128 contiguous bytes): the
+//     tensor maps view a row of U or SV^T as rank/8 pieces of 16 bytes, with
+//     the piece index as the outermost box dimension, so one copy of box
+//     {8 elements, rows, rank/8} lands piece-major.  SV^T of the head is one
+//     copy (rows 16 bytes apart, pieces 2 KiB apart), requested before the
+//     chunk ids are known; the U rows of each chunk are one copy of 8 rows
+//     (pieces 128 bytes apart, chunks rank*16 bytes apart).  16-byte cp.async
+//     loads through the SM's load/store path held a CTA's 112 KB of operands
+//     to about 25 GB/s per SM; the copies do not take that path.  The cos/sin
+//     rows of the epilogue still come in by cp.async (padded rows);
 //   * one thread issues K/16 tcgen05.mma (kind::f16, bf16 x bf16 -> fp32,
 //     M=128, N=128) into 128 columns of tensor memory and commits them to an
 //     mbarrier (bounded wait);
@@ -22,6 +29,8 @@
 //     the GLM pairs (2i, 2i+1) of a row are in one thread; RoPE on the fp32
 //     values (cos/sin rows staged in shared memory), one rounding, rows
 //     staged in shared memory and written as coalesced 256-byte rows.
+#include <cuda.h>
+
 #include "gather_gemm.cuh"
 
 namespace skv {
@@ -32,9 +41,10 @@ constexpr int TC_N = 128;                   // N = head_dim
 constexpr int TC_THREADS = 256;             // warps w and w+4 read tensor-memory lanes 32w .. 32w+31
 constexpr int TC_PITCH = 136;               // row pitch (bf16) of the cos/sin and output staging tiles
 constexpr uint32_t TC_TMEM_COLS = 128;      // fp32 accumulator: one column per output dim
-// byte distance between the 16-byte k-chunks of one operand (M/8 core matrices)
-constexpr uint32_t TC_LBO = (TC_ROWS / 8) * 128;
-constexpr uint32_t TC_SBO = 128;            // between 8-row groups
+// SV^T operand: byte distance between its 16-byte k-pieces (N/8 core matrices)
+// and between its 8-row groups
+constexpr uint32_t TC_LBO = (TC_N / 8) * 128;
+constexpr uint32_t TC_SBO = 128;
 
 // Instruction descriptor, kind::f16: D fp32 (bits 4-5 = 1), A bf16 (bits 7-9 = 1),
 // B bf16 (bits 10-12 = 1), A and B K-major (bits 15, 16 = 0), N/8 at bits 17-22,
@@ -50,10 +60,19 @@ __device__ __forceinline__ uint64_t tc_sdesc(uint32_t saddr, uint32_t lbo, uint3
            ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
 }
 
-// Element offset of (row r, k) in the K-major core-matrix layout of an operand with TC_ROWS rows.
-__device__ __forceinline__ int tc_off(int r, int k)
+// Tensor-map copy of one box into shared memory, completion (transaction
+// bytes) on the mbarrier; the innermost coordinate is always 0 (aligned).
+__device__ __forceinline__ void tc_tma3(void *smem, const CUtensorMap *map, int y, int z, uint64_t *bar)
 {
-    return ((k >> 3) * (TC_ROWS / 8) + (r >> 3)) * 64 + (r & 7) * 8 + (k & 7);
+    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%2, %3, %4}], [%5];"
+                 ::"r"(smem_u32(smem)), "l"(map), "r"(0), "r"(y), "r"(z), "r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void tc_tma4(void *smem, const CUtensorMap *map, int w, uint64_t *bar)
+{
+    asm volatile("cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%2, %3, %4, %5}], [%6];"
+                 ::"r"(smem_u32(smem)), "l"(map), "r"(0), "r"(0), "r"(0), "r"(w), "r"(smem_u32(bar)) : "memory");
 }
 
 __device__ __forceinline__ void tc_cp16(void *smem, const void *gmem)
@@ -75,22 +94,27 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, float *v)
 }
 
 // ROPE: 0 none, 1 rotate-half (cos_sin width 128), 2 GLM interleaved (width 64)
+// tmU: U as [rows = B*ctx][rank/8 pieces][8], box {8, 8, rank/8} (one chunk);
+// tmB: SV^T as [B*H][128][rank/8 pieces][8], box {8, 128, rank/8, 1} (one head).
 template <int ROPE>
-__global__ void __launch_bounds__(TC_THREADS) gather_gemm_tc_kernel(GatherGemmArgs a)
+__global__ void __launch_bounds__(TC_THREADS) gather_gemm_tc_kernel(GatherGemmArgs a, const __grid_constant__ CUtensorMap tmU,
+                                                                    const __grid_constant__ CUtensorMap tmB)
 {
     extern __shared__ __align__(128) unsigned char smem_raw[];
-    // operand tiles start on a 1024-byte boundary: the descriptors address a
-    // matrix from an aligned base (an unaligned start shifted the rows read)
+    // operand tiles start on a 1024-byte boundary (the tensor copies need 128;
+    // the MMA descriptors of U step through it in 256-byte pieces of K)
     unsigned char *smem = reinterpret_cast<unsigned char *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    __nv_bfloat16 *sA = reinterpret_cast<__nv_bfloat16 *>(smem);       // U rows  [K/8][16][8][8]
-    __nv_bfloat16 *sB = sA + TC_ROWS * a.rank;                         // SV^T    [K/8][16][8][8]
+    __nv_bfloat16 *sA = reinterpret_cast<__nv_bfloat16 *>(smem);       // U rows  [16 chunks][K/8][8][8]
+    __nv_bfloat16 *sB = sA + TC_ROWS * a.rank;                         // SV^T    [K/8][128][8]
     __nv_bfloat16 *sCS = sB + TC_N * a.rank;                           // cos/sin rows [128][TC_PITCH]
     // output rows [128][TC_PITCH]: in the operand tiles once the MMAs have
     // consumed them, past the cos/sin rows when the tiles are smaller (low rank)
     const bool o_in_ops = 2 * a.rank >= TC_PITCH;
     __nv_bfloat16 *sO = o_in_ops ? sA : sCS + TC_ROWS * TC_PITCH;
     __shared__ uint32_t s_tmem;
-    __shared__ __align__(8) uint64_t s_bar;
+    __shared__ __align__(8) uint64_t s_bar;    // the MMAs are complete
+    __shared__ __align__(8) uint64_t s_bar_a;  // the U rows have landed
+    __shared__ __align__(8) uint64_t s_bar_b;  // SV^T has landed
     __shared__ int s_chunk[TC_CHUNKS], s_dst[TC_CHUNKS];
 
     const int bh = blockIdx.y;
@@ -100,7 +124,18 @@ __global__ void __launch_bounds__(TC_THREADS) gather_gemm_tc_kernel(GatherGemmAr
     const int hi = a.hi ? a.hi[bh] : a.M;
     if (j0 + TC_CHUNKS <= lo || j0 >= hi) return;  // uniform: before any tensor-memory use
     const int tid = threadIdx.x, warp = tid >> 5;
+    const int kc = a.rank / 8;
+    const unsigned chunk_bytes = (unsigned)kc * 128u;  // 8 rows x rank, bf16
 
+    if (tid == 0) {
+        mbar_init(&s_bar, 1);
+        mbar_init(&s_bar_a, 1);
+        mbar_init(&s_bar_b, 1);
+        mbar_fence_init();
+        // SV^T of the head does not depend on the chunk ids: requested first
+        mbar_arrive_expect_tx(&s_bar_b, 16u * chunk_bytes);
+        tc_tma4(sB, &tmB, bh, &s_bar_b);
+    }
     if (tid < TC_CHUNKS) {
         const int j = j0 + tid;
         int c = -1, d = -1;
@@ -125,28 +160,21 @@ __global__ void __launch_bounds__(TC_THREADS) gather_gemm_tc_kernel(GatherGemmAr
                      ::"r"(smem_u32(&s_tmem)), "r"(TC_TMEM_COLS) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
-    if (tid == 0) {
-        mbar_init(&s_bar, 1);
-        mbar_fence_init();
-    }
     __syncthreads();
 
-    // ---- operands into the core-matrix layout (rows of missing chunks are zero)
-    const int kc = a.rank / 8;
+    // ---- U rows of the chunks: one tensor copy per chunk, straight into the
+    //      core-matrix layout; the rows of missing chunks are zero
+    if (tid == 0) {
+        unsigned n = 0;
+        for (int e = 0; e < TC_CHUNKS; ++e) n += s_chunk[e] >= 0 ? 1u : 0u;
+        mbar_arrive_expect_tx(&s_bar_a, n * chunk_bytes);
+    }
+    __syncwarp();
+    if (tid < TC_CHUNKS && s_chunk[tid] >= 0)
+        tc_tma3(sA + tid * kc * 64, &tmU, b * a.ctx + s_chunk[tid] * 8, 0, &s_bar_a);
+    for (int p = tid; p < TC_CHUNKS * kc * 8; p += TC_THREADS)
+        if (s_chunk[p / (kc * 8)] < 0) st_v4(sA + p * 8, make_uint4(0, 0, 0, 0));
     {
-        const __nv_bfloat16 *Ub = a.U + (int64_t)b * a.ctx * a.rank;
-        for (int p = tid; p < TC_ROWS * kc; p += TC_THREADS) {
-            const int r = p / kc, c = p % kc;
-            const int ch = s_chunk[r >> 3];
-            __nv_bfloat16 *dst = sA + tc_off(r, c * 8);
-            if (ch >= 0) tc_cp16(dst, Ub + ((int64_t)ch * 8 + (r & 7)) * a.rank + c * 8);
-            else st_v4(dst, make_uint4(0, 0, 0, 0));
-        }
-        const __nv_bfloat16 *Bb = a.SVt + (int64_t)bh * TC_N * a.rank;
-        for (int p = tid; p < TC_N * kc; p += TC_THREADS) {
-            const int n = p / kc, c = p % kc;
-            tc_cp16(sB + tc_off(n, c * 8), Bb + (int64_t)n * a.rank + c * 8);
-        }
         if (ROPE != 0) {
             // cos/sin rows of the output rows' positions, for the epilogue
             const int csp = ROPE == 1 ? 16 : 8;  // 16-byte pieces per row
@@ -157,9 +185,15 @@ __global__ void __launch_bounds__(TC_THREADS) gather_gemm_tc_kernel(GatherGemmAr
                 if (ch >= 0 && pos < a.cs_rows) tc_cp16(sCS + r * TC_PITCH + c * 8, a.cos_sin + pos * a.cs_stride + c * 8);
             }
         }
-        asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
-        // generic-proxy writes of shared memory become visible to the tensor core
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        // generic-proxy writes of shared memory (zero rows) become visible to the tensor core
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    // bounded waits: a copy that never lands is reported, it does not hang the GPU
+    if (!mbar_wait(&s_bar_b, 0) || !mbar_wait(&s_bar_a, 0)) {
+        if ((tid & 31) == 0) report_dev_error(DEV_ERR_WAIT);
+        mbar_wait(&s_bar_b, 0);  // the copies must land before the memory is reused
+        mbar_wait(&s_bar_a, 0);
     }
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -169,7 +203,8 @@ __global__ void __launch_bounds__(TC_THREADS) gather_gemm_tc_kernel(GatherGemmAr
     if (tid == 0) {
         const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
         for (int ks = 0; ks < a.rank / 16; ++ks) {
-            const uint64_t ad = tc_sdesc(a0 + (uint32_t)ks * 2u * TC_LBO, TC_LBO, TC_SBO);
+            // A: pieces 128 bytes apart, 8-row groups (chunks) rank*16 bytes apart
+            const uint64_t ad = tc_sdesc(a0 + (uint32_t)ks * 256u, 128u, chunk_bytes);
             const uint64_t bd = tc_sdesc(b0 + (uint32_t)ks * 2u * TC_LBO, TC_LBO, TC_SBO);
             const uint32_t acc = ks > 0 ? 1u : 0u;
             asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
@@ -184,6 +219,9 @@ __global__ void __launch_bounds__(TC_THREADS) gather_gemm_tc_kernel(GatherGemmAr
         if ((tid & 31) == 0) report_dev_error(DEV_ERR_WAIT);
         mbar_wait(&s_bar, 0);  // the MMAs must be done before the memory is released
     }
+    // the cos/sin rows of the epilogue (every thread's cp.async) have landed
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 
     // ---- epilogue: warp w (and w+4) reads rows 32(w%4) .. +31, one row per
@@ -258,17 +296,71 @@ size_t gg_tc_smem_bytes(int rank)
     return ops + tile + (2 * rank >= TC_PITCH ? 0 : tile) + 1024;
 }
 
+typedef CUresult (*TensorMapEncodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                         const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
+                                         CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                         CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled, reached through the runtime's driver entry points
+// (the library does not link libcuda itself); null if it cannot be found.
+static TensorMapEncodeTiled tensor_map_encoder()
+{
+    static const TensorMapEncodeTiled fn = []() -> TensorMapEncodeTiled {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        return reinterpret_cast<TensorMapEncodeTiled>(p);
+    }();
+    return fn;
+}
+
+// Tensor map of a bf16 matrix whose rows are rank/8 pieces of 16 bytes, viewed
+// as [outer][rows][pieces][8] with the pieces as the outer box dimension
+// (dims innermost first: 8 elements, rows, pieces, outer).
+static int tc_tensor_map(CUtensorMap *m, const void *base, uint64_t rows, uint64_t outer, bool four_d, int rank,
+                         uint32_t box_rows, const char *name)
+{
+    const TensorMapEncodeTiled enc = tensor_map_encoder();
+    SKV_CHECK_SUPPORTED(enc != nullptr, "cuTensorMapEncodeTiled is not available from the driver");
+    const uint64_t row_bytes = (uint64_t)rank * 2;
+    const cuuint64_t dims[4] = {8, rows, (cuuint64_t)(rank / 8), outer};
+    const cuuint64_t strides[3] = {row_bytes, 16, row_bytes * rows};  // of dims 1..3, bytes
+    const cuuint32_t box[4] = {8, box_rows, (cuuint32_t)(rank / 8), 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, four_d ? 4u : 3u, const_cast<void *>(base), dims,
+                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled failed for %s (CUresult %d)", name, (int)r);
+        return SKV_ERR_CUDA;
+    }
+    return SKV_OK;
+}
+
 int launch_gather_gemm_tc(const GatherGemmArgs &a, int rope, int nbh, cudaStream_t stream)
 {
+    SKV_CHECK_ARG(aligned(a.U, 16) && aligned(a.SVt, 16), "U and SV^T must be 16-byte aligned");
+    SKV_CHECK_ARG(nbh % a.H == 0, "batch x heads must be a multiple of heads");
     const int smem = (int)gg_tc_smem_bytes(a.rank);
     dim3 grid(ceil_div(a.M, TC_CHUNKS), nbh);
     const void *fn = rope == 0 ? (const void *)gather_gemm_tc_kernel<0>
                    : rope == 1 ? (const void *)gather_gemm_tc_kernel<1> : (const void *)gather_gemm_tc_kernel<2>;
     int st = ensure_smem_attr(fn, smem, "gather_gemm_tc_kernel");
     if (st) return st;
-    if (rope == 0) gather_gemm_tc_kernel<0><<<grid, TC_THREADS, smem, stream>>>(a);
-    else if (rope == 1) gather_gemm_tc_kernel<1><<<grid, TC_THREADS, smem, stream>>>(a);
-    else gather_gemm_tc_kernel<2><<<grid, TC_THREADS, smem, stream>>>(a);
+    CUtensorMap tmU, tmB;
+    // U: every sequence's rows in one dimension (B * ctx rows), one chunk of 8 rows per box
+    st = tc_tensor_map(&tmU, a.U, (uint64_t)(nbh / a.H) * (uint64_t)a.ctx, 1, false, a.rank, 8, "U");
+    if (st) return st;
+    // SV^T: 128 rows per (sequence, head), one head per box
+    st = tc_tensor_map(&tmB, a.SVt, TC_N, (uint64_t)nbh, true, a.rank, TC_N, "SV^T");
+    if (st) return st;
+    if (rope == 0) gather_gemm_tc_kernel<0><<<grid, TC_THREADS, smem, stream>>>(a, tmU, tmB);
+    else if (rope == 1) gather_gemm_tc_kernel<1><<<grid, TC_THREADS, smem, stream>>>(a, tmU, tmB);
+    else gather_gemm_tc_kernel<2><<<grid, TC_THREADS, smem, stream>>>(a, tmU, tmB);
     return check_launch("gather_gemm_tc_kernel");
 }
 
