@@ -153,30 +153,29 @@ def link_bandwidth_gbs(sizes=(64 << 20, 256 << 20), reps=8) -> float:
     return best
 
 
-def sm_read_link(cache, flush, misses_per_head=(2048, 256), reps=5) -> dict:
-    """Host-link rate of reads issued by the SMs, measured in-run with the library's own
-    zero-copy fetch kernel (``skv_decode_gather_values`` -> ``fetch_misses_kernel``, 16 chunks
-    of 2 KiB per CTA) from layer 0's page-locked value store: random distinct chunks of every
-    kv head of sequence 0 into a scratch buffer, the L2 flushed before each launch, CUDA events
-    on the launching stream.  For each entry of ``misses_per_head``: the median duration of a
-    launch and its rate; the first entry (32 MB at config 1) gives the sustained rate, the second
-    (the step's 4 MB of misses) the rate of one step-sized burst, ramp-up and drain included."""
+def sm_read_link(flush, heads=8, chunks=4096, misses_per_head=(2048, 256), reps=5) -> dict:
+    """Host-link rate of reads issued by the SMs: a zero-copy pinned-read microbenchmark run
+    in-run with the library's own fetch kernel (``skv_decode_gather_values`` ->
+    ``fetch_misses_kernel``, 16 chunks of 2 KiB per CTA).  The source is a 64 MB page-locked
+    buffer allocated after the NUMA binding, like the value store, viewed as ``heads`` heads of
+    ``chunks`` chunks; each launch reads random distinct chunks of every head into a device
+    buffer, with the L2 flushed before it and CUDA events on the launching stream.  For each
+    entry of ``misses_per_head``: the median duration of a launch and its rate; the first
+    entry (32 MB) gives the sustained rate, the second (4 MB, one config-1 step's misses) the
+    rate of one step-sized burst, ramp-up and drain included."""
     import ctypes
     from shadowkv_b200._lib import DecodeGeom, check, lib
-    host = cache.v_cache_cpu[0][:1]  # [1][H][host_chunks][1024], contiguous, page-locked
-    H, nch = host.shape[1], host.shape[2]
-    valid = min(nch, cache.k_landmark.shape[-2])  # chunks that hold prompt values
+    host = torch.empty(1, heads, chunks, 1024, dtype=torch.bfloat16).pin_memory()
     gen = torch.Generator().manual_seed(7)
     out = {}
     for M in misses_per_head:
-        M = min(M, valid)
-        geom = DecodeGeom(1, H, H, 128, 8, 8, M, 0, nch, nch * 8, 8 * M, 0, 0, 128, 0, 1.0)
-        v_buf = torch.empty(H, 8 * M, 128, dtype=torch.bfloat16, device="cuda")
-        slot = torch.arange(M, dtype=torch.int32).repeat(H, 1).cuda()
-        count = torch.full((H,), M, dtype=torch.int32, device="cuda")
+        geom = DecodeGeom(1, heads, heads, 128, 8, 8, M, 0, chunks, chunks * 8, 8 * M, 0, 0, 128, 0, 1.0)
+        v_buf = torch.empty(heads, 8 * M, 128, dtype=torch.bfloat16, device="cuda")
+        slot = torch.arange(M, dtype=torch.int32).repeat(heads, 1).cuda()
+        count = torch.full((heads,), M, dtype=torch.int32, device="cuda")
         times = []
         for r in range(reps + 1):
-            chunk = torch.stack([torch.randperm(valid, generator=gen)[:M] for _ in range(H)]).to(torch.int32).cuda()
+            chunk = torch.stack([torch.randperm(chunks, generator=gen)[:M] for _ in range(heads)]).to(torch.int32).cuda()
             flush.zero_()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             st = torch.cuda.current_stream()
@@ -189,23 +188,22 @@ def sm_read_link(cache, flush, misses_per_head=(2048, 256), reps=5) -> dict:
             if r:  # the first launch warms the kernel up
                 times.append(a.elapsed_time(b) * 1e3)
         us = statistics.median(times)
-        nbytes = H * M * 2048
+        nbytes = heads * M * 2048
         out[M] = {"bytes": nbytes, "us": us, "gbs": nbytes / (us * 1e-6) / 1e9}
         del v_buf
+    del host
     return out
 
 
-def sm_link_fields(sm_link: dict, host_b: float, hbm_b: float, hbm_peak: float, ms_step: float) -> dict:
-    """``step_roofline`` context from ``sm_read_link``: the sustained rate of SM-issued host
-    reads, the roofline time at that rate, and the duration of one step-sized burst."""
+def zero_copy_peak(sm_link: dict) -> tuple[float, str, dict]:
+    """The host-link peak of the roofline from ``sm_read_link``: the sustained rate of the
+    zero-copy pinned-read microbenchmark (its largest size), how it was measured, and the
+    step-sized burst beside it."""
     big, burst = (sm_link[k] for k in sorted(sm_link, reverse=True)[:2])
-    t_sm = max(hbm_b / (hbm_peak * 1e9), host_b / (big["gbs"] * 1e9))
-    return {"link_sm_read_gbs": big["gbs"],
-            "link_sm_read_kind": (f"measured in-run: fetch_misses_kernel (zero-copy, 16 chunks of 2 KiB per "
-                                  f"CTA) over {big['bytes'] / 1e6:.1f} MB of random chunks of the value store, "
-                                  f"L2 flushed, median of 5 launches"),
-            "link_sm_read_burst": {"bytes": burst["bytes"], "us": burst["us"], "gbs": burst["gbs"]},
-            "t_roof_sm_read_us": t_sm * 1e6, "frac_sm_read": t_sm / (ms_step * 1e-3)}
+    kind = (f"measured in-run: zero-copy pinned-read microbenchmark, the library's fetch_misses_kernel "
+            f"(16 chunks of 2 KiB per CTA) over {big['bytes'] / 1e6:.1f} MB of random 2 KiB chunks of a "
+            f"64 MB page-locked buffer, L2 flushed, median of 5 launches")
+    return big["gbs"], kind, {"bytes": burst["bytes"], "us": burst["us"], "gbs": burst["gbs"]}
 
 
 def algorithmic_bytes(cache, misses: int, seq_len: int):
@@ -467,9 +465,12 @@ def run_b200(args, world, rank, local):
     # link peak is the best of the measurements before and after the timed steps
     link_samples = [link_peak, link_bandwidth_gbs()]
     link_peak = max(link_samples)
-    # the same link read by the SMs (the step's own fetch path), sustained and as one
-    # step-sized burst: what the attention phase can reach, against the copy-engine peak
-    sm_link = sm_read_link(cache, flush) if NL == 1 else None
+    # the link as the step's kernels read it: the zero-copy pinned-read microbenchmark (the
+    # library's own fetch kernel), sustained and as one step-sized burst.  Its sustained rate
+    # is the host-link peak of the roofline (the step's reads are issued by the SMs: the
+    # missed chunks are known only on the device); the copy-engine figure is reported beside it
+    link_ce = link_peak
+    link_zc, link_zc_kind, link_burst = zero_copy_peak(sm_read_link(flush))
 
     # ---- per-kernel times.  The one-call step: the same step captured once more with CUDA
     # events around each kv-head group's kernels (skv_decode_step_timing: event nodes on the
@@ -529,7 +530,8 @@ def run_b200(args, world, rank, local):
     hit_rate = 1.0 - misses / (B * Hkv * cache.select_sets)
     hbm_1, host_1 = algorithmic_bytes(cache, misses, statistics.mean(seqlens))  # one layer, one launch
     hbm_b, host_b = hbm_1 * NL, host_1 * NL  # the misses of layer 0 stand for every layer of the step
-    t_roof = max(hbm_b / (hbm_peak * 1e9), host_b / (link_peak * 1e9))
+    t_roof = max(hbm_b / (hbm_peak * 1e9), host_b / (link_zc * 1e9))
+    t_roof_ce = max(hbm_b / (hbm_peak * 1e9), host_b / (link_ce * 1e9))
     if graph_timed and link_bytes_us[1]:
         # host bytes of the step over the attention phase of the graph-replayed step
         link_achieved = link_bytes_us[0] / (link_bytes_us[1] * 1e-6) / 1e9
@@ -592,7 +594,7 @@ def run_b200(args, world, rank, local):
         e2e_ms.append(s.elapsed_time(e))
     e2e_step = max_over_ranks(sum(e2e_ms) / len(e2e_ms), world)
     # every rank's own figures (the slowest rank sets the step; the links are per GPU)
-    mine = [rank, ms_step * 1e3, link_peak, link_achieved, hit_rate]
+    mine = [rank, ms_step * 1e3, link_zc, link_achieved, hit_rate, link_ce]
     per_rank = [mine]
     if world > 1:
         t = torch.tensor(mine, dtype=torch.float64, device="cuda")
@@ -638,17 +640,21 @@ def run_b200(args, world, rank, local):
         "roofline": {"kernel": ("fetch_misses_kernel (zero-copy V gather)" if args.split else
                                 "sparse_attend_kernel (zero-copy V gather + key reconstruction + attention)"),
                      "bound": "host_link",
-                     "achieved": link_achieved, "peak": link_peak, "unit": "GB/s",
-                     "frac": link_achieved / link_peak if link_peak else None,
+                     "achieved": link_achieved, "peak": link_zc, "unit": "GB/s",
+                     "frac": link_achieved / link_zc if link_zc else None,
                      # host-link bytes per launch: the missed chunks of this run (2048 B each);
                      # the ncu capture of this workload read exactly the missed bytes over the link
                      "traffic": host_1,
                      "traffic_kind": ("computed: missed chunks x 2048 B per "
                                       + ("step (every kv-head group's launch)" if graph_timed else "launch")
                                       + " (equal to the ncu sysmem read bytes of the capture in profiles/)"),
-                     "peak_kind": "measured in-run: pinned H2D copy-engine bandwidth (best of the "
-                                  "measurements before and after the timed steps)",
-                     "peak_samples": link_samples,
+                     "peak_kind": link_zc_kind,
+                     "peak_copy_engine": link_ce,
+                     "frac_copy_engine": link_achieved / link_ce if link_ce else None,
+                     "peak_copy_engine_kind": "measured in-run: pinned H2D copy-engine bandwidth, 64 and "
+                                              "256 MB copies (best of the measurements before and after "
+                                              "the timed steps)",
+                     "peak_copy_engine_samples": link_samples,
                      "achieved_kind": ("host bytes of the step / attention phase of the graph-replayed step "
                                        "(first attention CTA past its wait to the last attention CTA's end: "
                                        "global-timer stamps of skv_decode_step_timing)" if graph_timed else
@@ -656,8 +662,11 @@ def run_b200(args, world, rank, local):
                      "per_launch": per_launch},
         "step_roofline": {"t_roof_us": t_roof * 1e6, "t_step_us": ms_step * 1e3,
                           "frac": t_roof / (ms_step * 1e-3), "hbm_bytes": hbm_b, "host_bytes": host_b,
-                          "hbm_peak_gbs": hbm_peak, "hbm_peak_kind": peak_kind, "link_peak_gbs": link_peak,
-                          **(sm_link_fields(sm_link, host_b, hbm_b, hbm_peak, ms_step) if sm_link else {})},
+                          "hbm_peak_gbs": hbm_peak, "hbm_peak_kind": peak_kind,
+                          "link_peak_gbs": link_zc, "link_peak_kind": link_zc_kind,
+                          "link_burst": link_burst,
+                          "t_roof_copy_engine_us": t_roof_ce * 1e6, "frac_copy_engine": t_roof_ce / (ms_step * 1e-3),
+                          "link_copy_engine_gbs": link_ce},
         "e2e": {"value": tokens / (e2e_step / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
                 "inputs": ("read from page-locked host memory by the step (staging kernel in the timed region)"
@@ -670,8 +679,9 @@ def run_b200(args, world, rank, local):
                            "L2 flushed before each replay" if graph_timed else
                            "eager launches, one kernel group at a time, L2 flushed before each step"),
         "per_rank": [{"rank": int(r), "step_us": round(st, 2), "link_peak_gbs": round(lp, 2),
-                      "link_achieved_gbs": round(la, 2), "hit_rate": round(hr, 4)}
-                     for r, st, lp, la, hr in per_rank],
+                      "link_achieved_gbs": round(la, 2), "hit_rate": round(hr, 4),
+                      "link_copy_engine_gbs": round(lc, 2)}
+                     for r, st, lp, la, hr, lc in per_rank],
         "graph": used_graph,
         "gpu_launches": (select_kernels(cache) + (3 if args.split else 1)) * NL * args.steps
                         * (args.microbatch if args.microbatch > 1 and not args.split and not heads_sharded else 1)
@@ -883,6 +893,7 @@ def other_partitions(args, world, rank, local):
         out[name]["config"] = {k: r["config"][k] for k in ("workload", "global_batch", "parallelism")}
         out[name]["link_gbs"] = r["roofline"]["achieved"]
         out[name]["step_roofline_frac"] = r["step_roofline"]["frac"]
+        out[name]["step_roofline_frac_copy_engine"] = r["step_roofline"]["frac_copy_engine"]
         out[name]["clocks"] = r["clocks"]
     return out
 
