@@ -137,6 +137,37 @@ int in_to_device_ptr(const void *p, const void **dev, bool *host, const char *na
     return SKV_ERR_INVALID_ARGUMENT;
 }
 
+typedef CUresult (*TensorMapEncodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                         const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
+                                         CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                         CUtensorMapFloatOOBfill);
+
+int encode_tensor_map_bf16(CUtensorMap *m, const void *base, unsigned rank, const cuuint64_t *dims,
+                           const cuuint64_t *strides, const cuuint32_t *box, CUtensorMapSwizzle swizzle,
+                           const char *name)
+{
+    static const TensorMapEncodeTiled enc = []() -> TensorMapEncodeTiled {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        return reinterpret_cast<TensorMapEncodeTiled>(p);
+    }();
+    SKV_CHECK_SUPPORTED(enc != nullptr, "cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void *>(base), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled failed for %s (CUresult %d)", name, (int)r);
+        return SKV_ERR_CUDA;
+    }
+    return SKV_OK;
+}
+
 int device_sm_count()
 {
     static std::atomic<int> cached[64];  // 0: not queried yet (host threads may race here)

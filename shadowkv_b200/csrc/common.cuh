@@ -1,6 +1,7 @@
 // Shared helpers of the shadowkv_b200 CUDA library (sm_100a).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -69,6 +70,15 @@ inline bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_
 // Streaming multiprocessors of the current device (queried once per device;
 // 148 on a B200).  Grids are sized from it, not from a constant.
 int device_sm_count();
+
+// Tiled tensor map of a bf16 tensor for the bulk tensor copies
+// (cuTensorMapEncodeTiled, reached through the runtime's driver entry points:
+// the library does not link libcuda itself).  dims, strides (bytes, of dims
+// 1.. rank-1) and box as the driver takes them, element strides 1, no
+// interleave, 256-byte L2 promotion, zero fill out of bounds.
+int encode_tensor_map_bf16(CUtensorMap *m, const void *base, unsigned rank, const cuuint64_t *dims,
+                           const cuuint64_t *strides, const cuuint32_t *box, CUtensorMapSwizzle swizzle,
+                           const char *name);
 
 // Span pairs (see span_begin) of the kernels this host thread launches next;
 // null: no stamps.  Set by skv_decode_step while it enqueues a timed group.

@@ -29,8 +29,6 @@
 //     the GLM pairs (2i, 2i+1) of a row are in one thread; RoPE on the fp32
 //     values (cos/sin rows staged in shared memory), one rounding, rows
 //     staged in shared memory and written as coalesced 256-byte rows.
-#include <cuda.h>
-
 #include "gather_gemm.cuh"
 
 namespace skv {
@@ -296,49 +294,17 @@ size_t gg_tc_smem_bytes(int rank)
     return ops + tile + (2 * rank >= TC_PITCH ? 0 : tile) + 1024;
 }
 
-typedef CUresult (*TensorMapEncodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                         const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
-                                         CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
-                                         CUtensorMapFloatOOBfill);
-
-// cuTensorMapEncodeTiled, reached through the runtime's driver entry points
-// (the library does not link libcuda itself); null if it cannot be found.
-static TensorMapEncodeTiled tensor_map_encoder()
-{
-    static const TensorMapEncodeTiled fn = []() -> TensorMapEncodeTiled {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
-            q != cudaDriverEntryPointSuccess) {
-            cudaGetLastError();
-            return nullptr;
-        }
-        return reinterpret_cast<TensorMapEncodeTiled>(p);
-    }();
-    return fn;
-}
-
 // Tensor map of a bf16 matrix whose rows are rank/8 pieces of 16 bytes, viewed
 // as [outer][rows][pieces][8] with the pieces as the outer box dimension
 // (dims innermost first: 8 elements, rows, pieces, outer).
 static int tc_tensor_map(CUtensorMap *m, const void *base, uint64_t rows, uint64_t outer, bool four_d, int rank,
                          uint32_t box_rows, const char *name)
 {
-    const TensorMapEncodeTiled enc = tensor_map_encoder();
-    SKV_CHECK_SUPPORTED(enc != nullptr, "cuTensorMapEncodeTiled is not available from the driver");
     const uint64_t row_bytes = (uint64_t)rank * 2;
     const cuuint64_t dims[4] = {8, rows, (cuuint64_t)(rank / 8), outer};
     const cuuint64_t strides[3] = {row_bytes, 16, row_bytes * rows};  // of dims 1..3, bytes
     const cuuint32_t box[4] = {8, box_rows, (cuuint32_t)(rank / 8), 1};
-    const cuuint32_t estr[4] = {1, 1, 1, 1};
-    const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, four_d ? 4u : 3u, const_cast<void *>(base), dims,
-                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) {
-        set_error("cuTensorMapEncodeTiled failed for %s (CUresult %d)", name, (int)r);
-        return SKV_ERR_CUDA;
-    }
-    return SKV_OK;
+    return encode_tensor_map_bf16(m, base, four_d ? 4u : 3u, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE, name);
 }
 
 int launch_gather_gemm_tc(const GatherGemmArgs &a, int rope, int nbh, cudaStream_t stream)

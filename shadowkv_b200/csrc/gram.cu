@@ -10,15 +10,20 @@
 //
 // One CTA per (128 x 128 output tile of the upper triangle, slice of the T
 // rows):
-//   * 256 threads stream 64-row slices of the tile's two 128-column blocks of
-//     K through a 4-stage ring with 16-byte cp.async, straight into the
-//     no-swizzle MN-major core-matrix layout (a 16-byte piece of a K row holds
-//     8 consecutive columns = one core-matrix row; 8 rows of the slice make a
-//     core matrix; column blocks SBO = 128 B apart, 8-row groups LBO = 2 KB
-//     apart), so K needs no transposition;
-//   * one thread issues 4 tcgen05.mma (kind::f16, bf16 -> fp32, M = N = 128,
-//     K = 16, both operands MN-major) per slice, committed to the slice's
-//     mbarrier, which frees the stage for the next load (bounded waits);
+//   * one thread streams 64-row slices of the tile's two 128-column blocks of
+//     K through a 4-stage ring of tensor-map (TMA) copies, two boxes of 64
+//     columns x 64 rows per block, in the 128-byte-swizzled MN-major layout
+//     the tensor cores read (a 64-column half is 64 rows of 128 bytes, the
+//     16-byte pieces of row r permuted by r % 8; halves LBO = 8 KB apart,
+//     8-row groups SBO = 1 KB apart), so K needs no transposition.  Rows past
+//     the end of K are zero-filled by the copy.  (16-byte cp.async loads by
+//     all threads into the no-swizzle layout held the kernel to the load
+//     path's rate, long-scoreboard stalls, ~0.13 of the tensor peak);
+//   * the same thread issues 4 tcgen05.mma (kind::f16, bf16 -> fp32,
+//     M = N = 128, K = 16, both operands MN-major) per slice once its copies
+//     have landed (the stage's mbarrier), committed to the slice's MMA
+//     mbarrier, which frees the stage for the slice four ahead (bounded
+//     waits);
 //   * the fp32 accumulator (128 tensor-memory columns) is read back with
 //     tcgen05.ld and stored as the slice's partial tile.
 // gram_reduce_kernel then sums the partials of every tile in float64 and
@@ -32,11 +37,10 @@ constexpr int GR_ROWS = 64;                      // K rows (the contraction dim)
 constexpr int GR_STAGES = 4;
 constexpr int GR_OPER_BYTES = GR_ROWS * 128 * 2;  // one 128-column operand slice: 16 KB
 constexpr int GR_STAGE_BYTES = 2 * GR_OPER_BYTES;
-// stages, then slack: a descriptor read of the layout with its two offsets
-// exchanged still lands inside the allocation
-constexpr int GR_SMEM = GR_STAGES * GR_STAGE_BYTES + 32 * 1024 + 1024;
-constexpr uint32_t GR_SBO = 128;   // between 8-column blocks (MN direction)
-constexpr uint32_t GR_LBO = 2048;  // between 8-row groups (K direction): 16 column blocks x 128 B
+// stages, and the slack of the 1024-byte alignment of the swizzled tiles
+constexpr int GR_SMEM = GR_STAGES * GR_STAGE_BYTES + 1024;
+constexpr uint32_t GR_LBO = 8192;  // between the 64-column halves of an operand (MN direction)
+constexpr uint32_t GR_SBO = 1024;  // between 8-row groups (K direction): 8 rows x 128 B
 constexpr uint32_t GR_TMEM_COLS = 128;
 // kind::f16: D fp32, A and B bf16, A and B MN-major (bits 15, 16), N/8 at 17, M/16 at 24
 constexpr uint32_t GR_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) | (1u << 16) | ((128u >> 3) << 17) |
@@ -44,13 +48,17 @@ constexpr uint32_t GR_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) | 
 
 __device__ __forceinline__ uint64_t gr_sdesc(uint32_t saddr)
 {
+    // version 1 (bit 46), layout 128-byte swizzle (2 at bits 61-63)
     return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((GR_LBO >> 4) & 0x3FFFu) << 16) |
-           ((uint64_t)((GR_SBO >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+           ((uint64_t)((GR_SBO >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
 }
 
-__device__ __forceinline__ void gr_cp16(void *smem, const void *gmem)
+// Tensor-map copy of the 64 x 64 box at (column x, row y) of K, completion on bar
+__device__ __forceinline__ void gr_tma(void *smem, const CUtensorMap *map, int x, int y, uint64_t *bar)
 {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem));
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%2, %3}], [%4];"
+                 ::"r"(smem_u32(smem)), "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)) : "memory");
 }
 
 struct GramArgs {
@@ -71,12 +79,14 @@ __device__ __forceinline__ void gr_pair(int p, int nb, int *bi, int *bj)
     *bj = i + p;
 }
 
-__global__ void __launch_bounds__(GR_THREADS, 1) gram_tc_kernel(GramArgs a)
+// tmK: K as [T rows][D columns] (row stride ld), box 64 x 64, 128-byte swizzle
+__global__ void __launch_bounds__(GR_THREADS, 1) gram_tc_kernel(GramArgs a, const __grid_constant__ CUtensorMap tmK)
 {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     __shared__ uint32_t s_tmem;
-    __shared__ __align__(8) uint64_t s_mma[GR_STAGES];  // MMAs of the slice in the stage are done
+    __shared__ __align__(8) uint64_t s_full[GR_STAGES];  // the copies of the slice in the stage have landed
+    __shared__ __align__(8) uint64_t s_mma[GR_STAGES];   // MMAs of the slice in the stage are done
     __shared__ __align__(8) uint64_t s_fin;
 
     const int pair = blockIdx.x, split = blockIdx.y;
@@ -93,7 +103,10 @@ __global__ void __launch_bounds__(GR_THREADS, 1) gram_tc_kernel(GramArgs a)
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     if (tid == 0) {
-        for (int s = 0; s < GR_STAGES; ++s) mbar_init(&s_mma[s], 1);
+        for (int s = 0; s < GR_STAGES; ++s) {
+            mbar_init(&s_full[s], 1);
+            mbar_init(&s_mma[s], 1);
+        }
         mbar_init(&s_fin, 1);
         mbar_fence_init();
     }
@@ -101,64 +114,57 @@ __global__ void __launch_bounds__(GR_THREADS, 1) gram_tc_kernel(GramArgs a)
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = s_tmem;
 
-    // slice it of the CTA's rows into stage it % GR_STAGES: operand A = columns
-    // 128 bi .. +127, B = columns 128 bj .. (not loaded on the diagonal)
+    // slice it of the CTA's rows into stage it % GR_STAGES (thread 0): operand A =
+    // columns 128 bi .. +127, B = columns 128 bj .. (not loaded on the diagonal);
+    // rows past the end of K land as zeros.  The split's rows are a multiple of
+    // 64, so a slice never reaches into the next split's rows.
     auto load = [&](int it) {
-        unsigned char *st = smem + (size_t)(it % GR_STAGES) * GR_STAGE_BYTES;
+        const int s = it % GR_STAGES;
+        unsigned char *st = smem + (size_t)s * GR_STAGE_BYTES;
         const int r0 = t0 + it * GR_ROWS;
-        const int nops = diag ? 1 : 2;
-        for (int p = tid; p < nops * GR_ROWS * 16; p += GR_THREADS) {
-            const int op = p / (GR_ROWS * 16), q = p % (GR_ROWS * 16);
-            const int r = q >> 4, c = q & 15;  // row of the slice, 8-column block
-            unsigned char *dst = st + (size_t)op * GR_OPER_BYTES + (size_t)(r >> 3) * GR_LBO + (size_t)c * GR_SBO +
-                                 (size_t)(r & 7) * 16;
-            const int t = r0 + r;
-            if (t < t1) gr_cp16(dst, a.k + (int64_t)t * a.ld + (op == 0 ? bi : bj) * 128 + c * 8);
-            else st_v4(dst, make_uint4(0, 0, 0, 0));
+        mbar_arrive_expect_tx(&s_full[s], (diag ? 1u : 2u) * (unsigned)GR_OPER_BYTES);
+        for (int h = 0; h < 2; ++h) {
+            gr_tma(st + h * GR_LBO, &tmK, bi * 128 + h * 64, r0, &s_full[s]);
+            if (!diag) gr_tma(st + GR_OPER_BYTES + h * GR_LBO, &tmK, bj * 128 + h * 64, r0, &s_full[s]);
         }
     };
 
-    // GR_STAGES - 1 copy groups in flight before the loop, empty ones too: the
-    // wait_group count below assumes it however few slices the CTA has
-    for (int it = 0; it < GR_STAGES - 1; ++it) {
-        if (it < nk) load(it);
-        asm volatile("cp.async.commit_group;" ::: "memory");
-    }
-    bool ok = true;
-    for (int it = 0; it < nk; ++it) {
-        // this thread's copies of slice `it` are done, then everyone's are visible to the tensor core
-        asm volatile("cp.async.wait_group %0;" ::"n"(GR_STAGES - 2) : "memory");
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncthreads();
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        if (tid == 0) {
-            const uint32_t sa = smem_u32(smem + (size_t)(it % GR_STAGES) * GR_STAGE_BYTES);
+    if (tid == 0) {
+        for (int it = 0; it < min(GR_STAGES, nk); ++it) load(it);
+        for (int it = 0; it < nk; ++it) {
+            const int s = it % GR_STAGES;
+            // bounded waits: a copy or an MMA that never completes is reported, it does not hang the GPU
+            if (!mbar_wait(&s_full[s], (it / GR_STAGES) & 1)) {
+                report_dev_error(DEV_ERR_WAIT);
+                mbar_wait(&s_full[s], (it / GR_STAGES) & 1);
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t sa = smem_u32(smem + (size_t)s * GR_STAGE_BYTES);
             const uint32_t sb = diag ? sa : sa + GR_OPER_BYTES;
 #pragma unroll
             for (int ks = 0; ks < GR_ROWS / 16; ++ks) {
-                const uint64_t ad = gr_sdesc(sa + (uint32_t)ks * 2u * GR_LBO);
-                const uint64_t bd = gr_sdesc(sb + (uint32_t)ks * 2u * GR_LBO);
+                // 16 rows = two 8-row groups per MMA
+                const uint64_t ad = gr_sdesc(sa + (uint32_t)ks * 2u * GR_SBO);
+                const uint64_t bd = gr_sdesc(sb + (uint32_t)ks * 2u * GR_SBO);
                 const uint32_t acc = (it > 0 || ks > 0) ? 1u : 0u;
                 asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
                              "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
                              ::"r"(tmem), "l"(ad), "l"(bd), "r"(GR_IDESC), "r"(acc), "r"(0u) : "memory");
             }
             asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-                         ::"r"(smem_u32(&s_mma[it % GR_STAGES])) : "memory");
-        }
-        // the next load reuses the stage of slice it - 1: wait for that slice's MMAs
-        const int nxt = it + GR_STAGES - 1;
-        if (nxt < nk) {
-            if (it >= 1 && !mbar_wait(&s_mma[(it - 1) % GR_STAGES], ((it - 1) / GR_STAGES) & 1)) {
-                ok = false;
-                if ((tid & 31) == 0) report_dev_error(DEV_ERR_WAIT);
-                mbar_wait(&s_mma[(it - 1) % GR_STAGES], ((it - 1) / GR_STAGES) & 1);
+                         ::"r"(smem_u32(&s_mma[s])) : "memory");
+            // the stage of slice it - 1 takes slice it - 1 + GR_STAGES once that slice's MMAs are done
+            const int nxt = it - 1 + GR_STAGES;
+            if (it >= 1 && nxt < nk) {
+                const int ps = (it - 1) % GR_STAGES;
+                if (!mbar_wait(&s_mma[ps], ((it - 1) / GR_STAGES) & 1)) {
+                    report_dev_error(DEV_ERR_WAIT);
+                    mbar_wait(&s_mma[ps], ((it - 1) / GR_STAGES) & 1);
+                }
+                load(nxt);
             }
-            load(nxt);
         }
-        asm volatile("cp.async.commit_group;" ::: "memory");
     }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
     // every MMA issued so far is complete once the last commit arrives
     if (tid == 0) {
         asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
@@ -170,7 +176,6 @@ __global__ void __launch_bounds__(GR_THREADS, 1) gram_tc_kernel(GramArgs a)
         mbar_wait(&s_fin, 0);  // the MMAs must be done before the tensor memory is read or released
     }
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    (void)ok;
 
     // epilogue: warp w reads tensor-memory lanes 32 (w % 4) .. +31 (one output
     // row per thread), warps 0-3 columns 0..63, warps 4-7 columns 64..127
@@ -262,6 +267,14 @@ int skv_gram(const void *k, int tokens, int dim, int ld, double *gram, void *wor
                   workspace_bytes);
     int st = ensure_smem_attr((const void *)gram_tc_kernel, GR_SMEM, "gram_tc_kernel");
     if (st) return st;
+    CUtensorMap tmK;
+    {
+        const cuuint64_t dims[2] = {(cuuint64_t)dim, (cuuint64_t)tokens};
+        const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+        const cuuint32_t box[2] = {64, (cuuint32_t)GR_ROWS};
+        st = encode_tensor_map_bf16(&tmK, k, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, "K");
+        if (st) return st;
+    }
     GramArgs a;
     a.k = (const __nv_bfloat16 *)k;
     a.part = (float *)workspace;
@@ -273,7 +286,7 @@ int skv_gram(const void *k, int tokens, int dim, int ld, double *gram, void *wor
     a.splits = p.splits;
     a.rows_per_split = p.rows_per_split;
     cudaStream_t s = (cudaStream_t)stream;
-    gram_tc_kernel<<<dim3(p.pairs, p.splits), GR_THREADS, GR_SMEM, s>>>(a);
+    gram_tc_kernel<<<dim3(p.pairs, p.splits), GR_THREADS, GR_SMEM, s>>>(a, tmK);
     st = check_launch("gram_tc_kernel");
     if (st) return st;
     gram_reduce_kernel<<<dim3(p.pairs, 128), 128, 0, s>>>(a.part, gram, dim, p.nb, p.pairs, p.splits);
