@@ -23,7 +23,9 @@ def _keys(T, D, r_true, seed):
     return (U0 @ W0 + 0.05 * torch.randn(T, D, generator=g, device=DEV)).to(torch.bfloat16)
 
 
-@pytest.mark.parametrize("T,D", [(5000, 256), (777, 128), (122880, 1024)])
+# (5, 384): one 64-row slice with 59 rows past the end of K (zero-filled by the tensor copies),
+# three column blocks; (64, 128): exactly one slice, the diagonal block only
+@pytest.mark.parametrize("T,D", [(5000, 256), (777, 128), (122880, 1024), (5, 384), (64, 128)])
 def test_gram_matches_float64(T, D):
     from shadowkv_b200 import decode
     from shadowkv_b200._lib import device_errors
