@@ -8,11 +8,11 @@
 // singular vectors, and U = K V / s.  The T x D x D contraction (D = H*128,
 // T up to 1M) is the heavy part; the D x D eigensolve stays a library call.
 //
-// One CTA per (128 x 128 output tile of the upper triangle, slice of the T
-// rows):
-//   * one thread streams 64-row slices of the tile's two 128-column blocks of
-//     K through a 4-stage ring of tensor-map (TMA) copies, two boxes of 64
-//     columns x 64 rows per block, in the 128-byte-swizzled MN-major layout
+// One CTA per (256 x 256 output block of the upper triangle -- four 128 x 128
+// tiles, the lower one left out on the diagonal --, slice of the T rows):
+//   * one thread streams 64-row slices of the block's two 256-column operands
+//     of K through a 3-stage ring of tensor-map (TMA) copies, two boxes of 64
+//     columns x 64 rows per 128 columns, in the 128-byte-swizzled MN-major layout
 //     the tensor cores read (a 64-column half is 64 rows of 128 bytes, the
 //     16-byte pieces of row r permuted by r % 8; halves LBO = 8 KB apart,
 //     8-row groups SBO = 1 KB apart), so K needs no transposition.  Rows past
@@ -20,12 +20,14 @@
 //     all threads into the no-swizzle layout held the kernel to the load
 //     path's rate, long-scoreboard stalls, ~0.13 of the tensor peak);
 //   * the same thread issues 4 tcgen05.mma (kind::f16, bf16 -> fp32,
-//     M = N = 128, K = 16, both operands MN-major) per slice once its copies
-//     have landed (the stage's mbarrier), committed to the slice's MMA
-//     mbarrier, which frees the stage for the slice four ahead (bounded
-//     waits);
-//   * the fp32 accumulator (128 tensor-memory columns) is read back with
-//     tcgen05.ld and stored as the slice's partial tile.
+//     M = N = 128, K = 16, both operands MN-major) per tile and slice once the
+//     slice's copies have landed (the stage's mbarrier), committed to the
+//     slice's MMA mbarrier, which frees the stage for the slice three ahead
+//     (bounded waits).  A 256 x 256 block takes two operand bytes per 256
+//     flops where a single 128 x 128 tile took one per 64: the operand feed
+//     into the SM, not the tensor cores, bounded the 128 x 128 version;
+//   * the four fp32 accumulators (all 512 tensor-memory columns) are read
+//     back with tcgen05.ld and stored as the slice's partial tiles.
 // gram_reduce_kernel then sums the partials of every tile in float64 and
 // writes both triangles of the D x D result.
 #include "common.cuh"
@@ -33,15 +35,16 @@
 namespace skv {
 
 constexpr int GR_THREADS = 256;
-constexpr int GR_ROWS = 64;                      // K rows (the contraction dim) per stage
-constexpr int GR_STAGES = 4;
-constexpr int GR_OPER_BYTES = GR_ROWS * 128 * 2;  // one 128-column operand slice: 16 KB
+constexpr int GR_ROWS = 64;                        // K rows (the contraction dim) per stage
+constexpr int GR_STAGES = 3;
+constexpr int GR_BLOCK_BYTES = GR_ROWS * 128 * 2;  // one 128-column operand block of a stage: 16 KB
+constexpr int GR_OPER_BYTES = 2 * GR_BLOCK_BYTES;  // one 256-column operand of a stage: 32 KB
 constexpr int GR_STAGE_BYTES = 2 * GR_OPER_BYTES;
 // stages, and the slack of the 1024-byte alignment of the swizzled tiles
 constexpr int GR_SMEM = GR_STAGES * GR_STAGE_BYTES + 1024;
-constexpr uint32_t GR_LBO = 8192;  // between the 64-column halves of an operand (MN direction)
+constexpr uint32_t GR_LBO = 8192;  // between the 64-column halves of a 128-column block (MN direction)
 constexpr uint32_t GR_SBO = 1024;  // between 8-row groups (K direction): 8 rows x 128 B
-constexpr uint32_t GR_TMEM_COLS = 128;
+constexpr uint32_t GR_TMEM_COLS = 512;  // four 128 x 128 fp32 accumulators
 // kind::f16: D fp32, A and B bf16, A and B MN-major (bits 15, 16), N/8 at 17, M/16 at 24
 constexpr uint32_t GR_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) | (1u << 16) | ((128u >> 3) << 17) |
                               ((128u >> 4) << 24);
@@ -62,24 +65,29 @@ __device__ __forceinline__ void gr_tma(void *smem, const CUtensorMap *map, int x
 }
 
 struct GramArgs {
-    const __nv_bfloat16 *k;  // [T][ld]
-    float *part;             // [splits][pairs][128][128]
-    int T, D, ld, nb, pairs, splits, rows_per_split;
+    float *part;  // [splits][pairs][128][128], pairs of 128-column blocks
+    int T, D;
+    int nb, pairs;    // 128-column blocks and their upper-triangle pairs
+    int nb2;          // 256-column blocks (the CTAs' column blocks)
+    int splits, rows_per_split;
 };
 
-__device__ __forceinline__ void gr_pair(int p, int nb, int *bi, int *bj)
+// p enumerates the upper-triangle block pairs (bi <= bj) of n blocks row by row
+__device__ __forceinline__ void gr_pair(int p, int n, int *bi, int *bj)
 {
-    // p enumerates the upper-triangle block pairs (bi <= bj) row by row
     int i = 0;
-    while (p >= nb - i) {
-        p -= nb - i;
+    while (p >= n - i) {
+        p -= n - i;
         ++i;
     }
     *bi = i;
     *bj = i + p;
 }
 
-// tmK: K as [T rows][D columns] (row stride ld), box 64 x 64, 128-byte swizzle
+// tmK: K as [T rows][D columns] (row stride ld), box 64 x 64, 128-byte swizzle.
+// CTA (pair of 256-column blocks BI <= BJ, split): the 128 x 128 tiles (2 BI + ti,
+// 2 BJ + tj) of the upper triangle, ti, tj in {0, 1}, accumulated in tensor-memory
+// columns 128 (2 ti + tj) over the split's rows.
 __global__ void __launch_bounds__(GR_THREADS, 1) gram_tc_kernel(GramArgs a, const __grid_constant__ CUtensorMap tmK)
 {
     extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -90,12 +98,17 @@ __global__ void __launch_bounds__(GR_THREADS, 1) gram_tc_kernel(GramArgs a, cons
     __shared__ __align__(8) uint64_t s_fin;
 
     const int pair = blockIdx.x, split = blockIdx.y;
-    int bi, bj;
-    gr_pair(pair, a.nb, &bi, &bj);
-    const bool diag = bi == bj;
+    int BI, BJ;
+    gr_pair(pair, a.nb2, &BI, &BJ);
+    const bool diag = BI == BJ;
     const int t0 = split * a.rows_per_split, t1 = min(a.T, t0 + a.rows_per_split);
     const int nk = t1 > t0 ? (t1 - t0 + GR_ROWS - 1) / GR_ROWS : 0;
     const int tid = threadIdx.x, warp = tid >> 5;
+    // 128-column blocks inside K: the second block of the last 256-column block
+    // is past the end when D is an odd number of 128-column blocks
+    const int nti = min(2, a.nb - 2 * BI), ntj = min(2, a.nb - 2 * BJ);
+    // the tile (ti, tj) is computed when it is inside K and in the upper triangle
+    auto live = [&](int ti, int tj) { return ti < nti && tj < ntj && (!diag || ti <= tj); };
 
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
@@ -115,17 +128,23 @@ __global__ void __launch_bounds__(GR_THREADS, 1) gram_tc_kernel(GramArgs a, cons
     const uint32_t tmem = s_tmem;
 
     // slice it of the CTA's rows into stage it % GR_STAGES (thread 0): operand A =
-    // columns 128 bi .. +127, B = columns 128 bj .. (not loaded on the diagonal);
-    // rows past the end of K land as zeros.  The split's rows are a multiple of
-    // 64, so a slice never reaches into the next split's rows.
+    // columns 256 BI .. +255, B = columns 256 BJ .. (not loaded on the diagonal),
+    // the 128-column blocks inside K only; rows past the end of K land as zeros.
+    // The split's rows are a multiple of 64, so a slice never reaches into the
+    // next split's rows.
     auto load = [&](int it) {
         const int s = it % GR_STAGES;
         unsigned char *st = smem + (size_t)s * GR_STAGE_BYTES;
         const int r0 = t0 + it * GR_ROWS;
-        mbar_arrive_expect_tx(&s_full[s], (diag ? 1u : 2u) * (unsigned)GR_OPER_BYTES);
-        for (int h = 0; h < 2; ++h) {
-            gr_tma(st + h * GR_LBO, &tmK, bi * 128 + h * 64, r0, &s_full[s]);
-            if (!diag) gr_tma(st + GR_OPER_BYTES + h * GR_LBO, &tmK, bj * 128 + h * 64, r0, &s_full[s]);
+        mbar_arrive_expect_tx(&s_full[s], (unsigned)((nti + (diag ? 0 : ntj)) * GR_BLOCK_BYTES));
+        for (int c = 0; c < 2; ++c) {
+            for (int h = 0; h < 2; ++h) {
+                if (c < nti)
+                    gr_tma(st + c * GR_BLOCK_BYTES + h * GR_LBO, &tmK, (2 * BI + c) * 128 + h * 64, r0, &s_full[s]);
+                if (!diag && c < ntj)
+                    gr_tma(st + GR_OPER_BYTES + c * GR_BLOCK_BYTES + h * GR_LBO, &tmK, (2 * BJ + c) * 128 + h * 64,
+                           r0, &s_full[s]);
+            }
         }
     };
 
@@ -141,15 +160,21 @@ __global__ void __launch_bounds__(GR_THREADS, 1) gram_tc_kernel(GramArgs a, cons
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t sa = smem_u32(smem + (size_t)s * GR_STAGE_BYTES);
             const uint32_t sb = diag ? sa : sa + GR_OPER_BYTES;
+            for (int ti = 0; ti < 2; ++ti) {
+                for (int tj = 0; tj < 2; ++tj) {
+                    if (!live(ti, tj)) continue;
+                    const uint32_t d = tmem + (uint32_t)(2 * ti + tj) * 128u;
 #pragma unroll
-            for (int ks = 0; ks < GR_ROWS / 16; ++ks) {
-                // 16 rows = two 8-row groups per MMA
-                const uint64_t ad = gr_sdesc(sa + (uint32_t)ks * 2u * GR_SBO);
-                const uint64_t bd = gr_sdesc(sb + (uint32_t)ks * 2u * GR_SBO);
-                const uint32_t acc = (it > 0 || ks > 0) ? 1u : 0u;
-                asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-                             "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
-                             ::"r"(tmem), "l"(ad), "l"(bd), "r"(GR_IDESC), "r"(acc), "r"(0u) : "memory");
+                    for (int ks = 0; ks < GR_ROWS / 16; ++ks) {
+                        // 16 rows = two 8-row groups per MMA
+                        const uint64_t ad = gr_sdesc(sa + (uint32_t)(ti * GR_BLOCK_BYTES) + (uint32_t)ks * 2u * GR_SBO);
+                        const uint64_t bd = gr_sdesc(sb + (uint32_t)(tj * GR_BLOCK_BYTES) + (uint32_t)ks * 2u * GR_SBO);
+                        const uint32_t acc = (it > 0 || ks > 0) ? 1u : 0u;
+                        asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                                     "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
+                                     ::"r"(d), "l"(ad), "l"(bd), "r"(GR_IDESC), "r"(acc), "r"(0u) : "memory");
+                    }
+                }
             }
             asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                          ::"r"(smem_u32(&s_mma[s])) : "memory");
@@ -177,26 +202,32 @@ __global__ void __launch_bounds__(GR_THREADS, 1) gram_tc_kernel(GramArgs a, cons
     }
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 
-    // epilogue: warp w reads tensor-memory lanes 32 (w % 4) .. +31 (one output
-    // row per thread), warps 0-3 columns 0..63, warps 4-7 columns 64..127
-    {
-        const int q = warp & 3, half = warp >> 2;
-        const int r = q * 32 + (tid & 31);
-        float *dst = a.part + (((int64_t)split * a.pairs + pair) * 128 + r) * 128 + half * 64;
-        const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(half * 64);
+    // epilogue: per live tile, warp w reads tensor-memory lanes 32 (w % 4) .. +31
+    // (one output row per thread), warps 0-3 columns 0..63, warps 4-7 columns
+    // 64..127, into the partial of its 128-column block pair
+    for (int ti = 0; ti < 2; ++ti) {
+        for (int tj = 0; tj < 2; ++tj) {
+            if (!live(ti, tj)) continue;
+            const int bi = 2 * BI + ti, bj = 2 * BJ + tj;
+            const int p128 = bi * a.nb - bi * (bi - 1) / 2 + (bj - bi);  // row-major upper-triangle index
+            const int q = warp & 3, half = warp >> 2;
+            const int r = q * 32 + (tid & 31);
+            float *dst = a.part + (((int64_t)split * a.pairs + p128) * 128 + r) * 128 + half * 64;
+            const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((2 * ti + tj) * 128 + half * 64);
 #pragma unroll
-        for (int c = 0; c < 64; c += 16) {
-            uint32_t v[16];
-            asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-                         "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-                         : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
-                           "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
-                           "=r"(v[14]), "=r"(v[15])
-                         : "r"(trow + (uint32_t)c));
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            for (int c = 0; c < 64; c += 16) {
+                uint32_t v[16];
+                asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+                             "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                             : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+                               "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),
+                               "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+                             : "r"(trow + (uint32_t)c));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-            for (int i = 0; i < 16; i += 4)
-                *reinterpret_cast<uint4 *>(dst + c + i) = make_uint4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+                for (int i = 0; i < 16; i += 4)
+                    *reinterpret_cast<uint4 *>(dst + c + i) = make_uint4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+            }
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -224,7 +255,7 @@ __global__ void __launch_bounds__(128) gram_reduce_kernel(const float *part, dou
 }
 
 struct GramPlan {
-    int nb, pairs, splits, rows_per_split;
+    int nb, pairs, nb2, pairs2, splits, rows_per_split;
     size_t part_bytes;
 };
 
@@ -233,8 +264,10 @@ static GramPlan plan_gram(int T, int D)
     GramPlan p;
     p.nb = D / 128;
     p.pairs = p.nb * (p.nb + 1) / 2;
+    p.nb2 = (p.nb + 1) / 2;
+    p.pairs2 = p.nb2 * (p.nb2 + 1) / 2;
     const int sms = device_sm_count();
-    int s = max(1, sms / p.pairs);  // one CTA per SM
+    int s = max(1, sms / p.pairs2);  // one CTA per SM
     s = min(s, ceil_div(T, GR_ROWS));
     p.rows_per_split = ceil_div(ceil_div(T, s), GR_ROWS) * GR_ROWS;
     p.splits = ceil_div(T, p.rows_per_split);
@@ -276,17 +309,16 @@ int skv_gram(const void *k, int tokens, int dim, int ld, double *gram, void *wor
         if (st) return st;
     }
     GramArgs a;
-    a.k = (const __nv_bfloat16 *)k;
     a.part = (float *)workspace;
     a.T = tokens;
     a.D = dim;
-    a.ld = ld;
     a.nb = p.nb;
     a.pairs = p.pairs;
+    a.nb2 = p.nb2;
     a.splits = p.splits;
     a.rows_per_split = p.rows_per_split;
     cudaStream_t s = (cudaStream_t)stream;
-    gram_tc_kernel<<<dim3(p.pairs, p.splits), GR_THREADS, GR_SMEM, s>>>(a, tmK);
+    gram_tc_kernel<<<dim3(p.pairs2, p.splits), GR_THREADS, GR_SMEM, s>>>(a, tmK);
     st = check_launch("gram_tc_kernel");
     if (st) return st;
     gram_reduce_kernel<<<dim3(p.pairs, 128), 128, 0, s>>>(a.part, gram, dim, p.nb, p.pairs, p.splits);
