@@ -66,6 +66,20 @@ __device__ __forceinline__ void tc_tma3(void *smem, const CUtensorMap *map, int 
                  " [%0], [%1, {%2, %3, %4}], [%5];"
                  ::"r"(smem_u32(smem)), "l"(map), "r"(0), "r"(y), "r"(z), "r"(smem_u32(bar)) : "memory");
 }
+__device__ __forceinline__ void tc_tma2(void *smem, const CUtensorMap *map, int x, int y, uint64_t *bar)
+{
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%2, %3}], [%4];"
+                 ::"r"(smem_u32(smem)), "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)) : "memory");
+}
+// K-major operand in the 128-byte-swizzled layout: 64-element k-blocks of 8-row
+// atoms (8 rows x 128 bytes, the 16-byte pieces of row r permuted by r % 8),
+// 8-row groups 1 KB apart; the start steps 32 bytes per 16 k inside a block
+__device__ __forceinline__ uint64_t tc_sdesc_sw(uint32_t saddr)
+{
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | (1ull << 16) | ((uint64_t)(1024u >> 4) << 32) | (1ull << 46) |
+           (2ull << 61);
+}
 __device__ __forceinline__ void tc_tma4(void *smem, const CUtensorMap *map, int w, uint64_t *bar)
 {
     asm volatile("cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
@@ -91,10 +105,22 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, float *v)
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// ROPE: 0 none, 1 rotate-half (cos_sin width 128), 2 GLM interleaved (width 64)
-// tmU: U as [rows = B*ctx][rank/8 pieces][8], box {8, 8, rank/8} (one chunk);
-// tmB: SV^T as [B*H][128][rank/8 pieces][8], box {8, 128, rank/8, 1} (one head).
-template <int ROPE>
+// Operand bytes of U (A) or SV^T (B) in shared memory: 128 rows of rank
+// elements, padded to whole 64-element k-blocks in the swizzled layout.
+__host__ __device__ __forceinline__ int tc_oper_bytes(int rank, bool sw)
+{
+    return sw ? ((rank + 63) / 64) * 16384 : 128 * rank * 2;
+}
+
+// ROPE: 0 none, 1 rotate-half (cos_sin width 128), 2 GLM interleaved (width 64).
+// SW (rank >= 64): the operands in the 128-byte-swizzled K-major layout,
+//   tmU: U as [rows = B*ctx][rank], box {64, 8} (one chunk, one k-block),
+//   tmB: SV^T as [B*H*128][rank], box {64, 128} (one head, one k-block);
+//   a copy moves whole 128-byte rows (768 row requests per CTA at rank 160).
+// Otherwise the no-swizzle layout of 16-byte pieces,
+//   tmU: U as [rows = B*ctx][rank/8 pieces][8], box {8, 8, rank/8} (one chunk),
+//   tmB: SV^T as [B*H][128][rank/8 pieces][8], box {8, 128, rank/8, 1} (one head).
+template <int ROPE, bool SW>
 __global__ void __launch_bounds__(TC_THREADS) gather_gemm_tc_kernel(GatherGemmArgs a, const __grid_constant__ CUtensorMap tmU,
                                                                     const __grid_constant__ CUtensorMap tmB)
 {
@@ -102,12 +128,15 @@ __global__ void __launch_bounds__(TC_THREADS) gather_gemm_tc_kernel(GatherGemmAr
     // operand tiles start on a 1024-byte boundary (the tensor copies need 128;
     // the MMA descriptors of U step through it in 256-byte pieces of K)
     unsigned char *smem = reinterpret_cast<unsigned char *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    __nv_bfloat16 *sA = reinterpret_cast<__nv_bfloat16 *>(smem);       // U rows  [16 chunks][K/8][8][8]
-    __nv_bfloat16 *sB = sA + TC_ROWS * a.rank;                         // SV^T    [K/8][128][8]
-    __nv_bfloat16 *sCS = sB + TC_N * a.rank;                           // cos/sin rows [128][TC_PITCH]
+    // U rows: SW [k-block][16 chunks][8 rows x 128 B], else [16 chunks][K/8][8][8];
+    // SV^T: SW [k-block][128 rows x 128 B], else [K/8][128][8]
+    const int opb = tc_oper_bytes(a.rank, SW);
+    __nv_bfloat16 *sA = reinterpret_cast<__nv_bfloat16 *>(smem);
+    __nv_bfloat16 *sB = sA + opb / 2;
+    __nv_bfloat16 *sCS = sB + opb / 2;                                 // cos/sin rows [128][TC_PITCH]
     // output rows [128][TC_PITCH]: in the operand tiles once the MMAs have
     // consumed them, past the cos/sin rows when the tiles are smaller (low rank)
-    const bool o_in_ops = 2 * a.rank >= TC_PITCH;
+    const bool o_in_ops = opb >= TC_ROWS * TC_PITCH * 2;
     __nv_bfloat16 *sO = o_in_ops ? sA : sCS + TC_ROWS * TC_PITCH;
     __shared__ uint32_t s_tmem;
     __shared__ __align__(8) uint64_t s_bar;    // the MMAs are complete
@@ -124,6 +153,7 @@ __global__ void __launch_bounds__(TC_THREADS) gather_gemm_tc_kernel(GatherGemmAr
     const int tid = threadIdx.x, warp = tid >> 5;
     const int kc = a.rank / 8;
     const unsigned chunk_bytes = (unsigned)kc * 128u;  // 8 rows x rank, bf16
+    const int nkb = (a.rank + 63) / 64;                // 64-element k-blocks (SW)
 
     if (tid == 0) {
         mbar_init(&s_bar, 1);
@@ -131,8 +161,13 @@ __global__ void __launch_bounds__(TC_THREADS) gather_gemm_tc_kernel(GatherGemmAr
         mbar_init(&s_bar_b, 1);
         mbar_fence_init();
         // SV^T of the head does not depend on the chunk ids: requested first
-        mbar_arrive_expect_tx(&s_bar_b, 16u * chunk_bytes);
-        tc_tma4(sB, &tmB, bh, &s_bar_b);
+        if (SW) {
+            mbar_arrive_expect_tx(&s_bar_b, (unsigned)nkb * 16384u);  // whole boxes, k past rank zero-filled
+            for (int kb = 0; kb < nkb; ++kb) tc_tma2(sB + kb * 8192, &tmB, kb * 64, bh * TC_N, &s_bar_b);
+        } else {
+            mbar_arrive_expect_tx(&s_bar_b, 16u * chunk_bytes);
+            tc_tma4(sB, &tmB, bh, &s_bar_b);
+        }
     }
     if (tid < TC_CHUNKS) {
         const int j = j0 + tid;
@@ -165,13 +200,22 @@ __global__ void __launch_bounds__(TC_THREADS) gather_gemm_tc_kernel(GatherGemmAr
     if (tid == 0) {
         unsigned n = 0;
         for (int e = 0; e < TC_CHUNKS; ++e) n += s_chunk[e] >= 0 ? 1u : 0u;
-        mbar_arrive_expect_tx(&s_bar_a, n * chunk_bytes);
+        mbar_arrive_expect_tx(&s_bar_a, n * (SW ? (unsigned)nkb * 1024u : chunk_bytes));
     }
     __syncwarp();
-    if (tid < TC_CHUNKS && s_chunk[tid] >= 0)
-        tc_tma3(sA + tid * kc * 64, &tmU, b * a.ctx + s_chunk[tid] * 8, 0, &s_bar_a);
-    for (int p = tid; p < TC_CHUNKS * kc * 8; p += TC_THREADS)
-        if (s_chunk[p / (kc * 8)] < 0) st_v4(sA + p * 8, make_uint4(0, 0, 0, 0));
+    if (tid < TC_CHUNKS && s_chunk[tid] >= 0) {
+        if (SW) {
+            for (int kb = 0; kb < nkb; ++kb)
+                tc_tma2(sA + kb * 8192 + tid * 512, &tmU, kb * 64, b * a.ctx + s_chunk[tid] * 8, &s_bar_a);
+        } else {
+            tc_tma3(sA + tid * kc * 64, &tmU, b * a.ctx + s_chunk[tid] * 8, 0, &s_bar_a);
+        }
+    }
+    // rows of missing chunks are zero (16-byte pieces: SW 64 per chunk and k-block)
+    for (int p = tid; p < (SW ? nkb * TC_CHUNKS * 64 : TC_CHUNKS * kc * 8); p += TC_THREADS) {
+        const int e = SW ? (p >> 6) & (TC_CHUNKS - 1) : p / (kc * 8);
+        if (s_chunk[e] < 0) st_v4(sA + p * 8, make_uint4(0, 0, 0, 0));
+    }
     {
         if (ROPE != 0) {
             // cos/sin rows of the output rows' positions, for the epilogue
@@ -201,9 +245,17 @@ __global__ void __launch_bounds__(TC_THREADS) gather_gemm_tc_kernel(GatherGemmAr
     if (tid == 0) {
         const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
         for (int ks = 0; ks < a.rank / 16; ++ks) {
-            // A: pieces 128 bytes apart, 8-row groups (chunks) rank*16 bytes apart
-            const uint64_t ad = tc_sdesc(a0 + (uint32_t)ks * 256u, 128u, chunk_bytes);
-            const uint64_t bd = tc_sdesc(b0 + (uint32_t)ks * 2u * TC_LBO, TC_LBO, TC_SBO);
+            uint64_t ad, bd;
+            if (SW) {
+                // k-block ks / 4, 32 bytes per 16 k inside it
+                const uint32_t off = (uint32_t)(ks >> 2) * 16384u + (uint32_t)(ks & 3) * 32u;
+                ad = tc_sdesc_sw(a0 + off);
+                bd = tc_sdesc_sw(b0 + off);
+            } else {
+                // A: pieces 128 bytes apart, 8-row groups (chunks) rank*16 bytes apart
+                ad = tc_sdesc(a0 + (uint32_t)ks * 256u, 128u, chunk_bytes);
+                bd = tc_sdesc(b0 + (uint32_t)ks * 2u * TC_LBO, TC_LBO, TC_SBO);
+            }
             const uint32_t acc = ks > 0 ? 1u : 0u;
             asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
                          "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
@@ -287,11 +339,13 @@ __global__ void __launch_bounds__(TC_THREADS) gather_gemm_tc_kernel(GatherGemmAr
     }
 }
 
+static bool tc_swizzled(int rank) { return rank >= 64; }
+
 size_t gg_tc_smem_bytes(int rank)
 {
     // operands, cos/sin rows, output rows (in the operand tiles when they fit), alignment slack
-    const size_t ops = (size_t)(TC_ROWS + TC_N) * rank * 2, tile = (size_t)TC_ROWS * TC_PITCH * 2;
-    return ops + tile + (2 * rank >= TC_PITCH ? 0 : tile) + 1024;
+    const size_t opb = (size_t)tc_oper_bytes(rank, tc_swizzled(rank)), tile = (size_t)TC_ROWS * TC_PITCH * 2;
+    return 2 * opb + tile + (opb >= tile ? 0 : tile) + 1024;
 }
 
 // Tensor map of a bf16 matrix whose rows are rank/8 pieces of 16 bytes, viewed
@@ -313,20 +367,35 @@ int launch_gather_gemm_tc(const GatherGemmArgs &a, int rope, int nbh, cudaStream
     SKV_CHECK_ARG(nbh % a.H == 0, "batch x heads must be a multiple of heads");
     const int smem = (int)gg_tc_smem_bytes(a.rank);
     dim3 grid(ceil_div(a.M, TC_CHUNKS), nbh);
-    const void *fn = rope == 0 ? (const void *)gather_gemm_tc_kernel<0>
-                   : rope == 1 ? (const void *)gather_gemm_tc_kernel<1> : (const void *)gather_gemm_tc_kernel<2>;
-    int st = ensure_smem_attr(fn, smem, "gather_gemm_tc_kernel");
-    if (st) return st;
+    int st = SKV_OK;
     CUtensorMap tmU, tmB;
-    // U: every sequence's rows in one dimension (B * ctx rows), one chunk of 8 rows per box
-    st = tc_tensor_map(&tmU, a.U, (uint64_t)(nbh / a.H) * (uint64_t)a.ctx, 1, false, a.rank, 8, "U");
+    const bool sw = tc_swizzled(a.rank);
+    const uint64_t urows = (uint64_t)(nbh / a.H) * (uint64_t)a.ctx;  // every sequence's rows of U
+    if (sw) {
+        const cuuint64_t ustr[1] = {(cuuint64_t)a.rank * 2};
+        const cuuint64_t udims[2] = {(cuuint64_t)a.rank, urows}, bdims[2] = {(cuuint64_t)a.rank, (cuuint64_t)nbh * TC_N};
+        const cuuint32_t ubox[2] = {64, 8}, bbox[2] = {64, (cuuint32_t)TC_N};
+        st = encode_tensor_map_bf16(&tmU, a.U, 2, udims, ustr, ubox, CU_TENSOR_MAP_SWIZZLE_128B, "U");
+        if (st) return st;
+        st = encode_tensor_map_bf16(&tmB, a.SVt, 2, bdims, ustr, bbox, CU_TENSOR_MAP_SWIZZLE_128B, "SV^T");
+        if (st) return st;
+    } else {
+        // U: one chunk of 8 rows per box; SV^T: 128 rows per (sequence, head), one head per box
+        st = tc_tensor_map(&tmU, a.U, urows, 1, false, a.rank, 8, "U");
+        if (st) return st;
+        st = tc_tensor_map(&tmB, a.SVt, TC_N, (uint64_t)nbh, true, a.rank, TC_N, "SV^T");
+        if (st) return st;
+    }
+    const void *fn = sw ? (rope == 0 ? (const void *)gather_gemm_tc_kernel<0, true>
+                           : rope == 1 ? (const void *)gather_gemm_tc_kernel<1, true>
+                                       : (const void *)gather_gemm_tc_kernel<2, true>)
+                        : (rope == 0 ? (const void *)gather_gemm_tc_kernel<0, false>
+                           : rope == 1 ? (const void *)gather_gemm_tc_kernel<1, false>
+                                       : (const void *)gather_gemm_tc_kernel<2, false>);
+    st = ensure_smem_attr(fn, smem, "gather_gemm_tc_kernel");
     if (st) return st;
-    // SV^T: 128 rows per (sequence, head), one head per box
-    st = tc_tensor_map(&tmB, a.SVt, TC_N, (uint64_t)nbh, true, a.rank, TC_N, "SV^T");
-    if (st) return st;
-    if (rope == 0) gather_gemm_tc_kernel<0><<<grid, TC_THREADS, smem, stream>>>(a, tmU, tmB);
-    else if (rope == 1) gather_gemm_tc_kernel<1><<<grid, TC_THREADS, smem, stream>>>(a, tmU, tmB);
-    else gather_gemm_tc_kernel<2><<<grid, TC_THREADS, smem, stream>>>(a, tmU, tmB);
+    void *args[] = {const_cast<GatherGemmArgs *>(&a), &tmU, &tmB};
+    SKV_CUDA(cudaLaunchKernel(fn, grid, dim3(TC_THREADS), args, (size_t)smem, stream));
     return check_launch("gather_gemm_tc_kernel");
 }
 
