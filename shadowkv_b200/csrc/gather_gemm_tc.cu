@@ -10,17 +10,22 @@
 // One CTA computes 16 chunks (M = 128 rows) x 128 output dims over the full
 // rank K:
 //   * the operands come in through tensor-map (TMA) copies that write the
-//     no-swizzle K-major core-matrix layout of the tensor-core descriptors
-//     directly (8-row x 16-byte core matrices of 128 contiguous bytes): the
-//     tensor maps view a row of U or SV^T as rank/8 pieces of 16 bytes, with
-//     the piece index as the outermost box dimension, so one copy of box
-//     {8 elements, rows, rank/8} lands piece-major.  SV^T of the head is one
-//     copy (rows 16 bytes apart, pieces 2 KiB apart), requested before the
-//     chunk ids are known; the U rows of each chunk are one copy of 8 rows
-//     (pieces 128 bytes apart, chunks rank*16 bytes apart).  16-byte cp.async
-//     loads through the SM's load/store path held a CTA's 112 KB of operands
-//     to about 25 GB/s per SM; the copies do not take that path.  The cos/sin
-//     rows of the epilogue still come in by cp.async (padded rows);
+//     tensor cores' shared-memory layout directly, with no relayout pass and
+//     without the SM's load/store path (16-byte cp.async loads through it held
+//     a CTA's 112 KB of operands to about 25 GB/s per SM).  SV^T of the head
+//     is requested before the chunk ids are known.
+//       - rank >= 64: the 128-byte-swizzled K-major layout.  A copy of a box of
+//         64 k x 8 rows (one chunk of U) or 64 k x 128 rows (SV^T of the head)
+//         per 64-element k-block writes 8-row x 128-byte atoms, 8-row groups
+//         1 KB apart; k past the rank is zero-filled.  Every request moves a
+//         whole 128-byte row.
+//       - smaller ranks: the no-swizzle K-major core-matrix layout (8-row x
+//         16-byte core matrices).  The maps view a row as rank/8 pieces of 16
+//         bytes with the piece index as the outermost box dimension, so one
+//         copy of box {8 elements, rows, rank/8} lands piece-major: SV^T rows
+//         16 bytes apart and pieces 2 KiB apart, a chunk's pieces 128 bytes
+//         apart and chunks rank*16 bytes apart.
+//     The cos/sin rows of the epilogue come in by cp.async (padded rows);
 //   * one thread issues K/16 tcgen05.mma (kind::f16, bf16 x bf16 -> fp32,
 //     M=128, N=128) into 128 columns of tensor memory and commits them to an
 //     mbarrier (bounded wait);
