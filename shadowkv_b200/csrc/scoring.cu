@@ -165,6 +165,10 @@ __global__ void __launch_bounds__(ST_THREADS, 2) score_tma_kernel(ScoreArgs a)
             bulk_g2s(sT + (size_t)i * ST_ROWS * 128, lmh + (int64_t)r0 * 128, (unsigned)nr * 256u, &full[i]);
         }
     }
+    // Everything above reads only the landmarks.  A launch that follows the
+    // step's input staging kernel as its programmatic dependent waits here for
+    // the staged inputs (a no-op for an ordinary launch).
+    pdl_wait();
     // query rows of the group in shared memory (rows >= G are zero).  The raw
     // rows (and the cos/sin row) are loaded in one parallel round first, so the
     // prologue costs one memory latency, not one per loop trip.
@@ -523,7 +527,7 @@ static int check_geom(const skv_decode_geom *g)
 static int run_select(const skv_decode_geom *g, const ScoreArgs &sa_in, const int64_t *landmark_idx,
                       int32_t *slots, int32_t *miss_slot, int32_t *miss_chunk, int32_t *miss_count,
                       void *workspace, size_t workspace_bytes, bool append, cudaStream_t s,
-                      const SelectArgs *fetch = nullptr, bool *fetched = nullptr)
+                      const SelectArgs *fetch = nullptr, bool *fetched = nullptr, bool after_stage = false)
 {
     if (fetched) *fetched = false;
     const SelectPlan p = plan_select(g);
@@ -548,7 +552,23 @@ static int run_select(const skv_decode_geom *g, const ScoreArgs &sa_in, const in
     int st = ensure_smem_attr(fn, smem, "score_tma_kernel");
     if (st) return st;
     void *kargs[] = {&sa};
-    SKV_CUDA(cudaLaunchKernel(fn, dim3(p.nsplit, BH), dim3(ST_THREADS), kargs, (size_t)smem, s));
+    if (after_stage) {
+        // programmatic dependent of the staging kernel: the landmark tiles are
+        // requested before the kernel waits for the staged inputs (pdl_wait)
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(p.nsplit, BH, 1);
+        cfg.blockDim = dim3(ST_THREADS, 1, 1);
+        cfg.dynamicSmemBytes = (size_t)smem;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        SKV_CUDA(cudaLaunchKernelExC(&cfg, fn, kargs));
+    } else {
+        SKV_CUDA(cudaLaunchKernel(fn, dim3(p.nsplit, BH), dim3(ST_THREADS), kargs, (size_t)smem, s));
+    }
     st = check_launch("score_tma_kernel");
     if (st) return st;
     SelectArgs a = {};
@@ -665,7 +685,7 @@ int append_select_launch(const skv_decode_geom *g, const void *q, const void *k_
                          int row, const void *landmarks, const int64_t *landmark_idx, int32_t *slots,
                          int32_t *miss_slot, int32_t *miss_chunk, int32_t *miss_count, void *workspace,
                          size_t workspace_bytes, cudaStream_t stream, const int32_t *row_dev,
-                         const SelectArgs *fetch, bool *fetched)
+                         const SelectArgs *fetch, bool *fetched, bool after_stage)
 {
     int st = check_geom(g);
     if (st) return st;
@@ -695,7 +715,7 @@ int append_select_launch(const skv_decode_geom *g, const void *q, const void *k_
     sa.cs_stride = g->cos_sin_stride;
     sa.cs_rows = g->cos_sin_rows;
     return run_select(g, sa, landmark_idx, slots, miss_slot, miss_chunk, miss_count, workspace, workspace_bytes,
-                      true, stream, fetch, fetched);
+                      true, stream, fetch, fetched, after_stage);
 }
 
 }  // namespace skv

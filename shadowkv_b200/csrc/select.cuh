@@ -160,12 +160,16 @@ int append_select_launch(const skv_decode_geom *g, const void *q, const void *k_
                          int row, const void *landmarks, const int64_t *landmark_idx, int32_t *slots,
                          int32_t *miss_slot, int32_t *miss_chunk, int32_t *miss_count, void *workspace,
                          size_t workspace_bytes, cudaStream_t stream, const int32_t *row_dev,
-                         const SelectArgs *fetch = nullptr, bool *fetched = nullptr);
+                         const SelectArgs *fetch = nullptr, bool *fetched = nullptr, bool after_stage = false);
 // fetch (optional): the early-fetch fields of SelectArgs (v_host .. v_buf and
 // q_rot .. seq_len, pstride; already validated); when the geometry allows it
 // the selection runs as the FETCH variant, which leaves the missed rows' keys
 // and values in k_buf / v_buf and writes the step's attention output, and
 // *fetched is set.
+// after_stage: the kernel before this call on the stream is the step's input
+// staging kernel; the scoring kernel is then launched as its programmatic
+// dependent and streams its first landmark tiles while the staged inputs are
+// still crossing the host link.
 
 // skv_decode_sparse_attention with a device-side position: row_dev (optional)
 // holds the row the step appended at; the attention covers [0, *row_dev + 1),

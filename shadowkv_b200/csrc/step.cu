@@ -146,6 +146,9 @@ struct StageArgs {
 
 __global__ void __launch_bounds__(256) stage_inputs_kernel(StageArgs a)
 {
+    // the scoring kernel after it may start (its landmark tiles) at once; it
+    // waits for this grid before reading the staged inputs
+    pdl_launch_dependents();
     int p = blockIdx.x * blockDim.x + threadIdx.x;  // piece over the staged inputs, in order
 #pragma unroll
     for (int j = 0; j < STAGE_INPUTS; ++j) {
@@ -342,7 +345,7 @@ int skv_decode_step(const skv_decode_geom *g, const void *q, const void *k_new, 
                                       cos_sin, qo, kb, vb, row,
                                       (const __nv_bfloat16 *)landmarks + h0 * g->num_landmarks * 128,
                                       landmark_idx + h0 * g->num_landmarks, slots + h0 * g->select_sets, ms, mc, mn,
-                                      w + L.sel, L.sel_bytes, s, row_dev, early ? &fx : nullptr, &fetched);
+                                      w + L.sel, L.sel_bytes, s, row_dev, early ? &fx : nullptr, &fetched, any_host);
         if (st) return st;
         if (fetched) return SKV_OK;  // the selection kernel computed the attention too
         return sparse_attention_launch(&gp, qo, U, svt, cos_sin,
