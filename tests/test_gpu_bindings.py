@@ -233,7 +233,9 @@ def test_rope_push_cache(skv, glm, variant):
 
 # --------------------------------------------------------------------------- GEMMs
 
-@pytest.mark.parametrize("rank", [160, 64, 256])
+# ranks >= 64 take the 128-byte-swizzled operand layout (160: a partial last
+# k-block), 32 and 48 the 16-byte-piece layout
+@pytest.mark.parametrize("rank", [160, 64, 256, 32, 48])
 def test_batch_gather_gemm(skv, rank):
     rng = np.random.default_rng(rank)
     B, H, T, budget = 2, 3, 4096, 512
